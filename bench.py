@@ -1,0 +1,476 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 W4A4 prefix-LM GEMM path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+One step = the W4A4 work of the Gemma-2B prefix LM for one 776-token robot
+observation prefix (the metric's "776-tok prefix"):
+18 layers x {int4_gemm3 q/k/v (2048 -> 2048+256+256), int4_gemm o_proj
+(2048 -> 2048), int4_gemm2_tiled gate/up (2048 -> 2 x 16384, fragment-major
+weights), int4_gemm down_proj (16384 -> 2048)}, every op = one fused
+Hadamard+INT4 activation quant + one tensor-core GEMM launch.  The ops are
+chained (q -> o_proj input, o -> gate/up input, gate -> down input, down ->
+next layer) so each consumes the previous op's output as in the model; the
+attention / GeGLU glue between them is not part of this path.  Weights are
+random-init N(0, 1/sqrt(K)) packed with the reference's format; activations
+are synthetic N(0, 1) with 1% outlier channels x20.  The 18 layers' weights
+(~1 GB) stream through HBM every step, far more than the 126 MB L2, so no
+L2 flush is needed between steps.
+
+Printed JSON (rank 0): ``value`` = prefixes/s of the whole job measured on
+the device (CUDA graph of the 72 ops, inputs resident), ``e2e`` = the same
+through the public torch ops with pinned-host input/output copies in the
+timed region, ``roofline`` = the gate/up GEMM (61% of the prefix's ops)
+against the int8 tensor peak, ``cpu_baseline`` = the CPU oracle port.
+With N > 1, every rank runs its own observations (data parallel, weak
+scaling); the step time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "W4A4 prefix-LM ms per 776-tok prefix; GEMM int TOPS; obs/s at 1/2/4/8 B200"
+UNIT = "obs/s (776-token W4A4 prefixes per second)"
+HIDDEN, INTER, N_Q, N_KV = 2048, 16384, 2048, 256
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch at
+# M=776 from ncu (profiles/); None until captured.
+GATE_UP_DRAM_BYTES = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=1, help="observations per GPU per step")
+    ap.add_argument("--prefix", type=int, default=776, help="tokens per observation prefix")
+    ap.add_argument("--layers", type=int, default=18)
+    ap.add_argument("--staging", choices=("fp16", "fp32"), default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--roofline-reps", type=int, default=20)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def ops_per_prefix(m: int, layers: int) -> float:
+    """Algorithmic integer ops (2 per MAC) of one prefix's GEMMs."""
+    per_layer = 2 * m * HIDDEN * (N_Q + 2 * N_KV) + 2 * m * HIDDEN * HIDDEN \
+        + 2 * m * HIDDEN * 2 * INTER + 2 * m * INTER * HIDDEN
+    return float(per_layer * layers)
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.isfile(path):
+        with open(path) as f:
+            d = json.load(f)
+        d["_source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "_source": "fallback"}
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, clock-event reasons) every 10 ms on a thread."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device_index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._handle = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid if not uuid.startswith("GPU-") else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self.error = repr(e)
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _reasons(self):
+        n = self._nvml
+        fn = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            n.nvmlDeviceGetCurrentClocksThrottleReasons
+        return fn(self._handle)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self._nvml.nvmlDeviceGetClockInfo(self._handle, self._nvml.NVML_CLOCK_SM)
+                self.samples.append((mhz, int(self._reasons())))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.01)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._handle is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self._handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "error": getattr(self, "error", "nvml unavailable")}
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = sorted(name for bit, name in self.REASONS.items() if mask & bit and bit != 0x1)
+        mhz = [s for s, _ in self.samples]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz)}
+
+
+# ----------------------------------------------------------------------------- model
+def build_layers(n_layers: int, device, seed: int):
+    """Packed weights of n_layers Gemma-2B decoder layers in the layouts the
+    reference's loader produces (rows padded to K/8+8; gate/up fragment-major)."""
+    import torch
+
+    from pi05_pytorch_fast_b200.w4a4.pack import pack_linear_weight, preshuffle_wmma_weight
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def packed(n, k, pad=True):
+        w = torch.randn(n, k, device=device, generator=gen) * (1.0 / math.sqrt(k))
+        p = pack_linear_weight(w, device=device)
+        return torch.nn.functional.pad(p, (0, 7)) if pad else p
+
+    layers = []
+    for _ in range(n_layers):
+        qkv = packed(N_Q + 2 * N_KV, HIDDEN)
+        layers.append({
+            "q": qkv[:N_Q].contiguous(), "k": qkv[N_Q:N_Q + N_KV].contiguous(),
+            "v": qkv[N_Q + N_KV:].contiguous(),
+            "o": packed(HIDDEN, HIDDEN),
+            "gate": preshuffle_wmma_weight(packed(INTER, HIDDEN, pad=False), HIDDEN),
+            "up": preshuffle_wmma_weight(packed(INTER, HIDDEN, pad=False), HIDDEN),
+            "down": packed(HIDDEN, INTER),
+        })
+    return layers
+
+
+def prefix_forward(x, layers):
+    """The 72 W4A4 ops of one prefix pass, chained through their outputs."""
+    import torch
+
+    ops = torch.ops.pi05_w4a4
+    for lw in layers:
+        q, _, _ = ops.int4_gemm3(x, lw["q"], lw["k"], lw["v"])
+        o = ops.int4_gemm(q, lw["o"])
+        g, _ = ops.int4_gemm2_tiled(o, lw["gate"], lw["up"])
+        x = ops.int4_gemm(g, lw["down"])
+    return x
+
+
+def synthetic_prefix(rows: int, device, seed: int):
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(rows, HIDDEN, device=device, generator=gen)
+    ch = torch.randperm(HIDDEN, device=device, generator=gen)[: HIDDEN // 100]
+    x[:, ch] *= 20
+    return x.half()
+
+
+# ----------------------------------------------------------------------------- timing
+def time_device(fn, steps: int, warmup: int, dist_on: bool, device) -> float:
+    """ms per step: events on the current stream, barrier + sync both sides,
+    max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / steps
+    if dist_on:
+        dist.barrier()
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def oracle_layer(m: int, staging: str):
+    """One decoder layer's W4A4 ops through the CPU oracle port (numpy; exact
+    integer products in fp32 BLAS), with weights in the reference's layouts:
+    q/k/v as one N=2560 GEMM (shared quant, like int4_gemm3), o_proj, gate and
+    up fragment-major, down_proj.  Returns a zero-argument callable."""
+    from oracle import w4a4_oracle as orc
+
+    qkv = orc.random_packed_weight(N_Q + 2 * N_KV, HIDDEN, 1)
+    o = orc.random_packed_weight(HIDDEN, HIDDEN, 2)
+    gate = orc.preshuffle_wmma_weight(orc.random_packed_weight(INTER, HIDDEN, 3), HIDDEN)
+    up = orc.preshuffle_wmma_weight(orc.random_packed_weight(INTER, HIDDEN, 4), HIDDEN)
+    down = orc.random_packed_weight(HIDDEN, INTER, 5)
+    x = orc.make_activations(m, HIDDEN, 0)
+    h = orc.make_activations(m, INTER, 1)
+
+    def run():
+        orc.int4_gemm_ref(x, qkv, staging=staging)
+        orc.int4_gemm_ref(x, o, staging=staging)
+        orc.int4_gemm_ref(x, gate, staging=staging, layout="fragment")
+        orc.int4_gemm_ref(x, up, staging=staging, layout="fragment")
+        orc.int4_gemm_ref(h, down, staging=staging)
+
+    return run
+
+
+def cpu_baseline_sample(m: int, staging: str, layers: int) -> dict:
+    """The CPU oracle port timed on this host for ONE decoder layer at M=m
+    (median of 3), scaled to the prefix's layers.  A reported baseline only."""
+    run = oracle_layer(m, staging)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    per_prefix = statistics.median(times) * layers
+    return {"value": 1.0 / per_prefix, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 decoder layer's W4A4 ops (qkv, o, gate, up, down) at M={m}, median of 3, "
+                      f"x{layers} layers; numpy oracle port of int4_gemm_ref (BLAS threads = cores, "
+                      "elementwise numpy on 1 thread)",
+            "ms_per_prefix": per_prefix * 1e3}
+
+
+# ----------------------------------------------------------------------------- arms
+def run_ours(args, rank, world, local_rank, dist_on):
+    import torch
+
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    if args.staging:
+        os.environ["PI05_W4A4_STAGING"] = args.staging
+    staging = os.environ.get("PI05_W4A4_STAGING", "fp16")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ext.preload()
+    m = args.batch * args.prefix
+    layers = build_layers(args.layers, device, seed=1234)
+    x_static = synthetic_prefix(m, device, seed=100 + rank)
+    torch.cuda.synchronize(device)
+
+    # --- CUDA graph of the whole prefix pass (device-resident inputs)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            prefix_forward(x_static, layers)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y_static = prefix_forward(x_static, layers)
+    with ClockSampler(local_rank) as clocks:
+        ms = time_device(graph.replay, args.steps, args.warmup, dist_on, device)
+    launches_per_step = args.layers * 4 * 2
+
+    # --- end to end through the public ops: pinned host in/out every step
+    x_host = synthetic_prefix(m, device, seed=200 + rank).cpu().pin_memory()
+    y_host = torch.empty((m, HIDDEN), dtype=torch.float16).pin_memory()
+    x_dev = torch.empty((m, HIDDEN), dtype=torch.float16, device=device)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = prefix_forward(x_dev, layers)
+        y_host.copy_(y, non_blocking=True)
+
+    e2e_steps = max(5, min(args.steps, 50))
+    ms_e2e = time_device(e2e_step, e2e_steps, max(3, args.warmup), dist_on, device)
+
+    # --- roofline of the dominant kernel: the gate/up GEMM (one launch, two
+    # weights) cycling over the layers so weights always come from HBM.
+    codes, scales = ext.quantize(x_static)
+    stream = torch.cuda.current_stream(device)
+    ga = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ga):
+        for lw in layers:
+            ext.gemm_from_codes(codes, scales, [lw["gate"], lw["up"]], fragment_major=True)
+    ms_gu = time_device(ga.replay, args.roofline_reps, 3, dist_on, device) / len(layers)
+    gu_ops = 2.0 * m * 2 * INTER * HIDDEN
+    gu_tops = gu_ops / (ms_gu * 1e-3) / 1e12
+    # quant kernel at K = 16384 (HBM-bound)
+    h16 = torch.randn(m, INTER, device=device).half()
+    gq = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gq):
+        for _ in range(10):
+            ext.quantize(h16)
+    ms_q = time_device(gq.replay, args.roofline_reps, 3, dist_on, device) / 10
+    q_bytes = 2 * m * INTER + m * INTER + 4 * m
+    del graph, ga, gq
+    torch.cuda.synchronize(device)
+
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    total_ops = ops_per_prefix(m, args.layers)
+    prefixes_per_step = args.batch * world
+    result = {
+        "metric": METRIC,
+        "value": prefixes_per_step / (ms * 1e-3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "ms_per_prefix": ms / args.batch,
+        "gemm_int_tops": total_ops / (ms * 1e-3) / 1e12,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 codes x int4 codes -> int32 (tcgen05 kind::i8), fp16 in/out",
+        "data": "synthetic: random-init N(0,1/sqrt(K)) weights in the reference's packed format; "
+                "N(0,1) activations with 1% outlier channels x20",
+        "config": {
+            "workload": f"config 2 W4A4 path: {args.layers} Gemma-2B layers x (int4_gemm3 qkv, int4_gemm o, "
+                        f"int4_gemm2_tiled gate/up, int4_gemm down), prefix M={args.prefix}, "
+                        f"{args.batch} observation(s) per GPU per step",
+            "rows_per_gpu": m,
+            "layers": args.layers,
+            "staging": staging,
+            "parallelism": f"dp{world} (independent observations per GPU, no collective in the step)",
+            "l2": "working set ~1.0 GB of packed weights per step >> 126 MB L2 (no flush needed)",
+            "timing": "CUDA graph replay of the 144 launches, CUDA events, max over ranks",
+        },
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+        "e2e": {
+            "value": prefixes_per_step / (ms_e2e * 1e-3),
+            "unit": UNIT,
+            "h2d_bytes_per_step": int(x_host.numel() * 2),
+            "d2h_bytes_per_step": int(y_host.numel() * 2),
+            "mode": "eager torch.ops.pi05_w4a4 calls, pinned host input copied in and output "
+                    "copied out inside the timed region",
+            "steps": e2e_steps,
+        },
+        "roofline": {
+            "kernel": "w4a4_gemm_kernel<fragment-major> (gate+up, one launch)",
+            "bound": "tensor",
+            "achieved": gu_tops,
+            "peak": int8_peak,
+            "unit": "TFLOP/s",
+            "op_kind": "int8 tensor ops (1 MAC = 2 ops); peak = 2 x bf16 dense "
+                       f"({peaks['_source']}: {peaks['bf16_tflops']} TFLOP/s), the i8:f16 rate ratio",
+            "frac": gu_tops / int8_peak,
+            "traffic": GATE_UP_DRAM_BYTES,
+            "ms_per_launch": ms_gu,
+            "algorithmic_ops_per_launch": gu_ops,
+        },
+        "kernels": {
+            "quant_k16384": {"ms": ms_q, "gbs": q_bytes / (ms_q * 1e-3) / 1e9,
+                             "peak_gbs": peaks["hbm_gbs"],
+                             "frac": q_bytes / (ms_q * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        },
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline_sample(m, staging, args.layers)
+    return result
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU implementation of the path (this repo's oracle port
+    of int4_gemm_ref; the reference itself is Python + HIP and cannot run
+    here), timed on the host cores.  Rank 0 only."""
+    import numpy as np
+
+    if rank != 0:
+        return None
+    staging = args.staging or os.environ.get("PI05_W4A4_STAGING", "fp16")
+    m = args.batch * args.prefix
+    one_layer = oracle_layer(m, staging)
+
+    t0 = time.perf_counter()
+    one_layer()
+    t_first = time.perf_counter() - t0
+    budget = 150.0
+    steps = max(1, min(args.steps, int(budget / max(t_first, 1e-3)) - args.warmup))
+    for _ in range(max(0, args.warmup - 1)):
+        one_layer()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_layer()
+    t_layer = (time.perf_counter() - t0) / steps
+    value = 1.0 / (t_layer * args.layers) * args.batch
+    sample = (f"each step = 1 decoder layer's W4A4 ops at M={m} (q/k/v as one N=2560 GEMM), "
+              f"scaled x{args.layers} layers; numpy oracle port of int4_gemm_ref")
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": t_layer * 1e3,
+        "ms_per_prefix": t_layer * args.layers * 1e3 / args.batch,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int32 codes in fp32 BLAS (exact), fp16 out", "data": "synthetic",
+        "config": {"workload": f"config 2 W4A4 path, {args.layers} layers, prefix M={args.prefix}, "
+                               f"{args.batch} observation(s)", "rows": m, "staging": staging},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "numpy": np.__version__,
+    }
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+
+    dist_on = world > 1
+    if dist_on:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_ours(args, rank, world, local_rank, dist_on)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if dist_on:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+/*
+ * w4a4_sm100.h -- C ABI of libw4a4_sm100.so, the B200 (sm_100a) W4A4
+ * prefix-LM GEMM path.
+ *
+ * Plain C: device pointers, sizes and an opaque CUDA stream handle
+ * (cudaStream_t passed as void*; NULL = the legacy default stream).  No torch
+ * types.  Every entry point is asynchronous on `stream` (nothing
+ * synchronises except w4a4_device_error), returns W4A4_OK or an error code,
+ * and on error leaves a message retrievable with w4a4_last_error() (thread
+ * local).  All device pointers must belong to the CURRENT CUDA device.
+ *
+ * Reference interfaces replaced (paths relative to the reference project,
+ * harrysocool/pi05-pytorch-fast):
+ *   pi05_fast/w4a4/csrc/int4_gemm.cu:496-531  quantize_x      -> w4a4_quant
+ *   pi05_fast/w4a4/csrc/int4_gemm.cu:566-616  gemm_from_q     -> w4a4_gemm
+ *   pi05_fast/w4a4/csrc/int4_gemm.cu:618-642  int4_gemm{,_tiled,2,2_tiled,3}
+ *                                                             -> w4a4_int4_gemm
+ *   pi05_fast/w4a4/apply.py:68-69             row padding     -> w4a4_pad_rows
+ *   pi05_fast/w4a4/csrc/int4_gemm.cu:487-501  TORCH_CHECK text-> w4a4_last_error
+ */
+#ifndef W4A4_SM100_H_
+#define W4A4_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define W4A4_OK 0
+#define W4A4_ERR_INVALID 1     /* bad argument (shape, stride, pointer, layout) */
+#define W4A4_ERR_UNSUPPORTED 2 /* valid in the reference, not supported here    */
+#define W4A4_ERR_CUDA 3        /* a CUDA runtime / driver call failed            */
+
+/* ---- FWHT staging of the activation quant ----
+ * FP16: the reference HIP kernel's arithmetic (int4_gemm.cu:404-426).
+ * FP32: the reference CPU emulation's arithmetic (pack.py:113-131). */
+#define W4A4_STAGING_FP16 0
+#define W4A4_STAGING_FP32 1
+
+/* ---- activation code formats written by w4a4_quant ----
+ * INT8:   one signed code per byte, row-major [M, K] (what w4a4_gemm reads).
+ * PACKED: the reference's int32 words [M, K/8], element j at bits 4j. */
+#define W4A4_CODES_INT8 0
+#define W4A4_CODES_PACKED 1
+
+/* ---- weight layouts (the reference's in-memory formats) ----
+ * ROW_MAJOR: int32 [N, row_words], word p of row n holds k = 8p..8p+7
+ *   (element j at bits 4j), word K/8 holds the fp32 scale bits
+ *   (pack.py:85-101); row_words >= K/8+1.  w4a4_gemm needs row_words*4 to be
+ *   a multiple of 16 (the default load-time pad K/8+8 is); pad others with
+ *   w4a4_pad_rows.
+ * FRAGMENT_MAJOR: payload flat as [K/16][N][2 words], then N fp32 scales,
+ *   inside a tensor declared [N, K/8+9] (pack.py:45-68). */
+#define W4A4_LAYOUT_ROW_MAJOR 0
+#define W4A4_LAYOUT_FRAGMENT_MAJOR 1
+
+/* rotate argument of w4a4_quant */
+#define W4A4_ROTATE_BY_K (-1) /* rotate iff K in {1024, 2048, 16384}: the op's dispatch */
+
+typedef struct w4a4_weight {
+  const int32_t* data; /* device pointer to the packed tensor's storage      */
+  int32_t n;           /* output features (tensor size(0))                   */
+  int32_t row_words;   /* tensor size(1)                                     */
+  int32_t layout;      /* W4A4_LAYOUT_*                                      */
+} w4a4_weight;
+
+/* Fused Hadamard rotation + per-token symmetric INT4 quantisation.
+ * Replaces quantize_x / quant_rot_rb / quant_rows (int4_gemm.cu:396-531).
+ *   x          fp16 [m, k], row stride ldx elements (ldx >= k, ldx % 8 == 0,
+ *              16-byte aligned base)
+ *   k          > 0, multiple of 64
+ *   rotate     W4A4_ROTATE_BY_K, 0 (never) or 1 (k must be 1024/2048/16384)
+ *   staging    W4A4_STAGING_*
+ *   codes      int8 [m, k] or int32 [m, k/8] (codes_format), 8-byte aligned
+ *   row_scale  fp32 [m]: sdiv/sqrt(k) when rotated, sdiv otherwise          */
+int w4a4_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
+               int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+               void* stream);
+
+/* W4A4 GEMM of int8 activation codes against 1..3 packed weights that share
+ * them (one launch).  Replaces gemm_from_q / gemm_iu4 / gemm_iu4_shape
+ * (int4_gemm.cu:66-394, :566-616).
+ *   codes      int8 [m, k] from w4a4_quant (W4A4_CODES_INT8), 16-byte aligned
+ *   row_scale  fp32 [m]
+ *   weights    n_weights descriptors, all the same layout, all K = k
+ *   y          n_weights fp16 outputs, y[i] is [m, weights[i].n] row-major  */
+int w4a4_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
+              int32_t n_weights, const w4a4_weight* weights, void* const* y, void* stream);
+
+/* Test hook: the same GEMM, but writes the raw int32 accumulators
+ * acc[i] = int32 [m, weights[i].n] (sum_k qa*qw, before any scaling) so
+ * tests can check them bit-exactly; row scales are not used. */
+int w4a4_gemm_accumulators(const void* codes, int64_t m, int32_t k, int32_t n_weights,
+                           const w4a4_weight* weights, int32_t* const* acc, void* stream);
+
+/* The reference's op contract in one call: quantise x once, then run the
+ * GEMM against every weight (int4_gemm: 1, int4_gemm2: 2, int4_gemm3: 3
+ * weights; int4_gemm.cu:618-642).  The caller provides the intermediate
+ * buffers: codes_scratch int8 [m, k] (16-byte aligned) and
+ * scale_scratch fp32 [m].  rotate = W4A4_ROTATE_BY_K gives the op's behaviour. */
+int w4a4_int4_gemm(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
+                   int32_t staging, int32_t n_weights, const w4a4_weight* weights,
+                   void* const* y, void* codes_scratch, float* scale_scratch, void* stream);
+
+/* Copy a row-major packed weight [n, src_row_words] into [n, dst_row_words]
+ * (dst_row_words >= src_row_words), zero-filling the new words: the
+ * load-time row pad of apply.py:68-69, done on the device. */
+int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words,
+                  int32_t dst_row_words, int32_t* dst, void* stream);
+
+/* Copies the last error message of this thread into buf (NUL-terminated,
+ * truncated to len) and returns the last status code. */
+int w4a4_last_error(char* buf, size_t len);
+
+/* Reads (and with clear != 0, resets) the current device's error word: a
+ * bit mask set by kernels whose bounded waits ran out (0 = no error).
+ * Synchronises the device. */
+int w4a4_device_error(uint32_t* bits, int32_t clear);
+
+/* Limit, in nanoseconds, of every bounded wait inside kernels launched
+ * after this call (default 1e9).  Process-wide. */
+int w4a4_set_wait_limit_ns(uint64_t limit_ns);
+
+/* Test hook: launches one CTA that waits on a barrier nobody arrives at, with
+ * the given limit; the kernel must give up, set its error bit and return. */
+int w4a4_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
+/* Library ABI version (major * 100 + minor). */
+int w4a4_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W4A4_SM100_H_ */

@@ -1,0 +1,292 @@
+// Fused Walsh-Hadamard rotation + per-token symmetric INT4 activation quant.
+//
+// Replaces the reference's quant_rot_rb<K,R> and quant_rows
+// (pi05_fast/w4a4/csrc/int4_gemm.cu:396-477) with a register/warp-shuffle
+// design for sm_100a:
+//
+//  * each row is held in registers: lane l of a warp loads 16-byte vectors
+//    (8 fp16) at element offsets 256*c + 8*l, so element index bits 0-2 live
+//    inside a thread, bits 3-7 across the 32 lanes and bits 8-10 across the
+//    thread's chunks c;
+//  * butterflies run in ascending stride order (h = 1, 2, 4, ...), exactly the
+//    order of the reference, so every value is bit-identical: stride bits 0-2
+//    and 8-10 are in-register, bits 3-7 use __shfl_xor_sync, and for
+//    K = 16384 bits 11-13 go through one shared-memory transpose between the
+//    8 warps of the CTA;
+//  * staging FP16 = the HIP kernel's arithmetic: stages with stride < R
+//    (R = K/256) in fp32, then the values are rounded to fp16 and every later
+//    stage adds/subtracts in fp32 and rounds back to fp16 (int4_gemm.cu:404-426);
+//    staging FP32 = the reference's CPU emulation (pack.py:113-131);
+//  * amax, sdiv = amax/7 + 1e-12 and codes = clamp(rint(v/sdiv), -7, 7) with
+//    IEEE division and round-half-even (int4_gemm.cu:427-449);
+//  * codes are written either as int8 (one code per byte, the layout the
+//    tensor-core GEMM consumes) or as the reference's packed int32 words
+//    (8 nibbles per word, element j at bits 4j).
+#pragma once
+
+#include "common.cuh"
+
+namespace w4a4 {
+
+constexpr int kQuantThreads = 256;
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void load8_half_as_float(const __half* p, float (&v)[8]) {
+  const uint4 raw = ld_nc_v4(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ float round_fp16(float v) { return __half2float(__float2half_rn(v)); }
+
+template <int C>
+__device__ __forceinline__ void round_all(float (&v)[C][8]) {
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[c][j] = round_fp16(v[c][j]);
+}
+
+// Butterfly between elements whose index differs in bit log2(h), h < 8.
+template <int C>
+__device__ __forceinline__ void stage_in_vector(float (&v)[C][8], int h) {
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (!(j & h)) {
+        const float a = v[c][j], b = v[c][j + h];
+        v[c][j] = __fadd_rn(a, b);
+        v[c][j + h] = __fsub_rn(a, b);
+      }
+}
+
+// Butterfly across lanes: partner lane = lane ^ m.  The lane with the bit
+// clear holds the lower element a and keeps a + b; its partner keeps a - b.
+template <int C>
+__device__ __forceinline__ void stage_across_lanes(float (&v)[C][8], int lane, int m) {
+  const bool upper = (lane & m) != 0;
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float mine = v[c][j];
+      const float other = __shfl_xor_sync(0xffffffffu, mine, m);
+      v[c][j] = upper ? __fsub_rn(other, mine) : __fadd_rn(mine, other);
+    }
+}
+
+// Butterfly between chunks c and c + h (element index bit log2(h) + 8).
+template <int C>
+__device__ __forceinline__ void stage_across_chunks(float (&v)[C][8], int h) {
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+    if (!(c & h))
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float a = v[c][j], b = v[c + h][j];
+        v[c][j] = __fadd_rn(a, b);
+        v[c + h][j] = __fsub_rn(a, b);
+      }
+}
+
+// All stages for index bits [0, min(LOGK, 11)) of a warp-resident block of
+// 256*C elements.  In fp16 staging, values are rounded to fp16 after stage
+// RBITS-1 (the reference's fp32 -> fp16 hand-off) and after every later stage.
+template <int C, int NBITS, int RBITS, bool FP16>
+__device__ __forceinline__ void fwht_warp_block(float (&v)[C][8], int lane) {
+#pragma unroll
+  for (int b = 0; b < NBITS; ++b) {
+    if (b < 3)
+      stage_in_vector<C>(v, 1 << b);
+    else if (b < 8)
+      stage_across_lanes<C>(v, lane, 1 << (b - 3));
+    else
+      stage_across_chunks<C>(v, 1 << (b - 8));
+    if (FP16 && b >= RBITS - 1) round_all<C>(v);
+  }
+}
+
+__device__ __forceinline__ int quant_code(float v, float sdiv) {
+  const int q = __float2int_rn(__fdiv_rn(v, sdiv));
+  return max(-7, min(7, q));
+}
+
+__device__ __forceinline__ float warp_max(float m) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return m;
+}
+
+// Eight codes -> either 8 int8 bytes or one packed nibble word.
+template <bool PACKED>
+__device__ __forceinline__ void store_codes8(void* out, long long elem, const float (&v)[8],
+                                             float sdiv) {
+  if constexpr (PACKED) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= (static_cast<uint32_t>(quant_code(v[j], sdiv)) & 0xFu) << (4 * j);
+    reinterpret_cast<uint32_t*>(out)[elem >> 3] = w;
+  } else {
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      w0 |= (static_cast<uint32_t>(quant_code(v[j], sdiv)) & 0xFFu) << (8 * j);
+      w1 |= (static_cast<uint32_t>(quant_code(v[j + 4], sdiv)) & 0xFFu) << (8 * j);
+    }
+    *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(out) + elem) = make_uint2(w0, w1);
+  }
+}
+
+// K = 1024 / 2048: one warp per row, 8 rows per 256-thread CTA.
+template <int LOGK, bool FP16, bool PACKED>
+__global__ void __launch_bounds__(kQuantThreads) quant_rot_warp_kernel(
+    const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
+    float* __restrict__ row_scale, float inv_sqrt_k) {
+  constexpr int K = 1 << LOGK;
+  constexpr int C = K / 256;
+  constexpr int RBITS = LOGK - 8;  // log2(K / 256): stages kept in fp32
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (kQuantThreads / 32) + (threadIdx.x >> 5);
+  if (row >= m) return;
+  float v[C][8];
+  const __half* xr = x + row * ldx + 8 * lane;
+#pragma unroll
+  for (int c = 0; c < C; ++c) load8_half_as_float(xr + 256 * c, v[c]);
+  fwht_warp_block<C, LOGK, RBITS, FP16>(v, lane);
+  float mx = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+  mx = warp_max(mx);
+  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  if (lane == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+#pragma unroll
+  for (int c = 0; c < C; ++c) store_codes8<PACKED>(codes, row * K + 256 * c + 8 * lane, v[c], sdiv);
+}
+
+// K = 16384: one 256-thread CTA per row.  Phase 1: warp w transforms its
+// 2048-element slice (index bits 0-10) in registers.  Phase 2: after a
+// shared-memory transpose, thread (c, l) = (warp, lane) holds the 8 slices'
+// values at offsets 256c + 8l + j and finishes bits 11-13 in registers.
+template <bool FP16, bool PACKED>
+__global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
+    const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
+    float* __restrict__ row_scale, float inv_sqrt_k) {
+  constexpr int K = 16384;
+  constexpr int RBITS = 6;  // log2(16384 / 256)
+  using Stage = typename std::conditional<FP16, __half, float>::type;
+  extern __shared__ __align__(16) unsigned char quant_smem[];
+  Stage* buf = reinterpret_cast<Stage*>(quant_smem);
+  __shared__ float warp_amax[kQuantThreads / 32];
+
+  const long long row = blockIdx.x;
+  if (row >= m) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    float v[8][8];
+    const __half* xr = x + row * ldx + 2048 * warp + 8 * lane;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) load8_half_as_float(xr + 256 * c, v[c]);
+    fwht_warp_block<8, 11, RBITS, FP16>(v, lane);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      Stage* dst = buf + 2048 * warp + 256 * c + 8 * lane;
+      if constexpr (FP16) {
+        uint4 packed;
+        __half2* h = reinterpret_cast<__half2*>(&packed);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[c][2 * i], v[c][2 * i + 1]);
+        *reinterpret_cast<uint4*>(dst) = packed;
+      } else {
+        *reinterpret_cast<float4*>(dst) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(v[c][4], v[c][5], v[c][6], v[c][7]);
+      }
+    }
+  }
+  __syncthreads();
+  // Phase 2: v[w][j] = element 2048w + 256*warp + 8*lane + j.
+  float v[8][8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const Stage* src = buf + 2048 * w + 256 * warp + 8 * lane;
+    if constexpr (FP16) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src);
+      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        v[w][2 * i] = f.x;
+        v[w][2 * i + 1] = f.y;
+      }
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 b = *reinterpret_cast<const float4*>(src + 4);
+      v[w][0] = a.x; v[w][1] = a.y; v[w][2] = a.z; v[w][3] = a.w;
+      v[w][4] = b.x; v[w][5] = b.y; v[w][6] = b.z; v[w][7] = b.w;
+    }
+  }
+#pragma unroll
+  for (int b = 11; b < 14; ++b) {
+    stage_across_chunks<8>(v, 1 << (b - 11));
+    if (FP16) round_all<8>(v);
+  }
+  float mx = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[w][j]));
+  mx = warp_max(mx);
+  if (lane == 0) warp_amax[warp] = mx;
+  __syncthreads();
+  mx = warp_amax[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, warp_amax[w]);
+  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  if (threadIdx.x == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    store_codes8<PACKED>(codes, row * K + 2048 * w + 256 * warp + 8 * lane, v[w], sdiv);
+}
+
+// Any K (multiple of 64) without rotation: one warp per row, two passes
+// (amax, then codes).  Replaces quant_rows (int4_gemm.cu:451-477).
+template <bool PACKED>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(
+    const __half* __restrict__ x, long long ldx, long long m, int k, void* __restrict__ codes,
+    float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (kQuantThreads / 32) + (threadIdx.x >> 5);
+  if (row >= m) return;
+  const __half* xr = x + row * ldx;
+  float mx = 0.f;
+  for (int e = 8 * lane; e < k; e += 256) {
+    float v[8];
+    load8_half_as_float(xr + e, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+  }
+  mx = warp_max(mx);
+  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  if (lane == 0) row_scale[row] = sdiv;
+  for (int e = 8 * lane; e < k; e += 256) {
+    float v[8];
+    load8_half_as_float(xr + e, v);
+    store_codes8<PACKED>(codes, row * k + e, v, sdiv);
+  }
+}
+
+}  // namespace w4a4

@@ -1,0 +1,474 @@
+// libw4a4_sm100.so: the C ABI declared in include/w4a4_sm100.h.
+//
+// One translation unit holds every kernel (so the single device error word
+// g_w4a4_device_error is shared), the launchers, a cache of TMA descriptors
+// and the extern "C" entry points.  Argument checks mirror the reference's
+// TORCH_CHECKs (pi05_fast/w4a4/csrc/int4_gemm.cu:487-501, :570-577) and keep
+// their message text where the reference's tests match on it.
+#include "w4a4_sm100.h"
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <type_traits>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "quant.cuh"
+
+namespace w4a4 {
+namespace {
+
+thread_local std::string t_last_error;
+thread_local int t_last_status = W4A4_OK;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  t_last_status = code;
+  return code;
+}
+
+int ok() {
+  t_last_status = W4A4_OK;
+  return W4A4_OK;
+}
+
+#define W4A4_CUDA_TRY(expr)                                                                 \
+  do {                                                                                     \
+    const cudaError_t e_ = (expr);                                                         \
+    if (e_ != cudaSuccess) return fail(W4A4_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+std::atomic<unsigned long long> g_wait_limit_ns{1000000000ull};
+
+// ------------------------------------------------------------- device info
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+unsigned g_attr_done[kMaxDevices];  // bit per kernel whose smem attribute is set
+std::mutex g_dev_mu;
+
+int current_device(int* dev) {
+  W4A4_CUDA_TRY(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(W4A4_ERR_UNSUPPORTED, "device %d out of range", *dev);
+  return W4A4_OK;
+}
+
+int sm_count(int dev, int* out) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_sm_count[dev] == 0) {
+    int v = 0;
+    W4A4_CUDA_TRY(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    g_sm_count[dev] = v;
+  }
+  *out = g_sm_count[dev];
+  return W4A4_OK;
+}
+
+template <class Kernel>
+int ensure_smem_attr(int dev, unsigned bit, Kernel kernel, int bytes) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!(g_attr_done[dev] & bit)) {
+    W4A4_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    g_attr_done[dev] |= bit;
+  }
+  return W4A4_OK;
+}
+
+// ------------------------------------------------------------- TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t ptr;
+  uint64_t d0, d1, stride;
+  uint32_t b0, b1;
+  int dtype, swizzle;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && stride == o.stride && b0 == o.b0 &&
+           b1 == o.b1 && dtype == o.dtype && swizzle == o.swizzle;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.ptr * 0x9E3779B97F4A7C15ull;
+    for (uint64_t v : {k.d0, k.d1, k.stride, static_cast<uint64_t>(k.b0) << 32 | k.b1,
+                       static_cast<uint64_t>(k.dtype) << 8 | static_cast<uint64_t>(k.swizzle)})
+      h = (h ^ v) * 0x100000001B3ull;
+    return static_cast<size_t>(h);
+  }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// 2-D tiled tensor map: dim0 innermost (elements), dim1 rows, row stride in bytes.
+int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, uint64_t d0,
+                uint64_t d1, uint64_t stride_bytes, uint32_t b0, uint32_t b1,
+                CUtensorMapSwizzle swizzle) {
+  const MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_bytes, b0, b1,
+                   static_cast<int>(dtype), static_cast<int>(swizzle)};
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return W4A4_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(W4A4_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {stride_bytes};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap map;
+  const CUresult r = fn(&map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(W4A4_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (%d): dims {%llu, %llu}, stride %llu B, box {%u, %u}",
+                static_cast<int>(r), (unsigned long long)d0, (unsigned long long)d1,
+                (unsigned long long)stride_bytes, b0, b1);
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, map);
+  *out = map;
+  return W4A4_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ------------------------------------------------------------- quant
+int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
+                 int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                 cudaStream_t stream) {
+  if (k <= 0) return fail(W4A4_ERR_INVALID, "K must be positive, got %d", k);
+  if (k % 64 != 0) return fail(W4A4_ERR_INVALID, "K must be a multiple of 64, got %d", k);
+  if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative, got %lld", (long long)m);
+  if (staging != W4A4_STAGING_FP16 && staging != W4A4_STAGING_FP32)
+    return fail(W4A4_ERR_INVALID, "unknown staging mode %d", staging);
+  if (codes_format != W4A4_CODES_INT8 && codes_format != W4A4_CODES_PACKED)
+    return fail(W4A4_ERR_INVALID, "unknown codes format %d", codes_format);
+  bool rot;
+  if (rotate == W4A4_ROTATE_BY_K)
+    rot = (k == 1024 || k == 2048 || k == 16384);
+  else if (rotate == 0 || rotate == 1)
+    rot = rotate == 1;
+  else
+    return fail(W4A4_ERR_INVALID, "rotate must be -1, 0 or 1, got %d", rotate);
+  if (rot && !(k == 1024 || k == 2048 || k == 16384))
+    return fail(W4A4_ERR_UNSUPPORTED, "Hadamard rotation is implemented for K in {1024, 2048, 16384}, got %d", k);
+  if (m == 0) return ok();
+  if (!x || !codes || !row_scale) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (ldx < k || ldx % 8 != 0)
+    return fail(W4A4_ERR_INVALID, "activation row stride %lld must be >= K and a multiple of 8", (long long)ldx);
+  if (!aligned(x, 16)) return fail(W4A4_ERR_INVALID, "activation pointer must be 16-byte aligned");
+  if (!aligned(codes, 8)) return fail(W4A4_ERR_INVALID, "codes pointer must be 8-byte aligned");
+  int dev;
+  if (int e = current_device(&dev)) return e;
+
+  const __half* xh = static_cast<const __half*>(x);
+  const bool fp16 = staging == W4A4_STAGING_FP16;
+  const bool packed = codes_format == W4A4_CODES_PACKED;
+  const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
+  const unsigned rows_grid = static_cast<unsigned>((m + 7) / 8);
+  if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large: %lld", (long long)m);
+
+#define W4A4_LAUNCH_WARP(LOGK)                                                                \
+  do {                                                                                       \
+    if (fp16 && packed) quant_rot_warp_kernel<LOGK, true, true><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
+    else if (fp16) quant_rot_warp_kernel<LOGK, true, false><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
+    else if (packed) quant_rot_warp_kernel<LOGK, false, true><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
+    else quant_rot_warp_kernel<LOGK, false, false><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
+  } while (0)
+
+  if (rot && k == 1024) {
+    W4A4_LAUNCH_WARP(10);
+  } else if (rot && k == 2048) {
+    W4A4_LAUNCH_WARP(11);
+  } else if (rot) {
+    const unsigned grid = static_cast<unsigned>(m);
+    if (fp16) {
+      const int smem = 16384 * 2;
+      if (packed) quant_rot_16k_kernel<true, true><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
+      else quant_rot_16k_kernel<true, false><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
+    } else {
+      const int smem = 16384 * 4;
+      if (packed) {
+        if (int e = ensure_smem_attr(dev, 1u << 0, quant_rot_16k_kernel<false, true>, smem)) return e;
+        quant_rot_16k_kernel<false, true><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
+      } else {
+        if (int e = ensure_smem_attr(dev, 1u << 1, quant_rot_16k_kernel<false, false>, smem)) return e;
+        quant_rot_16k_kernel<false, false><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
+      }
+    }
+  } else {
+    if (packed) quant_rows_kernel<true><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, k, codes, row_scale);
+    else quant_rows_kernel<false><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, k, codes, row_scale);
+  }
+#undef W4A4_LAUNCH_WARP
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+// ------------------------------------------------------------- GEMM
+// Token-tile width: the tile count T is chosen to minimise
+// waves(T) * (tile + kTileOverhead), where the overhead term models the
+// per-K-step cost that does not scale with the tile (the 128-row weight
+// operand).  Tiles are multiples of 16 (the UMMA N granularity).
+int choose_tok_tile(int64_t m, int w_tiles, int sms) {
+  constexpr int kTileOverhead = 64;
+  int best_tile = 16;
+  double best_cost = 1e300;
+  const int64_t t_min = (m + kMaxTokTile - 1) / kMaxTokTile;
+  for (int64_t t = t_min; t <= t_min + 64; ++t) {
+    const int64_t per = (m + t - 1) / t;
+    const int tile = static_cast<int>(((per + 15) / 16) * 16);
+    if (tile < 16) break;
+    const int64_t tiles = (m + tile - 1) / tile;
+    const int64_t ctas = tiles * w_tiles;
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const double cost = static_cast<double>(waves) * (tile + kTileOverhead);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best_tile = tile;
+    }
+    if (tile <= 32) break;
+  }
+  return best_tile;
+}
+
+int check_weight(const w4a4_weight& w, int32_t k, int idx) {
+  if (!w.data) return fail(W4A4_ERR_INVALID, "packed W %d: null data pointer", idx);
+  if (w.n <= 0) return fail(W4A4_ERR_INVALID, "packed W %d: N must be positive, got %d", idx, w.n);
+  if (w.row_words < k / 8 + 1)
+    return fail(W4A4_ERR_INVALID, "packed W second dim must contain K/8 packed words plus a scale");
+  if (!aligned(w.data, 16)) return fail(W4A4_ERR_INVALID, "packed W %d must be 16-byte aligned", idx);
+  if (w.layout == W4A4_LAYOUT_ROW_MAJOR) {
+    if ((static_cast<int64_t>(w.row_words) * 4) % 16 != 0)
+      return fail(W4A4_ERR_UNSUPPORTED,
+                  "row-major packed W row stride (%d words) must be a multiple of 4 words; pad the rows "
+                  "(w4a4_pad_rows / the K/8+8 load-time pad)",
+                  w.row_words);
+  } else if (w.layout == W4A4_LAYOUT_FRAGMENT_MAJOR) {
+    if (w.row_words != k / 8 + 9)
+      return fail(W4A4_ERR_INVALID, "WMMA-fragment-major weights must use the K/8+9 marker stride");
+    if (k % 16 != 0 || (w.n % 2) != 0)
+      return fail(W4A4_ERR_UNSUPPORTED, "fragment-major weights need K %% 16 == 0 and an even N");
+  } else {
+    return fail(W4A4_ERR_INVALID, "unknown weight layout %d", w.layout);
+  }
+  return W4A4_OK;
+}
+
+int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
+                const w4a4_weight* weights, void* const* y, cudaStream_t stream,
+                bool acc_out = false) {
+  if (k <= 0 || k % 64 != 0) return fail(W4A4_ERR_INVALID, "K must be a multiple of 64, got %d", k);
+  if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative");
+  if (n_weights < 1 || n_weights > kMaxSegments)
+    return fail(W4A4_ERR_INVALID, "n_weights must be 1..%d, got %d", kMaxSegments, n_weights);
+  if (!weights || !y) return fail(W4A4_ERR_INVALID, "null weights/outputs array");
+  const int layout = weights[0].layout;
+  for (int i = 0; i < n_weights; ++i) {
+    if (weights[i].layout != layout)
+      return fail(W4A4_ERR_INVALID, "all weights of one call must share a layout");
+    if (int e = check_weight(weights[i], k, i)) return e;
+    if (m > 0 && !y[i]) return fail(W4A4_ERR_INVALID, "output %d is null", i);
+  }
+  if (m == 0) return ok();
+  if (!codes || (!row_scale && !acc_out)) return fail(W4A4_ERR_INVALID, "null codes/scale pointer");
+  if (!aligned(codes, 16)) return fail(W4A4_ERR_INVALID, "codes pointer must be 16-byte aligned");
+  if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large");
+  int dev, sms;
+  if (int e = current_device(&dev)) return e;
+  if (int e = sm_count(dev, &sms)) return e;
+
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  int w_tiles = 0;
+  for (int i = 0; i < n_weights; ++i) {
+    const w4a4_weight& w = weights[i];
+    GemmSegment& s = p.seg[i];
+    if (layout == W4A4_LAYOUT_ROW_MAJOR) {
+      if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT32, k / 8, w.n,
+                              static_cast<uint64_t>(w.row_words) * 4, kBlockK / 8, kBlockW,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+        return e;
+      s.scale = reinterpret_cast<const float*>(w.data + k / 8);
+      s.scale_stride = w.row_words;
+    } else {
+      if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT32,
+                              static_cast<uint64_t>(w.n) * 2, k / 16,
+                              static_cast<uint64_t>(w.n) * 8, 2 * kBlockW, kBlockK / 16,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+        return e;
+      s.scale = reinterpret_cast<const float*>(w.data + static_cast<int64_t>(w.n) * (k / 8));
+      s.scale_stride = 1;
+    }
+    s.y = static_cast<__half*>(y[i]);
+    s.n = w.n;
+    s.tile_begin = w_tiles;
+    w_tiles += (w.n + kBlockW - 1) / kBlockW;
+  }
+  const int tok_tile = choose_tok_tile(m, w_tiles, sms);
+  if (int e = make_map_2d(&p.tmap_tok, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, m, k, kBlockK,
+                          tok_tile, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  p.row_scale = row_scale;
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  p.m = m;
+  p.k = k;
+  p.tok_tile = tok_tile;
+  p.n_seg = n_weights;
+  p.k_tiles = (k + kBlockK - 1) / kBlockK;
+  const dim3 grid(static_cast<unsigned>((m + tok_tile - 1) / tok_tile), static_cast<unsigned>(w_tiles));
+#define W4A4_LAUNCH_GEMM(L, ACC, BIT)                                                          \
+  do {                                                                                        \
+    if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC>, kGemmSmemBytes)) \
+      return e;                                                                               \
+    w4a4_gemm_kernel<L, ACC><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(p);              \
+  } while (0)
+  if (layout == W4A4_LAYOUT_ROW_MAJOR) {
+    if (acc_out) W4A4_LAUNCH_GEMM(kRowMajor, true, 4);
+    else W4A4_LAUNCH_GEMM(kRowMajor, false, 2);
+  } else {
+    if (acc_out) W4A4_LAUNCH_GEMM(kFragmentMajor, true, 5);
+    else W4A4_LAUNCH_GEMM(kFragmentMajor, false, 3);
+  }
+#undef W4A4_LAUNCH_GEMM
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+__global__ void pad_rows_kernel(const int32_t* __restrict__ src, int32_t n, int32_t sw,
+                                int32_t dw, int32_t* __restrict__ dst) {
+  const int64_t total = static_cast<int64_t>(n) * dw;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / dw;
+    const int32_t c = static_cast<int32_t>(i - r * dw);
+    dst[i] = c < sw ? src[r * sw + c] : 0;
+  }
+}
+
+}  // namespace
+}  // namespace w4a4
+
+using namespace w4a4;
+
+extern "C" {
+
+int w4a4_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate, int32_t staging,
+               int32_t codes_format, void* codes, float* row_scale, void* stream) {
+  return launch_quant(x, m, k, ldx, rotate, staging, codes_format, codes, row_scale,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
+              const w4a4_weight* weights, void* const* y, void* stream) {
+  return launch_gemm(codes, row_scale, m, k, n_weights, weights, y,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_gemm_accumulators(const void* codes, int64_t m, int32_t k, int32_t n_weights,
+                           const w4a4_weight* weights, int32_t* const* acc, void* stream) {
+  return launch_gemm(codes, nullptr, m, k, n_weights, weights,
+                     reinterpret_cast<void* const*>(acc), static_cast<cudaStream_t>(stream), true);
+}
+
+int w4a4_int4_gemm(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
+                   int32_t staging, int32_t n_weights, const w4a4_weight* weights, void* const* y,
+                   void* codes_scratch, float* scale_scratch, void* stream) {
+  // Validate the weights before launching anything.
+  if (n_weights < 1 || n_weights > kMaxSegments)
+    return fail(W4A4_ERR_INVALID, "n_weights must be 1..%d, got %d", kMaxSegments, n_weights);
+  if (!weights) return fail(W4A4_ERR_INVALID, "null weights array");
+  if (k > 0 && k % 64 == 0)
+    for (int i = 0; i < n_weights; ++i)
+      if (int e = check_weight(weights[i], k, i)) return e;
+  if (int e = launch_quant(x, m, k, ldx, rotate, staging, W4A4_CODES_INT8, codes_scratch,
+                           scale_scratch, static_cast<cudaStream_t>(stream)))
+    return e;
+  return launch_gemm(codes_scratch, scale_scratch, m, k, n_weights, weights, y,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,
+                  int32_t* dst, void* stream) {
+  if (n < 0 || src_row_words <= 0 || dst_row_words < src_row_words)
+    return fail(W4A4_ERR_INVALID, "invalid pad: n=%d, %d -> %d words", n, src_row_words, dst_row_words);
+  if (n == 0) return ok();
+  if (!src || !dst) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  const int64_t total = static_cast<int64_t>(n) * dst_row_words;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  pad_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(src, n, src_row_words,
+                                                                         dst_row_words, dst);
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int w4a4_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    std::strncpy(buf, t_last_error.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return t_last_status;
+}
+
+int w4a4_device_error(uint32_t* bits, int32_t clear) {
+  if (!bits) return fail(W4A4_ERR_INVALID, "null output pointer");
+  W4A4_CUDA_TRY(cudaDeviceSynchronize());
+  unsigned v = 0;
+  W4A4_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_w4a4_device_error, sizeof(v)));
+  *bits = v;
+  if (clear) {
+    const unsigned zero = 0;
+    W4A4_CUDA_TRY(cudaMemcpyToSymbol(g_w4a4_device_error, &zero, sizeof(zero)));
+  }
+  return ok();
+}
+
+int w4a4_set_wait_limit_ns(uint64_t limit_ns) {
+  if (limit_ns == 0) return fail(W4A4_ERR_INVALID, "wait limit must be positive");
+  g_wait_limit_ns.store(limit_ns);
+  return ok();
+}
+
+int w4a4_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(W4A4_ERR_INVALID, "self-test limit must be in (0, 10 s]");
+  w4a4_selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns);
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int w4a4_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,137 @@
+"""CPU-only tests: the C-ABI library loads and exports every declared symbol,
+host-side argument validation (no CUDA call is reached), the packed-format
+helpers against the reference's golden vectors, and the op layer's
+refusal of CPU tensors (there is no CPU fallback)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from pi05_pytorch_fast_b200 import _native as nat
+from pi05_pytorch_fast_b200.w4a4 import pack as bpack
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions() -> list[str]:
+    text = open(os.path.join(ROOT, "include", "w4a4_sm100.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*int\s+(w4a4_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_binding_symbols():
+    assert declared_functions() == sorted(nat.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(nat.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert nat.lib().w4a4_version() == 100
+
+
+def _err(status):
+    assert status != nat.W4A4_OK
+    return nat.last_error()
+
+
+def test_quant_argument_validation_without_gpu():
+    lib = nat.lib()
+    assert "multiple of 64, got 100" in _err(lib.w4a4_quant(None, 4, 100, 100, -1, 0, 0, None, None, None))
+    assert "positive" in _err(lib.w4a4_quant(None, 4, 0, 0, -1, 0, 0, None, None, None))
+    assert "staging" in _err(lib.w4a4_quant(None, 4, 64, 64, -1, 7, 0, None, None, None))
+    assert "rotation" in _err(lib.w4a4_quant(None, 4, 4096, 4096, 1, 0, 0, None, None, None))
+    # M == 0 is a no-op that succeeds before any device call
+    assert lib.w4a4_quant(None, 0, 2048, 2048, -1, 0, 0, None, None, None) == nat.W4A4_OK
+
+
+def test_gemm_argument_validation_without_gpu():
+    lib = nat.lib()
+    k = 2048
+    fake = 0x1000  # never dereferenced: validation fails first
+    w = nat.weights_array([(fake, 16384, k // 8 + 1, nat.LAYOUT_FRAGMENT_MAJOR)])
+    y = nat.pointer_array([fake])
+    assert "K/8+9 marker stride" in _err(lib.w4a4_gemm(fake, fake, 4, k, 1, w, y, None))
+    w = nat.weights_array([(fake, 64, k // 8 + 1, nat.LAYOUT_ROW_MAJOR)])
+    assert "multiple of 4 words" in _err(lib.w4a4_gemm(fake, fake, 4, k, 1, w, y, None))
+    w = nat.weights_array([(fake, 64, k // 8, nat.LAYOUT_ROW_MAJOR)])
+    assert "K/8 packed words plus a scale" in _err(lib.w4a4_gemm(fake, fake, 4, k, 1, w, y, None))
+    w = nat.weights_array([(fake, 64, 264, 0), (fake, 64, 265, 1)])
+    assert "share a layout" in _err(lib.w4a4_gemm(fake, fake, 4, k, 2, w, nat.pointer_array([fake, fake]), None))
+    assert "n_weights" in _err(lib.w4a4_gemm(fake, fake, 4, k, 4, w, y, None))
+    w = nat.weights_array([(fake + 4, 64, 264, nat.LAYOUT_ROW_MAJOR)])
+    assert "16-byte aligned" in _err(lib.w4a4_gemm(fake, fake, 4, k, 1, w, y, None))
+
+
+def test_ops_refuse_cpu_tensors():
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    x = torch.randn(3, 2048).half()
+    w = torch.zeros(16, 264, dtype=torch.int32)
+    for op in (lambda: ext.int4_gemm(x, w), lambda: ext.int4_gemm3(x, w, w, w),
+               lambda: ext.int4_gemm2(x, w, w)):
+        with pytest.raises(RuntimeError, match="expects CUDA/HIP tensors"):
+            op()
+
+
+def test_fake_impls_give_reference_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        x = torch.empty(2, 776, 2048, dtype=torch.float16, device="cuda")
+        w = torch.empty(2048, 264, dtype=torch.int32, device="cuda")
+        y = torch.ops.pi05_w4a4.int4_gemm(x, w)
+        q, k, v = torch.ops.pi05_w4a4.int4_gemm3(x, w, w[:256], w[:256])
+    assert y.shape == (2, 776, 2048) and y.dtype == torch.float16
+    assert k.shape == (2, 776, 256)
+
+
+@pytest.mark.parametrize("name", ["w2048", "w1024", "w16384", "w128", "wzero"])
+def test_product_packer_matches_reference(golden, name):
+    packed = bpack.pack_linear_weight(torch.from_numpy(golden[f"{name}_w"]))
+    np.testing.assert_array_equal(packed.numpy(), golden[f"{name}_packed"])
+
+
+@pytest.mark.parametrize("name,k", [("pre64", 64), ("pre2048", 2048)])
+def test_product_preshuffle_matches_reference(golden, name, k):
+    tiled = bpack.preshuffle_wmma_weight(torch.from_numpy(golden[f"{name}_packed"]), k)
+    np.testing.assert_array_equal(tiled.numpy(), golden[f"{name}_tiled"])
+
+
+def test_w4a4_linear_constructor_checks():
+    from pi05_pytorch_fast_b200.w4a4 import W4A4Linear
+
+    with pytest.raises(ValueError, match="K/8\\+9 marker stride"):
+        W4A4Linear(torch.zeros(16384, 257, dtype=torch.int32), preshuffled=True)
+    with pytest.raises(ValueError, match="too short"):
+        W4A4Linear(torch.zeros(8, 100, dtype=torch.int32), in_features=2048)
+    lin = W4A4Linear(torch.zeros(8, 264, dtype=torch.int32), in_features=2048)
+    assert lin.rotate and lin.in_features == 2048 and lin.weight.dtype == torch.float16
+
+
+def test_replace_and_fuse_on_a_gemma_model():
+    """Load-time install on a small random Gemma: pad rows to K/8+8, fragment-
+    major gate/up only at K=2048 x N=16384, rebind forwards (no GPU needed)."""
+    from transformers import GemmaConfig
+    from transformers.models.gemma.modeling_gemma import GemmaModel
+
+    from pi05_pytorch_fast_b200.w4a4 import W4A4Linear
+    from pi05_pytorch_fast_b200.w4a4.apply import (fuse_shared_activation_quant, pack_model_linears,
+                                                    replace_linears_from_packed)
+
+    cfg = GemmaConfig(hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=2, num_key_value_heads=1, head_dim=64, vocab_size=64)
+    model = GemmaModel(cfg)
+    tensors, layers = pack_model_linears(model, name_prefixes=("layers.",))
+    assert len(layers) == 14
+    n = replace_linears_from_packed(model, tensors, layers)
+    assert n == 14
+    q = model.layers[0].self_attn.q_proj
+    assert isinstance(q, W4A4Linear) and q.packed.shape[1] == 128 // 8 + 8 and not q.preshuffled
+    assert fuse_shared_activation_quant(model) == 4
