@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--staging", choices=("fp16", "fp32"), default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--roofline-reps", type=int, default=20)
+    ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k"),
+                    default=None, help="run one op 3 times at the bench shape and exit "
+                                       "(a small, self-contained case for ncu)")
     return ap.parse_args()
 
 
@@ -315,8 +318,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
 
     # --- roofline of the dominant kernel: the gate/up GEMM (one launch, two
     # weights) cycling over the layers so weights always come from HBM.
-    codes, scales = ext.quantize(x_static)
-    stream = torch.cuda.current_stream(device)
+    codes, scales = ext.quantize(x_static, fmt="gemm")
     ga = torch.cuda.CUDAGraph()
     with torch.cuda.graph(ga):
         for lw in layers:
@@ -329,7 +331,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
     gq = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gq):
         for _ in range(10):
-            ext.quantize(h16)
+            ext.quantize(h16, fmt="gemm")
     ms_q = time_device(gq.replay, args.roofline_reps, 3, dist_on, device) / 10
     q_bytes = 2 * m * INTER + m * INTER + 4 * m
     del graph, ga, gq
@@ -397,7 +399,8 @@ def run_ours(args, rank, world, local_rank, dist_on):
         },
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline_sample(m, staging, args.layers)
+        # the reference's CPU path is int4_gemm_ref: fp32 FWHT staging
+        result["cpu_baseline"] = cpu_baseline_sample(m, "fp32", args.layers)
     return result
 
 
@@ -409,7 +412,7 @@ def run_reference(args, rank, world):
 
     if rank != 0:
         return None
-    staging = args.staging or os.environ.get("PI05_W4A4_STAGING", "fp16")
+    staging = "fp32"  # int4_gemm_ref's arithmetic (pack.py:113-145)
     m = args.batch * args.prefix
     one_layer = oracle_layer(m, staging)
 
@@ -442,8 +445,44 @@ def run_reference(args, rank, world):
     }
 
 
+def run_case(args):
+    """One op of one layer, 3 launches, for profiling (no timing, no JSON)."""
+    import torch
+
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    if args.staging:
+        os.environ["PI05_W4A4_STAGING"] = args.staging
+    m = args.batch * args.prefix
+    lw = build_layers(1, device, seed=1234)[0]
+    x = synthetic_prefix(m, device, seed=100)
+    h = torch.randn(m, INTER, device=device).half()
+    codes, scales = ext.quantize(x, fmt="gemm")
+    codes_h, scales_h = ext.quantize(h, fmt="gemm")
+    for _ in range(3):
+        if args.case == "qkv":
+            ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]])
+        elif args.case == "o":
+            ext.gemm_from_codes(codes, scales, [lw["o"]])
+        elif args.case == "gateup":
+            ext.gemm_from_codes(codes, scales, [lw["gate"], lw["up"]], fragment_major=True)
+        elif args.case == "down":
+            ext.gemm_from_codes(codes_h, scales_h, [lw["down"]])
+        elif args.case == "quant2k":
+            ext.quantize(x, fmt="gemm")
+        elif args.case == "quant16k":
+            ext.quantize(h, fmt="gemm")
+    torch.cuda.synchronize(device)
+    print(f"case {args.case} done (M={m})")
+
+
 def main():
     args = parse_args()
+    if args.case:
+        run_case(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

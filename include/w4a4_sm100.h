@@ -41,10 +41,14 @@ extern "C" {
 #define W4A4_STAGING_FP32 1
 
 /* ---- activation code formats written by w4a4_quant ----
- * INT8:   one signed code per byte, row-major [M, K] (what w4a4_gemm reads).
- * PACKED: the reference's int32 words [M, K/8], element j at bits 4j. */
+ * INT8:   one signed code per byte, row-major [M, K], natural order.
+ * PACKED: the reference's int32 words [M, K/8], element j at bits 4j.
+ * GEMM:   one signed code per byte, row-major [M, K], each group of 8
+ *         elements stored in the order 0,2,4,6,1,3,5,7 (what w4a4_gemm reads;
+ *         it matches the K order of the GEMM's in-register nibble expansion). */
 #define W4A4_CODES_INT8 0
 #define W4A4_CODES_PACKED 1
+#define W4A4_CODES_GEMM 2
 
 /* ---- weight layouts (the reference's in-memory formats) ----
  * ROW_MAJOR: int32 [N, row_words], word p of row n holds k = 8p..8p+7
@@ -83,7 +87,7 @@ int w4a4_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
 /* W4A4 GEMM of int8 activation codes against 1..3 packed weights that share
  * them (one launch).  Replaces gemm_from_q / gemm_iu4 / gemm_iu4_shape
  * (int4_gemm.cu:66-394, :566-616).
- *   codes      int8 [m, k] from w4a4_quant (W4A4_CODES_INT8), 16-byte aligned
+ *   codes      int8 [m, k] from w4a4_quant (W4A4_CODES_GEMM), 16-byte aligned
  *   row_scale  fp32 [m]
  *   weights    n_weights descriptors, all the same layout, all K = k
  *   y          n_weights fp16 outputs, y[i] is [m, weights[i].n] row-major  */

@@ -30,6 +30,8 @@ Parity status
 from __future__ import annotations
 
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
@@ -68,17 +70,18 @@ def fwht_fp32(x: np.ndarray) -> np.ndarray:
     if n <= 0 or n & (n - 1):
         raise ValueError(f"FWHT length must be a power of 2, got {n}")
     lead = x.shape[:-1]
-    y = x.reshape(-1, n).copy()
-    rows = y.shape[0]
+    src = x.reshape(-1, n).copy()
+    dst = np.empty_like(src)
+    rows = src.shape[0]
     h = 1
     while h < n:
-        v = y.reshape(rows, n // (2 * h), 2, h)
-        a = v[:, :, 0, :].copy()
-        b = v[:, :, 1, :]
-        v[:, :, 0, :] = a + b
-        v[:, :, 1, :] = a - b
+        v = src.reshape(rows, n // (2 * h), 2, h)
+        o = dst.reshape(rows, n // (2 * h), 2, h)
+        np.add(v[:, :, 0, :], v[:, :, 1, :], out=o[:, :, 0, :])
+        np.subtract(v[:, :, 0, :], v[:, :, 1, :], out=o[:, :, 1, :])
+        src, dst = dst, src
         h *= 2
-    return y.reshape(*lead, n)
+    return src.reshape(*lead, n)
 
 
 def fwht_fp16_staged(x: np.ndarray) -> np.ndarray:
@@ -116,6 +119,33 @@ def fwht_fp16_staged(x: np.ndarray) -> np.ndarray:
 # ----------------------------------------------------------------------------
 # Activation quantisation
 # ----------------------------------------------------------------------------
+def _quant_rows(xf: np.ndarray, rot: bool, staging: str, k: int):
+    if rot:
+        if staging == "fp16":
+            xf = fwht_fp16_staged(xf)
+        elif staging == "fp32":
+            xf = fwht_fp32(xf)
+        else:
+            raise ValueError(f"unknown staging {staging!r}")
+    amax = np.abs(xf).max(axis=-1)
+    sdiv = (amax / F32(7.0)).astype(F32) + F32(1e-12)
+    scale = (sdiv * inv_sqrt_k(k)).astype(F32) if rot else sdiv.astype(F32)
+    with np.errstate(invalid="ignore"):
+        q = np.clip(np.rint(xf / sdiv[:, None]), -7, 7)
+    return q.astype(np.int8), scale
+
+
+def _row_chunks(m: int, k: int):
+    """Row blocks for thread-parallel evaluation (numpy releases the GIL on
+    large array operations); rows are independent, so results are identical
+    to a single pass."""
+    if m * k < (1 << 20) or m < 16:
+        return [(0, m)]
+    nchunks = min(m, 4 * (os.cpu_count() or 1))
+    step = -(-m // nchunks)
+    return [(i, min(m, i + step)) for i in range(0, m, step)]
+
+
 def quant_activation(
     x: np.ndarray, rotate: bool | None = None, staging: str = "fp32"
 ) -> tuple[np.ndarray, np.ndarray]:
@@ -134,23 +164,24 @@ def quant_activation(
     if x.ndim != 2:
         raise ValueError("quant_activation expects [M, K]")
     m, k = x.shape
-    xf = x.astype(F32)
-    rot = should_rotate(k, rotate)
-    if rot:
-        if staging == "fp16":
-            xf = fwht_fp16_staged(xf)
-        elif staging == "fp32":
-            xf = fwht_fp32(xf)
-        else:
-            raise ValueError(f"unknown staging {staging!r}")
+    if staging not in ("fp16", "fp32"):
+        raise ValueError(f"unknown staging {staging!r}")
     if m == 0:
         return np.zeros((0, k), np.int8), np.zeros((0,), F32)
-    amax = np.abs(xf).max(axis=-1)
-    sdiv = (amax / F32(7.0)).astype(F32) + F32(1e-12)
-    scale = (sdiv * inv_sqrt_k(k)).astype(F32) if rot else sdiv.astype(F32)
-    with np.errstate(invalid="ignore"):
-        q = np.clip(np.rint(xf / sdiv[:, None]), -7, 7)
-    return q.astype(np.int8), scale
+    rot = should_rotate(k, rotate)
+    chunks = _row_chunks(m, k)
+    if len(chunks) == 1:
+        return _quant_rows(x.astype(F32), rot, staging, k)
+    codes = np.empty((m, k), np.int8)
+    scale = np.empty((m,), F32)
+
+    def work(span):
+        a, b = span
+        codes[a:b], scale[a:b] = _quant_rows(x[a:b].astype(F32), rot, staging, k)
+
+    with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
+        list(pool.map(work, chunks))
+    return codes, scale
 
 
 def quant_rot_rb_loops(x_row: np.ndarray) -> tuple[np.ndarray, np.float32]:
@@ -211,12 +242,16 @@ def pack_nibbles(q: np.ndarray) -> np.ndarray:
 
 
 def unpack_nibbles(packed: np.ndarray, k: int) -> np.ndarray:
-    """int32 [..., K/8] -> int8 [..., K], two's-complement nibbles (pack.py:71-76)."""
-    w = np.asarray(packed).astype(np.int64) & 0xFFFFFFFF
-    shifts = 4 * np.arange(8, dtype=np.int64)
-    nib = (w[..., None] >> shifts) & 0xF
-    q = np.where(nib >= 8, nib - 16, nib).astype(np.int8)
-    return q.reshape(*w.shape[:-1], k)
+    """int32 [..., K/8] -> int8 [..., K], two's-complement nibbles (pack.py:71-76).
+    Little-endian bytes: byte b of a word holds elements 2b (low nibble) and
+    2b+1 (high nibble)."""
+    w = np.ascontiguousarray(packed, dtype=np.int32)
+    b = w.view(np.uint8).reshape(*w.shape[:-1], w.shape[-1] * 4)
+    out = np.empty((*w.shape[:-1], k), dtype=np.uint8)
+    np.bitwise_and(b, 0xF, out=out[..., 0::2])
+    np.right_shift(b, 4, out=out[..., 1::2])
+    out ^= 8
+    return (out.view(np.int8) - np.int8(8)).astype(np.int8)
 
 
 def pack_linear_weight(weight: np.ndarray, rotate: bool | None = None) -> np.ndarray:

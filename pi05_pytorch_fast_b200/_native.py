@@ -22,6 +22,7 @@ STAGING_FP16 = 0
 STAGING_FP32 = 1
 CODES_INT8 = 0
 CODES_PACKED = 1
+CODES_GEMM = 2
 LAYOUT_ROW_MAJOR = 0
 LAYOUT_FRAGMENT_MAJOR = 1
 ROTATE_BY_K = -1

@@ -68,6 +68,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase has not completed
+// sleeps (up to about `hint_ns`) instead of spinning, so waiting warps do not
+// steal issue slots from the single-thread TMA and MMA issuers that share
+// their SM sub-partition.  It wakes when the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up when the
 // CTA's abort flag is raised by another role, or after `limit_ns`; in the
 // latter case it raises the abort flag and ORs `err_bit` into `*err`.
@@ -76,18 +93,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   unsigned err_bit, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > limit_ns) {
-        *abort_flag = 1;
-        atomicOr(err, err_bit);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > limit_ns) {
+      *abort_flag = 1;
+      atomicOr(err, err_bit);
+      return false;
     }
   }
 }
+
+// Position in a ring of `n` slots: slot index and the parity of the current
+// round (flips each time the index wraps).
+struct RingPos {
+  int idx = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void advance(int n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
@@ -103,6 +131,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+
+// Prefetch a 2-D tile into L2 (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -136,6 +172,18 @@ __device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t adesc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, int8 x int8 -> int32, K = 32.  A is
+// M rows in TMEM lanes, 32 K-bytes in 8 consecutive 32-bit columns.
+__device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every previously issued tcgen05.mma of this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -154,6 +202,22 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+// 32 lanes x 32 consecutive 32-bit columns from registers: thread i of the
+// warp writes lane (warp quarter base + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -185,32 +249,18 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
 }
 
-// ---------------------------------------------------------------- misc
-// Byte-wise sign extension of the 4-bit two's-complement value held in the
-// low nibble of each byte (the byte's high nibble must be zero).
-__device__ __forceinline__ uint32_t sext_nibbles_in_bytes(uint32_t b) {
-  return ((b ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
-}
-
-// Two packed words (16 nibbles: element j of word w at bits 4j) -> 16 int8
-// values in element order.
-__device__ __forceinline__ uint4 unpack16_nibbles(uint32_t w0, uint32_t w1) {
-  const uint32_t e0 = sext_nibbles_in_bytes(w0 & 0x0F0F0F0Fu);         // k 0,2,4,6
-  const uint32_t o0 = sext_nibbles_in_bytes((w0 >> 4) & 0x0F0F0F0Fu);  // k 1,3,5,7
-  const uint32_t e1 = sext_nibbles_in_bytes(w1 & 0x0F0F0F0Fu);
-  const uint32_t o1 = sext_nibbles_in_bytes((w1 >> 4) & 0x0F0F0F0Fu);
-  uint4 r;
-  r.x = prmt(e0, o0, 0x5140u);
-  r.y = prmt(e0, o0, 0x7362u);
-  r.z = prmt(e1, o1, 0x5140u);
-  r.w = prmt(e1, o1, 0x7362u);
-  return r;
+// ---------------------------------------------------------------- nibbles
+// One packed weight word (element j of the group at bits 4j..4j+3, two's
+// complement) -> two words of int8 values, each equal to 16 x the element:
+//   lo = elements 0, 2, 4, 6 (the nibble moved to the top of each byte)
+//   hi = elements 1, 3, 5, 7 (already at the top of each byte)
+// A signed nibble in the top half of a byte IS that byte's int8 value / 16,
+// so no sign extension is needed; the GEMM divides the int32 sum by 16
+// exactly.  Activation codes are stored in the same per-8 byte order
+// (0,2,4,6,1,3,5,7), so both operands agree on K.
+__device__ __forceinline__ void expand_nibbles_x16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = (w << 4) & 0xF0F0F0F0u;
+  hi = w & 0xF0F0F0F0u;
 }
 
 }  // namespace w4a4

@@ -15,7 +15,12 @@
 //    8 warps of the CTA;
 //  * staging FP16 = the HIP kernel's arithmetic: stages with stride < R
 //    (R = K/256) in fp32, then the values are rounded to fp16 and every later
-//    stage adds/subtracts in fp32 and rounds back to fp16 (int4_gemm.cu:404-426);
+//    stage adds/subtracts in fp32 and rounds back to fp16 (int4_gemm.cu:404-426).
+//    Here those later stages run as packed half2 adds (__hadd2/__hsub2): for
+//    fp16 a, b the single rounding fl16(a + b) equals fl16(fl32(a + b)),
+//    because binary32 carries at least 2 x 11 + 2 significand bits (double
+//    rounding through it is innocuous), so the result is bit-identical while
+//    two values move per instruction and no conversions are needed;
 //    staging FP32 = the reference's CPU emulation (pack.py:113-131);
 //  * amax, sdiv = amax/7 + 1e-12 and codes = clamp(rint(v/sdiv), -7, 7) with
 //    IEEE division and round-half-even (int4_gemm.cu:427-449);
@@ -47,16 +52,6 @@ __device__ __forceinline__ void load8_half_as_float(const __half* p, float (&v)[
     v[2 * i] = f.x;
     v[2 * i + 1] = f.y;
   }
-}
-
-__device__ __forceinline__ float round_fp16(float v) { return __half2float(__float2half_rn(v)); }
-
-template <int C>
-__device__ __forceinline__ void round_all(float (&v)[C][8]) {
-#pragma unroll
-  for (int c = 0; c < C; ++c)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[c][j] = round_fp16(v[c][j]);
 }
 
 // Butterfly between elements whose index differs in bit log2(h), h < 8.
@@ -102,20 +97,101 @@ __device__ __forceinline__ void stage_across_chunks(float (&v)[C][8], int h) {
       }
 }
 
-// All stages for index bits [0, min(LOGK, 11)) of a warp-resident block of
-// 256*C elements.  In fp16 staging, values are rounded to fp16 after stage
-// RBITS-1 (the reference's fp32 -> fp16 hand-off) and after every later stage.
-template <int C, int NBITS, int RBITS, bool FP16>
-__device__ __forceinline__ void fwht_warp_block(float (&v)[C][8], int lane) {
+// ---- packed-half2 stages: h[c][i] holds elements (8c' + 2i, 8c' + 2i + 1) of
+// the float layout v[c][2i], v[c][2i + 1]; index bit b >= 1 of the 8-vector is
+// bit b - 1 of i.
+template <int C>
+__device__ __forceinline__ void pack_half2(const float (&v)[C][8], __half2 (&h)[C][4]) {
 #pragma unroll
-  for (int b = 0; b < NBITS; ++b) {
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[c][i] = __floats2half2_rn(v[c][2 * i], v[c][2 * i + 1]);
+}
+
+template <int C>
+__device__ __forceinline__ void h2_stage_in_vector(__half2 (&h)[C][4], int hi) {
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (!(i & hi)) {
+        const __half2 a = h[c][i], b = h[c][i + hi];
+        h[c][i] = __hadd2(a, b);
+        h[c][i + hi] = __hsub2(a, b);
+      }
+}
+
+template <int C>
+__device__ __forceinline__ void h2_stage_across_lanes(__half2 (&h)[C][4], int lane, int m) {
+  const bool upper = (lane & m) != 0;
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 mine = h[c][i];
+      const __half2 other = __shfl_xor_sync(0xffffffffu, mine, m);
+      h[c][i] = upper ? __hsub2(other, mine) : __hadd2(mine, other);
+    }
+}
+
+template <int C>
+__device__ __forceinline__ void h2_stage_across_chunks(__half2 (&h)[C][4], int hc) {
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+    if (!(c & hc))
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 a = h[c][i], b = h[c + hc][i];
+        h[c][i] = __hadd2(a, b);
+        h[c + hc][i] = __hsub2(a, b);
+      }
+}
+
+// Stages for index bits [BEGIN, END) on packed half2 values (BEGIN >= 1).
+template <int C, int BEGIN, int END>
+__device__ __forceinline__ void fwht_h2_bits(__half2 (&h)[C][4], int lane) {
+#pragma unroll
+  for (int b = BEGIN; b < END; ++b) {
+    if (b < 3)
+      h2_stage_in_vector<C>(h, 1 << (b - 1));
+    else if (b < 8)
+      h2_stage_across_lanes<C>(h, lane, 1 << (b - 3));
+    else
+      h2_stage_across_chunks<C>(h, 1 << (b - 8));
+  }
+}
+
+// Stages for index bits [BEGIN, END) on fp32 values (no rounding).
+template <int C, int BEGIN, int END>
+__device__ __forceinline__ void fwht_f32_bits(float (&v)[C][8], int lane) {
+#pragma unroll
+  for (int b = BEGIN; b < END; ++b) {
     if (b < 3)
       stage_in_vector<C>(v, 1 << b);
     else if (b < 8)
       stage_across_lanes<C>(v, lane, 1 << (b - 3));
     else
       stage_across_chunks<C>(v, 1 << (b - 8));
-    if (FP16 && b >= RBITS - 1) round_all<C>(v);
+  }
+}
+
+template <int C>
+__device__ __forceinline__ float amax_h2(const __half2 (&h)[C][4]) {
+  __half2 m = __float2half2_rn(0.f);
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m = __hmax2(m, __habs2(h[c][i]));
+  return fmaxf(__low2float(m), __high2float(m));
+}
+
+template <int C>
+__device__ __forceinline__ void unpack_half2(const __half2 (&h)[4], float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
   }
 }
 
@@ -130,125 +206,153 @@ __device__ __forceinline__ float warp_max(float m) {
   return m;
 }
 
-// Eight codes -> either 8 int8 bytes or one packed nibble word.
-template <bool PACKED>
+// Output formats of the activation codes.
+enum CodesMode : int {
+  kCodesInt8 = 0,    // one code per byte, natural element order
+  kCodesPacked = 1,  // the reference's int32 words: 8 nibbles, element j at bits 4j
+  kCodesGemm = 2,    // one code per byte, each group of 8 stored as elements 0,2,4,6,1,3,5,7
+                     // (the K order the GEMM's nibble expansion produces)
+};
+
+// Eight codes (elements elem .. elem+7) in the chosen format.
+template <int MODE>
 __device__ __forceinline__ void store_codes8(void* out, long long elem, const float (&v)[8],
                                              float sdiv) {
-  if constexpr (PACKED) {
+  int q[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) q[j] = quant_code(v[j], sdiv);
+  if constexpr (MODE == kCodesPacked) {
     uint32_t w = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) w |= (static_cast<uint32_t>(quant_code(v[j], sdiv)) & 0xFu) << (4 * j);
+    for (int j = 0; j < 8; ++j) w |= (static_cast<uint32_t>(q[j]) & 0xFu) << (4 * j);
     reinterpret_cast<uint32_t*>(out)[elem >> 3] = w;
   } else {
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      w0 |= (static_cast<uint32_t>(quant_code(v[j], sdiv)) & 0xFFu) << (8 * j);
-      w1 |= (static_cast<uint32_t>(quant_code(v[j + 4], sdiv)) & 0xFFu) << (8 * j);
+      const int a = MODE == kCodesGemm ? 2 * j : j;
+      const int b = MODE == kCodesGemm ? 2 * j + 1 : j + 4;
+      w0 |= (static_cast<uint32_t>(q[a]) & 0xFFu) << (8 * j);
+      w1 |= (static_cast<uint32_t>(q[b]) & 0xFFu) << (8 * j);
     }
     *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(out) + elem) = make_uint2(w0, w1);
   }
 }
 
-// K = 1024 / 2048: one warp per row, 8 rows per 256-thread CTA.
-template <int LOGK, bool FP16, bool PACKED>
-__global__ void __launch_bounds__(kQuantThreads) quant_rot_warp_kernel(
+// K = 1024 / 2048: one warp per row, 4 rows per 128-thread CTA.
+template <int LOGK, bool FP16, int MODE>
+__global__ void __launch_bounds__(128) quant_rot_warp_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k) {
   constexpr int K = 1 << LOGK;
   constexpr int C = K / 256;
   constexpr int RBITS = LOGK - 8;  // log2(K / 256): stages kept in fp32
   const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * (kQuantThreads / 32) + (threadIdx.x >> 5);
+  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
   if (row >= m) return;
   float v[C][8];
   const __half* xr = x + row * ldx + 8 * lane;
 #pragma unroll
   for (int c = 0; c < C; ++c) load8_half_as_float(xr + 256 * c, v[c]);
-  fwht_warp_block<C, LOGK, RBITS, FP16>(v, lane);
-  float mx = 0.f;
+  fwht_f32_bits<C, 0, RBITS>(v, lane);
+  float mx;
+  if constexpr (FP16) {
+    __half2 h[C][4];
+    pack_half2<C>(v, h);
+    fwht_h2_bits<C, RBITS, LOGK>(h, lane);
+    mx = amax_h2<C>(h);
 #pragma unroll
-  for (int c = 0; c < C; ++c)
+    for (int c = 0; c < C; ++c) unpack_half2<C>(h[c], v[c]);
+  } else {
+    fwht_f32_bits<C, RBITS, LOGK>(v, lane);
+    mx = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+    for (int c = 0; c < C; ++c)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+  }
   mx = warp_max(mx);
   const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
   if (lane == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
 #pragma unroll
-  for (int c = 0; c < C; ++c) store_codes8<PACKED>(codes, row * K + 256 * c + 8 * lane, v[c], sdiv);
+  for (int c = 0; c < C; ++c) store_codes8<MODE>(codes, row * K + 256 * c + 8 * lane, v[c], sdiv);
 }
 
 // K = 16384: one 256-thread CTA per row.  Phase 1: warp w transforms its
 // 2048-element slice (index bits 0-10) in registers.  Phase 2: after a
 // shared-memory transpose, thread (c, l) = (warp, lane) holds the 8 slices'
 // values at offsets 256c + 8l + j and finishes bits 11-13 in registers.
-template <bool FP16, bool PACKED>
+template <bool FP16, int MODE>
 __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k) {
   constexpr int K = 16384;
   constexpr int RBITS = 6;  // log2(16384 / 256)
-  using Stage = typename std::conditional<FP16, __half, float>::type;
   extern __shared__ __align__(16) unsigned char quant_smem[];
-  Stage* buf = reinterpret_cast<Stage*>(quant_smem);
   __shared__ float warp_amax[kQuantThreads / 32];
 
   const long long row = blockIdx.x;
   if (row >= m) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float v[8][8];
   {
-    float v[8][8];
     const __half* xr = x + row * ldx + 2048 * warp + 8 * lane;
 #pragma unroll
     for (int c = 0; c < 8; ++c) load8_half_as_float(xr + 256 * c, v[c]);
-    fwht_warp_block<8, 11, RBITS, FP16>(v, lane);
+    fwht_f32_bits<8, 0, RBITS>(v, lane);
+    if constexpr (FP16) {
+      __half2 h[8][4];
+      pack_half2<8>(v, h);
+      fwht_h2_bits<8, RBITS, 11>(h, lane);
+      __half* buf = reinterpret_cast<__half*>(quant_smem);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      Stage* dst = buf + 2048 * warp + 256 * c + 8 * lane;
-      if constexpr (FP16) {
-        uint4 packed;
-        __half2* h = reinterpret_cast<__half2*>(&packed);
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(buf + 2048 * warp + 256 * c + 8 * lane) =
+            *reinterpret_cast<const uint4*>(h[c]);
+    } else {
+      fwht_f32_bits<8, RBITS, 11>(v, lane);
+      float* buf = reinterpret_cast<float*>(quant_smem);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[c][2 * i], v[c][2 * i + 1]);
-        *reinterpret_cast<uint4*>(dst) = packed;
-      } else {
+      for (int c = 0; c < 8; ++c) {
+        float* dst = buf + 2048 * warp + 256 * c + 8 * lane;
         *reinterpret_cast<float4*>(dst) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
         *reinterpret_cast<float4*>(dst + 4) = make_float4(v[c][4], v[c][5], v[c][6], v[c][7]);
       }
     }
   }
   __syncthreads();
-  // Phase 2: v[w][j] = element 2048w + 256*warp + 8*lane + j.
-  float v[8][8];
+  // Phase 2: slot w holds element 2048w + 256*warp + 8*lane + j.
+  float mx;
+  if constexpr (FP16) {
+    const __half* buf = reinterpret_cast<const __half*>(quant_smem);
+    __half2 h[8][4];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const Stage* src = buf + 2048 * w + 256 * warp + 8 * lane;
-    if constexpr (FP16) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(src);
-      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+    for (int w = 0; w < 8; ++w)
+      *reinterpret_cast<uint4*>(h[w]) =
+          *reinterpret_cast<const uint4*>(buf + 2048 * w + 256 * warp + 8 * lane);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(h[i]);
-        v[w][2 * i] = f.x;
-        v[w][2 * i + 1] = f.y;
-      }
-    } else {
+    for (int b = 11; b < 14; ++b) h2_stage_across_chunks<8>(h, 1 << (b - 11));
+    mx = amax_h2<8>(h);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) unpack_half2<8>(h[w], v[w]);
+  } else {
+    const float* buf = reinterpret_cast<const float*>(quant_smem);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float* src = buf + 2048 * w + 256 * warp + 8 * lane;
       const float4 a = *reinterpret_cast<const float4*>(src);
       const float4 b = *reinterpret_cast<const float4*>(src + 4);
       v[w][0] = a.x; v[w][1] = a.y; v[w][2] = a.z; v[w][3] = a.w;
       v[w][4] = b.x; v[w][5] = b.y; v[w][6] = b.z; v[w][7] = b.w;
     }
+#pragma unroll
+    for (int b = 11; b < 14; ++b) stage_across_chunks<8>(v, 1 << (b - 11));
+    mx = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[w][j]));
   }
-#pragma unroll
-  for (int b = 11; b < 14; ++b) {
-    stage_across_chunks<8>(v, 1 << (b - 11));
-    if (FP16) round_all<8>(v);
-  }
-  float mx = 0.f;
-#pragma unroll
-  for (int w = 0; w < 8; ++w)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[w][j]));
   mx = warp_max(mx);
   if (lane == 0) warp_amax[warp] = mx;
   __syncthreads();
@@ -259,12 +363,12 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
   if (threadIdx.x == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
 #pragma unroll
   for (int w = 0; w < 8; ++w)
-    store_codes8<PACKED>(codes, row * K + 2048 * w + 256 * warp + 8 * lane, v[w], sdiv);
+    store_codes8<MODE>(codes, row * K + 2048 * w + 256 * warp + 8 * lane, v[w], sdiv);
 }
 
 // Any K (multiple of 64) without rotation: one warp per row, two passes
 // (amax, then codes).  Replaces quant_rows (int4_gemm.cu:451-477).
-template <bool PACKED>
+template <int MODE>
 __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(
     const __half* __restrict__ x, long long ldx, long long m, int k, void* __restrict__ codes,
     float* __restrict__ row_scale) {
@@ -285,7 +389,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(
   for (int e = 8 * lane; e < k; e += 256) {
     float v[8];
     load8_half_as_float(xr + e, v);
-    store_codes8<PACKED>(codes, row * k + e, v, sdiv);
+    store_codes8<MODE>(codes, row * k + e, v, sdiv);
   }
 }
 

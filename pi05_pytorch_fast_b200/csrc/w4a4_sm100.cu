@@ -173,7 +173,8 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
   if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative, got %lld", (long long)m);
   if (staging != W4A4_STAGING_FP16 && staging != W4A4_STAGING_FP32)
     return fail(W4A4_ERR_INVALID, "unknown staging mode %d", staging);
-  if (codes_format != W4A4_CODES_INT8 && codes_format != W4A4_CODES_PACKED)
+  if (codes_format != W4A4_CODES_INT8 && codes_format != W4A4_CODES_PACKED &&
+      codes_format != W4A4_CODES_GEMM)
     return fail(W4A4_ERR_INVALID, "unknown codes format %d", codes_format);
   bool rot;
   if (rotate == W4A4_ROTATE_BY_K)
@@ -195,65 +196,75 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
 
   const __half* xh = static_cast<const __half*>(x);
   const bool fp16 = staging == W4A4_STAGING_FP16;
-  const bool packed = codes_format == W4A4_CODES_PACKED;
   const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
   const unsigned rows_grid = static_cast<unsigned>((m + 7) / 8);
+  const unsigned rows_grid4 = static_cast<unsigned>((m + 3) / 4);
   if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large: %lld", (long long)m);
 
-#define W4A4_LAUNCH_WARP(LOGK)                                                                \
-  do {                                                                                       \
-    if (fp16 && packed) quant_rot_warp_kernel<LOGK, true, true><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
-    else if (fp16) quant_rot_warp_kernel<LOGK, true, false><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
-    else if (packed) quant_rot_warp_kernel<LOGK, false, true><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
-    else quant_rot_warp_kernel<LOGK, false, false><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, codes, row_scale, isk); \
-  } while (0)
-
-  if (rot && k == 1024) {
-    W4A4_LAUNCH_WARP(10);
-  } else if (rot && k == 2048) {
-    W4A4_LAUNCH_WARP(11);
+  // Instantiate a kernel for every (staging, format) pair.
+  auto dispatch = [&](auto launch) {
+    const auto by_mode = [&](auto fp16_tag) {
+      constexpr bool F = decltype(fp16_tag)::value;
+      switch (codes_format) {
+        case W4A4_CODES_PACKED: launch(std::integral_constant<bool, F>{}, std::integral_constant<int, kCodesPacked>{}); break;
+        case W4A4_CODES_GEMM: launch(std::integral_constant<bool, F>{}, std::integral_constant<int, kCodesGemm>{}); break;
+        default: launch(std::integral_constant<bool, F>{}, std::integral_constant<int, kCodesInt8>{}); break;
+      }
+    };
+    if (fp16) by_mode(std::true_type{});
+    else by_mode(std::false_type{});
+  };
+  int err_code = W4A4_OK;
+  if (rot && (k == 1024 || k == 2048)) {
+    dispatch([&](auto f, auto mode) {
+      constexpr bool F = decltype(f)::value;
+      constexpr int MODE = decltype(mode)::value;
+      if (k == 1024)
+        quant_rot_warp_kernel<10, F, MODE><<<rows_grid4, 128, 0, stream>>>(xh, ldx, m, codes, row_scale, isk);
+      else
+        quant_rot_warp_kernel<11, F, MODE><<<rows_grid4, 128, 0, stream>>>(xh, ldx, m, codes, row_scale, isk);
+    });
   } else if (rot) {
     const unsigned grid = static_cast<unsigned>(m);
-    if (fp16) {
-      const int smem = 16384 * 2;
-      if (packed) quant_rot_16k_kernel<true, true><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
-      else quant_rot_16k_kernel<true, false><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
-    } else {
-      const int smem = 16384 * 4;
-      if (packed) {
-        if (int e = ensure_smem_attr(dev, 1u << 0, quant_rot_16k_kernel<false, true>, smem)) return e;
-        quant_rot_16k_kernel<false, true><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
-      } else {
-        if (int e = ensure_smem_attr(dev, 1u << 1, quant_rot_16k_kernel<false, false>, smem)) return e;
-        quant_rot_16k_kernel<false, false><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
+    dispatch([&](auto f, auto mode) {
+      constexpr bool F = decltype(f)::value;
+      constexpr int MODE = decltype(mode)::value;
+      const int smem = F ? 16384 * 2 : 16384 * 4;
+      if (!F) {
+        if (int e = ensure_smem_attr(dev, 1u << (8 + MODE), quant_rot_16k_kernel<false, MODE>, smem)) {
+          err_code = e;
+          return;
+        }
       }
-    }
+      quant_rot_16k_kernel<F, MODE><<<grid, kQuantThreads, smem, stream>>>(xh, ldx, m, codes, row_scale, isk);
+    });
   } else {
-    if (packed) quant_rows_kernel<true><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, k, codes, row_scale);
-    else quant_rows_kernel<false><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, k, codes, row_scale);
+    dispatch([&](auto, auto mode) {
+      constexpr int MODE = decltype(mode)::value;
+      quant_rows_kernel<MODE><<<rows_grid, kQuantThreads, 0, stream>>>(xh, ldx, m, k, codes, row_scale);
+    });
   }
-#undef W4A4_LAUNCH_WARP
+  if (err_code) return err_code;
   W4A4_CUDA_TRY(cudaGetLastError());
   return ok();
 }
 
 // ------------------------------------------------------------- GEMM
-// Token-tile width: the tile count T is chosen to minimise
-// waves(T) * (tile + kTileOverhead), where the overhead term models the
-// per-K-step cost that does not scale with the tile (the 128-row weight
+// Token-tile width for the persistent GEMM.  The tile count T is chosen to
+// minimise ceil(tiles / SMs) * (tile + kTileOverhead): the busiest CTA's tile
+// count times a per-tile cost in which the overhead term models the work that
+// does not scale with the tile (streaming and unpacking the 128-row weight
 // operand).  Tiles are multiples of 16 (the UMMA N granularity).
 int choose_tok_tile(int64_t m, int w_tiles, int sms) {
   constexpr int kTileOverhead = 64;
   int best_tile = 16;
   double best_cost = 1e300;
-  const int64_t t_min = (m + kMaxTokTile - 1) / kMaxTokTile;
+  const int64_t t_min = (m + kTokTileMax - 1) / kTokTileMax;
   for (int64_t t = t_min; t <= t_min + 64; ++t) {
     const int64_t per = (m + t - 1) / t;
     const int tile = static_cast<int>(((per + 15) / 16) * 16);
-    if (tile < 16) break;
-    const int64_t tiles = (m + tile - 1) / tile;
-    const int64_t ctas = tiles * w_tiles;
-    const int64_t waves = (ctas + sms - 1) / sms;
+    const int64_t tiles = ((m + tile - 1) / tile) * w_tiles;
+    const int64_t waves = (tiles + sms - 1) / sms;
     const double cost = static_cast<double>(waves) * (tile + kTileOverhead);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
@@ -319,7 +330,7 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     if (layout == W4A4_LAYOUT_ROW_MAJOR) {
       if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT32, k / 8, w.n,
                               static_cast<uint64_t>(w.row_words) * 4, kBlockK / 8, kBlockW,
-                              CU_TENSOR_MAP_SWIZZLE_NONE))
+                              CU_TENSOR_MAP_SWIZZLE_64B))
         return e;
       s.scale = reinterpret_cast<const float*>(w.data + k / 8);
       s.scale_stride = w.row_words;
@@ -332,9 +343,10 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
       s.scale = reinterpret_cast<const float*>(w.data + static_cast<int64_t>(w.n) * (k / 8));
       s.scale_stride = 1;
     }
-    s.y = static_cast<__half*>(y[i]);
+    s.y = y[i];
     s.n = w.n;
     s.tile_begin = w_tiles;
+    s.vec_store = (!acc_out && w.n % 8 == 0 && aligned(y[i], 16)) ? 1 : 0;
     w_tiles += (w.n + kBlockW - 1) / kBlockW;
   }
   const int tok_tile = choose_tok_tile(m, w_tiles, sms);
@@ -348,12 +360,18 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   p.tok_tile = tok_tile;
   p.n_seg = n_weights;
   p.k_tiles = (k + kBlockK - 1) / kBlockK;
-  const dim3 grid(static_cast<unsigned>((m + tok_tile - 1) / tok_tile), static_cast<unsigned>(w_tiles));
+  p.stages = gemm_stages(tok_tile);
+  p.a_stages = gemm_a_stages(tok_tile);
+  p.n_tok_tiles = static_cast<int>((m + tok_tile - 1) / tok_tile);
+  p.w_tiles = w_tiles;
+  const int64_t total_tiles = static_cast<int64_t>(p.n_tok_tiles) * w_tiles;
+  if (total_tiles > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "too many tiles");
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
 #define W4A4_LAUNCH_GEMM(L, ACC, BIT)                                                          \
   do {                                                                                        \
-    if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC>, kGemmSmemBytes)) \
+    if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC>, kSmemLimit))     \
       return e;                                                                               \
-    w4a4_gemm_kernel<L, ACC><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(p);              \
+    w4a4_gemm_kernel<L, ACC><<<grid, kGemmThreads, gemm_smem_bytes(tok_tile), stream>>>(p);   \
   } while (0)
   if (layout == W4A4_LAYOUT_ROW_MAJOR) {
     if (acc_out) W4A4_LAUNCH_GEMM(kRowMajor, true, 4);
@@ -413,7 +431,7 @@ int w4a4_int4_gemm(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rot
   if (k > 0 && k % 64 == 0)
     for (int i = 0; i < n_weights; ++i)
       if (int e = check_weight(weights[i], k, i)) return e;
-  if (int e = launch_quant(x, m, k, ldx, rotate, staging, W4A4_CODES_INT8, codes_scratch,
+  if (int e = launch_quant(x, m, k, ldx, rotate, staging, W4A4_CODES_GEMM, codes_scratch,
                            scale_scratch, static_cast<cudaStream_t>(stream)))
     return e;
   return launch_gemm(codes_scratch, scale_scratch, m, k, n_weights, weights, y,

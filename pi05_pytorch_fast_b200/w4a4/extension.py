@@ -241,10 +241,23 @@ def preload() -> None:
 # ---------------------------------------------------------------------------
 # Lower-level entry points (used by tests and the benchmark)
 # ---------------------------------------------------------------------------
-def quantize(x: torch.Tensor, staging: int | None = None, packed: bool = False,
+_CODE_FORMATS = {"int8": nat.CODES_INT8, "packed": nat.CODES_PACKED, "gemm": nat.CODES_GEMM}
+# Byte order of each group of 8 codes in the GEMM format (include/w4a4_sm100.h).
+GEMM_GROUP_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
+
+
+def to_gemm_order(codes: torch.Tensor) -> torch.Tensor:
+    """int8 codes [..., K] in natural order -> the GEMM's byte order."""
+    k = codes.shape[-1]
+    idx = torch.tensor(GEMM_GROUP_ORDER, device=codes.device)
+    return codes.reshape(*codes.shape[:-1], k // 8, 8).index_select(-1, idx).reshape(codes.shape).contiguous()
+
+
+def quantize(x: torch.Tensor, staging: int | None = None, fmt: str = "int8",
              rotate: int = nat.ROTATE_BY_K) -> tuple[torch.Tensor, torch.Tensor]:
-    """Activation codes of x [..., K]: int8 [M, K] (or the reference's packed
-    int32 [M, K/8]) and row scales fp32 [M]."""
+    """Activation codes of x [..., K] and row scales fp32 [M].  ``fmt``:
+    "int8" (natural order int8 [M, K]), "gemm" (int8 [M, K] in the GEMM's
+    byte order) or "packed" (the reference's int32 words [M, K/8])."""
     k = _check_activation(x)
     x2 = x.contiguous()
     if x2.data_ptr() % 16:
@@ -252,21 +265,21 @@ def quantize(x: torch.Tensor, staging: int | None = None, packed: bool = False,
     m = x2.numel() // k
     dev = x.device
     with torch.cuda.device(dev):
-        if packed:
+        if fmt == "packed":
             codes = torch.empty((m, k // 8), dtype=torch.int32, device=dev)
         else:
             codes = torch.empty((m, k), dtype=torch.int8, device=dev)
         scales = torch.empty((m,), dtype=torch.float32, device=dev)
         st = staging_mode() if staging is None else staging
         nat.check(nat.lib().w4a4_quant(
-            x2.data_ptr(), m, k, k, rotate, st,
-            nat.CODES_PACKED if packed else nat.CODES_INT8,
+            x2.data_ptr(), m, k, k, rotate, st, _CODE_FORMATS[fmt],
             codes.data_ptr(), scales.data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
     return codes, scales
 
 
 def gemm_from_codes(codes: torch.Tensor, scales: torch.Tensor, weights, fragment_major=False):
-    """GEMM of int8 codes [M, K] + scales [M] against 1..3 packed weights."""
+    """GEMM of int8 codes [M, K] in the GEMM byte order (``quantize(fmt="gemm")``)
+    + scales [M] against 1..3 packed weights."""
     m, k = codes.shape
     layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment_major else nat.LAYOUT_ROW_MAJOR
     dev = codes.device

@@ -39,6 +39,12 @@ def assert_fp16_equal_and_within_tol(y: np.ndarray, y_ref: np.ndarray) -> None:
     np.testing.assert_array_equal(y.view(np.uint16), y_ref.view(np.uint16))
 
 
+def gemm_order(codes: np.ndarray) -> np.ndarray:
+    """Natural-order int8 codes -> the GEMM's byte order (0,2,4,6,1,3,5,7 per 8)."""
+    m, k = codes.shape
+    return np.ascontiguousarray(codes.reshape(m, k // 8, 8)[:, :, list(ext.GEMM_GROUP_ORDER)].reshape(m, k))
+
+
 def gemm_accumulators(codes: torch.Tensor, weights, fragment_major=False):
     m, k = codes.shape
     layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment_major else nat.LAYOUT_ROW_MAJOR
@@ -68,9 +74,11 @@ def test_quant_codes_and_scales_bit_exact(k, m, staging):
     codes, scale = ext.quantize(xd, staging=STAGINGS[staging])
     np.testing.assert_array_equal(to_np(codes), ref_codes)
     np.testing.assert_array_equal(to_np(scale).view(np.int32), ref_scale.view(np.int32))
-    packed, scale_p = ext.quantize(xd, staging=STAGINGS[staging], packed=True)
+    packed, scale_p = ext.quantize(xd, staging=STAGINGS[staging], fmt="packed")
     np.testing.assert_array_equal(to_np(packed), orc.pack_nibbles(ref_codes))
     np.testing.assert_array_equal(to_np(scale_p).view(np.int32), ref_scale.view(np.int32))
+    gemm_codes, _ = ext.quantize(xd, staging=STAGINGS[staging], fmt="gemm")
+    np.testing.assert_array_equal(to_np(gemm_codes), gemm_order(ref_codes))
 
 
 @pytest.mark.parametrize("k", [64, 192, 4096, 2048])
@@ -128,7 +136,7 @@ def test_gemm_accumulators_bit_exact(m, k, ns, layout):
     packs = [orc.random_packed_weight(n, k, seed=i + m) for i, n in enumerate(ns)]
     frag = layout == "fragment"
     ws = [to_dev(orc.preshuffle_wmma_weight(p, k)) if frag else _row_major(p) for p in packs]
-    accs = gemm_accumulators(to_dev(qa), ws, fragment_major=frag)
+    accs = gemm_accumulators(to_dev(gemm_order(qa)), ws, fragment_major=frag)
     for p, acc in zip(packs, accs):
         qw, _ = orc.weight_codes_scales(p, k, "row")
         np.testing.assert_array_equal(to_np(acc), orc.int_accumulate(qa, qw))
@@ -142,7 +150,7 @@ def test_gemm_fp16_epilogue_bit_exact(m, k, ns, layout):
     packs = [orc.random_packed_weight(n, k, seed=3 * i + m) for i, n in enumerate(ns)]
     frag = layout == "fragment"
     ws = [to_dev(orc.preshuffle_wmma_weight(p, k)) if frag else _row_major(p) for p in packs]
-    ys = ext.gemm_from_codes(to_dev(qa), to_dev(sa), ws, fragment_major=frag)
+    ys = ext.gemm_from_codes(to_dev(gemm_order(qa)), to_dev(sa), ws, fragment_major=frag)
     for p, y in zip(packs, ys):
         qw, sw = orc.weight_codes_scales(p, k, "row")
         ref = orc.dequant(orc.int_accumulate(qa, qw), sa, sw)
@@ -155,7 +163,7 @@ def test_gemm_ragged_token_counts(m):
     rng = np.random.default_rng(m)
     qa = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
     p = orc.random_packed_weight(n, k, seed=m)
-    acc = gemm_accumulators(to_dev(qa), [_row_major(p)])[0]
+    acc = gemm_accumulators(to_dev(gemm_order(qa)), [_row_major(p)])[0]
     qw, _ = orc.weight_codes_scales(p, k, "row")
     np.testing.assert_array_equal(to_np(acc), orc.int_accumulate(qa, qw))
 
@@ -169,7 +177,7 @@ def test_gemm_row_stride_variants_agree():
     qw, _ = orc.weight_codes_scales(p, k, "row")
     ref = orc.int_accumulate(qa, qw)
     for words in (k // 8 + 4, k // 8 + 8, k // 8 + 16):
-        acc = gemm_accumulators(to_dev(qa), [_row_major(p, words)])[0]
+        acc = gemm_accumulators(to_dev(gemm_order(qa)), [_row_major(p, words)])[0]
         np.testing.assert_array_equal(to_np(acc), ref)
 
 
