@@ -85,6 +85,19 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
+// Non-blocking test of a phase: returns immediately.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up when the
 // CTA's abort flag is raised by another role, or after `limit_ns`; in the
 // latter case it raises the abort flag and ORs `err_bit` into `*err`.
@@ -139,6 +152,25 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int 
                    reinterpret_cast<uint64_t>(tmap)),
                "r"(x), "r"(y)
                : "memory");
+}
+
+// Read-only global loads that bypass L1 allocation (streamed weights).
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // ---------------------------------------------------------------- tcgen05
