@@ -62,6 +62,9 @@ extern "C" {
 #define W4A4_LAYOUT_FRAGMENT_MAJOR 1
 
 /* rotate argument of w4a4_quant */
+#define W4A4_GEMM_SINGLE_CTA 0
+#define W4A4_GEMM_CTA_PAIR 1
+
 #define W4A4_ROTATE_BY_K (-1) /* rotate iff K in {1024, 2048, 16384}: the op's dispatch */
 
 typedef struct w4a4_weight {
@@ -127,6 +130,13 @@ int w4a4_device_error(uint32_t* bits, int32_t clear);
 /* Limit, in nanoseconds, of every bounded wait inside kernels launched
  * after this call (default 1e9).  Process-wide. */
 int w4a4_set_wait_limit_ns(uint64_t limit_ns);
+
+/* GEMM kernel variant for launches after this call: W4A4_GEMM_SINGLE_CTA
+ * (default) or W4A4_GEMM_CTA_PAIR (tcgen05 cta_group::2, two SMs per MMA);
+ * both give bit-identical results.  Process-wide; the environment variable
+ * W4A4_GEMM_PAIR=1 sets the initial value.  No counterpart in the reference,
+ * which has one kernel per op. */
+int w4a4_set_gemm_variant(int32_t variant);
 
 /* Test hook: launches one CTA that waits on a barrier nobody arrives at, with
  * the given limit; the kernel must give up, set its error bit and return. */

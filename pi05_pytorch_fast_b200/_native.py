@@ -26,6 +26,8 @@ CODES_GEMM = 2
 LAYOUT_ROW_MAJOR = 0
 LAYOUT_FRAGMENT_MAJOR = 1
 ROTATE_BY_K = -1
+GEMM_SINGLE_CTA = 0
+GEMM_CTA_PAIR = 1
 
 # Every symbol include/w4a4_sm100.h declares.
 EXPORTED_SYMBOLS = (
@@ -37,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "w4a4_last_error",
     "w4a4_device_error",
     "w4a4_set_wait_limit_ns",
+    "w4a4_set_gemm_variant",
     "w4a4_selftest_wait_timeout",
     "w4a4_version",
 )
@@ -123,6 +126,11 @@ def device_error(clear: bool = False) -> int:
 
 def set_wait_limit_ns(limit_ns: int) -> None:
     check(lib().w4a4_set_wait_limit_ns(int(limit_ns)))
+
+
+def set_gemm_variant(variant: int) -> None:
+    """GEMM_SINGLE_CTA (default) or GEMM_CTA_PAIR for launches after this call."""
+    check(lib().w4a4_set_gemm_variant(int(variant)))
 
 
 def weights_array(descs) -> ctypes.Array:

@@ -53,7 +53,11 @@ constexpr int kMaxSegments = 3;
 constexpr int kWpkBytes = kBlockW * kBlockK / 2;  // 8 KB packed weights per step
 constexpr int kEpiBytesPerWarp = 16 * 32 * 2;     // 16 tokens x 32 rows fp16
 constexpr int kEpiScaleBytes = kTokTileMax * 4;   // a tile's token scales, per epilogue warp
-constexpr int kNumBars = 2 * kMaxStages + kMaxAStages + 4 + 1;
+// mbarrier slots reserved in shared memory; sized for the larger of the two
+// layouts (1-CTA: 2 rings + A ring + 5; CTA pair: 3 rings + 5).
+constexpr int kNumBars1 = 2 * kMaxStages + kMaxAStages + 4 + 1;
+constexpr int kNumBarsPair = 3 * kMaxStages + 4 + 1;
+constexpr int kNumBars = kNumBars1 > kNumBarsPair ? kNumBars1 : kNumBarsPair;
 constexpr int kFixedSmem =
     4 * kEpiBytesPerWarp + 4 * kEpiScaleBytes + kNumBars * 8 + 16 + 1024 /*alignment slack*/;
 constexpr int kSmemLimit = 232448;

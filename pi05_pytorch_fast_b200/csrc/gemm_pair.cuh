@@ -1,0 +1,354 @@
+// The W4A4 GEMM on CTA pairs (tcgen05 cta_group::2): same contract, tiles
+// and roles as gemm.cuh's single-CTA kernel, but each MMA instruction spans
+// the two SMs of a cluster.
+//
+// Why: a 1-CTA step feeds each token byte to only 128 weight rows, so the
+// token copy alone needs ~64 B/clk of the ~123 B/clk an SM's TMA engine
+// moves (plus ~136 cycles per box); the kernel is copy-bound.  With a pair,
+// one MMA is M = 256 weight rows (128 per CTA, A in each CTA's own TMEM) x
+// N tokens, and each CTA loads only HALF of the token tile (B is split by N
+// across the pair's shared memory), halving the token traffic per SM.
+//
+// Per pair:
+//  * both CTAs' producers load their own 128 weight rows (1-CTA TMA, local
+//    barrier) and their half of the token tile (cta_group::2 TMA whose bytes
+//    are counted on the LEADER's ready barrier; the leader announces the
+//    whole tile's bytes);
+//  * both CTAs' unpack warps write their rows' A operand into their own TMEM
+//    and arrive remotely on the leader's ready barrier;
+//  * the leader's MMA thread issues the pair MMAs and multicasts its commits
+//    (step done / accumulator full / drain) to both CTAs;
+//  * both CTAs' epilogues read their own TMEM (their 128 weight rows x all N
+//    tokens) and arrive remotely on the leader's accumulator-empty barrier.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace w4a4 {
+
+constexpr int kPairTmemCols = 512;
+static_assert(kNumBarsPair <= kNumBars, "pair barrier layout exceeds the reserved slots");
+
+// Ring depth / shared memory of the pair kernel for a token tile of
+// `tok_tile` rows (each CTA holds tok_tile / 2 of them per stage).
+__host__ __device__ constexpr int gemm_pair_stages(int tok_tile) {
+  return (kSmemLimit - kFixedSmem) / (tok_tile / 2 * kBlockK + kWpkBytes) < kMaxStages
+             ? (kSmemLimit - kFixedSmem) / (tok_tile / 2 * kBlockK + kWpkBytes)
+             : kMaxStages;
+}
+__host__ __device__ constexpr int gemm_pair_smem_bytes(int tok_tile) {
+  return gemm_pair_stages(tok_tile) * (tok_tile / 2 * kBlockK + kWpkBytes) + kFixedSmem;
+}
+
+__device__ __forceinline__ TileCoord decode_pair_tile(const GemmParams& p, int tile, int rank) {
+  const int wt = tile / p.n_tok_tiles;  // 256-row weight tile (pair units)
+  const int tt = tile - wt * p.n_tok_tiles;
+  TileCoord c;
+  c.seg = 0;
+#pragma unroll
+  for (int s = 1; s < kMaxSegments; ++s)
+    if (s < p.n_seg && wt >= p.seg[s].tile_begin) c.seg = s;
+  c.n0 = (wt - p.seg[c.seg].tile_begin) * (2 * kBlockW) + rank * kBlockW;
+  c.t0 = static_cast<long long>(tt) * p.tok_tile;
+  c.rows = static_cast<int>(min(static_cast<long long>(p.tok_tile), p.m - c.t0));
+  return c;
+}
+
+template <int LAYOUT, bool ACC_OUT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    w4a4_gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ uint8_t gemm_smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+  const int S = p.stages, SA = p.a_stages;
+  const int half = p.tok_tile / 2;              // token rows held by each CTA
+  const int tok_bytes = half * kBlockK;         // per CTA per stage
+  uint8_t* tok_ring = base;                     // [S][half * 128], 1 KB aligned
+  uint8_t* wpk_ring = base + S * tok_bytes;     // [S][8 KB]
+  uint8_t* epi = wpk_ring + S * kWpkBytes;      // 4 warps x 1 KB
+  float* tile_scale = reinterpret_cast<float*>(epi + 4 * kEpiBytesPerWarp);  // [4 warps][208]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_scale + 4 * kTokTileMax);
+  // wfull[s]  local: this CTA's packed weights of step i landed.
+  // ready[s]  leader: both token halves landed + 8 unpack warps (both CTAs).
+  // empty[s]  both (multicast commit): MMA(i) completed.
+  // accfull/accempty[2]: accumulator handshake (accempty lives in the leader).
+  const auto bar_wfull = [&](int s) { return smem_addr(bars + s); };
+  const auto bar_ready = [&](int s) { return smem_addr(bars + kMaxStages + s); };
+  const auto bar_empty = [&](int s) { return smem_addr(bars + 2 * kMaxStages + s); };
+  const auto bar_accfull = [&](int b) { return smem_addr(bars + 3 * kMaxStages + b); };
+  const auto bar_accempty = [&](int b) { return smem_addr(bars + 3 * kMaxStages + 2 + b); };
+  const uint32_t bar_drain = smem_addr(bars + 3 * kMaxStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned* err = &g_w4a4_device_error;
+  const uint64_t limit = p.wait_limit_ns;
+  const int total_tiles = p.n_tok_tiles * p.w_tiles;
+  const int acc_cols = p.tok_tile;
+  const int a_col0 = 2 * acc_cols;
+
+  // ---- setup (both CTAs), then a cluster barrier before any remote traffic
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(bar_wfull(s), 1);
+      mbar_init(bar_ready(s), 1 + 8);  // leader producer (all token bytes) + 8 unpack warps
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_accfull(b), 1);
+      mbar_init(bar_accempty(b), 8);   // 4 epilogue warps per CTA
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tmap_tok);
+    for (int s = 0; s < p.n_seg; ++s) tma_prefetch_desc(&p.seg[s].tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_addr(tmem_slot), kPairTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (lane 0, both CTAs)
+    if (lane == 0) {
+      RingPos st;
+      int issued = 0;
+      bool alive = true;
+      for (int tile = cluster; alive && tile < total_tiles; tile += n_clusters) {
+        const TileCoord c = decode_pair_tile(p, tile, rank);
+        const CUtensorMap* wmap = &p.seg[c.seg].tmap_w;
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (issued >= S &&
+              !mbar_wait_bounded_cl(bar_empty(st.idx), st.phase ^ 1u, abort_flag, err,
+                                    kErrWaitEmpty, limit)) {
+            alive = false;
+            break;
+          }
+          const uint32_t wfull = bar_wfull(st.idx), ready = bar_ready(st.idx);
+          mbar_arrive_expect_tx(wfull, kWpkBytes);
+          const uint32_t wdst = smem_addr(wpk_ring + st.idx * kWpkBytes);
+          if constexpr (LAYOUT == kRowMajor)
+            tma_load_2d(wdst, wmap, kt * (kBlockK / 8), c.n0, wfull);
+          else
+            tma_load_2d(wdst, wmap, c.n0 * 2, kt * (kBlockK / 16), wfull);
+          if (leader) mbar_arrive_expect_tx(ready, static_cast<uint32_t>(2 * tok_bytes));
+          tma_load_2d_pair(smem_addr(tok_ring + st.idx * tok_bytes), &p.tmap_tok, kt * kBlockK,
+                           static_cast<int>(c.t0) + static_cast<int>(rank) * half, ready);
+          st.advance(S);
+          ++issued;
+        }
+      }
+      // Drain this CTA's weight copies (token copies are covered by the
+      // leader's MMA drain, which needs every ready phase).
+      for (int i = 0; i < S && i < issued; ++i) {
+        const int last = i + ((issued - 1 - i) / S) * S;
+        volatile int no_abort = 0;
+        mbar_wait_bounded(bar_wfull(i), (last / S) & 1, &no_abort, err, kErrWaitDrain, limit);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader lane 0)
+    if (lane == 0 && leader) {
+      RingPos st;
+      int a_idx = 0;
+      int tcount = 0;
+      bool alive = true;
+      const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
+      const uint32_t a_base = tmem_base + a_col0;
+      bool next_ready = false;
+      for (int tile = cluster; alive && tile < total_tiles; tile += n_clusters, ++tcount) {
+        // The pair splits B by N across the two CTAs' shared memory, so the
+        // MMA's N must equal the width the token halves were loaded for --
+        // the full tile, even when the last tile has fewer valid rows.
+        const uint32_t idesc = idesc_i8(2 * kBlockW, p.tok_tile);
+        const int buf = tcount & 1;
+        if (tcount >= 2 &&
+            !mbar_wait_bounded_cl(bar_accempty(buf), ((tcount >> 1) - 1) & 1, abort_flag, err,
+                                  kErrWaitAccum, limit))
+          break;
+        const uint32_t d_tmem = tmem_base + buf * acc_cols;
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!next_ready &&
+              !mbar_wait_bounded_cl(bar_ready(st.idx), st.phase, abort_flag, err, kErrWaitUnpack,
+                                    limit)) {
+            alive = false;
+            break;
+          }
+          RingPos nx = st;
+          nx.advance(S);
+          next_ready = mbar_test_wait_cl(bar_ready(nx.idx), nx.phase);
+          tc_fence_after();
+          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((st.idx * tok_bytes) >> 4);
+          const uint32_t a_tmem = a_base + a_idx * 32;
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 32; ++kk)
+            umma_i8_ts_pair(d_tmem, a_tmem + 8 * kk, bdesc + 2 * kk, idesc, (kt | kk) != 0);
+          umma_commit_pair_mc(bar_empty(st.idx), 0x3);
+          if (kt == p.k_tiles - 1) umma_commit_pair_mc(bar_accfull(buf), 0x3);
+          st = nx;
+          if (++a_idx == SA) a_idx = 0;
+        }
+      }
+      umma_commit_pair_mc(bar_drain, 0x3);
+    }
+    // Both CTAs: every MMA writing this CTA's TMEM has completed.
+    if (lane == 0) {
+      volatile int no_abort = 0;
+      mbar_wait_bounded_cl(bar_drain, 0, &no_abort, err, kErrWaitDrain, limit);
+    }
+    __syncwarp();
+  } else if (warp < kEpiWarp0) {
+    // ------------------------------------------------ unpack -> own TMEM (A operand)
+    const int group = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    RingPos st, at, lag;
+    int step = 0;
+    bool alive = true;
+    for (int tile = cluster; alive && tile < total_tiles; tile += n_clusters) {
+      for (int kt = 0; kt < p.k_tiles; ++kt) {
+        if ((step & 1) == group) {
+          bool ok = mbar_wait_bounded(bar_wfull(st.idx), st.phase, abort_flag, err, kErrWaitTma,
+                                      limit);
+          if (ok && step >= SA)
+            ok = mbar_wait_bounded_cl(bar_empty(lag.idx), lag.phase, abort_flag, err,
+                                      kErrWaitUnpack, limit);
+          if (!warp_all(ok)) {
+            alive = false;
+            break;
+          }
+          const uint8_t* src = wpk_ring + st.idx * kWpkBytes;
+          uint32_t w[16];
+          if constexpr (LAYOUT == kRowMajor) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint4 v =
+                  *reinterpret_cast<const uint4*>(src + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+              w[4 * c] = v.x;
+              w[4 * c + 1] = v.y;
+              w[4 * c + 2] = v.z;
+              w[4 * c + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const uint2 v = *reinterpret_cast<const uint2*>(src + (g * 128 + r) * 8);
+              w[2 * g] = v.x;
+              w[2 * g + 1] = v.y;
+            }
+          }
+          uint32_t o[32];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) expand_nibbles_x16(w[i], o[2 * i], o[2 * i + 1]);
+          tmem_st_32x32b_x32(tmem_base + lane_addr + a_col0 + at.idx * 32, o);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_ready(st.idx), 0));
+        }
+        ++step;
+        st.advance(S);
+        at.advance(SA);
+        if (step > SA) lag.advance(S);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int ew = warp - kEpiWarp0;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    __half* stage = reinterpret_cast<__half*>(epi + ew * kEpiBytesPerWarp);
+    float* ts = tile_scale + ew * kTokTileMax;
+    int tcount = 0;
+    for (int tile = cluster; tile < total_tiles; tile += n_clusters, ++tcount) {
+      const TileCoord c = decode_pair_tile(p, tile, rank);
+      const int buf = tcount & 1;
+      __syncwarp();
+      if (!ACC_OUT)
+        for (int i = lane; i < c.rows; i += 32) ts[i] = __ldg(p.row_scale + c.t0 + i);
+      __syncwarp();
+      const bool ok = mbar_wait_bounded_cl(bar_accfull(buf), (tcount >> 1) & 1, abort_flag, err,
+                                           kErrWaitAccum, limit);
+      if (!warp_all(ok)) break;
+      tc_fence_after();
+      const GemmSegment& seg = p.seg[c.seg];
+      const int n = c.n0 + quarter * 32 + lane;
+      const bool n_ok = n < seg.n;
+      const float sw =
+          (n_ok && !ACC_OUT) ? __ldg(seg.scale + static_cast<long long>(n) * seg.scale_stride) : 0.f;
+      const int mma_n = (c.rows + 15) & ~15;
+      const long long ldy = seg.n;
+      for (int c0 = 0; c0 < mma_n; c0 += 16) {
+        uint32_t acc[16];
+        tmem_ld_32x32b_x16(tmem_base + lane_addr + buf * acc_cols + c0, acc);
+        tmem_ld_wait();
+        if (c0 + 16 >= mma_n) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_accempty(buf), 0));
+        }
+        if constexpr (ACC_OUT) {
+          int32_t* y = static_cast<int32_t*>(seg.y);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (n_ok && c0 + i < c.rows)
+              y[(c.t0 + c0 + i) * ldy + n] = static_cast<int32_t>(acc[i]) >> 4;
+        } else {
+          __half* y = static_cast<__half*>(seg.y);
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float a0 = __fsub_rn(
+                __int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
+            const float a1 = __fsub_rn(
+                __int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
+            const bool ok0 = c0 + i < c.rows, ok1 = c0 + i + 1 < c.rows;
+            const float v0 = __fmul_rn(__fmul_rn(a0, ok0 ? ts[c0 + i] : 0.f), sw);
+            const float v1 = __fmul_rn(__fmul_rn(a1, ok1 ? ts[c0 + i + 1] : 0.f), sw);
+            const __half2 h = __floats2half2_rn(v0, v1);
+            stage[i * 32 + lane] = __low2half(h);
+            stage[(i + 1) * 32 + lane] = __high2half(h);
+          }
+          __syncwarp();
+          if (seg.vec_store) {
+#pragma unroll
+            for (int pass = 0; pass < 2; ++pass) {
+              const int i = pass * 8 + (lane >> 2);
+              const int ch = lane & 3;
+              const int nn = c.n0 + quarter * 32 + ch * 8;
+              if (c0 + i < c.rows && nn < seg.n)
+                *reinterpret_cast<uint4*>(y + (c.t0 + c0 + i) * ldy + nn) =
+                    *reinterpret_cast<const uint4*>(stage + i * 32 + ch * 8);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (n_ok && c0 + i < c.rows) y[(c.t0 + c0 + i) * ldy + n] = stage[i * 32 + lane];
+          }
+          __syncwarp();
+        }
+      }
+    }
+  }
+
+  // ---- teardown: both CTAs done (incl. every remote arrival and MMA) before
+  // the pair frees its TMEM.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kPairTmemCols);
+  }
+}
+
+}  // namespace w4a4

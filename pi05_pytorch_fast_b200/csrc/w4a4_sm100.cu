@@ -8,6 +8,7 @@
 #include "w4a4_sm100.h"
 
 #include <atomic>
+#include <cstdlib>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -19,6 +20,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "gemm_pair.cuh"
 #include "quant.cuh"
 
 namespace w4a4 {
@@ -298,6 +300,17 @@ int check_weight(const w4a4_weight& w, int32_t k, int idx) {
   return W4A4_OK;
 }
 
+// The single-CTA kernel is the default; W4A4_GEMM_PAIR=1 (or
+// w4a4_set_gemm_variant) selects the CTA-pair (cta_group::2) kernel, which is
+// bit-identical but measured slower on the prefix workload (4.41 vs 3.62 ms
+// per 776-token prefix).
+std::atomic<int> g_gemm_variant{[] {
+  const char* e = std::getenv("W4A4_GEMM_PAIR");
+  return (e && e[0] == '1') ? W4A4_GEMM_CTA_PAIR : W4A4_GEMM_SINGLE_CTA;
+}()};
+
+bool use_pair_kernel() { return g_gemm_variant.load() == W4A4_GEMM_CTA_PAIR; }
+
 int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
                 const w4a4_weight* weights, void* const* y, cudaStream_t stream,
                 bool acc_out = false) {
@@ -321,6 +334,8 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   if (int e = current_device(&dev)) return e;
   if (int e = sm_count(dev, &sms)) return e;
 
+  const bool pair = use_pair_kernel();
+  const int rows_per_wtile = pair ? 2 * kBlockW : kBlockW;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
   int w_tiles = 0;
@@ -347,11 +362,12 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     s.n = w.n;
     s.tile_begin = w_tiles;
     s.vec_store = (!acc_out && w.n % 8 == 0 && aligned(y[i], 16)) ? 1 : 0;
-    w_tiles += (w.n + kBlockW - 1) / kBlockW;
+    w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
-  const int tok_tile = choose_tok_tile(m, w_tiles, sms);
+  const int workers = pair ? sms / 2 : sms;
+  const int tok_tile = choose_tok_tile(m, w_tiles, workers);
   if (int e = make_map_2d(&p.tmap_tok, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, m, k, kBlockK,
-                          tok_tile, CU_TENSOR_MAP_SWIZZLE_128B))
+                          pair ? tok_tile / 2 : tok_tile, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   p.row_scale = row_scale;
   p.wait_limit_ns = g_wait_limit_ns.load();
@@ -360,18 +376,38 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   p.tok_tile = tok_tile;
   p.n_seg = n_weights;
   p.k_tiles = (k + kBlockK - 1) / kBlockK;
-  p.stages = gemm_stages(tok_tile);
+  p.stages = pair ? gemm_pair_stages(tok_tile) : gemm_stages(tok_tile);
   p.a_stages = gemm_a_stages(tok_tile);
   p.n_tok_tiles = static_cast<int>((m + tok_tile - 1) / tok_tile);
   p.w_tiles = w_tiles;
   const int64_t total_tiles = static_cast<int64_t>(p.n_tok_tiles) * w_tiles;
   if (total_tiles > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "too many tiles");
-  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
+  const dim3 grid(pair ? 2u * static_cast<unsigned>(std::min<int64_t>(total_tiles, workers))
+                       : static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
 #define W4A4_LAUNCH_GEMM(L, ACC, BIT)                                                          \
   do {                                                                                        \
-    if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC>, kSmemLimit))     \
-      return e;                                                                               \
-    w4a4_gemm_kernel<L, ACC><<<grid, kGemmThreads, gemm_smem_bytes(tok_tile), stream>>>(p);   \
+    if (pair) {                                                                               \
+      if (int e = ensure_smem_attr(dev, 1u << (16 + (BIT)), w4a4_gemm_pair_kernel<L, ACC>,     \
+                                   kSmemLimit))                                               \
+        return e;                                                                             \
+      cudaLaunchConfig_t cfg = {};                                                            \
+      cudaLaunchAttribute attr[1];                                                            \
+      attr[0].id = cudaLaunchAttributeClusterDimension;                                       \
+      attr[0].val.clusterDim.x = 2;                                                           \
+      attr[0].val.clusterDim.y = 1;                                                           \
+      attr[0].val.clusterDim.z = 1;                                                           \
+      cfg.gridDim = grid;                                                                     \
+      cfg.blockDim = dim3(kGemmThreads);                                                      \
+      cfg.dynamicSmemBytes = gemm_pair_smem_bytes(tok_tile);                                  \
+      cfg.stream = stream;                                                                    \
+      cfg.attrs = attr;                                                                       \
+      cfg.numAttrs = 1;                                                                       \
+      W4A4_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a4_gemm_pair_kernel<L, ACC>, p));              \
+    } else {                                                                                  \
+      if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC>, kSmemLimit))   \
+        return e;                                                                             \
+      w4a4_gemm_kernel<L, ACC><<<grid, kGemmThreads, gemm_smem_bytes(tok_tile), stream>>>(p); \
+    }                                                                                         \
   } while (0)
   if (layout == W4A4_LAYOUT_ROW_MAJOR) {
     if (acc_out) W4A4_LAUNCH_GEMM(kRowMajor, true, 4);
@@ -476,6 +512,13 @@ int w4a4_device_error(uint32_t* bits, int32_t clear) {
 int w4a4_set_wait_limit_ns(uint64_t limit_ns) {
   if (limit_ns == 0) return fail(W4A4_ERR_INVALID, "wait limit must be positive");
   g_wait_limit_ns.store(limit_ns);
+  return ok();
+}
+
+int w4a4_set_gemm_variant(int32_t variant) {
+  if (variant != W4A4_GEMM_SINGLE_CTA && variant != W4A4_GEMM_CTA_PAIR)
+    return fail(W4A4_ERR_INVALID, "unknown GEMM variant %d", variant);
+  g_gemm_variant.store(variant);
   return ok();
 }
 

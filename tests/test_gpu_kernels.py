@@ -56,6 +56,14 @@ def gemm_accumulators(codes: torch.Tensor, weights, fragment_major=False):
     return accs
 
 
+@pytest.fixture(params=["single_cta", "cta_pair"])
+def variant(request):
+    """Runs a GEMM test through each kernel variant; both must be bit-exact."""
+    nat.set_gemm_variant(nat.GEMM_CTA_PAIR if request.param == "cta_pair" else nat.GEMM_SINGLE_CTA)
+    yield request.param
+    nat.set_gemm_variant(nat.GEMM_SINGLE_CTA)
+
+
 @pytest.fixture(autouse=True, scope="module")
 def _no_device_errors():
     nat.device_error(clear=True)
@@ -130,7 +138,7 @@ GEMM_CASES = [
 
 
 @pytest.mark.parametrize("m,k,ns,layout", GEMM_CASES)
-def test_gemm_accumulators_bit_exact(m, k, ns, layout):
+def test_gemm_accumulators_bit_exact(m, k, ns, layout, variant):
     rng = np.random.default_rng(m * 31 + k)
     qa = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
     packs = [orc.random_packed_weight(n, k, seed=i + m) for i, n in enumerate(ns)]
@@ -143,7 +151,7 @@ def test_gemm_accumulators_bit_exact(m, k, ns, layout):
 
 
 @pytest.mark.parametrize("m,k,ns,layout", GEMM_CASES)
-def test_gemm_fp16_epilogue_bit_exact(m, k, ns, layout):
+def test_gemm_fp16_epilogue_bit_exact(m, k, ns, layout, variant):
     rng = np.random.default_rng(m * 17 + k)
     qa = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
     sa = (rng.random(m, dtype=np.float32) * np.float32(0.5) + np.float32(1e-3)).astype(np.float32)
@@ -158,7 +166,7 @@ def test_gemm_fp16_epilogue_bit_exact(m, k, ns, layout):
 
 
 @pytest.mark.parametrize("m", [1, 15, 16, 17, 100, 255, 256, 257, 640, 768, 776, 1000])
-def test_gemm_ragged_token_counts(m):
+def test_gemm_ragged_token_counts(m, variant):
     k, n = 2048, 384
     rng = np.random.default_rng(m)
     qa = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
@@ -168,7 +176,7 @@ def test_gemm_ragged_token_counts(m):
     np.testing.assert_array_equal(to_np(acc), orc.int_accumulate(qa, qw))
 
 
-def test_gemm_row_stride_variants_agree():
+def test_gemm_row_stride_variants_agree(variant):
     """Any 16-byte-multiple row stride is read directly (K/8+8 is the default pad)."""
     m, k, n = 50, 2048, 256
     rng = np.random.default_rng(1)

@@ -69,6 +69,13 @@ def test_gemm_argument_validation_without_gpu():
     assert "16-byte aligned" in _err(lib.w4a4_gemm(fake, fake, 4, k, 1, w, y, None))
 
 
+def test_gemm_variant_selection_validated():
+    lib = nat.lib()
+    assert "unknown GEMM variant 2" in _err(lib.w4a4_set_gemm_variant(2))
+    assert lib.w4a4_set_gemm_variant(nat.GEMM_CTA_PAIR) == nat.W4A4_OK
+    assert lib.w4a4_set_gemm_variant(nat.GEMM_SINGLE_CTA) == nat.W4A4_OK
+
+
 def test_ops_refuse_cpu_tensors():
     from pi05_pytorch_fast_b200.w4a4 import extension as ext
 
