@@ -46,8 +46,10 @@ METRIC = "W4A4 prefix-LM ms per 776-tok prefix; GEMM int TOPS; obs/s at 1/2/4/8 
 UNIT = "obs/s (776-token W4A4 prefixes per second)"
 HIDDEN, INTER, N_Q, N_KV = 2048, 16384, 2048, 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch at
-# M=776 from ncu (profiles/); None until captured.
-GATE_UP_DRAM_BYTES = None
+# M=776, from one `ncu --set full` capture of `bench.py --case gateup` (cold
+# L2; most of the fp16 output is still in L2 when the kernel ends, so writes
+# read low).  Re-captured whenever the GEMM changes.
+GATE_UP_DRAM_BYTES = 35_316_224 + 5_592_576
 
 
 def parse_args():
@@ -224,10 +226,26 @@ def time_device(fn, steps: int, warmup: int, dist_on: bool, device) -> float:
     ms = start.elapsed_time(end) / steps
     if dist_on:
         dist.barrier()
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = max_over_ranks(ms, device)
     return ms
+
+
+def max_over_ranks(value: float, device) -> float:
+    """The largest of every rank's `value` (the step time of the slowest
+    rank); every rank must call it at the same point."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(ms_per_step: float, per_rank_prefixes: int, world: int) -> float:
+    """Whole-job prefixes/s: every rank runs `per_rank_prefixes` independent
+    observations per step (weak scaling), the job's step lasts as long as its
+    slowest rank's."""
+    return per_rank_prefixes * world / (ms_per_step * 1e-3)
 
 
 def oracle_layer(m: int, staging: str):
@@ -340,10 +358,9 @@ def run_ours(args, rank, world, local_rank, dist_on):
     peaks = measured_peaks()
     int8_peak = 2.0 * peaks["bf16_tflops"]
     total_ops = ops_per_prefix(m, args.layers)
-    prefixes_per_step = args.batch * world
     result = {
         "metric": METRIC,
-        "value": prefixes_per_step / (ms * 1e-3),
+        "value": job_throughput(ms, args.batch, world),
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
@@ -371,7 +388,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
         "e2e": {
-            "value": prefixes_per_step / (ms_e2e * 1e-3),
+            "value": job_throughput(ms_e2e, args.batch, world),
             "unit": UNIT,
             "h2d_bytes_per_step": int(x_host.numel() * 2),
             "d2h_bytes_per_step": int(y_host.numel() * 2),

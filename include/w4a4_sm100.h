@@ -61,10 +61,11 @@ extern "C" {
 #define W4A4_LAYOUT_ROW_MAJOR 0
 #define W4A4_LAYOUT_FRAGMENT_MAJOR 1
 
-/* rotate argument of w4a4_quant */
+/* variant argument of w4a4_set_gemm_variant */
 #define W4A4_GEMM_SINGLE_CTA 0
 #define W4A4_GEMM_CTA_PAIR 1
 
+/* rotate argument of w4a4_quant */
 #define W4A4_ROTATE_BY_K (-1) /* rotate iff K in {1024, 2048, 16384}: the op's dispatch */
 
 typedef struct w4a4_weight {

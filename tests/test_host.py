@@ -87,6 +87,24 @@ def test_ops_refuse_cpu_tensors():
             op()
 
 
+def test_extension_module_serves_as_the_reference_compiled_module():
+    """The integration binding assigns this module to the reference's `_mod`
+    (the object load_int4_gemm() returns): it must expose the compiled
+    module's five functions, and the ops must already be registered so the
+    reference's registration returns early."""
+    import inspect
+
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    for name, n_weights in (("int4_gemm", 1), ("int4_gemm_tiled", 1), ("int4_gemm2", 2),
+                            ("int4_gemm2_tiled", 2), ("int4_gemm3", 3)):
+        fn = getattr(ext, name)
+        assert callable(fn)
+        assert len(inspect.signature(fn).parameters) == 1 + n_weights
+        assert hasattr(torch.ops.pi05_w4a4, name)
+    assert callable(ext.preload)
+
+
 def test_fake_impls_give_reference_shapes():
     from torch._subclasses.fake_tensor import FakeTensorMode
 
