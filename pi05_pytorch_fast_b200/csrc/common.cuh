@@ -22,6 +22,7 @@ enum DeviceError : unsigned {
   kErrWaitAccum = 1u << 3,     // the epilogue waited too long for the accumulator
   kErrWaitSelfTest = 1u << 4,  // the self-test wait ran out (expected in that test)
   kErrWaitDrain = 1u << 5,     // teardown gave up draining in-flight copies
+  kErrBadParams = 1u << 6,     // launch parameters outside the kernel's invariants
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -115,6 +116,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
       return false;
     }
   }
+}
+
+// The same bounded wait for single-thread issue loops: the first try_wait is
+// inlined and the bounded sleeping loop lives out of line, which keeps the
+// issuer's hot path short (an inlined slow path costs it ~100 cycles a step).
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                            unsigned* err, unsigned err_bit, uint64_t limit_ns) {
+  return mbar_wait_bounded(bar, parity, abort_flag, err, err_bit, limit_ns);
+}
+__device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, unsigned* err,
+                                               unsigned err_bit, uint64_t limit_ns) {
+  if (__builtin_expect(mbar_try_wait(bar, parity), 1)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, err, err_bit, limit_ns);
 }
 
 // ---- cluster (CTA pair) helpers

@@ -46,20 +46,20 @@ constexpr int kMaxStages = 12;    // shared-memory ring (tokens + packed weights
 constexpr int kMaxAStages = 8;    // TMEM ring of unpacked weights
 constexpr int kTmemCols = 512;
 constexpr int kUnpackGroups = 2;
-constexpr int kGemmThreads = 32 * (2 + 4 * kUnpackGroups + 4);  // 14 warps
+constexpr int kEpiWarps = 8;       // two per TMEM lane quarter, alternate 16-column chunks
+constexpr int kGemmThreads = 32 * (2 + 4 * kUnpackGroups + kEpiWarps);  // 18 warps
 constexpr int kEpiWarp0 = 2 + 4 * kUnpackGroups;
 constexpr int kMaxSegments = 3;
 
 constexpr int kWpkBytes = kBlockW * kBlockK / 2;  // 8 KB packed weights per step
 constexpr int kEpiBytesPerWarp = 16 * 32 * 2;     // 16 tokens x 32 rows fp16
 constexpr int kEpiScaleBytes = kTokTileMax * 4;   // a tile's token scales, per epilogue warp
-// mbarrier slots reserved in shared memory; sized for the larger of the two
-// layouts (1-CTA: 2 rings + A ring + 5; CTA pair: 3 rings + 5).
-constexpr int kNumBars1 = 2 * kMaxStages + kMaxAStages + 4 + 1;
-constexpr int kNumBarsPair = 3 * kMaxStages + 4 + 1;
-constexpr int kNumBars = kNumBars1 > kNumBarsPair ? kNumBars1 : kNumBarsPair;
+// mbarrier slots reserved in shared memory: full / ready / empty rings of
+// kMaxStages each, accfull[2], accempty[2], drain (both kernels' layouts).
+constexpr int kNumBars = 3 * kMaxStages + 4 + 1;
 constexpr int kFixedSmem =
-    4 * kEpiBytesPerWarp + 4 * kEpiScaleBytes + kNumBars * 8 + 16 + 1024 /*alignment slack*/;
+    kEpiWarps * kEpiBytesPerWarp + kEpiWarps * kEpiScaleBytes + kNumBars * 8 + 16 +
+    1024 /*alignment slack*/;
 constexpr int kSmemLimit = 232448;
 static_assert(2 * kTokTileMax + 3 * 32 <= kTmemCols, "TMEM budget");
 
@@ -130,6 +130,108 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) 
 
 __device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
 
+// Token scales of a tile into this warp's private copy, zero past the last
+// valid token (up to the MMA width), so the epilogue needs no per-value test.
+__device__ __forceinline__ void stage_tile_scales(float* ts, const float* row_scale,
+                                                  const TileCoord& c, int lane) {
+  const int mma_n = (c.rows + 15) & ~15;
+  __syncwarp();
+  for (int i = lane; i < mma_n; i += 32) ts[i] = i < c.rows ? __ldg(row_scale + c.t0 + i) : 0.f;
+  __syncwarp();
+}
+
+// One 16-token chunk of the epilogue for one warp: thread `lane` owns weight
+// row n (its TMEM lane) and acc[i] = 16 * sum_k qa[token c0+i] * qw[n].
+template <bool ACC_OUT>
+__device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const TileCoord& c, int n_warp,
+                                               int lane, int c0, float sw, const uint32_t (&acc)[16],
+                                               __half* stage, const float* ts) {
+  const long long ldy = seg.n;
+  const int n = n_warp + lane;
+  const bool n_ok = n < seg.n;
+  if constexpr (ACC_OUT) {
+    int32_t* y = static_cast<int32_t*>(seg.y);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n_ok && c0 + i < c.rows) y[(c.t0 + c0 + i) * ldy + n] = static_cast<int32_t>(acc[i]) >> 4;
+  } else {
+    __half* y = static_cast<__half*>(seg.y);
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(ts + c0 + i);
+      t[i] = v.x;
+      t[i + 1] = v.y;
+      t[i + 2] = v.z;
+      t[i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      // acc / 16 as fp32, exactly: |acc / 16| < 2^22, so adding it to the
+      // integer bits of 1.5 * 2^23 and subtracting that value is exact.
+      const float a0 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
+      const float a1 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
+      const __half2 h = __floats2half2_rn(__fmul_rn(__fmul_rn(a0, t[i]), sw),
+                                          __fmul_rn(__fmul_rn(a1, t[i + 1]), sw));
+      stage[i * 32 + lane] = __low2half(h);
+      stage[(i + 1) * 32 + lane] = __high2half(h);
+    }
+    __syncwarp();
+    if (seg.vec_store) {
+      // 16 tokens x 32 rows -> per token a 64-byte row segment, 16 B per thread
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int i = pass * 8 + (lane >> 2);
+        const int nn = n_warp + (lane & 3) * 8;
+        if (c0 + i < c.rows && nn < seg.n)
+          *reinterpret_cast<uint4*>(y + (c.t0 + c0 + i) * ldy + nn) =
+              *reinterpret_cast<const uint4*>(stage + i * 32 + (lane & 3) * 8);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n_ok && c0 + i < c.rows) y[(c.t0 + c0 + i) * ldy + n] = stage[i * 32 + lane];
+    }
+    __syncwarp();
+  }
+}
+
+// The epilogue of one tile for one warp: its TMEM lane quarter (weight rows
+// n_warp .. n_warp+31), 16-column chunks half, half+2, half+4, ...  The next
+// chunk's TMEM load is issued before the current chunk is processed, and
+// release() is called once, as soon as this warp's last TMEM load completed
+// (the accumulator buffer may then be overwritten).
+template <bool ACC_OUT, typename Release>
+__device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const TileCoord& c, int n_warp,
+                                              uint32_t tacc, int half, int lane, __half* stage,
+                                              const float* ts, Release release) {
+  const int nq = ((c.rows + 15) & ~15) >> 4;
+  const int my = (nq - half + 1) >> 1;  // chunks half + 2j, j < my
+  if (my <= 0) {
+    release();
+    return;
+  }
+  const int n = n_warp + lane;
+  const float sw =
+      (n < seg.n && !ACC_OUT) ? __ldg(seg.scale + static_cast<long long>(n) * seg.scale_stride) : 0.f;
+  uint32_t a0[16], a1[16];
+  tmem_ld_32x32b_x16(tacc + half * 16, a0);
+  tmem_ld_wait();
+  if (my == 1) release();
+  for (int j = 0; j < my; j += 2) {
+    if (j + 1 < my) tmem_ld_32x32b_x16(tacc + (half + 2 * (j + 1)) * 16, a1);
+    epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * j) * 16, sw, a0, stage, ts);
+    if (j + 1 >= my) break;
+    tmem_ld_wait();
+    if (j + 2 == my) release();
+    if (j + 2 < my) tmem_ld_32x32b_x16(tacc + (half + 2 * (j + 2)) * 16, a0);
+    epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * (j + 1)) * 16, sw, a1, stage, ts);
+    if (j + 2 >= my) break;
+    tmem_ld_wait();
+    if (j + 3 == my) release();
+  }
+}
+
 // ACC_OUT = true writes the raw int32 accumulators (seg.y as int32 [M, n])
 // instead of fp16: a test hook that proves the integer products bit-exact.
 template <int LAYOUT, bool ACC_OUT>
@@ -142,21 +244,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int tok_bytes = p.tok_tile * kBlockK;
   uint8_t* tok_ring = base;                              // [S][tok_tile * 128], 1 KB aligned
   uint8_t* wpk_ring = base + S * tok_bytes;              // [S][8 KB]
-  uint8_t* epi = wpk_ring + S * kWpkBytes;               // 4 warps x 1 KB
-  float* tile_scale = reinterpret_cast<float*>(epi + 4 * kEpiBytesPerWarp);  // [4 warps][208]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_scale + 4 * kTokTileMax);
-  // full[s]: TMA bytes of step i landed.  empty[s]: MMA(i) completed, which
-  // also means the unpack of step i finished (the MMA waited for it), so the
-  // token buffer, the packed-weight buffer and -- once the A ring has wrapped
-  // -- the TMEM A slot of step i are free.  One commit per step.
+  uint8_t* epi = wpk_ring + S * kWpkBytes;               // kEpiWarps x 1 KB
+  float* tile_scale = reinterpret_cast<float*>(epi + kEpiWarps * kEpiBytesPerWarp);  // [warps][208]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_scale + kEpiWarps * kTokTileMax);
+  // full[s]   TMA bytes (packed weights + tokens) of step i landed.
+  // ready[s]  the unpack group wrote step i's A operand into TMEM (4 warps,
+  //           each after observing full[s]): the MMA issuer's only wait.
+  // empty[s]  MMA(i) completed (one commit per step): ring slot s is free,
+  //           and so is the TMEM A slot of step i once the A ring wraps.
   const auto bar_full = [&](int s) { return smem_addr(bars + s); };
-  const auto bar_empty = [&](int s) { return smem_addr(bars + kMaxStages + s); };
-  const auto bar_afull = [&](int a) { return smem_addr(bars + 2 * kMaxStages + a); };
-  const auto bar_accfull = [&](int b) { return smem_addr(bars + 2 * kMaxStages + kMaxAStages + b); };
-  const auto bar_accempty = [&](int b) {
-    return smem_addr(bars + 2 * kMaxStages + kMaxAStages + 2 + b);
-  };
-  const uint32_t bar_drain = smem_addr(bars + 2 * kMaxStages + kMaxAStages + 4);
+  const auto bar_ready = [&](int s) { return smem_addr(bars + kMaxStages + s); };
+  const auto bar_empty = [&](int s) { return smem_addr(bars + 2 * kMaxStages + s); };
+  const auto bar_accfull = [&](int b) { return smem_addr(bars + 3 * kMaxStages + b); };
+  const auto bar_accempty = [&](int b) { return smem_addr(bars + 3 * kMaxStages + 2 + b); };
+  const uint32_t bar_drain = smem_addr(bars + 3 * kMaxStages + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -167,16 +268,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int acc_cols = p.tok_tile;
   const int a_col0 = 2 * acc_cols;
 
+  // The issue loop walks the ring in pairs of steps with two A slots: the ring
+  // depth and the step count must be even.  A launch that breaks this touches
+  // nothing and reports it.
+  if ((S & 1) || S < 2 || S > kMaxStages || SA != 2 || (p.k_tiles & 1) || p.k_tiles < 2) {
+    if (threadIdx.x == 0) atomicOr(&g_w4a4_device_error, kErrBadParams);
+    return;
+  }
+
   // ---- setup
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(bar_full(s), 1);
+      mbar_init(bar_ready(s), 4);
       mbar_init(bar_empty(s), 1);
     }
-    for (int a = 0; a < SA; ++a) mbar_init(bar_afull(a), 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accfull(b), 1);
-      mbar_init(bar_accempty(b), 4);
+      mbar_init(bar_accempty(b), kEpiWarps);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -234,12 +343,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (lane 0)
+    // The issue loop is the kernel's critical path: a 128 x T x 128 step is
+    // 2T tensor cycles (416 at T = 208).  It is unrolled over pairs of steps
+    // so that the A slot (2 slots) and the ring offset within a pair are
+    // compile-time; the host makes k_tiles and the ring depth even.  Measured
+    // on B200 this keeps one thread at ~430 cycles a step next to 16 busy
+    // warps, where a loop with per-step runtime ring indices needs ~620.
     if (lane == 0) {
-      RingPos st, at;
+      const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
+      const uint64_t bstep = static_cast<uint64_t>(tok_bytes >> 4);
+      const uint32_t a_slot0 = tmem_base + a_col0, a_slot1 = a_slot0 + 32;
+      const uint32_t ready0 = bar_ready(0), empty0 = bar_empty(0);
+      int sidx = 0;  // ring slot of the pair's first step (even)
+      uint32_t sphase = 0;
+      uint64_t bdesc = bdesc0;
       int tcount = 0;
       bool alive = true;
-      const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
-      const uint32_t a_base = tmem_base + a_col0;
       for (int tile = blockIdx.x; alive && tile < total_tiles; tile += gridDim.x, ++tcount) {
         const TileCoord c = decode_tile(p, tile);
         const uint32_t idesc = idesc_i8(kBlockW, (c.rows + 15) & ~15);
@@ -249,24 +368,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                kErrWaitAccum, limit))
           break;
         const uint32_t d_tmem = tmem_base + buf * acc_cols;
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!mbar_wait_bounded(bar_full(st.idx), st.phase, abort_flag, err, kErrWaitTma, limit) ||
-              !mbar_wait_bounded(bar_afull(at.idx), at.phase, abort_flag, err, kErrWaitUnpack,
-                                 limit)) {
+        for (int kt = 0; kt < p.k_tiles; kt += 2) {
+          const uint32_t rbar = ready0 + 8u * sidx, ebar = empty0 + 8u * sidx;
+          if (!mbar_wait_fast(rbar, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
             alive = false;
             break;
           }
           tc_fence_after();
-          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((st.idx * tok_bytes) >> 4);
-          const uint32_t a_tmem = a_base + at.idx * 32;
-#pragma unroll
-          for (int kk = 0; kk < kBlockK / 32; ++kk)
-            umma_i8_ts(d_tmem, a_tmem + 8 * kk, bdesc + 2 * kk, idesc, (kt | kk) != 0);
-          umma_commit(bar_empty(st.idx));
-          if (kt == p.k_tiles - 1) umma_commit(bar_accfull(buf));
-          st.advance(S);
-          at.advance(SA);
+          umma_i8_ts(d_tmem, a_slot0, bdesc, idesc, kt != 0);
+          umma_i8_ts(d_tmem, a_slot0 + 8, bdesc + 2, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot0 + 16, bdesc + 4, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot0 + 24, bdesc + 6, idesc, 1u);
+          umma_commit(ebar);
+          if (!mbar_wait_fast(rbar + 8, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc1 = bdesc + bstep;
+          umma_i8_ts(d_tmem, a_slot1, bdesc1, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot1 + 8, bdesc1 + 2, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot1 + 16, bdesc1 + 4, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot1 + 24, bdesc1 + 6, idesc, 1u);
+          umma_commit(ebar + 8);
+          sidx += 2;
+          if (sidx == S) {
+            sidx = 0;
+            sphase ^= 1u;
+            bdesc = bdesc0;
+          } else {
+            bdesc = bdesc1 + bstep;
+          }
         }
+        if (!alive) break;
+        umma_commit(bar_accfull(buf));
       }
       // Every MMA of this CTA has completed once this commit arrives.
       umma_commit(bar_drain);
@@ -326,7 +461,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_afull(at.idx));
+          if (lane == 0) mbar_arrive(bar_ready(st.idx));
         }
         ++step;
         st.advance(S);
@@ -338,81 +473,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int ew = warp - kEpiWarp0;
+    const int half = ew >> 2;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     __half* stage = reinterpret_cast<__half*>(epi + ew * kEpiBytesPerWarp);
+    float* ts = tile_scale + ew * kTokTileMax;  // warp-private
     int tcount = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
       const TileCoord c = decode_tile(p, tile);
       const int buf = tcount & 1;
-      // This warp's copy of the tile's token scales (warp-private: only the
-      // warp's own lanes write and read it).
-      float* ts = tile_scale + ew * kTokTileMax;
-      __syncwarp();
-      if (!ACC_OUT)
-        for (int i = lane; i < c.rows; i += 32) ts[i] = __ldg(p.row_scale + c.t0 + i);
-      __syncwarp();
+      if (!ACC_OUT) stage_tile_scales(ts, p.row_scale, c, lane);
       const bool ok = mbar_wait_bounded(bar_accfull(buf), (tcount >> 1) & 1, abort_flag, err,
                                         kErrWaitAccum, limit);
       if (!warp_all(ok)) break;
       tc_fence_after();
-      const GemmSegment& seg = p.seg[c.seg];
-      const int n = c.n0 + quarter * 32 + lane;
-      const bool n_ok = n < seg.n;
-      const float sw =
-          (n_ok && !ACC_OUT) ? __ldg(seg.scale + static_cast<long long>(n) * seg.scale_stride) : 0.f;
-      const int mma_n = (c.rows + 15) & ~15;
-      const long long ldy = seg.n;
-      for (int c0 = 0; c0 < mma_n; c0 += 16) {
-        uint32_t acc[16];
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + buf * acc_cols + c0, acc);
-        tmem_ld_wait();
-        if (c0 + 16 >= mma_n) {
-          // whole accumulator read: hand the buffer back to the MMA issuer
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_accempty(buf));
-        }
-        if constexpr (ACC_OUT) {
-          int32_t* y = static_cast<int32_t*>(seg.y);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (n_ok && c0 + i < c.rows)
-              y[(c.t0 + c0 + i) * ldy + n] = static_cast<int32_t>(acc[i]) >> 4;
-        } else {
-          __half* y = static_cast<__half*>(seg.y);
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            // acc / 16 as fp32, exactly: |acc / 16| < 2^22, so adding it to the
-            // integer bits of 1.5 * 2^23 and subtracting that value is exact.
-            const float a0 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
-            const float a1 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
-            const bool ok0 = c0 + i < c.rows, ok1 = c0 + i + 1 < c.rows;
-            const float v0 = __fmul_rn(__fmul_rn(a0, ok0 ? ts[c0 + i] : 0.f), sw);
-            const float v1 = __fmul_rn(__fmul_rn(a1, ok1 ? ts[c0 + i + 1] : 0.f), sw);
-            const __half2 h = __floats2half2_rn(v0, v1);
-            stage[i * 32 + lane] = __low2half(h);
-            stage[(i + 1) * 32 + lane] = __high2half(h);
-          }
-          __syncwarp();
-          if (seg.vec_store) {
-            // 16 tokens x 32 rows -> per token a 64-byte row segment, 16 B per thread
-#pragma unroll
-            for (int pass = 0; pass < 2; ++pass) {
-              const int i = pass * 8 + (lane >> 2);
-              const int ch = lane & 3;
-              const int nn = c.n0 + quarter * 32 + ch * 8;
-              if (c0 + i < c.rows && nn < seg.n)
-                *reinterpret_cast<uint4*>(y + (c.t0 + c0 + i) * ldy + nn) =
-                    *reinterpret_cast<const uint4*>(stage + i * 32 + ch * 8);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (n_ok && c0 + i < c.rows) y[(c.t0 + c0 + i) * ldy + n] = stage[i * 32 + lane];
-          }
-          __syncwarp();
-        }
-      }
+      const uint32_t accempty = bar_accempty(buf);
+      epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32,
+                             tmem_base + lane_addr + buf * acc_cols, half, lane, stage, ts, [&] {
+                               tc_fence_before();
+                               __syncwarp();
+                               if (lane == 0) mbar_arrive(accempty);
+                             });
     }
   }
 

@@ -27,7 +27,6 @@
 namespace w4a4 {
 
 constexpr int kPairTmemCols = 512;
-static_assert(kNumBarsPair <= kNumBars, "pair barrier layout exceeds the reserved slots");
 
 // Ring depth / shared memory of the pair kernel for a token tile of
 // `tok_tile` rows (each CTA holds tok_tile / 2 of them per stage).
@@ -68,9 +67,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int tok_bytes = half * kBlockK;         // per CTA per stage
   uint8_t* tok_ring = base;                     // [S][half * 128], 1 KB aligned
   uint8_t* wpk_ring = base + S * tok_bytes;     // [S][8 KB]
-  uint8_t* epi = wpk_ring + S * kWpkBytes;      // 4 warps x 1 KB
-  float* tile_scale = reinterpret_cast<float*>(epi + 4 * kEpiBytesPerWarp);  // [4 warps][208]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_scale + 4 * kTokTileMax);
+  uint8_t* epi = wpk_ring + S * kWpkBytes;      // kEpiWarps x 1 KB
+  float* tile_scale = reinterpret_cast<float*>(epi + kEpiWarps * kEpiBytesPerWarp);  // [warps][208]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_scale + kEpiWarps * kTokTileMax);
   // wfull[s]  local: this CTA's packed weights of step i landed.
   // ready[s]  leader: both token halves landed + 8 unpack warps (both CTAs).
   // empty[s]  both (multicast commit): MMA(i) completed.
@@ -100,7 +99,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accfull(b), 1);
-      mbar_init(bar_accempty(b), 8);   // 4 epilogue warps per CTA
+      mbar_init(bar_accempty(b), 2 * kEpiWarps);  // every epilogue warp of both CTAs
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -267,6 +266,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int ew = warp - kEpiWarp0;
+    const int half = ew >> 2;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     __half* stage = reinterpret_cast<__half*>(epi + ew * kEpiBytesPerWarp);
     float* ts = tile_scale + ew * kTokTileMax;
@@ -274,70 +274,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = cluster; tile < total_tiles; tile += n_clusters, ++tcount) {
       const TileCoord c = decode_pair_tile(p, tile, rank);
       const int buf = tcount & 1;
-      __syncwarp();
-      if (!ACC_OUT)
-        for (int i = lane; i < c.rows; i += 32) ts[i] = __ldg(p.row_scale + c.t0 + i);
-      __syncwarp();
+      if (!ACC_OUT) stage_tile_scales(ts, p.row_scale, c, lane);
       const bool ok = mbar_wait_bounded_cl(bar_accfull(buf), (tcount >> 1) & 1, abort_flag, err,
                                            kErrWaitAccum, limit);
       if (!warp_all(ok)) break;
       tc_fence_after();
-      const GemmSegment& seg = p.seg[c.seg];
-      const int n = c.n0 + quarter * 32 + lane;
-      const bool n_ok = n < seg.n;
-      const float sw =
-          (n_ok && !ACC_OUT) ? __ldg(seg.scale + static_cast<long long>(n) * seg.scale_stride) : 0.f;
-      const int mma_n = (c.rows + 15) & ~15;
-      const long long ldy = seg.n;
-      for (int c0 = 0; c0 < mma_n; c0 += 16) {
-        uint32_t acc[16];
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + buf * acc_cols + c0, acc);
-        tmem_ld_wait();
-        if (c0 + 16 >= mma_n) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_accempty(buf), 0));
-        }
-        if constexpr (ACC_OUT) {
-          int32_t* y = static_cast<int32_t*>(seg.y);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (n_ok && c0 + i < c.rows)
-              y[(c.t0 + c0 + i) * ldy + n] = static_cast<int32_t>(acc[i]) >> 4;
-        } else {
-          __half* y = static_cast<__half*>(seg.y);
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            const float a0 = __fsub_rn(
-                __int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
-            const float a1 = __fsub_rn(
-                __int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
-            const bool ok0 = c0 + i < c.rows, ok1 = c0 + i + 1 < c.rows;
-            const float v0 = __fmul_rn(__fmul_rn(a0, ok0 ? ts[c0 + i] : 0.f), sw);
-            const float v1 = __fmul_rn(__fmul_rn(a1, ok1 ? ts[c0 + i + 1] : 0.f), sw);
-            const __half2 h = __floats2half2_rn(v0, v1);
-            stage[i * 32 + lane] = __low2half(h);
-            stage[(i + 1) * 32 + lane] = __high2half(h);
-          }
-          __syncwarp();
-          if (seg.vec_store) {
-#pragma unroll
-            for (int pass = 0; pass < 2; ++pass) {
-              const int i = pass * 8 + (lane >> 2);
-              const int ch = lane & 3;
-              const int nn = c.n0 + quarter * 32 + ch * 8;
-              if (c0 + i < c.rows && nn < seg.n)
-                *reinterpret_cast<uint4*>(y + (c.t0 + c0 + i) * ldy + nn) =
-                    *reinterpret_cast<const uint4*>(stage + i * 32 + ch * 8);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (n_ok && c0 + i < c.rows) y[(c.t0 + c0 + i) * ldy + n] = stage[i * 32 + lane];
-          }
-          __syncwarp();
-        }
-      }
+      const uint32_t accempty = mapa_shared(bar_accempty(buf), 0);
+      epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32,
+                             tmem_base + lane_addr + buf * acc_cols, half, lane, stage, ts, [&] {
+                               tc_fence_before();
+                               __syncwarp();
+                               if (lane == 0) mbar_arrive_cluster(accempty);
+                             });
     }
   }
 
