@@ -6,8 +6,8 @@
 //
 //  * each row is held in registers: lane l of a warp loads 16-byte vectors
 //    (8 fp16) at element offsets 256*c + 8*l, so element index bits 0-2 live
-//    inside a thread, bits 3-7 across the 32 lanes and bits 8-10 across the
-//    thread's chunks c;
+//    inside a thread, bits 3-7 across the 32 lanes and bits 8 and up across
+//    the thread's chunks c and the row's warps;
 //  * butterflies run in ascending stride order (h = 1, 2, 4, ...), exactly the
 //    order of the reference, so every value is bit-identical: stride bits 0-2
 //    and 8-10 are in-register, bits 3-7 use __shfl_xor_sync, and for
@@ -23,7 +23,8 @@
 //    two values move per instruction and no conversions are needed;
 //    staging FP32 = the reference's CPU emulation (pack.py:113-131);
 //  * amax, sdiv = amax/7 + 1e-12 and codes = clamp(rint(v/sdiv), -7, 7) with
-//    IEEE division and round-half-even (int4_gemm.cu:427-449);
+//    the IEEE quotient and round-half-even (int4_gemm.cu:427-449), computed
+//    through a reciprocal with an exact fallback next to ties (quant_code);
 //  * codes are written either as int8 (one code per byte, the layout the
 //    tensor-core GEMM consumes) or as the reference's packed int32 words
 //    (8 nibbles per word, element j at bits 4j).
@@ -195,8 +196,19 @@ __device__ __forceinline__ void unpack_half2(const __half2 (&h)[4], float (&v)[8
   }
 }
 
-__device__ __forceinline__ int quant_code(float v, float sdiv) {
-  const int q = __float2int_rn(__fdiv_rn(v, sdiv));
+// clamp(rint(v / sdiv), -7, 7) with the IEEE quotient, bit for bit, but
+// without a division per element.  rs = fl(1 / sdiv); t = fl(v * rs) then
+// differs from the exact quotient Q by at most |Q| (2^-23 + 2^-48), and the
+// correctly rounded quotient fl(Q) by at most 1.8e-7 |Q| <= 1.5e-6 for
+// |Q| <= 8.  rint only changes at half-integers, so whenever t is farther
+// than 4e-6 from one, rint(t) == rint(fl(Q)); the rare values that close to a
+// tie (and NaN) take the IEEE division.  For |Q| > 8 both results clamp to
+// +-7 (t >= 8 implies fl(Q) > 7.5).
+__device__ __forceinline__ int quant_code(float v, float sdiv, float rs) {
+  const float t = __fmul_rn(v, rs);
+  const float frac = __fsub_rn(t, floorf(t));  // exact for |t| < 2^23
+  const int q = fabsf(__fsub_rn(frac, 0.5f)) > 4e-6f ? __float2int_rn(t)
+                                                      : __float2int_rn(__fdiv_rn(v, sdiv));
   return max(-7, min(7, q));
 }
 
@@ -217,10 +229,10 @@ enum CodesMode : int {
 // Eight codes (elements elem .. elem+7) in the chosen format.
 template <int MODE>
 __device__ __forceinline__ void store_codes8(void* out, long long elem, const float (&v)[8],
-                                             float sdiv) {
+                                             float sdiv, float rs) {
   int q[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) q[j] = quant_code(v[j], sdiv);
+  for (int j = 0; j < 8; ++j) q[j] = quant_code(v[j], sdiv, rs);
   if constexpr (MODE == kCodesPacked) {
     uint32_t w = 0;
 #pragma unroll
@@ -239,19 +251,27 @@ __device__ __forceinline__ void store_codes8(void* out, long long elem, const fl
   }
 }
 
-// K = 1024 / 2048: one warp per row, 4 rows per 128-thread CTA.
+// K = 1024 / 2048: one 64-thread CTA (two warps) per row, so that a 776-row
+// activation is resident in a single wave (~10 warps per SM).  Warp w holds
+// chunks [w C/2, (w+1) C/2): index bits 0-2 are in the thread, 3-7 across
+// lanes, 8 .. LOGK-2 across the warp's chunks and bit LOGK-1 across the two
+// warps, whose butterfly (the last stage, as in the reference's ascending
+// order) goes through shared memory.
 template <int LOGK, bool FP16, int MODE>
-__global__ void __launch_bounds__(128) quant_rot_warp_kernel(
+__global__ void __launch_bounds__(64) quant_rot_warp_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k) {
   constexpr int K = 1 << LOGK;
-  constexpr int C = K / 256;
+  constexpr int C = K / 512;       // chunks of 256 elements per warp
   constexpr int RBITS = LOGK - 8;  // log2(K / 256): stages kept in fp32
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  static_assert(RBITS <= 3, "fp32 stages must stay inside a thread");
+  __shared__ __align__(16) uint4 xchg[2][C][32][FP16 ? 1 : 2];
+  __shared__ float warp_amax[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = blockIdx.x;
   if (row >= m) return;
   float v[C][8];
-  const __half* xr = x + row * ldx + 8 * lane;
+  const __half* xr = x + row * ldx + 256 * C * warp + 8 * lane;
 #pragma unroll
   for (int c = 0; c < C; ++c) load8_half_as_float(xr + 256 * c, v[c]);
   fwht_f32_bits<C, 0, RBITS>(v, lane);
@@ -259,23 +279,54 @@ __global__ void __launch_bounds__(128) quant_rot_warp_kernel(
   if constexpr (FP16) {
     __half2 h[C][4];
     pack_half2<C>(v, h);
-    fwht_h2_bits<C, RBITS, LOGK>(h, lane);
+    fwht_h2_bits<C, RBITS, LOGK - 1>(h, lane);
+#pragma unroll
+    for (int c = 0; c < C; ++c) xchg[warp][c][lane][0] = *reinterpret_cast<const uint4*>(h[c]);
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const uint4 o = xchg[warp ^ 1][c][lane][0];
+      const __half2* oh = reinterpret_cast<const __half2*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) h[c][i] = warp ? __hsub2(oh[i], h[c][i]) : __hadd2(h[c][i], oh[i]);
+    }
     mx = amax_h2<C>(h);
 #pragma unroll
     for (int c = 0; c < C; ++c) unpack_half2<C>(h[c], v[c]);
   } else {
-    fwht_f32_bits<C, RBITS, LOGK>(v, lane);
+    fwht_f32_bits<C, RBITS, LOGK - 1>(v, lane);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      xchg[warp][c][lane][0] = make_uint4(__float_as_uint(v[c][0]), __float_as_uint(v[c][1]),
+                                          __float_as_uint(v[c][2]), __float_as_uint(v[c][3]));
+      xchg[warp][c][lane][1] = make_uint4(__float_as_uint(v[c][4]), __float_as_uint(v[c][5]),
+                                          __float_as_uint(v[c][6]), __float_as_uint(v[c][7]));
+    }
+    __syncthreads();
     mx = 0.f;
 #pragma unroll
-    for (int c = 0; c < C; ++c)
+    for (int c = 0; c < C; ++c) {
+      const uint4 o0 = xchg[warp ^ 1][c][lane][0], o1 = xchg[warp ^ 1][c][lane][1];
+      const float o[8] = {__uint_as_float(o0.x), __uint_as_float(o0.y), __uint_as_float(o0.z),
+                          __uint_as_float(o0.w), __uint_as_float(o1.x), __uint_as_float(o1.y),
+                          __uint_as_float(o1.z), __uint_as_float(o1.w)};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+      for (int j = 0; j < 8; ++j) {
+        v[c][j] = warp ? __fsub_rn(o[j], v[c][j]) : __fadd_rn(v[c][j], o[j]);
+        mx = fmaxf(mx, fabsf(v[c][j]));
+      }
+    }
   }
   mx = warp_max(mx);
+  if (lane == 0) warp_amax[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(warp_amax[0], warp_amax[1]);
   const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
-  if (lane == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+  const float rs = __frcp_rn(sdiv);
+  if (threadIdx.x == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
 #pragma unroll
-  for (int c = 0; c < C; ++c) store_codes8<MODE>(codes, row * K + 256 * c + 8 * lane, v[c], sdiv);
+  for (int c = 0; c < C; ++c)
+    store_codes8<MODE>(codes, row * K + 256 * (C * warp + c) + 8 * lane, v[c], sdiv, rs);
 }
 
 // K = 16384: one 256-thread CTA per row.  Phase 1: warp w transforms its
@@ -360,10 +411,11 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
 #pragma unroll
   for (int w = 1; w < 8; ++w) mx = fmaxf(mx, warp_amax[w]);
   const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  const float rs = __frcp_rn(sdiv);
   if (threadIdx.x == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
 #pragma unroll
   for (int w = 0; w < 8; ++w)
-    store_codes8<MODE>(codes, row * K + 2048 * w + 256 * warp + 8 * lane, v[w], sdiv);
+    store_codes8<MODE>(codes, row * K + 2048 * w + 256 * warp + 8 * lane, v[w], sdiv, rs);
 }
 
 // Any K (multiple of 64) without rotation: one warp per row, two passes
@@ -385,11 +437,12 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(
   }
   mx = warp_max(mx);
   const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  const float rs = __frcp_rn(sdiv);
   if (lane == 0) row_scale[row] = sdiv;
   for (int e = 8 * lane; e < k; e += 256) {
     float v[8];
     load8_half_as_float(xr + e, v);
-    store_codes8<MODE>(codes, row * k + e, v, sdiv);
+    store_codes8<MODE>(codes, row * k + e, v, sdiv, rs);
   }
 }
 

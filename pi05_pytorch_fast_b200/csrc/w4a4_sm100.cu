@@ -200,7 +200,6 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
   const bool fp16 = staging == W4A4_STAGING_FP16;
   const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
   const unsigned rows_grid = static_cast<unsigned>((m + 7) / 8);
-  const unsigned rows_grid4 = static_cast<unsigned>((m + 3) / 4);
   if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large: %lld", (long long)m);
 
   // Instantiate a kernel for every (staging, format) pair.
@@ -221,10 +220,11 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
     dispatch([&](auto f, auto mode) {
       constexpr bool F = decltype(f)::value;
       constexpr int MODE = decltype(mode)::value;
+      const unsigned grid = static_cast<unsigned>(m);  // one 64-thread CTA per row
       if (k == 1024)
-        quant_rot_warp_kernel<10, F, MODE><<<rows_grid4, 128, 0, stream>>>(xh, ldx, m, codes, row_scale, isk);
+        quant_rot_warp_kernel<10, F, MODE><<<grid, 64, 0, stream>>>(xh, ldx, m, codes, row_scale, isk);
       else
-        quant_rot_warp_kernel<11, F, MODE><<<rows_grid4, 128, 0, stream>>>(xh, ldx, m, codes, row_scale, isk);
+        quant_rot_warp_kernel<11, F, MODE><<<grid, 64, 0, stream>>>(xh, ldx, m, codes, row_scale, isk);
     });
   } else if (rot) {
     const unsigned grid = static_cast<unsigned>(m);

@@ -105,6 +105,29 @@ def test_quant_matches_reference_golden(golden, name):
     np.testing.assert_array_equal(to_np(scale).view(np.int32), golden[f"{name}_scale"].view(np.int32))
 
 
+def test_quant_ties_round_half_even():
+    """Codes next to and exactly at half-integers: the kernels compute
+    rint(v / sdiv) through a reciprocal with an IEEE-division fallback near
+    ties, which must match the plain IEEE quotient bit for bit.  With an
+    unrotated row whose amax is 7, sdiv = fl(fl(7/7) + 1e-12) = 1 exactly."""
+    ties = np.array([0.5, 1.5, 2.5, 3.5, 4.5, 5.5, 6.5], np.float16)
+    rows = []
+    for sign in (1, -1):
+        r = np.zeros(64, np.float16)
+        r[:7] = sign * ties
+        r[8:15] = sign * np.nextafter(ties, np.float16(8))    # one fp16 ulp above
+        r[16:23] = sign * np.nextafter(ties, np.float16(0))   # one fp16 ulp below
+        r[24] = np.float16(7.0)                               # amax = 7
+        rows.append(r)
+    x = np.stack(rows)
+    ref_codes, ref_scale = orc.quant_activation(x, rotate=False)
+    codes, scale = ext.quantize(to_dev(x), rotate=0)
+    np.testing.assert_array_equal(to_np(codes), ref_codes)
+    np.testing.assert_array_equal(to_np(scale).view(np.int32), ref_scale.view(np.int32))
+    assert ref_scale[0] == 1.0 and ref_codes[0, 2] == 2 and ref_codes[0, 3] == 4
+    assert ref_codes[1, 2] == -2
+
+
 def test_quant_zero_and_constant_rows():
     x = np.zeros((4, 2048), np.float16)
     x[1] = 1.0
