@@ -44,6 +44,7 @@ constexpr int kBlockK = 128;      // K elements per pipeline step
 constexpr int kTokTileMax = 208;  // max tokens per tile (UMMA N)
 constexpr int kMaxStages = 12;    // shared-memory ring (tokens + packed weights)
 constexpr int kMaxAStages = 8;    // TMEM ring of unpacked weights
+constexpr int kGemmRing = 6;      // single-CTA kernel: shared-memory ring depth (compile time)
 constexpr int kTmemCols = 512;
 constexpr int kUnpackGroups = 2;
 constexpr int kEpiWarps = 8;       // two per TMEM lane quarter, alternate 16-column chunks
@@ -54,9 +55,10 @@ constexpr int kMaxSegments = 3;
 constexpr int kWpkBytes = kBlockW * kBlockK / 2;  // 8 KB packed weights per step
 constexpr int kEpiBytesPerWarp = 16 * 32 * 2;     // 16 tokens x 32 rows fp16
 constexpr int kEpiScaleBytes = kTokTileMax * 4;   // a tile's token scales, per epilogue warp
-// mbarrier slots reserved in shared memory: full / ready / empty rings of
-// kMaxStages each, accfull[2], accempty[2], drain (both kernels' layouts).
-constexpr int kNumBars = 3 * kMaxStages + 4 + 1;
+// mbarrier slots reserved in shared memory: up to four rings of kMaxStages
+// (single CTA: full / ready / empty; CTA pair: wfull / tfull / ready / empty),
+// accfull[2], accempty[2] and drain.
+constexpr int kNumBars = 4 * kMaxStages + 4 + 1;
 constexpr int kFixedSmem =
     kEpiWarps * kEpiBytesPerWarp + kEpiWarps * kEpiScaleBytes + kNumBars * 8 + 16 +
     1024 /*alignment slack*/;
@@ -70,8 +72,16 @@ __host__ __device__ constexpr int gemm_stages(int tok_tile) {
              : kMaxStages;
 }
 __host__ __device__ constexpr int gemm_smem_bytes(int tok_tile) {
-  return gemm_stages(tok_tile) * (tok_tile * kBlockK + kWpkBytes) + kFixedSmem;
+  return kGemmRing * (tok_tile * kBlockK + kWpkBytes) + kFixedSmem;
 }
+// TMEM A slots of the single-CTA kernel: a divisor of kGemmRing that fits
+// beside the two accumulators (6 up to 160-token tiles, else 3).
+__host__ __device__ constexpr int gemm_ring_a_stages(int tok_tile) {
+  return 2 * tok_tile + 6 * 32 <= kTmemCols ? 6 : 3;
+}
+static_assert(kGemmRing * (kTokTileMax * kBlockK + kWpkBytes) + kFixedSmem <= kSmemLimit,
+              "the single-CTA ring must fit the widest tile");
+static_assert(2 * kTokTileMax + 3 * 32 <= kTmemCols, "three A slots must fit beside the widest tile");
 __host__ __device__ constexpr int gemm_a_stages(int tok_tile) {
   return (kTmemCols - 2 * tok_tile) / 32 < kMaxAStages ? (kTmemCols - 2 * tok_tile) / 32
                                                        : kMaxAStages;
@@ -268,10 +278,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int acc_cols = p.tok_tile;
   const int a_col0 = 2 * acc_cols;
 
-  // The issue loop walks the ring in pairs of steps with two A slots: the ring
-  // depth and the step count must be even.  A launch that breaks this touches
-  // nothing and reports it.
-  if ((S & 1) || S < 2 || S > kMaxStages || SA != 2 || (p.k_tiles & 1) || p.k_tiles < 2) {
+  // The issue loop is unrolled over the compile-time ring (kGemmRing slots,
+  // SA a divisor of it).  A launch that breaks this touches nothing and
+  // reports it.
+  if (S != kGemmRing || (SA != 3 && SA != 6) || 2 * p.tok_tile + 32 * SA > kTmemCols ||
+      p.k_tiles < 1) {
     if (threadIdx.x == 0) atomicOr(&g_w4a4_device_error, kErrBadParams);
     return;
   }
@@ -344,64 +355,61 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (lane 0)
     // The issue loop is the kernel's critical path: a 128 x T x 128 step is
-    // 2T tensor cycles (416 at T = 208).  It is unrolled over pairs of steps
-    // so that the A slot (2 slots) and the ring offset within a pair are
-    // compile-time; the host makes k_tiles and the ring depth even.  Measured
-    // on B200 this keeps one thread at ~430 cycles a step next to 16 busy
-    // warps, where a loop with per-step runtime ring indices needs ~620.
+    // 2T tensor cycles (416 at T = 208).  It is unrolled over the whole
+    // shared-memory ring, so every barrier address, B descriptor and A slot
+    // is a compile-time offset or a register; tile switches are handled in
+    // place.  Measured on B200 next to 16 busy warps, this keeps one thread
+    // at ~430 cycles a step, where a loop that advances runtime ring
+    // positions costs ~100 cycles more.
     if (lane == 0) {
       const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
       const uint64_t bstep = static_cast<uint64_t>(tok_bytes >> 4);
-      const uint32_t a_slot0 = tmem_base + a_col0, a_slot1 = a_slot0 + 32;
+      uint64_t bd[kGemmRing];
+#pragma unroll
+      for (int r = 0; r < kGemmRing; ++r) bd[r] = bdesc0 + r * bstep;
+      const uint32_t a_base = tmem_base + a_col0;
+      const bool sa6 = SA == 6;
       const uint32_t ready0 = bar_ready(0), empty0 = bar_empty(0);
-      int sidx = 0;  // ring slot of the pair's first step (even)
-      uint32_t sphase = 0;
-      uint64_t bdesc = bdesc0;
-      int tcount = 0;
-      bool alive = true;
-      for (int tile = blockIdx.x; alive && tile < total_tiles; tile += gridDim.x, ++tcount) {
+      uint32_t phase = 0;
+      int tile = blockIdx.x, tcount = 0, kt = 0, buf = 0;
+      uint32_t d_tmem = tmem_base, idesc = 0;
+      // Starts tile `tile` (the tcount-th of this CTA): its accumulator buffer
+      // must have been drained by the epilogue two tiles ago.
+      const auto begin_tile = [&]() -> bool {
         const TileCoord c = decode_tile(p, tile);
-        const uint32_t idesc = idesc_i8(kBlockW, (c.rows + 15) & ~15);
-        const int buf = tcount & 1;
-        if (tcount >= 2 &&
-            !mbar_wait_bounded(bar_accempty(buf), ((tcount >> 1) - 1) & 1, abort_flag, err,
-                               kErrWaitAccum, limit))
-          break;
-        const uint32_t d_tmem = tmem_base + buf * acc_cols;
-        for (int kt = 0; kt < p.k_tiles; kt += 2) {
-          const uint32_t rbar = ready0 + 8u * sidx, ebar = empty0 + 8u * sidx;
-          if (!mbar_wait_fast(rbar, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
+        idesc = idesc_i8(kBlockW, (c.rows + 15) & ~15);
+        buf = tcount & 1;
+        d_tmem = tmem_base + buf * acc_cols;
+        return tcount < 2 || mbar_wait_bounded(bar_accempty(buf), ((tcount >> 1) - 1) & 1,
+                                               abort_flag, err, kErrWaitAccum, limit);
+      };
+      bool alive = tile < total_tiles && begin_tile();
+      while (alive) {
+#pragma unroll
+        for (int r = 0; r < kGemmRing; ++r) {
+          if (!mbar_wait_fast(ready0 + 8u * r, phase, abort_flag, err, kErrWaitUnpack, limit)) {
             alive = false;
             break;
           }
           tc_fence_after();
-          umma_i8_ts(d_tmem, a_slot0, bdesc, idesc, kt != 0);
-          umma_i8_ts(d_tmem, a_slot0 + 8, bdesc + 2, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot0 + 16, bdesc + 4, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot0 + 24, bdesc + 6, idesc, 1u);
-          umma_commit(ebar);
-          if (!mbar_wait_fast(rbar + 8, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t bdesc1 = bdesc + bstep;
-          umma_i8_ts(d_tmem, a_slot1, bdesc1, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot1 + 8, bdesc1 + 2, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot1 + 16, bdesc1 + 4, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot1 + 24, bdesc1 + 6, idesc, 1u);
-          umma_commit(ebar + 8);
-          sidx += 2;
-          if (sidx == S) {
-            sidx = 0;
-            sphase ^= 1u;
-            bdesc = bdesc0;
-          } else {
-            bdesc = bdesc1 + bstep;
+          const uint32_t a_slot = a_base + 32u * (sa6 ? r : r % 3);
+          umma_i8_ts(d_tmem, a_slot, bd[r], idesc, kt != 0);
+          umma_i8_ts(d_tmem, a_slot + 8, bd[r] + 2, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot + 16, bd[r] + 4, idesc, 1u);
+          umma_i8_ts(d_tmem, a_slot + 24, bd[r] + 6, idesc, 1u);
+          umma_commit(empty0 + 8u * r);
+          if (++kt == p.k_tiles) {
+            umma_commit(bar_accfull(buf));
+            kt = 0;
+            tile += gridDim.x;
+            ++tcount;
+            if (tile >= total_tiles || !begin_tile()) {
+              alive = false;
+              break;
+            }
           }
         }
-        if (!alive) break;
-        umma_commit(bar_accfull(buf));
+        phase ^= 1u;
       }
       // Every MMA of this CTA has completed once this commit arrives.
       umma_commit(bar_drain);

@@ -71,15 +71,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   float* tile_scale = reinterpret_cast<float*>(epi + kEpiWarps * kEpiBytesPerWarp);  // [warps][208]
   uint64_t* bars = reinterpret_cast<uint64_t*>(tile_scale + kEpiWarps * kTokTileMax);
   // wfull[s]  local: this CTA's packed weights of step i landed.
-  // ready[s]  leader: both token halves landed + 8 unpack warps (both CTAs).
+  // tfull[s]  leader: both CTAs' token halves of step i landed (the peer's
+  //           .cta_group::2 copy completes on the leader's barrier).
+  // ready[s]  leader: the 8 unpack warps of step i (4 per CTA) wrote their A
+  //           rows; the leader's warps wait tfull first, so ready implies the
+  //           whole B operand landed: the MMA issuer's only wait.
   // empty[s]  both (multicast commit): MMA(i) completed.
   // accfull/accempty[2]: accumulator handshake (accempty lives in the leader).
   const auto bar_wfull = [&](int s) { return smem_addr(bars + s); };
-  const auto bar_ready = [&](int s) { return smem_addr(bars + kMaxStages + s); };
-  const auto bar_empty = [&](int s) { return smem_addr(bars + 2 * kMaxStages + s); };
-  const auto bar_accfull = [&](int b) { return smem_addr(bars + 3 * kMaxStages + b); };
-  const auto bar_accempty = [&](int b) { return smem_addr(bars + 3 * kMaxStages + 2 + b); };
-  const uint32_t bar_drain = smem_addr(bars + 3 * kMaxStages + 4);
+  const auto bar_tfull = [&](int s) { return smem_addr(bars + kMaxStages + s); };
+  const auto bar_ready = [&](int s) { return smem_addr(bars + 2 * kMaxStages + s); };
+  const auto bar_empty = [&](int s) { return smem_addr(bars + 3 * kMaxStages + s); };
+  const auto bar_accfull = [&](int b) { return smem_addr(bars + 4 * kMaxStages + b); };
+  const auto bar_accempty = [&](int b) { return smem_addr(bars + 4 * kMaxStages + 2 + b); };
+  const uint32_t bar_drain = smem_addr(bars + 4 * kMaxStages + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -90,11 +95,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int acc_cols = p.tok_tile;
   const int a_col0 = 2 * acc_cols;
 
+  // Both rings are walked in pairs of steps (see the single-CTA kernel): a
+  // launch whose ring depths or step count break that touches nothing.
+  if ((S & 1) || S < 2 || S > kMaxStages || (SA & 1) || SA < 2 || SA > kMaxAStages ||
+      2 * p.tok_tile + 32 * SA > kPairTmemCols || (p.k_tiles & 1) || p.k_tiles < 2) {
+    if (threadIdx.x == 0) atomicOr(&g_w4a4_device_error, kErrBadParams);
+    return;
+  }
+
   // ---- setup (both CTAs), then a cluster barrier before any remote traffic
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(bar_wfull(s), 1);
-      mbar_init(bar_ready(s), 1 + 8);  // leader producer (all token bytes) + 8 unpack warps
+      mbar_init(bar_tfull(s), 1);   // leader: its producer's expect_tx of both halves
+      mbar_init(bar_ready(s), 8);   // leader: 4 unpack warps per CTA
       mbar_init(bar_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -132,71 +146,100 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             alive = false;
             break;
           }
-          const uint32_t wfull = bar_wfull(st.idx), ready = bar_ready(st.idx);
+          const uint32_t wfull = bar_wfull(st.idx), tfull = bar_tfull(st.idx);
           mbar_arrive_expect_tx(wfull, kWpkBytes);
           const uint32_t wdst = smem_addr(wpk_ring + st.idx * kWpkBytes);
           if constexpr (LAYOUT == kRowMajor)
             tma_load_2d(wdst, wmap, kt * (kBlockK / 8), c.n0, wfull);
           else
             tma_load_2d(wdst, wmap, c.n0 * 2, kt * (kBlockK / 16), wfull);
-          if (leader) mbar_arrive_expect_tx(ready, static_cast<uint32_t>(2 * tok_bytes));
+          if (leader) mbar_arrive_expect_tx(tfull, static_cast<uint32_t>(2 * tok_bytes));
           tma_load_2d_pair(smem_addr(tok_ring + st.idx * tok_bytes), &p.tmap_tok, kt * kBlockK,
-                           static_cast<int>(c.t0) + static_cast<int>(rank) * half, ready);
+                           static_cast<int>(c.t0) + static_cast<int>(rank) * half, tfull);
           st.advance(S);
           ++issued;
         }
       }
-      // Drain this CTA's weight copies (token copies are covered by the
-      // leader's MMA drain, which needs every ready phase).
+      // Drain: this CTA's weight copies, and on the leader every token copy
+      // of both CTAs (they complete on the leader's tfull); the exit cluster
+      // barrier keeps the peer resident until then.
       for (int i = 0; i < S && i < issued; ++i) {
         const int last = i + ((issued - 1 - i) / S) * S;
         volatile int no_abort = 0;
         mbar_wait_bounded(bar_wfull(i), (last / S) & 1, &no_abort, err, kErrWaitDrain, limit);
+        if (leader)
+          mbar_wait_bounded_cl(bar_tfull(i), (last / S) & 1, &no_abort, err, kErrWaitDrain, limit);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (leader lane 0)
+    // Pair-unrolled like the single-CTA issuer; each instruction spans both
+    // SMs (M = 256), and every commit is multicast to both CTAs.
     if (lane == 0 && leader) {
-      RingPos st;
-      int a_idx = 0;
+      const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
+      const uint64_t bstep = static_cast<uint64_t>(tok_bytes >> 4);
+      const uint32_t a_base = tmem_base + a_col0;
+      const uint32_t ready0 = bar_ready(0), empty0 = bar_empty(0);
+      // The pair splits B by N across the two CTAs' shared memory, so the
+      // MMA's N is the width the token halves were loaded for: the full tile.
+      const uint32_t idesc = idesc_i8(2 * kBlockW, p.tok_tile);
+      int sidx = 0, aidx = 0;
+      uint32_t sphase = 0;
+      uint64_t bdesc = bdesc0;
+      uint32_t a_slot0 = a_base;
       int tcount = 0;
       bool alive = true;
-      const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
-      const uint32_t a_base = tmem_base + a_col0;
-      bool next_ready = false;
       for (int tile = cluster; alive && tile < total_tiles; tile += n_clusters, ++tcount) {
-        // The pair splits B by N across the two CTAs' shared memory, so the
-        // MMA's N must equal the width the token halves were loaded for --
-        // the full tile, even when the last tile has fewer valid rows.
-        const uint32_t idesc = idesc_i8(2 * kBlockW, p.tok_tile);
         const int buf = tcount & 1;
         if (tcount >= 2 &&
             !mbar_wait_bounded_cl(bar_accempty(buf), ((tcount >> 1) - 1) & 1, abort_flag, err,
                                   kErrWaitAccum, limit))
           break;
         const uint32_t d_tmem = tmem_base + buf * acc_cols;
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!next_ready &&
-              !mbar_wait_bounded_cl(bar_ready(st.idx), st.phase, abort_flag, err, kErrWaitUnpack,
-                                    limit)) {
+        for (int kt = 0; kt < p.k_tiles; kt += 2) {
+          const uint32_t rbar = ready0 + 8u * sidx, ebar = empty0 + 8u * sidx;
+          if (!mbar_try_wait_cl(rbar, sphase) &&
+              !mbar_wait_bounded_cl(rbar, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
             alive = false;
             break;
           }
-          RingPos nx = st;
-          nx.advance(S);
-          next_ready = mbar_test_wait_cl(bar_ready(nx.idx), nx.phase);
           tc_fence_after();
-          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((st.idx * tok_bytes) >> 4);
-          const uint32_t a_tmem = a_base + a_idx * 32;
-#pragma unroll
-          for (int kk = 0; kk < kBlockK / 32; ++kk)
-            umma_i8_ts_pair(d_tmem, a_tmem + 8 * kk, bdesc + 2 * kk, idesc, (kt | kk) != 0);
-          umma_commit_pair_mc(bar_empty(st.idx), 0x3);
-          if (kt == p.k_tiles - 1) umma_commit_pair_mc(bar_accfull(buf), 0x3);
-          st = nx;
-          if (++a_idx == SA) a_idx = 0;
+          umma_i8_ts_pair(d_tmem, a_slot0, bdesc, idesc, kt != 0);
+          umma_i8_ts_pair(d_tmem, a_slot0 + 8, bdesc + 2, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot0 + 16, bdesc + 4, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot0 + 24, bdesc + 6, idesc, 1u);
+          umma_commit_pair_mc(ebar, 0x3);
+          if (!mbar_try_wait_cl(rbar + 8, sphase) &&
+              !mbar_wait_bounded_cl(rbar + 8, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc1 = bdesc + bstep;
+          umma_i8_ts_pair(d_tmem, a_slot0 + 32, bdesc1, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot0 + 40, bdesc1 + 2, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot0 + 48, bdesc1 + 4, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot0 + 56, bdesc1 + 6, idesc, 1u);
+          umma_commit_pair_mc(ebar + 8, 0x3);
+          sidx += 2;
+          if (sidx == S) {
+            sidx = 0;
+            sphase ^= 1u;
+            bdesc = bdesc0;
+          } else {
+            bdesc = bdesc1 + bstep;
+          }
+          aidx += 2;
+          if (aidx == SA) {
+            aidx = 0;
+            a_slot0 = a_base;
+          } else {
+            a_slot0 += 64;
+          }
         }
+        if (!alive) break;
+        umma_commit_pair_mc(bar_accfull(buf), 0x3);
       }
       umma_commit_pair_mc(bar_drain, 0x3);
     }
@@ -219,6 +262,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int kt = 0; kt < p.k_tiles; ++kt) {
         if ((step & 1) == group) {
           bool ok = mbar_wait_bounded(bar_wfull(st.idx), st.phase, abort_flag, err, kErrWaitTma,
+                                      limit);
+          if (ok && leader)
+            ok = mbar_wait_bounded_cl(bar_tfull(st.idx), st.phase, abort_flag, err, kErrWaitTma,
                                       limit);
           if (ok && step >= SA)
             ok = mbar_wait_bounded_cl(bar_empty(lag.idx), lag.phase, abort_flag, err,
@@ -254,7 +300,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_ready(st.idx), 0));
+          if (lane == 0) {
+            if (leader) mbar_arrive(bar_ready(st.idx));
+            else mbar_arrive_cluster(mapa_shared(bar_ready(st.idx), 0));
+          }
         }
         ++step;
         st.advance(S);
