@@ -132,6 +132,18 @@ __device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity,
   return mbar_wait_slow(bar, parity, abort_flag, err, err_bit, limit_ns);
 }
 
+// ---- programmatic dependent launch (kernels launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization)
+// Lets the next kernel in the stream be scheduled once every CTA of this one
+// has executed it (or exited); that kernel still waits in pdl_wait() for this
+// grid to complete before touching anything this grid writes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Blocks until every prerequisite grid has completed and its memory is
+// visible; a no-op when the kernel was launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- cluster (CTA pair) helpers
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

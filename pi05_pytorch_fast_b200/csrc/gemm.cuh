@@ -287,6 +287,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     return;
   }
 
+  // The next kernel may be scheduled as soon as every CTA got here; it waits
+  // for this grid's completion itself before reading the outputs.
+  pdl_launch_dependents();
+
   // ---- setup
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -317,28 +321,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------ TMA producer (lane 0)
     if (lane == 0) {
       const uint32_t tx_bytes = kWpkBytes + static_cast<uint32_t>(tok_bytes);
+      const auto load_weights = [&](const TileCoord& c, int kt, int slot) {
+        const uint32_t wdst = smem_addr(wpk_ring + slot * kWpkBytes);
+        const CUtensorMap* wmap = &p.seg[c.seg].tmap_w;
+        if constexpr (LAYOUT == kRowMajor)
+          tma_load_2d(wdst, wmap, kt * (kBlockK / 8), c.n0, bar_full(slot));
+        else
+          tma_load_2d(wdst, wmap, c.n0 * 2, kt * (kBlockK / 16), bar_full(slot));
+      };
+      // Weights do not depend on the previous kernel: fill the first ring
+      // pass with them before waiting for that kernel's tokens.
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < total_tiles) {
+        const TileCoord c0 = decode_tile(p, blockIdx.x);
+        pre = min(S, p.k_tiles);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(bar_full(i), tx_bytes);
+          load_weights(c0, i, i);
+        }
+      }
+      pdl_wait();
       RingPos st;
       int issued = 0;
       bool alive = true;
       for (int tile = blockIdx.x; alive && tile < total_tiles; tile += gridDim.x) {
         const TileCoord c = decode_tile(p, tile);
-        const CUtensorMap* wmap = &p.seg[c.seg].tmap_w;
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (issued >= S &&
-              !mbar_wait_bounded(bar_empty(st.idx), st.phase ^ 1u, abort_flag, err, kErrWaitEmpty,
-                                 limit)) {
-            alive = false;
-            break;
+          if (issued >= pre) {
+            if (issued >= S &&
+                !mbar_wait_bounded(bar_empty(st.idx), st.phase ^ 1u, abort_flag, err,
+                                   kErrWaitEmpty, limit)) {
+              alive = false;
+              break;
+            }
+            mbar_arrive_expect_tx(bar_full(st.idx), tx_bytes);
+            load_weights(c, kt, st.idx);
           }
-          const uint32_t full = bar_full(st.idx);
-          mbar_arrive_expect_tx(full, tx_bytes);
-          const uint32_t wdst = smem_addr(wpk_ring + st.idx * kWpkBytes);
-          if constexpr (LAYOUT == kRowMajor)
-            tma_load_2d(wdst, wmap, kt * (kBlockK / 8), c.n0, full);
-          else
-            tma_load_2d(wdst, wmap, c.n0 * 2, kt * (kBlockK / 16), full);
           tma_load_2d(smem_addr(tok_ring + st.idx * tok_bytes), &p.tmap_tok, kt * kBlockK,
-                      static_cast<int>(c.t0), full);
+                      static_cast<int>(c.t0), bar_full(st.idx));
           st.advance(S);
           ++issued;
         }
@@ -485,6 +505,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     __half* stage = reinterpret_cast<__half*>(epi + ew * kEpiBytesPerWarp);
     float* ts = tile_scale + ew * kTokTileMax;  // warp-private
+    pdl_wait();  // token scales come from the previous kernel; y may be read by it
     int tcount = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
       const TileCoord c = decode_tile(p, tile);

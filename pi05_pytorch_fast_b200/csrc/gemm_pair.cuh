@@ -103,6 +103,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     return;
   }
 
+  pdl_launch_dependents();
+  pdl_wait();
+
   // ---- setup (both CTAs), then a cluster barrier before any remote traffic
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {

@@ -269,6 +269,8 @@ __global__ void __launch_bounds__(64) quant_rot_warp_kernel(
   __shared__ float warp_amax[2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // x is the previous kernel's output
   if (row >= m) return;
   float v[C][8];
   const __half* xr = x + row * ldx + 256 * C * warp + 8 * lane;
@@ -343,6 +345,8 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
   __shared__ float warp_amax[kQuantThreads / 32];
 
   const long long row = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // x is the previous kernel's output
   if (row >= m) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float v[8][8];
@@ -426,6 +430,8 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(
     float* __restrict__ row_scale) {
   const int lane = threadIdx.x & 31;
   const long long row = static_cast<long long>(blockIdx.x) * (kQuantThreads / 32) + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait();  // x is the previous kernel's output
   if (row >= m) return;
   const __half* xr = x + row * ldx;
   float mx = 0.f;
