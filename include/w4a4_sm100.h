@@ -62,8 +62,10 @@ extern "C" {
 #define W4A4_LAYOUT_FRAGMENT_MAJOR 1
 
 /* variant argument of w4a4_set_gemm_variant */
-#define W4A4_GEMM_SINGLE_CTA 0
-#define W4A4_GEMM_CTA_PAIR 1
+#define W4A4_GEMM_SINGLE_CTA 0 /* single-CTA kernel; split-K where the planner finds it faster */
+#define W4A4_GEMM_CTA_PAIR 1   /* tcgen05 cta_group::2 kernel                                 */
+#define W4A4_GEMM_NO_SPLIT 2   /* single-CTA kernel, never split-K                            */
+#define W4A4_GEMM_SPLIT_K 3    /* split-K whenever possible: even K-step count, <= 1 tile per cluster */
 
 /* rotate argument of w4a4_quant */
 #define W4A4_ROTATE_BY_K (-1) /* rotate iff K in {1024, 2048, 16384}: the op's dispatch */
@@ -132,11 +134,12 @@ int w4a4_device_error(uint32_t* bits, int32_t clear);
  * after this call (default 1e9).  Process-wide. */
 int w4a4_set_wait_limit_ns(uint64_t limit_ns);
 
-/* GEMM kernel variant for launches after this call: W4A4_GEMM_SINGLE_CTA
- * (default) or W4A4_GEMM_CTA_PAIR (tcgen05 cta_group::2, two SMs per MMA);
- * both give bit-identical results.  Process-wide; the environment variable
- * W4A4_GEMM_PAIR=1 sets the initial value.  No counterpart in the reference,
- * which has one kernel per op. */
+/* GEMM kernel variant for launches after this call (W4A4_GEMM_*; default
+ * W4A4_GEMM_SINGLE_CTA).  Split-K runs a tile's two K halves on the two CTAs
+ * of a cluster and adds the partial sums through distributed shared memory.
+ * All variants give bit-identical results.  Process-wide; the environment
+ * variable W4A4_GEMM_PAIR=1 sets the initial value to W4A4_GEMM_CTA_PAIR.  No
+ * counterpart in the reference, which has one kernel per op. */
 int w4a4_set_gemm_variant(int32_t variant);
 
 /* Test hook: launches one CTA that waits on a barrier nobody arrives at, with

@@ -28,6 +28,8 @@ LAYOUT_FRAGMENT_MAJOR = 1
 ROTATE_BY_K = -1
 GEMM_SINGLE_CTA = 0
 GEMM_CTA_PAIR = 1
+GEMM_NO_SPLIT = 2
+GEMM_SPLIT_K = 3
 
 # Every symbol include/w4a4_sm100.h declares.
 EXPORTED_SYMBOLS = (
@@ -129,7 +131,8 @@ def set_wait_limit_ns(limit_ns: int) -> None:
 
 
 def set_gemm_variant(variant: int) -> None:
-    """GEMM_SINGLE_CTA (default) or GEMM_CTA_PAIR for launches after this call."""
+    """GEMM_SINGLE_CTA (default, split-K where faster), GEMM_CTA_PAIR,
+    GEMM_NO_SPLIT or GEMM_SPLIT_K for launches after this call."""
     check(lib().w4a4_set_gemm_variant(int(variant)))
 
 

@@ -55,10 +55,11 @@ constexpr int kMaxSegments = 3;
 constexpr int kWpkBytes = kBlockW * kBlockK / 2;  // 8 KB packed weights per step
 constexpr int kEpiBytesPerWarp = 16 * 32 * 2;     // 16 tokens x 32 rows fp16
 constexpr int kEpiScaleBytes = kTokTileMax * 4;   // a tile's token scales, per epilogue warp
+constexpr int kXchgChunkBytes = 16 * 32 * 4;      // split-K: one 16-column int32 chunk of one warp
 // mbarrier slots reserved in shared memory: up to four rings of kMaxStages
 // (single CTA: full / ready / empty; CTA pair: wfull / tfull / ready / empty),
 // accfull[2], accempty[2] and drain.
-constexpr int kNumBars = 4 * kMaxStages + 4 + 1;
+constexpr int kNumBars = 4 * kMaxStages + 4 + 1 + kEpiWarps + 1;  // + split-K xfull per epilogue warp, xready
 constexpr int kFixedSmem =
     kEpiWarps * kEpiBytesPerWarp + kEpiWarps * kEpiScaleBytes + kNumBars * 8 + 16 +
     1024 /*alignment slack*/;
@@ -79,9 +80,16 @@ __host__ __device__ constexpr int gemm_smem_bytes(int tok_tile) {
 __host__ __device__ constexpr int gemm_ring_a_stages(int tok_tile) {
   return 2 * tok_tile + 6 * 32 <= kTmemCols ? 6 : 3;
 }
+
 static_assert(kGemmRing * (kTokTileMax * kBlockK + kWpkBytes) + kFixedSmem <= kSmemLimit,
               "the single-CTA ring must fit the widest tile");
 static_assert(2 * kTokTileMax + 3 * 32 <= kTmemCols, "three A slots must fit beside the widest tile");
+// Split-K: rank 1 pushes its whole partial accumulator into rank 0's idle
+// ring (token and weight rings are contiguous): each epilogue warp's
+// ceil(T / 32) chunks of 2 KB, 8 T / 32 * 2 KB <= 512 T bytes in all, which
+// always fits in the ring's kGemmRing * (128 T + 8 KB) bytes.
+static_assert(kEpiWarps * 2 * kXchgChunkBytes <= kGemmRing * (16 * kBlockK + kWpkBytes),
+              "the split-K exchange must fit the ring of the narrowest tile");
 __host__ __device__ constexpr int gemm_a_stages(int tok_tile) {
   return (kTmemCols - 2 * tok_tile) / 32 < kMaxAStages ? (kTmemCols - 2 * tok_tile) / 32
                                                        : kMaxAStages;
@@ -210,11 +218,17 @@ __device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const Til
 // n_warp .. n_warp+31), 16-column chunks half, half+2, half+4, ...  The next
 // chunk's TMEM load is issued before the current chunk is processed, and
 // release() is called once, as soon as this warp's last TMEM load completed
-// (the accumulator buffer may then be overwritten).
-template <bool ACC_OUT, typename Release>
+// (the accumulator buffer may then be overwritten).  combine(acc) sees each
+// chunk first (split-K exchange) and returns whether to write it out.
+struct NoCombine {
+  __device__ __forceinline__ bool operator()(uint32_t (&)[16]) const { return true; }
+};
+
+template <bool ACC_OUT, typename Release, typename Combine = NoCombine>
 __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const TileCoord& c, int n_warp,
                                               uint32_t tacc, int half, int lane, __half* stage,
-                                              const float* ts, Release release) {
+                                              const float* ts, Release release,
+                                              Combine combine = Combine()) {
   const int nq = ((c.rows + 15) & ~15) >> 4;
   const int my = (nq - half + 1) >> 1;  // chunks half + 2j, j < my
   if (my <= 0) {
@@ -230,12 +244,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const Tile
   if (my == 1) release();
   for (int j = 0; j < my; j += 2) {
     if (j + 1 < my) tmem_ld_32x32b_x16(tacc + (half + 2 * (j + 1)) * 16, a1);
-    epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * j) * 16, sw, a0, stage, ts);
+    if (combine(a0)) epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * j) * 16, sw, a0, stage, ts);
     if (j + 1 >= my) break;
     tmem_ld_wait();
     if (j + 2 == my) release();
     if (j + 2 < my) tmem_ld_32x32b_x16(tacc + (half + 2 * (j + 2)) * 16, a0);
-    epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * (j + 1)) * 16, sw, a1, stage, ts);
+    if (combine(a1))
+      epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * (j + 1)) * 16, sw, a1, stage, ts);
     if (j + 2 >= my) break;
     tmem_ld_wait();
     if (j + 3 == my) release();
@@ -244,9 +259,18 @@ __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const Tile
 
 // ACC_OUT = true writes the raw int32 accumulators (seg.y as int32 [M, n])
 // instead of fp16: a test hook that proves the integer products bit-exact.
-template <int LAYOUT, bool ACC_OUT>
+//
+// SPLIT = true: split-K over clusters of two CTAs, each cluster one output
+// tile (the host launches it only when the tiles do not outnumber the
+// clusters).  Rank r runs K steps [r k_tiles, (r+1) k_tiles) through the same
+// pipeline into its own TMEM.  Once rank 0's MMAs are done its token ring is
+// idle: rank 1 then pushes its whole partial accumulator there (distributed
+// shared memory) and rank 0 adds it (int32, exact) and writes the output.
+template <int LAYOUT, bool ACC_OUT, bool SPLIT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a4_gemm_kernel(const __grid_constant__ GemmParams p) {
+  constexpr int RING = kGemmRing;
+  constexpr int SA_SMALL = 3;  // A slots when the full ring does not fit in TMEM
   extern __shared__ uint8_t gemm_smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -268,6 +292,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const auto bar_accfull = [&](int b) { return smem_addr(bars + 3 * kMaxStages + b); };
   const auto bar_accempty = [&](int b) { return smem_addr(bars + 3 * kMaxStages + 2 + b); };
   const uint32_t bar_drain = smem_addr(bars + 3 * kMaxStages + 4);
+  // split-K: xready (rank 1) rank 0's MMAs are done, its token ring is free
+  // (one arrival per rank-0 epilogue warp); xfull[w] (rank 0) the partner
+  // warp's partial sums landed (32 lane arrivals).
+  const auto bar_xfull = [&](int w) { return smem_addr(bars + 3 * kMaxStages + 5 + w); };
+  const uint32_t bar_xready = smem_addr(bars + 3 * kMaxStages + 5 + kEpiWarps);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -277,12 +306,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int total_tiles = p.n_tok_tiles * p.w_tiles;
   const int acc_cols = p.tok_tile;
   const int a_col0 = 2 * acc_cols;
+  // Tiles are dealt to CTAs (or, for split-K, to clusters) round robin.
+  const uint32_t rank = SPLIT ? cluster_ctarank() : 0u;
+  const int unit0 = SPLIT ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ustride = SPLIT ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int k_begin = static_cast<int>(rank) * p.k_tiles;  // first K step of this CTA
 
-  // The issue loop is unrolled over the compile-time ring (kGemmRing slots,
-  // SA a divisor of it).  A launch that breaks this touches nothing and
-  // reports it.
-  if (S != kGemmRing || (SA != 3 && SA != 6) || 2 * p.tok_tile + 32 * SA > kTmemCols ||
-      p.k_tiles < 1) {
+  // The issue loop is unrolled over the compile-time ring (RING slots, SA a
+  // divisor of it).  A launch that breaks this touches nothing and reports it.
+  if (S != RING || (SA != SA_SMALL && SA != RING) || 2 * p.tok_tile + 32 * SA > kTmemCols ||
+      p.k_tiles < 1 || (SPLIT && total_tiles > ustride)) {
     if (threadIdx.x == 0) atomicOr(&g_w4a4_device_error, kErrBadParams);
     return;
   }
@@ -303,6 +336,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(bar_accempty(b), kEpiWarps);
     }
     mbar_init(bar_drain, 1);
+    if (SPLIT) {
+      for (int w = 0; w < kEpiWarps; ++w) mbar_init(bar_xfull(w), 32);
+      mbar_init(bar_xready, kEpiWarps);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tmap_tok);
@@ -314,6 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (SPLIT) cluster_sync();  // the partner's barriers exist before any remote traffic
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -322,6 +360,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const uint32_t tx_bytes = kWpkBytes + static_cast<uint32_t>(tok_bytes);
       const auto load_weights = [&](const TileCoord& c, int kt, int slot) {
+        kt += k_begin;
         const uint32_t wdst = smem_addr(wpk_ring + slot * kWpkBytes);
         const CUtensorMap* wmap = &p.seg[c.seg].tmap_w;
         if constexpr (LAYOUT == kRowMajor)
@@ -332,8 +371,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Weights do not depend on the previous kernel: fill the first ring
       // pass with them before waiting for that kernel's tokens.
       int pre = 0;
-      if (static_cast<int>(blockIdx.x) < total_tiles) {
-        const TileCoord c0 = decode_tile(p, blockIdx.x);
+      if (unit0 < total_tiles) {
+        const TileCoord c0 = decode_tile(p, unit0);
         pre = min(S, p.k_tiles);
         for (int i = 0; i < pre; ++i) {
           mbar_arrive_expect_tx(bar_full(i), tx_bytes);
@@ -344,7 +383,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       RingPos st;
       int issued = 0;
       bool alive = true;
-      for (int tile = blockIdx.x; alive && tile < total_tiles; tile += gridDim.x) {
+      for (int tile = unit0; alive && tile < total_tiles; tile += ustride) {
         const TileCoord c = decode_tile(p, tile);
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           if (issued >= pre) {
@@ -357,7 +396,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_arrive_expect_tx(bar_full(st.idx), tx_bytes);
             load_weights(c, kt, st.idx);
           }
-          tma_load_2d(smem_addr(tok_ring + st.idx * tok_bytes), &p.tmap_tok, kt * kBlockK,
+          tma_load_2d(smem_addr(tok_ring + st.idx * tok_bytes), &p.tmap_tok, (kt + k_begin) * kBlockK,
                       static_cast<int>(c.t0), bar_full(st.idx));
           st.advance(S);
           ++issued;
@@ -384,14 +423,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
       const uint64_t bstep = static_cast<uint64_t>(tok_bytes >> 4);
-      uint64_t bd[kGemmRing];
+      uint64_t bd[RING];
 #pragma unroll
-      for (int r = 0; r < kGemmRing; ++r) bd[r] = bdesc0 + r * bstep;
+      for (int r = 0; r < RING; ++r) bd[r] = bdesc0 + r * bstep;
       const uint32_t a_base = tmem_base + a_col0;
-      const bool sa6 = SA == 6;
+      const bool sa_full = SA == RING;
       const uint32_t ready0 = bar_ready(0), empty0 = bar_empty(0);
       uint32_t phase = 0;
-      int tile = blockIdx.x, tcount = 0, kt = 0, buf = 0;
+      int tile = unit0, tcount = 0, kt = 0, buf = 0;
       uint32_t d_tmem = tmem_base, idesc = 0;
       // Starts tile `tile` (the tcount-th of this CTA): its accumulator buffer
       // must have been drained by the epilogue two tiles ago.
@@ -406,13 +445,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool alive = tile < total_tiles && begin_tile();
       while (alive) {
 #pragma unroll
-        for (int r = 0; r < kGemmRing; ++r) {
+        for (int r = 0; r < RING; ++r) {
           if (!mbar_wait_fast(ready0 + 8u * r, phase, abort_flag, err, kErrWaitUnpack, limit)) {
             alive = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_slot = a_base + 32u * (sa6 ? r : r % 3);
+          const uint32_t a_slot = a_base + 32u * (sa_full ? r : r % SA_SMALL);
           umma_i8_ts(d_tmem, a_slot, bd[r], idesc, kt != 0);
           umma_i8_ts(d_tmem, a_slot + 8, bd[r] + 2, idesc, 1u);
           umma_i8_ts(d_tmem, a_slot + 16, bd[r] + 4, idesc, 1u);
@@ -421,7 +460,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (++kt == p.k_tiles) {
             umma_commit(bar_accfull(buf));
             kt = 0;
-            tile += gridDim.x;
+            tile += ustride;
             ++tcount;
             if (tile >= total_tiles || !begin_tile()) {
               alive = false;
@@ -448,7 +487,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     RingPos st, at, lag;
     int step = 0;
     bool alive = true;
-    for (int tile = blockIdx.x; alive && tile < total_tiles; tile += gridDim.x) {
+    for (int tile = unit0; alive && tile < total_tiles; tile += ustride) {
       for (int kt = 0; kt < p.k_tiles; ++kt) {
         if ((step & 1) == group) {
           bool ok = mbar_wait_bounded(bar_full(st.idx), st.phase, abort_flag, err, kErrWaitTma,
@@ -507,27 +546,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     float* ts = tile_scale + ew * kTokTileMax;  // warp-private
     pdl_wait();  // token scales come from the previous kernel; y may be read by it
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = unit0; tile < total_tiles; tile += ustride, ++tcount) {
       const TileCoord c = decode_tile(p, tile);
       const int buf = tcount & 1;
-      if (!ACC_OUT) stage_tile_scales(ts, p.row_scale, c, lane);
+      if (!ACC_OUT && rank == 0) stage_tile_scales(ts, p.row_scale, c, lane);
       const bool ok = mbar_wait_bounded(bar_accfull(buf), (tcount >> 1) & 1, abort_flag, err,
                                         kErrWaitAccum, limit);
       if (!warp_all(ok)) break;
       tc_fence_after();
       const uint32_t accempty = bar_accempty(buf);
-      epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32,
-                             tmem_base + lane_addr + buf * acc_cols, half, lane, stage, ts, [&] {
-                               tc_fence_before();
-                               __syncwarp();
-                               if (lane == 0) mbar_arrive(accempty);
-                             });
+      const auto release = [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(accempty);
+      };
+      const uint32_t tacc = tmem_base + lane_addr + buf * acc_cols;
+      if constexpr (!SPLIT) {
+        epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
+                               release);
+      } else {
+        // This warp's exchange area in rank 0's ring: chunk j of the warp at
+        // [j][32 lanes][16 int32]; ceil(T / 32) chunks per warp.
+        const int xstride = ((p.tok_tile / 16 + 1) / 2) * kXchgChunkBytes;
+        const uint32_t xarea = smem_addr(tok_ring) + ew * xstride;
+        if (rank == 0) {
+          // our MMAs are done: the token ring is free for the partner's sums
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_xready, 1));
+          const bool got = warp_all(mbar_wait_bounded_cl(bar_xfull(ew), 0, abort_flag, err,
+                                                         kErrWaitAccum, limit));
+          int j = 0;
+          epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
+                                 release, [&](uint32_t (&acc)[16]) -> bool {
+            const uint4* src = reinterpret_cast<const uint4*>(tok_ring + ew * xstride +
+                                                              j * kXchgChunkBytes + lane * 64);
+            ++j;
+            if (!got) return true;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 v = src[q];
+              acc[4 * q] += v.x;
+              acc[4 * q + 1] += v.y;
+              acc[4 * q + 2] += v.z;
+              acc[4 * q + 3] += v.w;
+            }
+            return true;
+          });
+        } else {
+          // wait until rank 0's ring is free, push every chunk of our partial
+          // sums there, then signal this warp's part complete
+          const bool free = warp_all(mbar_wait_bounded_cl(bar_xready, 0, abort_flag, err,
+                                                          kErrWaitAccum, limit));
+          const uint32_t dst0 = mapa_shared(xarea, 0) + lane * 64;
+          int j = 0;
+          epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
+                                 release, [&](uint32_t (&acc)[16]) -> bool {
+            if (free) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                st_shared_cluster_v4(dst0 + j * kXchgChunkBytes + 16 * q, acc[4 * q],
+                                     acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+            }
+            ++j;
+            return false;
+          });
+          mbar_arrive_cluster(mapa_shared(bar_xfull(ew), 0));
+        }
+      }
     }
   }
 
   // ---- teardown
   tc_fence_before();
   __syncthreads();
+  if (SPLIT) cluster_sync();  // no remote store or arrival may target an exited CTA
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);

@@ -306,6 +306,44 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
 // count times a per-tile cost in which the overhead term models the work that
 // does not scale with the tile (streaming and unpacking the 128-row weight
 // operand).  Tiles are multiples of 16 (the UMMA N granularity).
+// Tile width and split-K for the single-CTA kernel.  A K step of a tile of
+// t tokens costs about 330 + 1.5 t SM cycles (per-step traces on B200: the
+// MMA issue loop, ~480 at t = 96 and ~640 at t = 208), a tile about 2000
+// more (pipeline fill, epilogue tail), and a split tile 12 t more for the
+// partial-sum exchange.  Split-K runs a tile's two K halves on the two CTAs
+// of a cluster, so it pays when the tiles do not fill the SMs.
+struct GemmPlan {
+  int tok_tile;
+  bool split;
+};
+GemmPlan choose_plan(int64_t m, int w_tiles, int k_steps, int sms, int variant) {
+  GemmPlan best{16, false};
+  double best_cost = 1e300;
+  const int64_t t_min = (m + kTokTileMax - 1) / kTokTileMax;
+  for (int64_t t = t_min; t <= t_min + 64; ++t) {
+    const int64_t per = (m + t - 1) / t;
+    const int tile = static_cast<int>(((per + 15) / 16) * 16);
+    const int64_t tiles = ((m + tile - 1) / tile) * w_tiles;
+    for (int split = 0; split < 2; ++split) {
+      // split-K needs an even K-step count and one tile per cluster
+      const bool can_split = k_steps % 2 == 0 && k_steps >= 2 && tiles <= sms / 2;
+      if (split && (!can_split || variant == W4A4_GEMM_NO_SPLIT)) continue;
+      if (!split && can_split && variant == W4A4_GEMM_SPLIT_K) continue;
+      const int64_t workers = split ? sms / 2 : sms;
+      const int64_t waves = (tiles + workers - 1) / workers;
+      const double steps = split ? k_steps / 2 : k_steps;
+      const double cost = static_cast<double>(waves) *
+                          (steps * (330.0 + 1.5 * tile) + 2000.0 + (split ? 12.0 * tile : 0.0));
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = {tile, split != 0};
+      }
+    }
+    if (tile <= 32) break;
+  }
+  return best;
+}
+
 int choose_tok_tile(int64_t m, int w_tiles, int sms) {
   constexpr int kTileOverhead = 64;
   int best_tile = 16;
@@ -415,7 +453,11 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
   const int workers = pair ? sms / 2 : sms;
-  const int tok_tile = choose_tok_tile(m, w_tiles, workers);
+  const int k_steps = (k + kBlockK - 1) / kBlockK;
+  const GemmPlan plan = pair ? GemmPlan{choose_tok_tile(m, w_tiles, workers), false}
+                             : choose_plan(m, w_tiles, k_steps, sms, g_gemm_variant.load());
+  const int tok_tile = plan.tok_tile;
+  const bool split = plan.split;
   if (int e = make_map_2d(&p.tmap_tok, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, m, k, kBlockK,
                           pair ? tok_tile / 2 : tok_tile, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
@@ -426,15 +468,21 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   p.tok_tile = tok_tile;
   p.n_seg = n_weights;
   // The single-CTA kernel's issue loop is unrolled over a compile-time ring
-  // (kGemmRing stages, 3 or 6 TMEM A slots).  The CTA-pair kernel issues in
-  // pairs of K steps from even rings; an odd step count gets one more step
-  // whose TMA boxes lie past K: they read as zeros and add nothing.
+  // (kGemmRing stages, 3 or 6 TMEM A slots; split-K: the same, each CTA of
+  // a cluster half the K steps).  The CTA-pair
+  // kernel issues in pairs of K steps from even rings; an odd step count gets
+  // one more step whose TMA boxes lie past K: they read as zeros and add
+  // nothing.
   if (pair) {
     p.k_tiles = 2 * ((k + 2 * kBlockK - 1) / (2 * kBlockK));
     p.stages = gemm_pair_stages(tok_tile) & ~1;
     p.a_stages = gemm_a_stages(tok_tile) & ~1;
+  } else if (split) {
+    p.k_tiles = k_steps / 2;
+    p.stages = kGemmRing;
+    p.a_stages = gemm_ring_a_stages(tok_tile);
   } else {
-    p.k_tiles = (k + kBlockK - 1) / kBlockK;
+    p.k_tiles = k_steps;
     p.stages = kGemmRing;
     p.a_stages = gemm_ring_a_stages(tok_tile);
   }
@@ -445,8 +493,8 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   if (pair && (p.stages < 2 || (p.stages & 1) || (p.k_tiles & 1) || p.a_stages < 2))
     return fail(W4A4_ERR_INVALID, "internal: GEMM ring depth %d / step count %d must be even", p.stages,
                 p.k_tiles);
-  const dim3 grid(pair ? 2u * static_cast<unsigned>(std::min<int64_t>(total_tiles, workers))
-                       : static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
+  const dim3 grid(pair || split ? 2u * static_cast<unsigned>(std::min<int64_t>(total_tiles, sms / 2))
+                                : static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
 #define W4A4_LAUNCH_GEMM(L, ACC, BIT)                                                          \
   do {                                                                                        \
     if (pair) {                                                                               \
@@ -455,10 +503,17 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
         return e;                                                                             \
       W4A4_CUDA_TRY(launch_kernel(w4a4_gemm_pair_kernel<L, ACC>, grid, dim3(kGemmThreads),    \
                                   gemm_pair_smem_bytes(tok_tile), stream, 2, p));             \
-    } else {                                                                                  \
-      if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC>, kSmemLimit))   \
+    } else if (split) {                                                                       \
+      if (int e = ensure_smem_attr(dev, 1u << (20 + (BIT)), w4a4_gemm_kernel<L, ACC, true>,    \
+                                   kSmemLimit))                                               \
         return e;                                                                             \
-      W4A4_CUDA_TRY(launch_kernel(w4a4_gemm_kernel<L, ACC>, grid, dim3(kGemmThreads),         \
+      W4A4_CUDA_TRY(launch_kernel(w4a4_gemm_kernel<L, ACC, true>, grid, dim3(kGemmThreads),   \
+                                  gemm_smem_bytes(tok_tile), stream, 2, p));                  \
+    } else {                                                                                  \
+      if (int e = ensure_smem_attr(dev, 1u << (BIT), w4a4_gemm_kernel<L, ACC, false>,          \
+                                   kSmemLimit))                                               \
+        return e;                                                                             \
+      W4A4_CUDA_TRY(launch_kernel(w4a4_gemm_kernel<L, ACC, false>, grid, dim3(kGemmThreads),  \
                                   gemm_smem_bytes(tok_tile), stream, 1, p));                  \
     }                                                                                         \
   } while (0)
@@ -569,7 +624,8 @@ int w4a4_set_wait_limit_ns(uint64_t limit_ns) {
 }
 
 int w4a4_set_gemm_variant(int32_t variant) {
-  if (variant != W4A4_GEMM_SINGLE_CTA && variant != W4A4_GEMM_CTA_PAIR)
+  if (variant != W4A4_GEMM_SINGLE_CTA && variant != W4A4_GEMM_CTA_PAIR &&
+      variant != W4A4_GEMM_NO_SPLIT && variant != W4A4_GEMM_SPLIT_K)
     return fail(W4A4_ERR_INVALID, "unknown GEMM variant %d", variant);
   g_gemm_variant.store(variant);
   return ok();

@@ -56,10 +56,14 @@ def gemm_accumulators(codes: torch.Tensor, weights, fragment_major=False):
     return accs
 
 
-@pytest.fixture(params=["single_cta", "cta_pair"])
+VARIANTS = {"single_cta": nat.GEMM_SINGLE_CTA, "cta_pair": nat.GEMM_CTA_PAIR,
+            "no_split": nat.GEMM_NO_SPLIT, "split_k": nat.GEMM_SPLIT_K}
+
+
+@pytest.fixture(params=list(VARIANTS))
 def variant(request):
-    """Runs a GEMM test through each kernel variant; both must be bit-exact."""
-    nat.set_gemm_variant(nat.GEMM_CTA_PAIR if request.param == "cta_pair" else nat.GEMM_SINGLE_CTA)
+    """Runs a GEMM test through each kernel variant; all must be bit-exact."""
+    nat.set_gemm_variant(VARIANTS[request.param])
     yield request.param
     nat.set_gemm_variant(nat.GEMM_SINGLE_CTA)
 
@@ -157,6 +161,8 @@ GEMM_CASES = [
     (776, 16384, [2048], "row"),               # config 1: down_proj
     (3, 16384, [128], "row"),
     (257, 1024, [384, 128], "row"),
+    (200, 4096, [256], "fragment"),            # split-K candidate, fragment-major
+    (776, 2048, [2048, 2048, 2048], "row"),    # split-K: more tiles than clusters
 ]
 
 

@@ -71,7 +71,9 @@ def test_gemm_argument_validation_without_gpu():
 
 def test_gemm_variant_selection_validated():
     lib = nat.lib()
-    assert "unknown GEMM variant 2" in _err(lib.w4a4_set_gemm_variant(2))
+    assert "unknown GEMM variant 7" in _err(lib.w4a4_set_gemm_variant(7))
+    for v in (nat.GEMM_NO_SPLIT, nat.GEMM_SPLIT_K):
+        assert lib.w4a4_set_gemm_variant(v) == nat.W4A4_OK
     assert lib.w4a4_set_gemm_variant(nat.GEMM_CTA_PAIR) == nat.W4A4_OK
     assert lib.w4a4_set_gemm_variant(nat.GEMM_SINGLE_CTA) == nat.W4A4_OK
 
