@@ -115,6 +115,21 @@ int w4a4_int4_gemm(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rot
                    int32_t staging, int32_t n_weights, const w4a4_weight* weights,
                    void* const* y, void* codes_scratch, float* scale_scratch, void* stream);
 
+/* No counterpart in the reference: w4a4_int4_gemm without caller-provided
+ * scratch.  The intermediate codes and row scales live in file-scope static
+ * device arrays of the library (at most W4A4_NOALLOC_MAX_ROWS rows and
+ * W4A4_NOALLOC_MAX_CODES = m * k codes; larger calls fail with
+ * W4A4_ERR_UNSUPPORTED), so the call allocates nothing.  Every call on a
+ * device shares that one scratch: calls that may overlap in time (other
+ * streams, other threads, or another launch before this one's GEMM has read
+ * the codes) race.  The arrays' addresses are looked up on the first call on
+ * each device; make that first call before any CUDA graph capture. */
+#define W4A4_NOALLOC_MAX_ROWS 65536
+#define W4A4_NOALLOC_MAX_CODES (16 * 1024 * 1024)
+int w4a4_int4_gemm_noalloc(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
+                           int32_t staging, int32_t n_weights, const w4a4_weight* weights,
+                           void* const* y, void* stream);
+
 /* Copy a row-major packed weight [n, src_row_words] into [n, dst_row_words]
  * (dst_row_words >= src_row_words), zero-filling the new words: the
  * load-time row pad of apply.py:68-69, done on the device. */

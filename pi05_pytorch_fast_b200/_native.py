@@ -30,6 +30,8 @@ GEMM_SINGLE_CTA = 0
 GEMM_CTA_PAIR = 1
 GEMM_NO_SPLIT = 2
 GEMM_SPLIT_K = 3
+NOALLOC_MAX_ROWS = 65536
+NOALLOC_MAX_CODES = 16 * 1024 * 1024
 
 # Every symbol include/w4a4_sm100.h declares.
 EXPORTED_SYMBOLS = (
@@ -37,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "w4a4_gemm",
     "w4a4_gemm_accumulators",
     "w4a4_int4_gemm",
+    "w4a4_int4_gemm_noalloc",
     "w4a4_pad_rows",
     "w4a4_last_error",
     "w4a4_device_error",
@@ -79,10 +82,13 @@ def _declare(lib: ctypes.CDLL) -> None:
                                            ctypes.POINTER(vp), vp]
     lib.w4a4_int4_gemm.argtypes = [vp, c_i64, c_i32, c_i64, c_i32, c_i32, c_i32,
                                    ctypes.POINTER(W4A4Weight), ctypes.POINTER(vp), vp, vp, vp]
+    lib.w4a4_int4_gemm_noalloc.argtypes = [vp, c_i64, c_i32, c_i64, c_i32, c_i32, c_i32,
+                                           ctypes.POINTER(W4A4Weight), ctypes.POINTER(vp), vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]
     lib.w4a4_set_wait_limit_ns.argtypes = [c_u64]
+    lib.w4a4_set_gemm_variant.argtypes = [c_i32]
     lib.w4a4_selftest_wait_timeout.argtypes = [c_u64, vp]
     lib.w4a4_version.argtypes = []
     for name in EXPORTED_SYMBOLS:

@@ -23,6 +23,12 @@
 #include "gemm_pair.cuh"
 #include "quant.cuh"
 
+// Scratch of w4a4_int4_gemm_noalloc: the intermediate activation codes and
+// row scales, as file-scope device arrays (one copy per device, shared by
+// every call on it; no allocation of any kind).
+__device__ __align__(256) int8_t g_w4a4_noalloc_codes[W4A4_NOALLOC_MAX_CODES];
+__device__ __align__(256) float g_w4a4_noalloc_scales[W4A4_NOALLOC_MAX_ROWS];
+
 namespace w4a4 {
 namespace {
 
@@ -540,6 +546,28 @@ __global__ void pad_rows_kernel(const int32_t* __restrict__ src, int32_t n, int3
   }
 }
 
+// Device addresses of the no-allocation scratch arrays on the current
+// device: looked up once per device, with that device current, and cached.
+void* g_noalloc_codes[kMaxDevices];
+float* g_noalloc_scales[kMaxDevices];
+
+int noalloc_buffers(void** codes, float** scales) {
+  int dev = 0;
+  if (int e = current_device(&dev)) return e;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_noalloc_codes[dev]) {
+    void* c = nullptr;
+    void* sc = nullptr;
+    W4A4_CUDA_TRY(cudaGetSymbolAddress(&c, g_w4a4_noalloc_codes));
+    W4A4_CUDA_TRY(cudaGetSymbolAddress(&sc, g_w4a4_noalloc_scales));
+    g_noalloc_scales[dev] = static_cast<float*>(sc);
+    g_noalloc_codes[dev] = c;
+  }
+  *codes = g_noalloc_codes[dev];
+  *scales = g_noalloc_scales[dev];
+  return W4A4_OK;
+}
+
 }  // namespace
 }  // namespace w4a4
 
@@ -580,6 +608,21 @@ int w4a4_int4_gemm(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rot
     return e;
   return launch_gemm(codes_scratch, scale_scratch, m, k, n_weights, weights, y,
                      static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_int4_gemm_noalloc(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
+                           int32_t staging, int32_t n_weights, const w4a4_weight* weights,
+                           void* const* y, void* stream) {
+  if (m < 0 || k <= 0) return fail(W4A4_ERR_INVALID, "invalid shape M=%lld K=%d", (long long)m, k);
+  if (m > W4A4_NOALLOC_MAX_ROWS || m * static_cast<int64_t>(k) > W4A4_NOALLOC_MAX_CODES)
+    return fail(W4A4_ERR_UNSUPPORTED,
+                "w4a4_int4_gemm_noalloc: M=%lld x K=%d exceeds its static scratch (at most %d rows "
+                "and %d codes); use w4a4_int4_gemm with caller-provided scratch",
+                (long long)m, k, W4A4_NOALLOC_MAX_ROWS, W4A4_NOALLOC_MAX_CODES);
+  void* codes = nullptr;
+  float* scales = nullptr;
+  if (int e = noalloc_buffers(&codes, &scales)) return e;
+  return w4a4_int4_gemm(x, m, k, ldx, rotate, staging, n_weights, weights, y, codes, scales, stream);
 }
 
 int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,
