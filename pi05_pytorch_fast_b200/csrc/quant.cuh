@@ -251,70 +251,112 @@ __device__ __forceinline__ void store_codes8(void* out, long long elem, const fl
   }
 }
 
-// K = 1024 / 2048: one 64-thread CTA (two warps) per row, so that a 776-row
-// activation is resident in a single wave (~10 warps per SM).  Warp w holds
-// chunks [w C/2, (w+1) C/2): index bits 0-2 are in the thread, 3-7 across
-// lanes, 8 .. LOGK-2 across the warp's chunks and bit LOGK-1 across the two
-// warps, whose butterfly (the last stage, as in the reference's ascending
-// order) goes through shared memory.
+// The last index bits of a row, held across NW warps (index bits 9 .. 9 +
+// log2(NW) - 1): every thread reads the NW warps' values at its own positions
+// and applies those butterfly stages in ascending order, keeping its warp's
+// outputs.  Stage bit 9 pairs warps w and w^1, bit 10 pairs w and w^2; the
+// lower partner keeps a + b, the upper a - b, each rounded (T = __half2 for
+// fp16 staging, float for fp32).
+template <int NW, typename T>
+__device__ __forceinline__ T cross_warp_stages(const T (&x)[NW], int w);
+template <>
+__device__ __forceinline__ __half2 cross_warp_stages<2, __half2>(const __half2 (&x)[2], int w) {
+  return w ? __hsub2(x[0], x[1]) : __hadd2(x[0], x[1]);
+}
+template <>
+__device__ __forceinline__ __half2 cross_warp_stages<4, __half2>(const __half2 (&x)[4], int w) {
+  // after the bit-9 stage: s[0] = x0 + x1, s[1] = x0 - x1, s[2] = x2 + x3,
+  // s[3] = x2 - x3; the bit-10 stage pairs s[w & 1] with s[(w & 1) + 2]
+  const __half2 a = (w & 1) ? __hsub2(x[0], x[1]) : __hadd2(x[0], x[1]);
+  const __half2 b = (w & 1) ? __hsub2(x[2], x[3]) : __hadd2(x[2], x[3]);
+  return (w & 2) ? __hsub2(a, b) : __hadd2(a, b);
+}
+template <>
+__device__ __forceinline__ float cross_warp_stages<2, float>(const float (&x)[2], int w) {
+  return w ? __fsub_rn(x[0], x[1]) : __fadd_rn(x[0], x[1]);
+}
+template <>
+__device__ __forceinline__ float cross_warp_stages<4, float>(const float (&x)[4], int w) {
+  const float a = (w & 1) ? __fsub_rn(x[0], x[1]) : __fadd_rn(x[0], x[1]);
+  const float b = (w & 1) ? __fsub_rn(x[2], x[3]) : __fadd_rn(x[2], x[3]);
+  return (w & 2) ? __fsub_rn(a, b) : __fadd_rn(a, b);
+}
+
+// K = 1024 / 2048: one CTA of K / 16 threads (2 or 4 warps) per row, so a
+// 776-row activation is resident in one wave at ~21 warps per SM with short
+// per-thread dependency chains.  Thread (w, l) holds elements
+// 512 w + 256 c + 8 l + j (c = 0, 1; j = 0..7): index bits 0-2 are in a
+// vector, 3-7 across lanes, bit 8 across the thread's two vectors and bits 9
+// and up across the row's warps, whose stages (the last, as in the
+// reference's ascending order) go through one shared-memory exchange.
 template <int LOGK, bool FP16, int MODE>
-__global__ void __launch_bounds__(64) quant_rot_warp_kernel(
+__global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k) {
   constexpr int K = 1 << LOGK;
-  constexpr int C = K / 512;       // chunks of 256 elements per warp
+  constexpr int NW = K / 512;      // warps per row (2 or 4)
   constexpr int RBITS = LOGK - 8;  // log2(K / 256): stages kept in fp32
-  static_assert(RBITS <= 3, "fp32 stages must stay inside a thread");
-  __shared__ __align__(16) uint4 xchg[2][C][32][FP16 ? 1 : 2];
-  __shared__ float warp_amax[2];
+  static_assert(RBITS <= 3, "fp32 stages must stay inside a vector");
+  __shared__ __align__(16) uint4 xchg[NW][2][32][FP16 ? 1 : 2];
+  __shared__ float warp_amax[NW];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = blockIdx.x;
   pdl_launch_dependents();
   pdl_wait();  // x is the previous kernel's output
   if (row >= m) return;
-  float v[C][8];
-  const __half* xr = x + row * ldx + 256 * C * warp + 8 * lane;
+  float v[2][8];
+  const __half* xr = x + row * ldx + 512 * warp + 8 * lane;
 #pragma unroll
-  for (int c = 0; c < C; ++c) load8_half_as_float(xr + 256 * c, v[c]);
-  fwht_f32_bits<C, 0, RBITS>(v, lane);
-  float mx;
+  for (int c = 0; c < 2; ++c) load8_half_as_float(xr + 256 * c, v[c]);
+  fwht_f32_bits<2, 0, RBITS>(v, lane);
+  float mx = 0.f;
   if constexpr (FP16) {
-    __half2 h[C][4];
-    pack_half2<C>(v, h);
-    fwht_h2_bits<C, RBITS, LOGK - 1>(h, lane);
+    __half2 h[2][4];
+    pack_half2<2>(v, h);
+    fwht_h2_bits<2, RBITS, 9>(h, lane);
 #pragma unroll
-    for (int c = 0; c < C; ++c) xchg[warp][c][lane][0] = *reinterpret_cast<const uint4*>(h[c]);
+    for (int c = 0; c < 2; ++c) xchg[warp][c][lane][0] = *reinterpret_cast<const uint4*>(h[c]);
     __syncthreads();
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const uint4 o = xchg[warp ^ 1][c][lane][0];
-      const __half2* oh = reinterpret_cast<const __half2*>(&o);
+    for (int c = 0; c < 2; ++c) {
+      __half2 all[4][NW];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) h[c][i] = warp ? __hsub2(oh[i], h[c][i]) : __hadd2(h[c][i], oh[i]);
+      for (int u = 0; u < NW; ++u) {
+        const uint4 q = xchg[u][c][lane][0];
+        const __half2* qh = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) all[i][u] = qh[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) h[c][i] = cross_warp_stages<NW, __half2>(all[i], warp);
     }
-    mx = amax_h2<C>(h);
+    mx = amax_h2<2>(h);
 #pragma unroll
-    for (int c = 0; c < C; ++c) unpack_half2<C>(h[c], v[c]);
+    for (int c = 0; c < 2; ++c) unpack_half2<2>(h[c], v[c]);
   } else {
-    fwht_f32_bits<C, RBITS, LOGK - 1>(v, lane);
+    fwht_f32_bits<2, RBITS, 9>(v, lane);
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
+    for (int c = 0; c < 2; ++c) {
       xchg[warp][c][lane][0] = make_uint4(__float_as_uint(v[c][0]), __float_as_uint(v[c][1]),
                                           __float_as_uint(v[c][2]), __float_as_uint(v[c][3]));
       xchg[warp][c][lane][1] = make_uint4(__float_as_uint(v[c][4]), __float_as_uint(v[c][5]),
                                           __float_as_uint(v[c][6]), __float_as_uint(v[c][7]));
     }
     __syncthreads();
-    mx = 0.f;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const uint4 o0 = xchg[warp ^ 1][c][lane][0], o1 = xchg[warp ^ 1][c][lane][1];
-      const float o[8] = {__uint_as_float(o0.x), __uint_as_float(o0.y), __uint_as_float(o0.z),
-                          __uint_as_float(o0.w), __uint_as_float(o1.x), __uint_as_float(o1.y),
-                          __uint_as_float(o1.z), __uint_as_float(o1.w)};
+    for (int c = 0; c < 2; ++c) {
+      float all[8][NW];
+#pragma unroll
+      for (int u = 0; u < NW; ++u) {
+        const uint4 q0 = xchg[u][c][lane][0], q1 = xchg[u][c][lane][1];
+        all[0][u] = __uint_as_float(q0.x); all[1][u] = __uint_as_float(q0.y);
+        all[2][u] = __uint_as_float(q0.z); all[3][u] = __uint_as_float(q0.w);
+        all[4][u] = __uint_as_float(q1.x); all[5][u] = __uint_as_float(q1.y);
+        all[6][u] = __uint_as_float(q1.z); all[7][u] = __uint_as_float(q1.w);
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        v[c][j] = warp ? __fsub_rn(o[j], v[c][j]) : __fadd_rn(v[c][j], o[j]);
+        v[c][j] = cross_warp_stages<NW, float>(all[j], warp);
         mx = fmaxf(mx, fabsf(v[c][j]));
       }
     }
@@ -322,13 +364,15 @@ __global__ void __launch_bounds__(64) quant_rot_warp_kernel(
   mx = warp_max(mx);
   if (lane == 0) warp_amax[warp] = mx;
   __syncthreads();
-  mx = fmaxf(warp_amax[0], warp_amax[1]);
+  mx = warp_amax[0];
+#pragma unroll
+  for (int u = 1; u < NW; ++u) mx = fmaxf(mx, warp_amax[u]);
   const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
   const float rs = __frcp_rn(sdiv);
   if (threadIdx.x == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
 #pragma unroll
-  for (int c = 0; c < C; ++c)
-    store_codes8<MODE>(codes, row * K + 256 * (C * warp + c) + 8 * lane, v[c], sdiv, rs);
+  for (int c = 0; c < 2; ++c)
+    store_codes8<MODE>(codes, row * K + 512 * warp + 256 * c + 8 * lane, v[c], sdiv, rs);
 }
 
 // K = 16384: one 256-thread CTA per row.  Phase 1: warp w transforms its

@@ -271,12 +271,12 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
     dispatch([&](auto f, auto mode) {
       constexpr bool F = decltype(f)::value;
       constexpr int MODE = decltype(mode)::value;
-      const unsigned grid = static_cast<unsigned>(m);  // one 64-thread CTA per row
+      const unsigned grid = static_cast<unsigned>(m);  // one CTA of K / 16 threads per row
       if (k == 1024)
         err_code = cuda_status(launch_kernel(quant_rot_warp_kernel<10, F, MODE>, dim3(grid), dim3(64), 0,
                                              stream, 1, xh, ldx, m, codes, row_scale, isk));
       else
-        err_code = cuda_status(launch_kernel(quant_rot_warp_kernel<11, F, MODE>, dim3(grid), dim3(64), 0,
+        err_code = cuda_status(launch_kernel(quant_rot_warp_kernel<11, F, MODE>, dim3(grid), dim3(128), 0,
                                              stream, 1, xh, ldx, m, codes, row_scale, isk));
     });
   } else if (rot) {
