@@ -466,6 +466,106 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
     store_codes8<MODE>(codes, row * K + 2048 * w + 256 * warp + 8 * lane, v[w], sdiv, rs);
 }
 
+// ---- K = 16384, fp16 staging: every butterfly stage in registers.
+// A row is 2048 16-byte vectors (8 fp16 elements, index bits 0-2 inside a
+// vector); each of the CTA's 256 threads holds 8 of them.  Between phases the
+// vectors move through a shared-memory buffer so that the next three index
+// bits become the thread's vector index c:
+//   A: vec = 8u + c                      -> element bits 3-5 across c (fp32, with 0-2)
+//   B: vec = (u>>3)<<6 | c<<3 | (u&7)    -> bits 6-8
+//   C: vec = (u>>6)<<9 | c<<6 | (u&63)   -> bits 9-11
+//   D: vec = (c&3)<<9 | (c>>2)<<8 | u    -> bits 12-13 (c bits 0-1)
+// Each thread writes back the vectors it read, so one barrier per transpose
+// suffices.  Slot swizzle vec ^ ((vec >> 3) & 7): in every phase the 8 lanes
+// of a quarter-warp hit 8 distinct 16-byte bank groups.
+__device__ __forceinline__ int q16k_slot(int vec) { return vec ^ ((vec >> 3) & 7); }
+
+__device__ __forceinline__ void load8_half_as_float_l1(const __half* p, float (&v)[8]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));  // L1-cached: lanes stride 128 B
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_fp16_kernel(
+    const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
+    float* __restrict__ row_scale, float inv_sqrt_k) {
+  constexpr int K = 16384;
+  extern __shared__ __align__(16) unsigned char quant_smem[];  // 2048 x 16 B
+  uint4* buf = reinterpret_cast<uint4*>(quant_smem);
+  __shared__ float warp_amax[kQuantThreads / 32];
+  const long long row = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // x is the previous kernel's output
+  if (row >= m) return;
+  const int u = threadIdx.x, warp = u >> 5, lane = u & 31;
+  __half2 h[8][4];
+  {
+    // phase A: index bits 0-5 in fp32
+    float v[8][8];
+    const __half* xr = x + row * ldx + 64 * u;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) load8_half_as_float_l1(xr + 8 * c, v[c]);
+#pragma unroll
+    for (int b = 0; b < 3; ++b) stage_in_vector<8>(v, 1 << b);
+#pragma unroll
+    for (int b = 0; b < 3; ++b) stage_across_chunks<8>(v, 1 << b);
+    pack_half2<8>(v, h);
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) buf[q16k_slot(8 * u + c)] = *reinterpret_cast<const uint4*>(h[c]);
+  __syncthreads();
+  // phase B: bits 6-8
+  {
+    const int base = ((u >> 3) << 6) | (u & 7);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(base | (c << 3))];
+#pragma unroll
+    for (int b = 0; b < 3; ++b) h2_stage_across_chunks<8>(h, 1 << b);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) buf[q16k_slot(base | (c << 3))] = *reinterpret_cast<const uint4*>(h[c]);
+  }
+  __syncthreads();
+  // phase C: bits 9-11
+  {
+    const int base = ((u >> 6) << 9) | (u & 63);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(base | (c << 6))];
+#pragma unroll
+    for (int b = 0; b < 3; ++b) h2_stage_across_chunks<8>(h, 1 << b);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) buf[q16k_slot(base | (c << 6))] = *reinterpret_cast<const uint4*>(h[c]);
+  }
+  __syncthreads();
+  // phase D: bits 12-13
+  const auto vec_d = [&](int c) { return ((c & 3) << 9) | ((c >> 2) << 8) | u; };
+#pragma unroll
+  for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(vec_d(c))];
+  h2_stage_across_chunks<8>(h, 1);
+  h2_stage_across_chunks<8>(h, 2);
+  float mx = amax_h2<8>(h);
+  mx = warp_max(mx);
+  if (lane == 0) warp_amax[warp] = mx;
+  __syncthreads();
+  mx = warp_amax[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) mx = fmaxf(mx, warp_amax[w]);
+  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  const float rs = __frcp_rn(sdiv);
+  if (u == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float v[8];
+    unpack_half2<8>(h[c], v);
+    store_codes8<MODE>(codes, row * K + 8 * vec_d(c), v, sdiv, rs);
+  }
+}
+
 // Any K (multiple of 64) without rotation: one warp per row, two passes
 // (amax, then codes).  Replaces quant_rows (int4_gemm.cu:451-477).
 template <int MODE>

@@ -291,8 +291,13 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
           return;
         }
       }
-      err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<F, MODE>, dim3(grid), dim3(kQuantThreads),
-                                           smem, stream, 1, xh, ldx, m, codes, row_scale, isk));
+      if (F)
+        err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE>, dim3(grid),
+                                             dim3(kQuantThreads), smem, stream, 1, xh, ldx, m, codes,
+                                             row_scale, isk));
+      else
+        err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<F, MODE>, dim3(grid), dim3(kQuantThreads),
+                                             smem, stream, 1, xh, ldx, m, codes, row_scale, isk));
     });
   } else {
     dispatch([&](auto, auto mode) {
