@@ -3,8 +3,10 @@
 Same op names, schemas, fake (meta) implementations, Python wrappers and
 error messages as the reference's ``pi05_fast/w4a4/extension.py:78-178``
 (argument checks follow ``pi05_fast/w4a4/csrc/int4_gemm.cu:487-501, :570-577``),
-but every op runs the sm_100a kernels of ``libw4a4_sm100.so`` through its C
-ABI.  There is no CPU path: CPU tensors raise, a missing library raises.
+but every op runs the sm_100a kernels of ``libw4a4_sm100.so``: the schemas
+and fakes are registered here, the op bodies are C++ (``_w4a4_ops.so``, built
+from ``csrc/torch_ops.cpp``) calling the library's C ABI.  There is no CPU
+path: CPU tensors raise, a missing library raises.
 
 Importing this module before the reference's ``pi05_fast.w4a4.extension``
 makes the reference's ``_register_custom_op`` see the ops as registered
@@ -99,64 +101,6 @@ def _prepare_row_major(w: torch.Tensor) -> torch.Tensor:
     return pad_rows_cuda(w, (w.size(1) + 3) // 4 * 4)
 
 
-# Weight descriptor arrays for the C ABI, keyed by (pointer, N, row words,
-# layout) of each weight: packed weights are long-lived, so the ctypes array
-# is built once per weight tuple.
-_desc_cache: dict = {}
-
-
-def _weight_descs(ws, layout: int):
-    key = tuple((w.data_ptr(), int(w.size(0)), int(w.size(1))) for w in ws) + (layout,)
-    descs = _desc_cache.get(key)
-    if descs is None:
-        if len(_desc_cache) > 4096:
-            _desc_cache.clear()
-        descs = nat.weights_array([(p, n, rw, layout) for p, n, rw in key[:-1]])
-        _desc_cache[key] = descs
-    return descs
-
-
-def _run(x: torch.Tensor, weights: tuple[torch.Tensor, ...], fragment_major: bool):
-    k = _check_activation(x)
-    for w in weights:
-        _check_packed(w, k, x.device)
-        if fragment_major:
-            # int4_gemm.cu:570-577
-            if k != 2048 or w.size(0) != 16384:
-                raise RuntimeError("WMMA-fragment-major weights currently support only K=2048, N=16384")
-            if w.size(1) != k // 8 + 9:
-                raise RuntimeError("WMMA-fragment-major weights must use the K/8+9 marker stride")
-    layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment_major else nat.LAYOUT_ROW_MAJOR
-    x2 = x.contiguous()
-    if x2.data_ptr() % 16:
-        x2 = x2.clone()
-    m = x2.numel() // k
-    lead = tuple(x.shape[:-1])
-    dev = x.device
-    switch = dev.index != torch.cuda.current_device()
-    if switch:
-        prev = torch.cuda.current_device()
-        torch.cuda.set_device(dev)
-    try:
-        ws = [w.contiguous() if fragment_major else _prepare_row_major(w) for w in weights]
-        ys = [torch.empty((*lead, int(w.size(0))), dtype=torch.float16, device=dev) for w in ws]
-        if m == 0:
-            return tuple(ys)
-        # one scratch allocation: int8 codes [m, k] then fp32 row scales [m]
-        codes_bytes = (m * k + 255) // 256 * 256
-        scratch = torch.empty((codes_bytes + 4 * m,), dtype=torch.uint8, device=dev)
-        base = scratch.data_ptr()
-        outs = nat.pointer_array([y.data_ptr() for y in ys])
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        nat.check(nat.lib().w4a4_int4_gemm(
-            x2.data_ptr(), m, k, k, nat.ROTATE_BY_K, staging_mode(), len(ws),
-            _weight_descs(ws, layout), outs, base, base + codes_bytes, stream))
-    finally:
-        if switch:
-            torch.cuda.set_device(prev)
-    return tuple(ys)
-
-
 def _fake_out(x: torch.Tensor, packed: torch.Tensor) -> torch.Tensor:
     return torch.empty(*x.shape[:-1], packed.shape[0], device=x.device, dtype=torch.float16)
 
@@ -171,31 +115,50 @@ def _ops_exist() -> bool:
 
 # The op library; kept alive for the life of the process.
 _library = None
+_ops_loaded = False
 
-# name, schema arguments / returns, implementation, fake implementation
+# name, schema arguments / returns, fake implementation
 _OPS = (
     ("int4_gemm", "(Tensor x, Tensor packed) -> Tensor",
-     lambda x, packed: _run(x, (packed,), False)[0], lambda x, packed: _fake_out(x, packed)),
+     lambda x, packed: _fake_out(x, packed)),
     ("int4_gemm_tiled", "(Tensor x, Tensor packed) -> Tensor",
-     lambda x, packed: _run(x, (packed,), True)[0], lambda x, packed: _fake_out(x, packed)),
+     lambda x, packed: _fake_out(x, packed)),
     ("int4_gemm2", "(Tensor x, Tensor w0, Tensor w1) -> (Tensor, Tensor)",
-     lambda x, w0, w1: _run(x, (w0, w1), False),
      lambda x, w0, w1: (_fake_out(x, w0), _fake_out(x, w1))),
     ("int4_gemm2_tiled", "(Tensor x, Tensor w0, Tensor w1) -> (Tensor, Tensor)",
-     lambda x, w0, w1: _run(x, (w0, w1), True),
      lambda x, w0, w1: (_fake_out(x, w0), _fake_out(x, w1))),
     ("int4_gemm3", "(Tensor x, Tensor w0, Tensor w1, Tensor w2) -> (Tensor, Tensor, Tensor)",
-     lambda x, w0, w1, w2: _run(x, (w0, w1, w2), False),
      lambda x, w0, w1, w2: (_fake_out(x, w0), _fake_out(x, w1), _fake_out(x, w2))),
 )
+
+OPS_LIB_NAME = "_w4a4_ops.so"
+OPS_LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), OPS_LIB_NAME)
+
+
+def _not_built(*_args):
+    raise RuntimeError(
+        f"{OPS_LIB_NAME} is not built (expected at {OPS_LIB_PATH}); run "
+        "`python -m pi05_pytorch_fast_b200.build`. The W4A4 path has no CPU fallback.")
+
+
+def _load_ops() -> bool:
+    """Loads the C++ op bodies (csrc/torch_ops.cpp, registered under
+    CompositeExplicitAutograd) if the library is built; they replace the
+    not-built stubs."""
+    global _ops_loaded
+    if not _ops_loaded and os.path.isfile(OPS_LIB_PATH):
+        torch.ops.load_library(OPS_LIB_PATH)
+        _ops_loaded = True
+    return _ops_loaded
 
 
 def _register_custom_op() -> None:
     """Registers the five pi05_w4a4 ops with the reference's schemas (the
     schemas torch.library.custom_op(..., mutates_args=()) gives them,
-    extension.py:92-138) and fake implementations for tracing.  They are
-    defined through torch.library.Library rather than torch.library.custom_op:
-    same op, but about 11 us less dispatch overhead per call on the host."""
+    extension.py:92-138) and fake implementations for tracing.  The op
+    bodies are C++ (_w4a4_ops.so): checks, output allocation and the call
+    into libw4a4_sm100.so cost about 2 us of host time per op.  Without that
+    library every op raises."""
     global _op_registered, _library
     if _op_registered:
         return
@@ -205,12 +168,14 @@ def _register_custom_op() -> None:
             "pi05_pytorch_fast_b200 before pi05_fast.w4a4.extension so the B200 kernels serve them."
         )
     lib = torch.library.Library("pi05_w4a4", "DEF")
-    for name, schema, impl, fake in _OPS:
+    for name, schema, fake in _OPS:
         lib.define(name + schema)
-        lib.impl(name, impl, "CompositeExplicitAutograd")
         torch.library.register_fake("pi05_w4a4::" + name, fake, lib=lib)
     _library = lib
     _op_registered = True
+    if not _load_ops():
+        for name, _, _ in _OPS:
+            lib.impl(name, _not_built, "CompositeExplicitAutograd")
 
 
 _register_custom_op()
@@ -242,9 +207,11 @@ def int4_gemm3(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor, w2: torch.Te
 
 
 def preload() -> None:
-    """Load the native library up front (the reference JIT-compiles here)."""
+    """Load the native libraries up front (the reference JIT-compiles here)."""
     nat.lib()
     _register_custom_op()
+    if not _load_ops():
+        _not_built()
 
 
 # ---------------------------------------------------------------------------

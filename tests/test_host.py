@@ -107,6 +107,35 @@ def test_extension_module_serves_as_the_reference_compiled_module():
     assert callable(ext.preload)
 
 
+def test_op_bodies_come_from_the_cpp_op_library():
+    """The five ops run the C++ bodies of _w4a4_ops.so (csrc/torch_ops.cpp),
+    not a Python body and not the not-built stub."""
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    assert ext._load_ops()
+    for name, _, _ in ext._OPS:
+        table = torch._C._dispatch_dump(f"pi05_w4a4::{name}")
+        line = next(ln for ln in table.splitlines() if ln.startswith("CompositeExplicitAutograd"))
+        assert "torch_ops.cpp" in line, table
+
+
+def test_op_library_uses_the_shared_cxx_runtime():
+    """_w4a4_ops.so must take libstdc++ from libstdc++.so.6, like torch: a
+    second, statically linked C++ runtime in it makes every exception torch
+    throws through an op body (a TORCH_CHECK with a formatted message) crash
+    the process while unwinding."""
+    import shutil
+    import subprocess
+
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    if shutil.which("readelf") is None:
+        pytest.skip("readelf not installed")
+    dyn = subprocess.run(["readelf", "-d", ext.OPS_LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    assert "[libstdc++.so.6]" in dyn
+
+
 def test_fake_impls_give_reference_shapes():
     from torch._subclasses.fake_tensor import FakeTensorMode
 
