@@ -7,7 +7,7 @@
 // which is the reference's gemm_iu4 / gemm_iu4_shape contract
 // (pi05_fast/w4a4/csrc/int4_gemm.cu:66-204, :207-394; epilogue :199-200).
 //
-// Design (one persistent CTA per SM, 14 warps):
+// Design (one persistent CTA per SM, 18 warps):
 //  * Tiles put weights on the MMA's M side (128 rows = UMMA M) and tokens on
 //    its N side (a multiple of 16, <= 208), so a ragged token count such as
 //    776 splits into near-equal tiles (4 x 208) instead of a mostly empty
@@ -15,8 +15,9 @@
 //    space, so each op is one launch.
 //  * warp 0 (TMA producer) streams, per 128-wide K step, the packed weight
 //    tile (8 KB, either reference layout, straight from the reference's
-//    tensors) and the int8 token tile (128-byte swizzle) into a ring whose
-//    depth is set by the token-tile size (6..12 stages).
+//    tensors) and the int8 token tile (128-byte swizzle) into a ring of
+//    kGemmRing (6) stages.  The ring depth is a compile-time constant, so
+//    every ring index below is a constant after unrolling.
 //  * warps 2-9 (unpack, two groups of 4 taking alternate K steps) each own
 //    32 weight rows: they read the staged nibbles, expand them to int8 (x16,
 //    see expand_nibbles_x16) in registers and write them with tcgen05.st
@@ -28,9 +29,13 @@
 //    the epilogue of a tile overlaps the mainloop of the next) and frees each
 //    step with ONE tcgen05.commit: the issuing thread has ~400 cycles of MMA
 //    time per step to spend, so its loop carries no warp syncs or divisions.
-//  * warps 10-13 (epilogue) read the accumulator with tcgen05.ld, divide by
-//    16 (exact), apply the token and weight scales in fp32, round to fp16 and
+//  * warps 10-17 (epilogue, two per TMEM lane quarter taking alternate
+//    16-column chunks) read the accumulator with tcgen05.ld, divide by 16
+//    (exact), apply the token and weight scales in fp32, round to fp16 and
 //    transpose 16x32 blocks through shared memory into 16-byte row stores.
+//  * SPLIT = true (split-K): the two CTAs of a cluster run the two K halves
+//    of one tile; rank 1 pushes its int32 partial sums into rank 0's idle
+//    ring through distributed shared memory, and rank 0's epilogue adds them.
 // TMEM map (512 columns): accumulators at [0, T) and [T, 2T) for a token tile
 // of T columns, then A stages of 32 columns (128 K-bytes per row) up to 512.
 #pragma once
