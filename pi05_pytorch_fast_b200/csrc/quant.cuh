@@ -230,6 +230,40 @@ enum CodesMode : int {
 template <int MODE>
 __device__ __forceinline__ void store_codes8(void* out, long long elem, const float (&v)[8],
                                              float sdiv, float rs) {
+  if constexpr (MODE != kCodesPacked) {
+    // Fast path, the same decision as quant_code: r = fl(t + 1.5 * 2^23) is
+    // 1.5 * 2^23 + rint(t) exactly (|t| < 2^22; the offset is even, so the
+    // sum's round-half-even is rint's), e = t - rint(t) is exact, and
+    // |e| < 0.5 - 4e-6 is quant_code's "farther than 4e-6 from a tie".  The
+    // low byte of r's bit pattern is then rint(t) as a two's-complement
+    // int8.  No clamp: |v| <= amax and sdiv >= fl(amax / 7) keep
+    // |t| <= 7 (1 + 2^-22) < 7.5.  A group with a value near a tie (or NaN)
+    // takes the exact path below.
+    constexpr float kRound = 12582912.0f;
+    uint32_t b[8];
+    bool fast = true;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float t = __fmul_rn(v[j], rs);
+      const float r = __fadd_rn(t, kRound);
+      const float e = __fsub_rn(t, __fsub_rn(r, kRound));
+      fast &= fabsf(e) < 0.499996f;
+      b[j] = __float_as_uint(r);
+    }
+    if (fast) {
+      // bytes of the first word: elements 0,2,4,6 (GEMM order) or 0-3
+      constexpr int a0 = 0, a1 = MODE == kCodesGemm ? 2 : 1, a2 = MODE == kCodesGemm ? 4 : 2,
+                    a3 = MODE == kCodesGemm ? 6 : 3;
+      constexpr int c0 = MODE == kCodesGemm ? 1 : 4, c1 = MODE == kCodesGemm ? 3 : 5,
+                    c2 = MODE == kCodesGemm ? 5 : 6, c3 = 7;
+      const uint32_t w0 = __byte_perm(__byte_perm(b[a0], b[a1], 0x0040),
+                                      __byte_perm(b[a2], b[a3], 0x0040), 0x5410);
+      const uint32_t w1 = __byte_perm(__byte_perm(b[c0], b[c1], 0x0040),
+                                      __byte_perm(b[c2], b[c3], 0x0040), 0x5410);
+      *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(out) + elem) = make_uint2(w0, w1);
+      return;
+    }
+  }
   int q[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) q[j] = quant_code(v[j], sdiv, rs);
