@@ -25,6 +25,10 @@ enum DeviceError : unsigned {
   kErrBadParams = 1u << 6,     // launch parameters outside the kernel's invariants
 };
 
+// The device error word: kernels OR the bits above into it (read and cleared
+// by w4a4_device_error).
+__device__ unsigned g_w4a4_device_error;
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -251,6 +255,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// 3-D tiled bulk tensor load global -> shared (x innermost, in elements).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
 

@@ -128,8 +128,6 @@ struct alignas(64) GemmParams {
   int k_tiles;
 };
 
-__device__ unsigned g_w4a4_device_error;
-
 struct TileCoord {
   int seg;
   int n0;

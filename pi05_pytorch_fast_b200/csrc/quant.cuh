@@ -16,7 +16,8 @@
 //  * staging FP16 = the HIP kernel's arithmetic: stages with stride < R
 //    (R = K/256) in fp32, then the values are rounded to fp16 and every later
 //    stage adds/subtracts in fp32 and rounds back to fp16 (int4_gemm.cu:404-426).
-//    Here those later stages run as packed half2 adds (__hadd2/__hsub2): for
+//    Here those later stages run as packed half2 adds (__hadd2/__hsub2, and
+//    __hfma2 with a +-1 factor across lanes): for
 //    fp16 a, b the single rounding fl16(a + b) equals fl16(fl32(a + b)),
 //    because binary32 carries at least 2 x 11 + 2 significand bits (double
 //    rounding through it is innocuous), so the result is bit-identical while
@@ -55,32 +56,58 @@ __device__ __forceinline__ void load8_half_as_float(const __half* p, float (&v)[
   }
 }
 
-// Butterfly between elements whose index differs in bit log2(h), h < 8.
+// Packed fp32 pairs: elements (2i, 2i + 1) of a vector go through the
+// sm_100 two-lane fp32 instructions (add / fma .rn.f32x2), each lane rounded
+// exactly like the scalar instruction.  a - b is fma(b, -1, a): the product is
+// exact, so its one rounding is that of the subtraction.
+__device__ __forceinline__ void bfly2(float& a0, float& a1, float& b0, float& b1) {
+  const float2 a = make_float2(a0, a1), b = make_float2(b0, b1);
+  const float2 s = __fadd2_rn(a, b);
+  const float2 d = __ffma2_rn(b, make_float2(-1.f, -1.f), a);
+  a0 = s.x;
+  a1 = s.y;
+  b0 = d.x;
+  b1 = d.y;
+}
+
+// Butterfly stage inside each 8-vector: pairs (j, j + h), lower keeps a + b,
+// upper a - b (fp32, round to nearest).
 template <int C>
 __device__ __forceinline__ void stage_in_vector(float (&v)[C][8], int h) {
 #pragma unroll
-  for (int c = 0; c < C; ++c)
+  for (int c = 0; c < C; ++c) {
+    if (h == 1) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (!(j & h)) {
-        const float a = v[c][j], b = v[c][j + h];
+      for (int j = 0; j < 8; j += 2) {
+        const float a = v[c][j], b = v[c][j + 1];
         v[c][j] = __fadd_rn(a, b);
-        v[c][j + h] = __fsub_rn(a, b);
+        v[c][j + 1] = __fsub_rn(a, b);
       }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j += 2)
+        if (!(j & h)) bfly2(v[c][j], v[c][j + 1], v[c][j + h], v[c][j + h + 1]);
+    }
+  }
 }
 
 // Butterfly across lanes: partner lane = lane ^ m.  The lane with the bit
-// clear holds the lower element a and keeps a + b; its partner keeps a - b.
+// clear holds the lower element a and keeps a + b; its partner keeps a - b:
+// both are fma(mine, +-1, other), one rounding of the exact sum.
 template <int C>
 __device__ __forceinline__ void stage_across_lanes(float (&v)[C][8], int lane, int m) {
-  const bool upper = (lane & m) != 0;
+  const float sg = (lane & m) ? -1.f : 1.f;
+  const float2 sg2 = make_float2(sg, sg);
 #pragma unroll
   for (int c = 0; c < C; ++c)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float mine = v[c][j];
-      const float other = __shfl_xor_sync(0xffffffffu, mine, m);
-      v[c][j] = upper ? __fsub_rn(other, mine) : __fadd_rn(mine, other);
+    for (int j = 0; j < 8; j += 2) {
+      const float2 mine = make_float2(v[c][j], v[c][j + 1]);
+      const float2 other = make_float2(__shfl_xor_sync(0xffffffffu, mine.x, m),
+                                       __shfl_xor_sync(0xffffffffu, mine.y, m));
+      const float2 r = __ffma2_rn(mine, sg2, other);
+      v[c][j] = r.x;
+      v[c][j + 1] = r.y;
     }
 }
 
@@ -91,11 +118,7 @@ __device__ __forceinline__ void stage_across_chunks(float (&v)[C][8], int h) {
   for (int c = 0; c < C; ++c)
     if (!(c & h))
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float a = v[c][j], b = v[c + h][j];
-        v[c][j] = __fadd_rn(a, b);
-        v[c + h][j] = __fsub_rn(a, b);
-      }
+      for (int j = 0; j < 8; j += 2) bfly2(v[c][j], v[c][j + 1], v[c + h][j], v[c + h][j + 1]);
 }
 
 // ---- packed-half2 stages: h[c][i] holds elements (8c' + 2i, 8c' + 2i + 1) of
@@ -122,16 +145,18 @@ __device__ __forceinline__ void h2_stage_in_vector(__half2 (&h)[C][4], int hi) {
       }
 }
 
+// Lower lane: mine + other; upper lane: other - mine; both fma(mine, +-1,
+// other) with one fp16 rounding of the exact result.
 template <int C>
 __device__ __forceinline__ void h2_stage_across_lanes(__half2 (&h)[C][4], int lane, int m) {
-  const bool upper = (lane & m) != 0;
+  const __half2 sg = __float2half2_rn((lane & m) ? -1.f : 1.f);
 #pragma unroll
   for (int c = 0; c < C; ++c)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const __half2 mine = h[c][i];
       const __half2 other = __shfl_xor_sync(0xffffffffu, mine, m);
-      h[c][i] = upper ? __hsub2(other, mine) : __hadd2(mine, other);
+      h[c][i] = __hfma2(mine, sg, other);
     }
 }
 
@@ -243,12 +268,15 @@ __device__ __forceinline__ void store_codes8(void* out, long long elem, const fl
     uint32_t b[8];
     bool fast = true;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float t = __fmul_rn(v[j], rs);
-      const float r = __fadd_rn(t, kRound);
-      const float e = __fsub_rn(t, __fsub_rn(r, kRound));
-      fast &= fabsf(e) < 0.499996f;
-      b[j] = __float_as_uint(r);
+    for (int j = 0; j < 8; j += 2) {
+      const float2 t = __fmul2_rn(make_float2(v[j], v[j + 1]), make_float2(rs, rs));
+      const float2 r = __fadd2_rn(t, make_float2(kRound, kRound));
+      const float2 d = __fadd2_rn(r, make_float2(-kRound, -kRound));  // rint(t), exact
+      const float2 e = __ffma2_rn(d, make_float2(-1.f, -1.f), t);     // t - rint(t), exact
+      fast &= fabsf(e.x) < 0.499996f;
+      fast &= fabsf(e.y) < 0.499996f;
+      b[j] = __float_as_uint(r.x);
+      b[j + 1] = __float_as_uint(r.y);
     }
     if (fast) {
       // bytes of the first word: elements 0,2,4,6 (GEMM order) or 0-3
@@ -509,94 +537,149 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
 //   B: vec = (u>>3)<<6 | c<<3 | (u&7)    -> bits 6-8
 //   C: vec = (u>>6)<<9 | c<<6 | (u&63)   -> bits 9-11
 //   D: vec = (c&3)<<9 | (c>>2)<<8 | u    -> bits 12-13 (c bits 0-1)
-// Each thread writes back the vectors it read, so one barrier per transpose
+// Phase A reads the row from the TMA buffer (line u = vec 8u .. 8u + 7);
+// every later phase reads and writes the transposed buffer in place.  Each
+// thread writes back the vectors it read, so one barrier per transpose
 // suffices.  Slot swizzle vec ^ ((vec >> 3) & 7): in every phase the 8 lanes
 // of a quarter-warp hit 8 distinct 16-byte bank groups.
 __device__ __forceinline__ int q16k_slot(int vec) { return vec ^ ((vec >> 3) & 7); }
 
-__device__ __forceinline__ void load8_half_as_float_l1(const __half* p, float (&v)[8]) {
-  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));  // L1-cached: lanes stride 128 B
-  const __half2* h = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
+// Shared memory of the K = 16384 fp16-staging kernel: two 32 KB row buffers
+// (TMA destination, then the transposes' workspace), 1024-byte aligned for
+// the 128-byte swizzle.
+constexpr int kQ16RowBytes = 16384 * 2;
+constexpr int kQ16Smem = 2 * kQ16RowBytes + 1024;
+constexpr int kQ16CtasPerSm = 3;
 
+// Persistent: each CTA quantises rows blockIdx.x, blockIdx.x + gridDim.x, ...
+// One thread loads the next row with TMA (a 3-D map {64, 256, M} of 128-byte
+// lines, 128-byte swizzle) while the CTA computes the current one, so the
+// load of a CTA's second row hides behind the compute of its first.  The
+// swizzle puts 16-byte chunk c of line u at chunk c ^ (u & 7): thread u reads
+// its line (elements 64u .. 64u + 63) without bank conflicts.
 template <int MODE>
-__global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_fp16_kernel(
-    const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
-    float* __restrict__ row_scale, float inv_sqrt_k) {
+__global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
+    const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
+    float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns) {
   constexpr int K = 16384;
-  extern __shared__ __align__(16) unsigned char quant_smem[];  // 2048 x 16 B
-  uint4* buf = reinterpret_cast<uint4*>(quant_smem);
+  extern __shared__ unsigned char quant_smem[];
   __shared__ float warp_amax[kQuantThreads / 32];
-  const long long row = blockIdx.x;
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int abort_flag;
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(quant_smem) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_addr(base);
+  const uint32_t bar0 = smem_addr(&bars[0]);
+  const int u = threadIdx.x, warp = u >> 5, lane = u & 31;
+  if (u == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_launch_dependents();
   pdl_wait();  // x is the previous kernel's output
+  long long row = blockIdx.x;
   if (row >= m) return;
-  const int u = threadIdx.x, warp = u >> 5, lane = u & 31;
-  __half2 h[8][4];
-  {
-    // phase A: index bits 0-5 in fp32
-    float v[8][8];
-    const __half* xr = x + row * ldx + 64 * u;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) load8_half_as_float_l1(xr + 8 * c, v[c]);
-#pragma unroll
-    for (int b = 0; b < 3; ++b) stage_in_vector<8>(v, 1 << b);
-#pragma unroll
-    for (int b = 0; b < 3; ++b) stage_across_chunks<8>(v, 1 << b);
-    pack_half2<8>(v, h);
+  const long long stride = gridDim.x;
+  if (u == 0) {
+    tma_prefetch_desc(&xmap);
+    mbar_arrive_expect_tx(bar0, kQ16RowBytes);
+    tma_load_3d(sbase, &xmap, 0, 0, static_cast<int>(row), bar0);
   }
+  for (int it = 0; row < m; ++it, row += stride) {
+    const int b = it & 1;
+    if (u == 0 && row + stride < m) {
+      // buffer b ^ 1 was released by the barrier that ended the previous row
+      mbar_arrive_expect_tx(bar0 + 8 * (b ^ 1), kQ16RowBytes);
+      tma_load_3d(sbase + (b ^ 1) * kQ16RowBytes, &xmap, 0, 0, static_cast<int>(row + stride),
+                  bar0 + 8 * (b ^ 1));
+    }
+    if (!mbar_wait_bounded(bar0 + 8 * b, (it >> 1) & 1, &abort_flag, &g_w4a4_device_error,
+                           kErrWaitTma, limit_ns)) {
+      if (u == 0 && row + stride < m) {
+        // the prefetch may still be landing: wait for it (bounded) before exiting
+        int no_abort = 0;
+        mbar_wait_bounded(bar0 + 8 * (b ^ 1), ((it + 1) >> 1) & 1, &no_abort,
+                          &g_w4a4_device_error, kErrWaitDrain, limit_ns);
+      }
+      return;
+    }
+    uint4* buf = reinterpret_cast<uint4*>(base + b * kQ16RowBytes);
+    __half2 h[8][4];
+    {
+      // phase A: index bits 0-5 in fp32
+      float v[8][8];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) buf[q16k_slot(8 * u + c)] = *reinterpret_cast<const uint4*>(h[c]);
-  __syncthreads();
-  // phase B: bits 6-8
-  {
-    const int base = ((u >> 3) << 6) | (u & 7);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 raw = buf[8 * u + (c ^ (u & 7))];
+        const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(base | (c << 3))];
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(hp[i]);
+          v[c][2 * i] = f.x;
+          v[c][2 * i + 1] = f.y;
+        }
+      }
 #pragma unroll
-    for (int b = 0; b < 3; ++b) h2_stage_across_chunks<8>(h, 1 << b);
+      for (int bb = 0; bb < 3; ++bb) stage_in_vector<8>(v, 1 << bb);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) buf[q16k_slot(base | (c << 3))] = *reinterpret_cast<const uint4*>(h[c]);
-  }
-  __syncthreads();
-  // phase C: bits 9-11
-  {
-    const int base = ((u >> 6) << 9) | (u & 63);
+      for (int bb = 0; bb < 3; ++bb) stage_across_chunks<8>(v, 1 << bb);
+      pack_half2<8>(v, h);
+    }
+    __syncthreads();  // every thread has read its line before the buffer is rewritten
 #pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(base | (c << 6))];
+    for (int c = 0; c < 8; ++c) buf[q16k_slot(8 * u + c)] = *reinterpret_cast<const uint4*>(h[c]);
+    __syncthreads();
+    // phase B: bits 6-8
+    {
+      const int bq = ((u >> 3) << 6) | (u & 7);
 #pragma unroll
-    for (int b = 0; b < 3; ++b) h2_stage_across_chunks<8>(h, 1 << b);
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(bq | (c << 3))];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) buf[q16k_slot(base | (c << 6))] = *reinterpret_cast<const uint4*>(h[c]);
-  }
-  __syncthreads();
-  // phase D: bits 12-13
-  const auto vec_d = [&](int c) { return ((c & 3) << 9) | ((c >> 2) << 8) | u; };
+      for (int bb = 0; bb < 3; ++bb) h2_stage_across_chunks<8>(h, 1 << bb);
 #pragma unroll
-  for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(vec_d(c))];
-  h2_stage_across_chunks<8>(h, 1);
-  h2_stage_across_chunks<8>(h, 2);
-  float mx = amax_h2<8>(h);
-  mx = warp_max(mx);
-  if (lane == 0) warp_amax[warp] = mx;
-  __syncthreads();
-  mx = warp_amax[0];
+      for (int c = 0; c < 8; ++c) buf[q16k_slot(bq | (c << 3))] = *reinterpret_cast<const uint4*>(h[c]);
+    }
+    __syncthreads();
+    // phase C: bits 9-11
+    {
+      const int bq = ((u >> 6) << 9) | (u & 63);
 #pragma unroll
-  for (int w = 1; w < kQuantThreads / 32; ++w) mx = fmaxf(mx, warp_amax[w]);
-  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
-  const float rs = __frcp_rn(sdiv);
-  if (u == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(bq | (c << 6))];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    float v[8];
-    unpack_half2<8>(h[c], v);
-    store_codes8<MODE>(codes, row * K + 8 * vec_d(c), v, sdiv, rs);
+      for (int bb = 0; bb < 3; ++bb) h2_stage_across_chunks<8>(h, 1 << bb);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) buf[q16k_slot(bq | (c << 6))] = *reinterpret_cast<const uint4*>(h[c]);
+    }
+    __syncthreads();
+    // phase D: bits 12-13
+    const auto vec_d = [&](int c) { return ((c & 3) << 9) | ((c >> 2) << 8) | u; };
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(vec_d(c))];
+    h2_stage_across_chunks<8>(h, 1);
+    h2_stage_across_chunks<8>(h, 2);
+    float mx = amax_h2<8>(h);
+    mx = warp_max(mx);
+    if (lane == 0) warp_amax[warp] = mx;
+    // the generic-proxy accesses to buffer b are over: order them before the
+    // TMA that refills it (issued after the barrier that ends this row)
+    fence_proxy_async_smem();
+    __syncthreads();
+    mx = warp_amax[0];
+#pragma unroll
+    for (int w = 1; w < kQuantThreads / 32; ++w) mx = fmaxf(mx, warp_amax[w]);
+    const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+    const float rs = __frcp_rn(sdiv);
+    if (u == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float v[8];
+      unpack_half2<8>(h[c], v);
+      store_codes8<MODE>(codes, row * K + 8 * vec_d(c), v, sdiv, rs);
+    }
+    // warp_amax is rewritten by the next row only after two more barriers
   }
 }
 

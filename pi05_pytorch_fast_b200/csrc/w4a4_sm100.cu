@@ -159,18 +159,21 @@ EncodeTiledFn encode_fn() {
 
 struct MapKey {
   uintptr_t ptr;
-  uint64_t d0, d1, stride;
-  uint32_t b0, b1;
-  int dtype, swizzle;
+  uint64_t d[3], stride[2];
+  uint32_t box[3];
+  int rank, dtype, swizzle;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && stride == o.stride && b0 == o.b0 &&
-           b1 == o.b1 && dtype == o.dtype && swizzle == o.swizzle;
+    return ptr == o.ptr && rank == o.rank && dtype == o.dtype && swizzle == o.swizzle &&
+           std::memcmp(d, o.d, sizeof(d)) == 0 && std::memcmp(stride, o.stride, sizeof(stride)) == 0 &&
+           std::memcmp(box, o.box, sizeof(box)) == 0;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     uint64_t h = k.ptr * 0x9E3779B97F4A7C15ull;
-    for (uint64_t v : {k.d0, k.d1, k.stride, static_cast<uint64_t>(k.b0) << 32 | k.b1,
+    for (uint64_t v : {k.d[0], k.d[1], k.d[2], k.stride[0], k.stride[1],
+                       static_cast<uint64_t>(k.box[0]) << 32 | k.box[1],
+                       static_cast<uint64_t>(k.box[2]) << 32 | static_cast<uint64_t>(k.rank),
                        static_cast<uint64_t>(k.dtype) << 8 | static_cast<uint64_t>(k.swizzle)})
       h = (h ^ v) * 0x100000001B3ull;
     return static_cast<size_t>(h);
@@ -179,12 +182,21 @@ struct MapKeyHash {
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
-// 2-D tiled tensor map: dim0 innermost (elements), dim1 rows, row stride in bytes.
-int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, uint64_t d0,
-                uint64_t d1, uint64_t stride_bytes, uint32_t b0, uint32_t b1,
-                CUtensorMapSwizzle swizzle) {
-  const MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_bytes, b0, b1,
-                   static_cast<int>(dtype), static_cast<int>(swizzle)};
+// Tiled tensor map of rank 2 or 3, cached by its parameters: dims[0]
+// innermost (elements), strides_bytes[i] the byte stride of dims[i + 1].
+int make_map(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int rank,
+             const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+             CUtensorMapSwizzle swizzle) {
+  MapKey key{};
+  key.ptr = reinterpret_cast<uintptr_t>(ptr);
+  key.rank = rank;
+  key.dtype = static_cast<int>(dtype);
+  key.swizzle = static_cast<int>(swizzle);
+  for (int i = 0; i < rank; ++i) {
+    key.d[i] = dims[i];
+    key.box[i] = box[i];
+    if (i + 1 < rank) key.stride[i] = strides_bytes[i];
+  }
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_maps.find(key);
@@ -195,24 +207,36 @@ int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, ui
   }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(W4A4_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-  const cuuint64_t dims[2] = {d0, d1};
-  const cuuint64_t strides[1] = {stride_bytes};
-  const cuuint32_t box[2] = {b0, b1};
-  const cuuint32_t estr[2] = {1, 1};
+  cuuint64_t cdims[3], cstrides[2];
+  cuuint32_t cbox[3], estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    cdims[i] = dims[i];
+    cbox[i] = box[i];
+    if (i + 1 < rank) cstrides[i] = strides_bytes[i];
+  }
   CUtensorMap map;
-  const CUresult r = fn(&map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = fn(&map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(ptr), cdims,
+                        cstrides, cbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(W4A4_ERR_CUDA,
-                "cuTensorMapEncodeTiled failed (%d): dims {%llu, %llu}, stride %llu B, box {%u, %u}",
-                static_cast<int>(r), (unsigned long long)d0, (unsigned long long)d1,
-                (unsigned long long)stride_bytes, b0, b1);
+                "cuTensorMapEncodeTiled failed (%d): rank %d, dims {%llu, %llu, %llu}, box {%u, %u, %u}",
+                static_cast<int>(r), rank, (unsigned long long)key.d[0], (unsigned long long)key.d[1],
+                (unsigned long long)key.d[2], key.box[0], key.box[1], key.box[2]);
   std::lock_guard<std::mutex> lk(g_map_mu);
   if (g_maps.size() > 4096) g_maps.clear();
   g_maps.emplace(key, map);
   *out = map;
   return W4A4_OK;
+}
+
+// 2-D tiled tensor map: dim0 innermost (elements), dim1 rows, row stride in bytes.
+int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, uint64_t d0,
+                uint64_t d1, uint64_t stride_bytes, uint32_t b0, uint32_t b1,
+                CUtensorMapSwizzle swizzle) {
+  const uint64_t dims[2] = {d0, d1};
+  const uint32_t box[2] = {b0, b1};
+  return make_map(out, ptr, dtype, 2, dims, &stride_bytes, box, swizzle);
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -291,11 +315,31 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
           return;
         }
       }
-      if (F)
-        err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE>, dim3(grid),
-                                             dim3(kQuantThreads), smem, stream, 1, xh, ldx, m, codes,
-                                             row_scale, isk));
-      else
+      if (F) {
+        // rows as {64 elements, 256 lines, m rows}: one 32 KB box per row
+        CUtensorMap xmap;
+        const uint64_t dims[3] = {64, 256, static_cast<uint64_t>(m)};
+        const uint64_t strides[2] = {128, static_cast<uint64_t>(ldx) * 2};
+        const uint32_t box[3] = {64, 256, 1};
+        if (int e = make_map(&xmap, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B)) {
+          err_code = e;
+          return;
+        }
+        if (int e = ensure_smem_attr(dev, 1u << (12 + MODE), quant_rot_16k_fp16_kernel<MODE>, kQ16Smem)) {
+          err_code = e;
+          return;
+        }
+        int sms = 0;
+        if (int e = sm_count(dev, &sms)) {
+          err_code = e;
+          return;
+        }
+        const unsigned pgrid = static_cast<unsigned>(std::min<int64_t>(m, int64_t(kQ16CtasPerSm) * sms));
+        err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE>, dim3(pgrid),
+                                             dim3(kQuantThreads), kQ16Smem, stream, 1, xmap, m, codes,
+                                             row_scale, isk, g_wait_limit_ns.load()));
+      } else
         err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<F, MODE>, dim3(grid), dim3(kQuantThreads),
                                              smem, stream, 1, xh, ldx, m, codes, row_scale, isk));
     });

@@ -93,6 +93,26 @@ def test_quant_codes_and_scales_bit_exact(k, m, staging):
     np.testing.assert_array_equal(to_np(gemm_codes), gemm_order(ref_codes))
 
 
+@pytest.mark.parametrize("staging", ["fp16", "fp32"])
+@pytest.mark.parametrize("k,m,pad", [(2048, 5, 8), (16384, 450, 64), (16384, 2, 8)])
+def test_quant_strided_rows_bit_exact(k, m, pad, staging):
+    """Rows of x at a stride of k + pad elements (w4a4_quant's ldx): only the
+    first k of each row are read.  450 rows at K = 16384 give some CTAs of the
+    persistent kernel two rows."""
+    x = orc.make_activations(m, k, seed=7 * k + m)
+    ref_codes, ref_scale = orc.quant_activation(x, staging=staging)
+    wide = np.full((m, k + pad), np.float16(1000.0))  # the pad would change amax if it were read
+    wide[:, :k] = x
+    xd = to_dev(wide)
+    codes = torch.empty((m, k), dtype=torch.int8, device=DEV)
+    scale = torch.empty((m,), dtype=torch.float32, device=DEV)
+    nat.check(nat.lib().w4a4_quant(xd.data_ptr(), m, k, k + pad, nat.ROTATE_BY_K, STAGINGS[staging],
+                                   nat.CODES_INT8, codes.data_ptr(), scale.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream))
+    np.testing.assert_array_equal(to_np(codes), ref_codes)
+    np.testing.assert_array_equal(to_np(scale).view(np.int32), ref_scale.view(np.int32))
+
+
 @pytest.mark.parametrize("k", [64, 192, 4096, 2048])
 def test_quant_without_rotation_bit_exact(k):
     x = orc.make_activations(13, k, seed=k)
