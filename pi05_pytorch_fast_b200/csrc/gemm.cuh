@@ -218,42 +218,47 @@ __device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const Til
 }
 
 // The epilogue of one tile for one warp: its TMEM lane quarter (weight rows
-// n_warp .. n_warp+31), 16-column chunks half, half+2, half+4, ...  The next
-// chunk's TMEM load is issued before the current chunk is processed, and
-// release() is called once, as soon as this warp's last TMEM load completed
-// (the accumulator buffer may then be overwritten).  combine(acc) sees each
-// chunk first (split-K exchange) and returns whether to write it out.
+// n_warp .. n_warp+31), 16-column chunks half + 2j for j = first, first +
+// step, ... (all of them by default).  The next chunk's TMEM load is issued
+// before the current chunk is processed, and release() is called once, as
+// soon as this warp's last TMEM load completed (the accumulator buffer may
+// then be overwritten).  combine(acc, j) sees each chunk first (split-K
+// exchange) and returns whether to write it out.
 struct NoCombine {
-  __device__ __forceinline__ bool operator()(uint32_t (&)[16]) const { return true; }
+  __device__ __forceinline__ bool operator()(uint32_t (&)[16], int) const { return true; }
 };
 
 template <bool ACC_OUT, typename Release, typename Combine = NoCombine>
 __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const TileCoord& c, int n_warp,
                                               uint32_t tacc, int half, int lane, __half* stage,
                                               const float* ts, Release release,
-                                              Combine combine = Combine()) {
+                                              Combine combine = Combine(), int first = 0,
+                                              int step = 1) {
   const int nq = ((c.rows + 15) & ~15) >> 4;
-  const int my = (nq - half + 1) >> 1;  // chunks half + 2j, j < my
+  const int all = (nq - half + 1) >> 1;                              // chunks half + 2j, j < all
+  const int my = all > first ? (all - first + step - 1) / step : 0;  // the ones taken here
   if (my <= 0) {
     release();
     return;
   }
+  const auto col = [&](int i) { return (half + 2 * (first + step * i)) * 16; };
   const int n = n_warp + lane;
   const float sw =
       (n < seg.n && !ACC_OUT) ? __ldg(seg.scale + static_cast<long long>(n) * seg.scale_stride) : 0.f;
   uint32_t a0[16], a1[16];
-  tmem_ld_32x32b_x16(tacc + half * 16, a0);
+  tmem_ld_32x32b_x16(tacc + col(0), a0);
   tmem_ld_wait();
   if (my == 1) release();
   for (int j = 0; j < my; j += 2) {
-    if (j + 1 < my) tmem_ld_32x32b_x16(tacc + (half + 2 * (j + 1)) * 16, a1);
-    if (combine(a0)) epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * j) * 16, sw, a0, stage, ts);
+    if (j + 1 < my) tmem_ld_32x32b_x16(tacc + col(j + 1), a1);
+    if (combine(a0, first + step * j))
+      epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, col(j), sw, a0, stage, ts);
     if (j + 1 >= my) break;
     tmem_ld_wait();
     if (j + 2 == my) release();
-    if (j + 2 < my) tmem_ld_32x32b_x16(tacc + (half + 2 * (j + 2)) * 16, a0);
-    if (combine(a1))
-      epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, (half + 2 * (j + 1)) * 16, sw, a1, stage, ts);
+    if (j + 2 < my) tmem_ld_32x32b_x16(tacc + col(j + 2), a0);
+    if (combine(a1, first + step * (j + 1)))
+      epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, col(j + 1), sw, a1, stage, ts);
     if (j + 2 >= my) break;
     tmem_ld_wait();
     if (j + 3 == my) release();
@@ -266,9 +271,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const Tile
 // SPLIT = true: split-K over clusters of two CTAs, each cluster one output
 // tile (the host launches it only when the tiles do not outnumber the
 // clusters).  Rank r runs K steps [r k_tiles, (r+1) k_tiles) through the same
-// pipeline into its own TMEM.  Once rank 0's MMAs are done its token ring is
-// idle: rank 1 then pushes its whole partial accumulator there (distributed
-// shared memory) and rank 0 adds it (int32, exact) and writes the output.
+// pipeline into its own TMEM.  Once a rank's MMAs are done its token ring is
+// idle: each rank pushes the partial sums of the half of the tile's columns
+// the partner writes out into the partner's ring (distributed shared memory),
+// then adds the partner's partial sums of its own half (int32, exact) and
+// writes that half.
 template <int LAYOUT, bool ACC_OUT, bool SPLIT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a4_gemm_kernel(const __grid_constant__ GemmParams p) {
@@ -552,7 +559,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = unit0; tile < total_tiles; tile += ustride, ++tcount) {
       const TileCoord c = decode_tile(p, tile);
       const int buf = tcount & 1;
-      if (!ACC_OUT && rank == 0) stage_tile_scales(ts, p.row_scale, c, lane);
+      if (!ACC_OUT) stage_tile_scales(ts, p.row_scale, c, lane);
       const bool ok = mbar_wait_bounded(bar_accfull(buf), (tcount >> 1) & 1, abort_flag, err,
                                         kErrWaitAccum, limit);
       if (!warp_all(ok)) break;
@@ -568,52 +575,54 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
                                release);
       } else {
-        // This warp's exchange area in rank 0's ring: chunk j of the warp at
-        // [j][32 lanes][16 int32]; ceil(T / 32) chunks per warp.
+        // Both ranks finish half of the tile: rank r writes the chunks with
+        // j % 2 == r (j indexes this warp's chunks half + 2j) and pushes its
+        // partial sums of the others into the partner's token ring, which is
+        // idle once the partner's MMAs are done.  Exchange area of a warp:
+        // chunk j at [j][32 lanes][16 int32]; ceil(T / 32) chunks per warp.
         const int xstride = ((p.tok_tile / 16 + 1) / 2) * kXchgChunkBytes;
         const uint32_t xarea = smem_addr(tok_ring) + ew * xstride;
-        if (rank == 0) {
-          // our MMAs are done: the token ring is free for the partner's sums
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_xready, 1));
-          const bool got = warp_all(mbar_wait_bounded_cl(bar_xfull(ew), 0, abort_flag, err,
-                                                         kErrWaitAccum, limit));
-          int j = 0;
-          epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
-                                 release, [&](uint32_t (&acc)[16]) -> bool {
-            const uint4* src = reinterpret_cast<const uint4*>(tok_ring + ew * xstride +
-                                                              j * kXchgChunkBytes + lane * 64);
-            ++j;
-            if (!got) return true;
+        const uint32_t peer = rank ^ 1u;
+        // our MMAs are done: our ring is free for the partner's sums
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_xready, peer));
+        const bool free = warp_all(mbar_wait_bounded_cl(bar_xready, 0, abort_flag, err,
+                                                        kErrWaitAccum, limit));
+        const uint32_t dst0 = mapa_shared(xarea, peer) + lane * 64;
+        bool released = false;
+        const auto release_once = [&] {
+          if (!released) release();
+          released = true;
+        };
+        epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
+                               [] {}, [&](uint32_t (&acc)[16], int j) -> bool {
+          if (free) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 v = src[q];
-              acc[4 * q] += v.x;
-              acc[4 * q + 1] += v.y;
-              acc[4 * q + 2] += v.z;
-              acc[4 * q + 3] += v.w;
-            }
-            return true;
-          });
-        } else {
-          // wait until rank 0's ring is free, push every chunk of our partial
-          // sums there, then signal this warp's part complete
-          const bool free = warp_all(mbar_wait_bounded_cl(bar_xready, 0, abort_flag, err,
-                                                          kErrWaitAccum, limit));
-          const uint32_t dst0 = mapa_shared(xarea, 0) + lane * 64;
-          int j = 0;
-          epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
-                                 release, [&](uint32_t (&acc)[16]) -> bool {
-            if (free) {
+            for (int q = 0; q < 4; ++q)
+              st_shared_cluster_v4(dst0 + j * kXchgChunkBytes + 16 * q, acc[4 * q],
+                                   acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+          }
+          return false;
+        }, static_cast<int>(peer), 2);
+        // every lane's stores are ordered before its arrival (release, cluster scope)
+        mbar_arrive_cluster(mapa_shared(bar_xfull(ew), peer));
+        const bool got = warp_all(mbar_wait_bounded_cl(bar_xfull(ew), 0, abort_flag, err,
+                                                       kErrWaitAccum, limit));
+        epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
+                               release_once, [&](uint32_t (&acc)[16], int j) -> bool {
+          if (!got) return true;
+          const uint4* src = reinterpret_cast<const uint4*>(tok_ring + ew * xstride +
+                                                            j * kXchgChunkBytes + lane * 64);
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                st_shared_cluster_v4(dst0 + j * kXchgChunkBytes + 16 * q, acc[4 * q],
-                                     acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-            }
-            ++j;
-            return false;
-          });
-          mbar_arrive_cluster(mapa_shared(bar_xfull(ew), 0));
-        }
+          for (int q = 0; q < 4; ++q) {
+            const uint4 v = src[q];
+            acc[4 * q] += v.x;
+            acc[4 * q + 1] += v.y;
+            acc[4 * q + 2] += v.z;
+            acc[4 * q + 3] += v.w;
+          }
+          return true;
+        }, static_cast<int>(rank), 2);
+        release_once();
       }
     }
   }
