@@ -65,16 +65,18 @@ int cuda_status(cudaError_t e) {
 
 std::atomic<unsigned long long> g_wait_limit_ns{1000000000ull};
 
-// Programmatic dependent launch (W4A4_PDL=1): the kernels call
-// griddepcontrol.launch_dependents early and griddepcontrol.wait before
-// touching the previous kernel's outputs, so a kernel's launch and prologue
-// may overlap its predecessor's tail.  Off by default: a GEMM CTA needs
-// nearly a whole SM's shared memory, so it cannot share an SM with the quant
-// CTAs it would overlap, and on the 776-token prefix the attribute measured
-// 3 % slower (2.65 vs 2.57 ms).  Without it the waits are no-ops.
+// Programmatic dependent launch (on by default; W4A4_PDL=0 turns it off):
+// the kernels call griddepcontrol.launch_dependents early and
+// griddepcontrol.wait before they read the previous kernel's outputs or write
+// anything, so a kernel's launch and prologue (barrier set-up, TMEM
+// allocation, descriptor prefetch, the first weight tiles, which no kernel
+// writes) overlap its predecessor's tail.  A dependent grid starts only once
+// every CTA of its predecessor has started, so the early CTAs cannot hold
+// resources a pending predecessor CTA needs.  On the 776-token prefix:
+// 2.28 vs 2.34 ms per prefix.  Without the attribute the waits are no-ops.
 const bool g_pdl = [] {
   const char* e = std::getenv("W4A4_PDL");
-  return e && e[0] == '1';
+  return !(e && e[0] == '0');
 }();
 
 template <typename... KArgs, typename... Args>
