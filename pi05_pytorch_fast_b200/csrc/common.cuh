@@ -386,6 +386,17 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
+// One lane of the (fully active) warp: the lowest, as elect.sync picks it.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 R;\n\t"
+      "elect.sync R|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive once on `bar` when every previously issued tcgen05.mma of this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {

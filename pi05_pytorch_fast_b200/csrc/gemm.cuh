@@ -422,15 +422,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer (lane 0)
+    // ------------------------------------------------ MMA issuer (one elected lane)
     // The issue loop is the kernel's critical path: a 128 x T x 128 step is
-    // 2T tensor cycles (416 at T = 208).  It is unrolled over the whole
-    // shared-memory ring, so every barrier address, B descriptor and A slot
-    // is a compile-time offset or a register; tile switches are handled in
-    // place.  Measured on B200 next to 16 busy warps, this keeps one thread
-    // at ~430 cycles a step, where a loop that advances runtime ring
-    // positions costs ~100 cycles more.
-    if (lane == 0) {
+    // 2T tensor cycles (416 at T = 208), and each tcgen05.mma takes ~85
+    // cycles to issue.  The whole warp runs the loop (warp-uniform control
+    // flow and operands) and one elected lane issues; the loop is unrolled
+    // over the shared-memory ring, so every barrier address, B descriptor and
+    // A slot is a compile-time offset or a register, and the next step's
+    // ready barrier is tested while this step's MMAs issue.
+    {
+      const bool issuer = elect_one();  // the one lane that issues every MMA and commit
       const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
       const uint64_t bstep = static_cast<uint64_t>(tok_bytes >> 4);
       uint64_t bd[RING];
@@ -449,26 +450,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         idesc = idesc_i8(kBlockW, (c.rows + 15) & ~15);
         buf = tcount & 1;
         d_tmem = tmem_base + buf * acc_cols;
-        return tcount < 2 || mbar_wait_bounded(bar_accempty(buf), ((tcount >> 1) - 1) & 1,
-                                               abort_flag, err, kErrWaitAccum, limit);
+        return tcount < 2 || warp_all(mbar_wait_bounded(bar_accempty(buf), ((tcount >> 1) - 1) & 1,
+                                                        abort_flag, err, kErrWaitAccum, limit));
       };
       bool alive = tile < total_tiles && begin_tile();
+      bool pre = false;  // the current step's ready, tested during the previous step's issue
       while (alive) {
 #pragma unroll
         for (int r = 0; r < RING; ++r) {
-          if (!mbar_wait_fast(ready0 + 8u * r, phase, abort_flag, err, kErrWaitUnpack, limit)) {
+          if (!pre && !warp_all(mbar_wait_fast(ready0 + 8u * r, phase, abort_flag, err,
+                                               kErrWaitUnpack, limit))) {
             alive = false;
             break;
           }
           tc_fence_after();
+          const bool pre_l =
+              mbar_test_wait(ready0 + 8u * ((r + 1) % RING), r + 1 == RING ? phase ^ 1u : phase);
           const uint32_t a_slot = a_base + 32u * (sa_full ? r : r % SA_SMALL);
-          umma_i8_ts(d_tmem, a_slot, bd[r], idesc, kt != 0);
-          umma_i8_ts(d_tmem, a_slot + 8, bd[r] + 2, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot + 16, bd[r] + 4, idesc, 1u);
-          umma_i8_ts(d_tmem, a_slot + 24, bd[r] + 6, idesc, 1u);
-          umma_commit(empty0 + 8u * r);
+          if (issuer) {
+            umma_i8_ts(d_tmem, a_slot, bd[r], idesc, kt != 0);
+            umma_i8_ts(d_tmem, a_slot + 8, bd[r] + 2, idesc, 1u);
+            umma_i8_ts(d_tmem, a_slot + 16, bd[r] + 4, idesc, 1u);
+            umma_i8_ts(d_tmem, a_slot + 24, bd[r] + 6, idesc, 1u);
+            umma_commit(empty0 + 8u * r);
+          }
+          pre = __all_sync(0xffffffffu, pre_l);
           if (++kt == p.k_tiles) {
-            umma_commit(bar_accfull(buf));
+            if (issuer) umma_commit(bar_accfull(buf));
             kt = 0;
             tile += ustride;
             ++tcount;
@@ -481,7 +489,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         phase ^= 1u;
       }
       // Every MMA of this CTA has completed once this commit arrives.
-      umma_commit(bar_drain);
+      if (issuer) umma_commit(bar_drain);
+      __syncwarp();
       volatile int no_abort = 0;
       mbar_wait_bounded(bar_drain, 0, &no_abort, err, kErrWaitDrain, limit);
     }

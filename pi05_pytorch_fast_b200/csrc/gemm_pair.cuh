@@ -28,15 +28,10 @@ namespace w4a4 {
 
 constexpr int kPairTmemCols = 512;
 
-// Ring depth / shared memory of the pair kernel for a token tile of
-// `tok_tile` rows (each CTA holds tok_tile / 2 of them per stage).
-__host__ __device__ constexpr int gemm_pair_stages(int tok_tile) {
-  return (kSmemLimit - kFixedSmem) / (tok_tile / 2 * kBlockK + kWpkBytes) < kMaxStages
-             ? (kSmemLimit - kFixedSmem) / (tok_tile / 2 * kBlockK + kWpkBytes)
-             : kMaxStages;
-}
+// Shared memory of the pair kernel for a token tile of `tok_tile` rows: a
+// kGemmRing-stage ring, each CTA holding tok_tile / 2 token rows per stage.
 __host__ __device__ constexpr int gemm_pair_smem_bytes(int tok_tile) {
-  return gemm_pair_stages(tok_tile) * (tok_tile / 2 * kBlockK + kWpkBytes) + kFixedSmem;
+  return kGemmRing * (tok_tile / 2 * kBlockK + kWpkBytes) + kFixedSmem;
 }
 
 __device__ __forceinline__ TileCoord decode_pair_tile(const GemmParams& p, int tile, int rank) {
@@ -95,10 +90,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int acc_cols = p.tok_tile;
   const int a_col0 = 2 * acc_cols;
 
-  // Both rings are walked in pairs of steps (see the single-CTA kernel): a
-  // launch whose ring depths or step count break that touches nothing.
-  if ((S & 1) || S < 2 || S > kMaxStages || (SA & 1) || SA < 2 || SA > kMaxAStages ||
-      2 * p.tok_tile + 32 * SA > kPairTmemCols || (p.k_tiles & 1) || p.k_tiles < 2) {
+  // The issue loop is unrolled over the compile-time ring (kGemmRing slots, SA
+  // a divisor of it), as in the single-CTA kernel: a launch that breaks this
+  // touches nothing and reports it.
+  constexpr int RING = kGemmRing;
+  constexpr int SA_SMALL = 3;
+  if (S != RING || (SA != SA_SMALL && SA != RING) || 2 * p.tok_tile + 32 * SA > kPairTmemCols ||
+      p.k_tiles < 1 || (p.tok_tile & 15)) {
     if (threadIdx.x == 0) atomicOr(&g_w4a4_device_error, kErrBadParams);
     return;
   }
@@ -177,72 +175,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (leader lane 0)
-    // Pair-unrolled like the single-CTA issuer; each instruction spans both
-    // SMs (M = 256), and every commit is multicast to both CTAs.
+    // Unrolled over the compile-time ring like the single-CTA issuer; each
+    // instruction spans both SMs (M = 256), so one thread issues a step for
+    // two SMs, and every commit is multicast to both CTAs.  With T = 208 the
+    // TMEM holds 3 A slots: the unpack of step i waits for MMA(i - 3), which
+    // leaves two steps of MMA time to hide the unpack -> ready -> issue loop.
     if (lane == 0 && leader) {
       const uint64_t bdesc0 = smem_desc_sw128(smem_addr(tok_ring));
       const uint64_t bstep = static_cast<uint64_t>(tok_bytes >> 4);
+      uint64_t bd[RING];
+#pragma unroll
+      for (int r = 0; r < RING; ++r) bd[r] = bdesc0 + r * bstep;
       const uint32_t a_base = tmem_base + a_col0;
+      const bool sa_full = SA == RING;
       const uint32_t ready0 = bar_ready(0), empty0 = bar_empty(0);
       // The pair splits B by N across the two CTAs' shared memory, so the
       // MMA's N is the width the token halves were loaded for: the full tile.
       const uint32_t idesc = idesc_i8(2 * kBlockW, p.tok_tile);
-      int sidx = 0, aidx = 0;
-      uint32_t sphase = 0;
-      uint64_t bdesc = bdesc0;
-      uint32_t a_slot0 = a_base;
-      int tcount = 0;
-      bool alive = true;
-      for (int tile = cluster; alive && tile < total_tiles; tile += n_clusters, ++tcount) {
-        const int buf = tcount & 1;
-        if (tcount >= 2 &&
-            !mbar_wait_bounded_cl(bar_accempty(buf), ((tcount >> 1) - 1) & 1, abort_flag, err,
-                                  kErrWaitAccum, limit))
-          break;
-        const uint32_t d_tmem = tmem_base + buf * acc_cols;
-        for (int kt = 0; kt < p.k_tiles; kt += 2) {
-          const uint32_t rbar = ready0 + 8u * sidx, ebar = empty0 + 8u * sidx;
-          if (!mbar_try_wait_cl(rbar, sphase) &&
-              !mbar_wait_bounded_cl(rbar, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
+      uint32_t phase = 0;
+      int tile = cluster, tcount = 0, kt = 0, buf = 0;
+      uint32_t d_tmem = tmem_base;
+      // Starts tile `tile` (the tcount-th of this pair): its accumulator
+      // buffer must have been drained by both epilogues two tiles ago.
+      const auto begin_tile = [&]() -> bool {
+        buf = tcount & 1;
+        d_tmem = tmem_base + buf * acc_cols;
+        return tcount < 2 || mbar_wait_bounded_cl(bar_accempty(buf), ((tcount >> 1) - 1) & 1,
+                                                  abort_flag, err, kErrWaitAccum, limit);
+      };
+      bool alive = tile < total_tiles && begin_tile();
+      while (alive) {
+#pragma unroll
+        for (int r = 0; r < RING; ++r) {
+          const uint32_t rbar = ready0 + 8u * r;
+          if (!mbar_try_wait_cl(rbar, phase) &&
+              !mbar_wait_bounded_cl(rbar, phase, abort_flag, err, kErrWaitUnpack, limit)) {
             alive = false;
             break;
           }
           tc_fence_after();
-          umma_i8_ts_pair(d_tmem, a_slot0, bdesc, idesc, kt != 0);
-          umma_i8_ts_pair(d_tmem, a_slot0 + 8, bdesc + 2, idesc, 1u);
-          umma_i8_ts_pair(d_tmem, a_slot0 + 16, bdesc + 4, idesc, 1u);
-          umma_i8_ts_pair(d_tmem, a_slot0 + 24, bdesc + 6, idesc, 1u);
-          umma_commit_pair_mc(ebar, 0x3);
-          if (!mbar_try_wait_cl(rbar + 8, sphase) &&
-              !mbar_wait_bounded_cl(rbar + 8, sphase, abort_flag, err, kErrWaitUnpack, limit)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t bdesc1 = bdesc + bstep;
-          umma_i8_ts_pair(d_tmem, a_slot0 + 32, bdesc1, idesc, 1u);
-          umma_i8_ts_pair(d_tmem, a_slot0 + 40, bdesc1 + 2, idesc, 1u);
-          umma_i8_ts_pair(d_tmem, a_slot0 + 48, bdesc1 + 4, idesc, 1u);
-          umma_i8_ts_pair(d_tmem, a_slot0 + 56, bdesc1 + 6, idesc, 1u);
-          umma_commit_pair_mc(ebar + 8, 0x3);
-          sidx += 2;
-          if (sidx == S) {
-            sidx = 0;
-            sphase ^= 1u;
-            bdesc = bdesc0;
-          } else {
-            bdesc = bdesc1 + bstep;
-          }
-          aidx += 2;
-          if (aidx == SA) {
-            aidx = 0;
-            a_slot0 = a_base;
-          } else {
-            a_slot0 += 64;
+          const uint32_t a_slot = a_base + 32u * (sa_full ? r : r % SA_SMALL);
+          umma_i8_ts_pair(d_tmem, a_slot, bd[r], idesc, kt != 0);
+          umma_i8_ts_pair(d_tmem, a_slot + 8, bd[r] + 2, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot + 16, bd[r] + 4, idesc, 1u);
+          umma_i8_ts_pair(d_tmem, a_slot + 24, bd[r] + 6, idesc, 1u);
+          umma_commit_pair_mc(empty0 + 8u * r, 0x3);
+          if (++kt == p.k_tiles) {
+            umma_commit_pair_mc(bar_accfull(buf), 0x3);
+            kt = 0;
+            tile += n_clusters;
+            ++tcount;
+            if (tile >= total_tiles || !begin_tile()) {
+              alive = false;
+              break;
+            }
           }
         }
-        if (!alive) break;
-        umma_commit_pair_mc(bar_accfull(buf), 0x3);
+        phase ^= 1u;
       }
       umma_commit_pair_mc(bar_drain, 0x3);
     }

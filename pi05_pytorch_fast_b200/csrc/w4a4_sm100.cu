@@ -524,16 +524,13 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   p.k = k;
   p.tok_tile = tok_tile;
   p.n_seg = n_weights;
-  // The single-CTA kernel's issue loop is unrolled over a compile-time ring
-  // (kGemmRing stages, 3 or 6 TMEM A slots; split-K: the same, each CTA of
-  // a cluster half the K steps).  The CTA-pair
-  // kernel issues in pairs of K steps from even rings; an odd step count gets
-  // one more step whose TMA boxes lie past K: they read as zeros and add
-  // nothing.
+  // Every kernel's issue loop is unrolled over a compile-time ring (kGemmRing
+  // stages, 3 or 6 TMEM A slots); split-K: the same, each CTA of a cluster
+  // half the K steps.
   if (pair) {
-    p.k_tiles = 2 * ((k + 2 * kBlockK - 1) / (2 * kBlockK));
-    p.stages = gemm_pair_stages(tok_tile) & ~1;
-    p.a_stages = gemm_a_stages(tok_tile) & ~1;
+    p.k_tiles = k_steps;
+    p.stages = kGemmRing;
+    p.a_stages = gemm_ring_a_stages(tok_tile);
   } else if (split) {
     p.k_tiles = k_steps / 2;
     p.stages = kGemmRing;
@@ -547,9 +544,6 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   p.w_tiles = w_tiles;
   const int64_t total_tiles = static_cast<int64_t>(p.n_tok_tiles) * w_tiles;
   if (total_tiles > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "too many tiles");
-  if (pair && (p.stages < 2 || (p.stages & 1) || (p.k_tiles & 1) || p.a_stages < 2))
-    return fail(W4A4_ERR_INVALID, "internal: GEMM ring depth %d / step count %d must be even", p.stages,
-                p.k_tiles);
   const dim3 grid(pair || split ? 2u * static_cast<unsigned>(std::min<int64_t>(total_tiles, sms / 2))
                                 : static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
 #define W4A4_LAUNCH_GEMM(L, ACC, BIT)                                                          \
