@@ -332,13 +332,7 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
           err_code = e;
           return;
         }
-        int sms = 0;
-        if (int e = sm_count(dev, &sms)) {
-          err_code = e;
-          return;
-        }
-        const unsigned pgrid = static_cast<unsigned>(std::min<int64_t>(m, int64_t(kQ16CtasPerSm) * sms));
-        err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE>, dim3(pgrid),
+        err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE>, dim3(grid),
                                              dim3(kQuantThreads), kQ16Smem, stream, 1, xmap, m, codes,
                                              row_scale, isk, g_wait_limit_ns.load()));
       } else
