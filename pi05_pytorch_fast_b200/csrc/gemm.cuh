@@ -593,7 +593,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t xarea = smem_addr(tok_ring) + ew * xstride;
         const uint32_t peer = rank ^ 1u;
         // our MMAs are done: our ring is free for the partner's sums
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_xready, peer));
+        if (lane == 0) mbar_arrive_remote(mapa_shared(bar_xready, peer));
         const bool free = warp_all(mbar_wait_bounded_cl(bar_xready, 0, abort_flag, err,
                                                         kErrWaitAccum, limit));
         const uint32_t dst0 = mapa_shared(xarea, peer) + lane * 64;

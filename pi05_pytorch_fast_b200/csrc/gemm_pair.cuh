@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) {
             if (leader) mbar_arrive(bar_ready(st.idx));
-            else mbar_arrive_cluster(mapa_shared(bar_ready(st.idx), 0));
+            else mbar_arrive_remote(mapa_shared(bar_ready(st.idx), 0));
           }
         }
         ++step;
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              tmem_base + lane_addr + buf * acc_cols, half, lane, stage, ts, [&] {
                                tc_fence_before();
                                __syncwarp();
-                               if (lane == 0) mbar_arrive_cluster(accempty);
+                               if (lane == 0) mbar_arrive_remote(accempty);
                              });
     }
   }
