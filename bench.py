@@ -359,6 +359,23 @@ def run_ours(args, rank, world, local_rank, dist_on):
             ext.quantize(x_static, fmt="gemm")
     ms_q2 = time_device(gq2.replay, args.roofline_reps, 3, dist_on, device) / 10
     q2_bytes = 2 * m * HIDDEN + m * HIDDEN + 4 * m
+    # the other GEMMs of a layer, each cycled over the layers' weights
+    codes16, scales16 = ext.quantize(h16, fmt="gemm")
+    other = {
+        "gemm_qkv": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]]),
+                     2.0 * m * (N_Q + 2 * N_KV) * HIDDEN),
+        "gemm_o": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["o"]]), 2.0 * m * HIDDEN * HIDDEN),
+        "gemm_down": (lambda lw: ext.gemm_from_codes(codes16, scales16, [lw["down"]]),
+                      2.0 * m * HIDDEN * INTER),
+    }
+    gemm_ms = {}
+    for name, (fn, _) in other.items():
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg):
+            for lw in layers:
+                fn(lw)
+        gemm_ms[name] = time_device(gg.replay, args.roofline_reps, 3, dist_on, device) / len(layers)
+        del gg
     del graph, ga, gq, gq2
     torch.cuda.synchronize(device)
 
@@ -417,6 +434,10 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "algorithmic_ops_per_launch": gu_ops,
         },
         "kernels": {
+            "gemm_gateup": {"ms": ms_gu, "tops": gu_tops, "frac": gu_tops / int8_peak},
+            **{name: {"ms": gemm_ms[name], "tops": ops / (gemm_ms[name] * 1e-3) / 1e12,
+                      "frac": ops / (gemm_ms[name] * 1e-3) / 1e12 / int8_peak}
+               for name, (_, ops) in other.items()},
             "quant_k16384": {"ms": ms_q, "gbs": q_bytes / (ms_q * 1e-3) / 1e9,
                              "peak_gbs": peaks["hbm_gbs"],
                              "frac": q_bytes / (ms_q * 1e-3) / 1e9 / peaks["hbm_gbs"],
