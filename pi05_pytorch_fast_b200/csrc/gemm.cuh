@@ -124,6 +124,7 @@ struct alignas(64) GemmParams {
   int a_stages;             // TMEM A ring depth (gemm_a_stages)
   int n_tok_tiles;
   int w_tiles;
+  int tok_group;            // token tiles per rasterisation group (decode_tile)
   int n_seg;
   int k_tiles;
 };
@@ -135,9 +136,19 @@ struct TileCoord {
   int rows;
 };
 
+// Tile order: token tiles in groups of p.tok_group; within a group the weight
+// tile changes every g tiles (g = the group's size), so the CTAs running at
+// one time share a few weight tiles and the group's token tiles.  With one
+// group (the activation codes fit in L2) each weight tile streams from HBM
+// once; with several (large M) each group's codes stay in L2 while the
+// weights stream once per group.
 __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) {
-  const int wt = tile / p.n_tok_tiles;
-  const int tt = tile - wt * p.n_tok_tiles;
+  const int per_group = p.tok_group * p.w_tiles;
+  const int group = tile / per_group;
+  const int r = tile - group * per_group;
+  const int g = min(p.tok_group, p.n_tok_tiles - group * p.tok_group);
+  const int wt = r / g;
+  const int tt = group * p.tok_group + (r - wt * g);
   TileCoord c;
   c.seg = 0;
 #pragma unroll

@@ -536,6 +536,14 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   }
   p.n_tok_tiles = static_cast<int>((m + tok_tile - 1) / tok_tile);
   p.w_tiles = w_tiles;
+  // Rasterisation: keep each group's activation codes (tok_group token tiles
+  // x K bytes) within ~48 MB of the 126 MB L2, so the codes are read from HBM
+  // once and the weights once per group.  Prefix-sized M is one group.
+  {
+    const int64_t tile_code_bytes = static_cast<int64_t>(tok_tile) * k;
+    const int64_t g = std::max<int64_t>(1, (48ll << 20) / std::max<int64_t>(1, tile_code_bytes));
+    p.tok_group = static_cast<int>(std::min<int64_t>(g, p.n_tok_tiles));
+  }
   const int64_t total_tiles = static_cast<int64_t>(p.n_tok_tiles) * w_tiles;
   if (total_tiles > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "too many tiles");
   const dim3 grid(pair || split ? 2u * static_cast<unsigned>(std::min<int64_t>(total_tiles, sms / 2))

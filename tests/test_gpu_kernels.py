@@ -97,8 +97,7 @@ def test_quant_codes_and_scales_bit_exact(k, m, staging):
 @pytest.mark.parametrize("k,m,pad", [(2048, 5, 8), (16384, 450, 64), (16384, 2, 8)])
 def test_quant_strided_rows_bit_exact(k, m, pad, staging):
     """Rows of x at a stride of k + pad elements (w4a4_quant's ldx): only the
-    first k of each row are read.  450 rows at K = 16384 give some CTAs of the
-    persistent kernel two rows."""
+    first k of each row are read (through the 3-D TMA map at K = 16384)."""
     x = orc.make_activations(m, k, seed=7 * k + m)
     ref_codes, ref_scale = orc.quant_activation(x, staging=staging)
     wide = np.full((m, k + pad), np.float16(1000.0))  # the pad would change amax if it were read
@@ -194,6 +193,21 @@ def test_gemm_accumulators_bit_exact(m, k, ns, layout, variant):
     frag = layout == "fragment"
     ws = [to_dev(orc.preshuffle_wmma_weight(p, k)) if frag else _row_major(p) for p in packs]
     accs = gemm_accumulators(to_dev(gemm_order(qa)), ws, fragment_major=frag)
+    for p, acc in zip(packs, accs):
+        qw, _ = orc.weight_codes_scales(p, k, "row")
+        np.testing.assert_array_equal(to_np(acc), orc.int_accumulate(qa, qw))
+
+
+@pytest.mark.parametrize("m,k,ns", [(4000, 16384, [384]), (25000, 2048, [640])])
+def test_gemm_grouped_rasterisation_bit_exact(m, k, ns, variant):
+    """Activation codes larger than ~48 MB are tiled in groups of token tiles
+    (each group's codes stay in L2): 4000 x 16384 gives two groups of 208-row
+    tiles (a split-K candidate), 25000 x 2048 two groups of 118 and 3 tiles."""
+    rng = np.random.default_rng(m + k)
+    qa = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
+    packs = [orc.random_packed_weight(n, k, seed=i + 5) for i, n in enumerate(ns)]
+    ws = [_row_major(p) for p in packs]
+    accs = gemm_accumulators(to_dev(gemm_order(qa)), ws, fragment_major=False)
     for p, acc in zip(packs, accs):
         qw, _ = orc.weight_codes_scales(p, k, "row")
         np.testing.assert_array_equal(to_np(acc), orc.int_accumulate(qa, qw))
