@@ -277,33 +277,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
-// Prefetch a 2-D tile into L2 (no shared-memory destination, no completion).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tmap)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
-// Read-only global loads that bypass L1 allocation (streamed weights).
-__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
-  uint2 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-               : "=r"(r.x), "=r"(r.y)
-               : "l"(p));
-  return r;
-}
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
 // 2-D tile load for a CTA pair (tcgen05 cta_group::2): the data lands in this
 // CTA's shared memory, the transaction bytes are counted on the mbarrier at
 // the same offset in the pair's even (leader) CTA.

@@ -48,7 +48,6 @@ constexpr int kBlockW = 128;      // weight rows per tile (UMMA M)
 constexpr int kBlockK = 128;      // K elements per pipeline step
 constexpr int kTokTileMax = 208;  // max tokens per tile (UMMA N)
 constexpr int kMaxStages = 12;    // shared-memory ring (tokens + packed weights)
-constexpr int kMaxAStages = 8;    // TMEM ring of unpacked weights
 constexpr int kGemmRing = 6;      // single-CTA kernel: shared-memory ring depth (compile time)
 constexpr int kTmemCols = 512;
 constexpr int kUnpackGroups = 2;
@@ -71,12 +70,6 @@ constexpr int kFixedSmem =
 constexpr int kSmemLimit = 232448;
 static_assert(2 * kTokTileMax + 3 * 32 <= kTmemCols, "TMEM budget");
 
-// Ring depth for a token tile of `tok_tile` rows.
-__host__ __device__ constexpr int gemm_stages(int tok_tile) {
-  return (kSmemLimit - kFixedSmem) / (tok_tile * kBlockK + kWpkBytes) < kMaxStages
-             ? (kSmemLimit - kFixedSmem) / (tok_tile * kBlockK + kWpkBytes)
-             : kMaxStages;
-}
 __host__ __device__ constexpr int gemm_smem_bytes(int tok_tile) {
   return kGemmRing * (tok_tile * kBlockK + kWpkBytes) + kFixedSmem;
 }
@@ -89,16 +82,12 @@ __host__ __device__ constexpr int gemm_ring_a_stages(int tok_tile) {
 static_assert(kGemmRing * (kTokTileMax * kBlockK + kWpkBytes) + kFixedSmem <= kSmemLimit,
               "the single-CTA ring must fit the widest tile");
 static_assert(2 * kTokTileMax + 3 * 32 <= kTmemCols, "three A slots must fit beside the widest tile");
-// Split-K: rank 1 pushes its whole partial accumulator into rank 0's idle
-// ring (token and weight rings are contiguous): each epilogue warp's
-// ceil(T / 32) chunks of 2 KB, 8 T / 32 * 2 KB <= 512 T bytes in all, which
-// always fits in the ring's kGemmRing * (128 T + 8 KB) bytes.
+// Split-K: each rank pushes partial sums into the partner's idle ring (token
+// and weight rings are contiguous), at most each epilogue warp's ceil(T / 32)
+// chunks of 2 KB, 8 T / 32 * 2 KB <= 512 T bytes in all, which always fits in
+// the ring's kGemmRing * (128 T + 8 KB) bytes.
 static_assert(kEpiWarps * 2 * kXchgChunkBytes <= kGemmRing * (16 * kBlockK + kWpkBytes),
               "the split-K exchange must fit the ring of the narrowest tile");
-__host__ __device__ constexpr int gemm_a_stages(int tok_tile) {
-  return (kTmemCols - 2 * tok_tile) / 32 < kMaxAStages ? (kTmemCols - 2 * tok_tile) / 32
-                                                       : kMaxAStages;
-}
 
 enum WeightLayout : int { kRowMajor = 0, kFragmentMajor = 1 };
 
@@ -120,8 +109,8 @@ struct alignas(64) GemmParams {
   long long m;
   int k;
   int tok_tile;
-  int stages;               // shared-memory ring depth (gemm_stages)
-  int a_stages;             // TMEM A ring depth (gemm_a_stages)
+  int stages;               // shared-memory ring depth (kGemmRing)
+  int a_stages;             // TMEM A ring depth (gemm_ring_a_stages)
   int n_tok_tiles;
   int w_tiles;
   int tok_group;            // token tiles per rasterisation group (decode_tile)
