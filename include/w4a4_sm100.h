@@ -157,6 +157,14 @@ int w4a4_set_wait_limit_ns(uint64_t limit_ns);
  * counterpart in the reference, which has one kernel per op. */
 int w4a4_set_gemm_variant(int32_t variant);
 
+/* Test hook (host only, no GPU needed): the launch shape w4a4_gemm would use
+ * for m tokens, K = k and n_weights weights of n[i] rows on `sms` SMs with
+ * GEMM variant `variant`.  out[6] receives the token tile, split-K (0/1), the
+ * grid size, the number of token tiles, the token tiles per rasterisation
+ * group and the number of weight tiles.  No counterpart in the reference. */
+int w4a4_gemm_plan(int64_t m, int32_t k, int32_t n_weights, const int32_t* n, int32_t sms,
+                   int32_t variant, int32_t* out);
+
 /* Test hook: launches one CTA that waits on a barrier nobody arrives at, with
  * the given limit; the kernel must give up, set its error bit and return. */
 int w4a4_selftest_wait_timeout(uint64_t limit_ns, void* stream);

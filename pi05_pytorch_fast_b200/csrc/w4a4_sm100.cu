@@ -415,6 +415,39 @@ int choose_tok_tile(int64_t m, int w_tiles, int sms) {
   return best_tile;
 }
 
+// Everything about a GEMM launch's shape that follows from (M, weight tiles,
+// K, SM count, variant): the token tile, split-K, rasterisation group and
+// grid.  Shared by launch_gemm and the w4a4_gemm_plan test hook.
+struct LaunchShape {
+  int tok_tile;
+  bool split;
+  int n_tok_tiles;
+  int tok_group;
+  int64_t total_tiles;
+  unsigned grid;
+};
+
+LaunchShape launch_shape(int64_t m, int w_tiles, int32_t k, int sms, bool pair, int variant) {
+  LaunchShape ls{};
+  const int workers = pair ? sms / 2 : sms;
+  const int k_steps = (k + kBlockK - 1) / kBlockK;
+  const GemmPlan plan = pair ? GemmPlan{choose_tok_tile(m, w_tiles, workers), false}
+                             : choose_plan(m, w_tiles, k_steps, sms, variant);
+  ls.tok_tile = plan.tok_tile;
+  ls.split = plan.split;
+  ls.n_tok_tiles = static_cast<int>((m + ls.tok_tile - 1) / ls.tok_tile);
+  // Rasterisation: keep each group's activation codes (tok_group token tiles
+  // x K bytes) within ~48 MB of the 126 MB L2, so the codes are read from HBM
+  // once and the weights once per group.  Prefix-sized M is one group.
+  const int64_t tile_code_bytes = static_cast<int64_t>(ls.tok_tile) * k;
+  const int64_t g = std::max<int64_t>(1, (48ll << 20) / std::max<int64_t>(1, tile_code_bytes));
+  ls.tok_group = static_cast<int>(std::min<int64_t>(g, ls.n_tok_tiles));
+  ls.total_tiles = static_cast<int64_t>(ls.n_tok_tiles) * w_tiles;
+  ls.grid = pair || ls.split ? 2u * static_cast<unsigned>(std::min<int64_t>(ls.total_tiles, sms / 2))
+                             : static_cast<unsigned>(std::min<int64_t>(ls.total_tiles, sms));
+  return ls;
+}
+
 int check_weight(const w4a4_weight& w, int32_t k, int idx) {
   if (!w.data) return fail(W4A4_ERR_INVALID, "packed W %d: null data pointer", idx);
   if (w.n <= 0) return fail(W4A4_ERR_INVALID, "packed W %d: N must be positive, got %d", idx, w.n);
@@ -503,12 +536,10 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     s.vec_store = (!acc_out && w.n % 8 == 0 && aligned(y[i], 16)) ? 1 : 0;
     w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
-  const int workers = pair ? sms / 2 : sms;
   const int k_steps = (k + kBlockK - 1) / kBlockK;
-  const GemmPlan plan = pair ? GemmPlan{choose_tok_tile(m, w_tiles, workers), false}
-                             : choose_plan(m, w_tiles, k_steps, sms, g_gemm_variant.load());
-  const int tok_tile = plan.tok_tile;
-  const bool split = plan.split;
+  const LaunchShape ls = launch_shape(m, w_tiles, k, sms, pair, g_gemm_variant.load());
+  const int tok_tile = ls.tok_tile;
+  const bool split = ls.split;
   if (int e = make_map_2d(&p.tmap_tok, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, m, k, kBlockK,
                           pair ? tok_tile / 2 : tok_tile, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
@@ -534,20 +565,11 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     p.stages = kGemmRing;
     p.a_stages = gemm_ring_a_stages(tok_tile);
   }
-  p.n_tok_tiles = static_cast<int>((m + tok_tile - 1) / tok_tile);
+  p.n_tok_tiles = ls.n_tok_tiles;
   p.w_tiles = w_tiles;
-  // Rasterisation: keep each group's activation codes (tok_group token tiles
-  // x K bytes) within ~48 MB of the 126 MB L2, so the codes are read from HBM
-  // once and the weights once per group.  Prefix-sized M is one group.
-  {
-    const int64_t tile_code_bytes = static_cast<int64_t>(tok_tile) * k;
-    const int64_t g = std::max<int64_t>(1, (48ll << 20) / std::max<int64_t>(1, tile_code_bytes));
-    p.tok_group = static_cast<int>(std::min<int64_t>(g, p.n_tok_tiles));
-  }
-  const int64_t total_tiles = static_cast<int64_t>(p.n_tok_tiles) * w_tiles;
-  if (total_tiles > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "too many tiles");
-  const dim3 grid(pair || split ? 2u * static_cast<unsigned>(std::min<int64_t>(total_tiles, sms / 2))
-                                : static_cast<unsigned>(std::min<int64_t>(total_tiles, sms)));
+  p.tok_group = ls.tok_group;
+  if (ls.total_tiles > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "too many tiles");
+  const dim3 grid(ls.grid);
 #define W4A4_LAUNCH_GEMM(L, ACC, BIT)                                                          \
   do {                                                                                        \
     if (pair) {                                                                               \
@@ -704,6 +726,31 @@ int w4a4_device_error(uint32_t* bits, int32_t clear) {
     const unsigned zero = 0;
     W4A4_CUDA_TRY(cudaMemcpyToSymbol(g_w4a4_device_error, &zero, sizeof(zero)));
   }
+  return ok();
+}
+
+int w4a4_gemm_plan(int64_t m, int32_t k, int32_t n_weights, const int32_t* n, int32_t sms,
+                   int32_t variant, int32_t* out) {
+  if (m <= 0 || k <= 0 || k % 64 != 0 || sms < 2 || !n || !out)
+    return fail(W4A4_ERR_INVALID, "invalid plan query");
+  if (n_weights < 1 || n_weights > kMaxSegments)
+    return fail(W4A4_ERR_INVALID, "n_weights must be 1..%d, got %d", kMaxSegments, n_weights);
+  if (variant < W4A4_GEMM_SINGLE_CTA || variant > W4A4_GEMM_SPLIT_K)
+    return fail(W4A4_ERR_INVALID, "unknown GEMM variant %d", variant);
+  const bool pair = variant == W4A4_GEMM_CTA_PAIR;
+  const int rows_per_wtile = pair ? 2 * kBlockW : kBlockW;
+  int w_tiles = 0;
+  for (int i = 0; i < n_weights; ++i) {
+    if (n[i] <= 0) return fail(W4A4_ERR_INVALID, "N must be positive");
+    w_tiles += (n[i] + rows_per_wtile - 1) / rows_per_wtile;
+  }
+  const LaunchShape ls = launch_shape(m, w_tiles, k, sms, pair, variant);
+  out[0] = ls.tok_tile;
+  out[1] = ls.split ? 1 : 0;
+  out[2] = static_cast<int32_t>(ls.grid);
+  out[3] = ls.n_tok_tiles;
+  out[4] = ls.tok_group;
+  out[5] = w_tiles;
   return ok();
 }
 

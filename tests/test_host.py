@@ -78,6 +78,60 @@ def test_gemm_variant_selection_validated():
     assert lib.w4a4_set_gemm_variant(nat.GEMM_SINGLE_CTA) == nat.W4A4_OK
 
 
+# The launch plans of the prefix's GEMMs at M = 776 on 148 SMs (as the ncu
+# launch list shows them): q/k/v, o, gate/up, down.
+PREFIX_PLANS = [
+    ("qkv", 776, 2048, [2048, 256, 256], dict(tok_tile=112, split=False, grid=140, tok_group=7)),
+    ("o", 776, 2048, [2048], dict(tok_tile=96, split=False, grid=144, tok_group=9)),
+    ("gate/up", 776, 2048, [16384, 16384], dict(tok_tile=208, split=False, grid=148, tok_group=4)),
+    ("down", 776, 16384, [2048], dict(tok_tile=208, split=True, grid=128, tok_group=4)),
+]
+
+
+@pytest.mark.parametrize("name,m,k,ns,want", PREFIX_PLANS)
+def test_prefix_gemm_plans(name, m, k, ns, want):
+    plan = nat.gemm_plan(m, k, ns)
+    assert {key: plan[key] for key in want} == want, (name, plan)
+
+
+@pytest.mark.parametrize("m", [1, 15, 16, 17, 208, 209, 640, 768, 776, 6208, 24832])
+@pytest.mark.parametrize("k,ns", [(2048, [2048, 256, 256]), (2048, [16384, 16384]),
+                                  (16384, [2048]), (1024, [384, 128]), (64, [24])])
+@pytest.mark.parametrize("variant", [nat.GEMM_SINGLE_CTA, nat.GEMM_CTA_PAIR, nat.GEMM_NO_SPLIT,
+                                     nat.GEMM_SPLIT_K])
+def test_gemm_plan_invariants(m, k, ns, variant):
+    """Whatever the shape, the plan covers every token with at most 208-token
+    MMA tiles, launches no more CTAs than SMs (pairs and split-K clusters: an
+    even grid, one tile per cluster for split-K), splits K only into two even
+    halves, and groups token tiles so one group's codes stay within ~48 MB."""
+    sms = 148
+    plan = nat.gemm_plan(m, k, ns, sms=sms, variant=variant)
+    t = plan["tok_tile"]
+    assert t % 16 == 0 and 16 <= t <= 208
+    assert plan["tok_tiles"] == -(-m // t)
+    total = plan["tok_tiles"] * plan["w_tiles"]
+    assert 1 <= plan["grid"] <= sms
+    k_steps = -(-k // 128)
+    if plan["split"]:
+        assert variant != nat.GEMM_NO_SPLIT and variant != nat.GEMM_CTA_PAIR
+        assert k_steps % 2 == 0 and plan["grid"] == 2 * total <= sms
+    elif variant == nat.GEMM_SPLIT_K:
+        assert k_steps % 2 == 1 or k_steps < 2 or total > sms // 2  # could not split
+    if variant == nat.GEMM_CTA_PAIR:
+        assert plan["grid"] % 2 == 0
+    g = plan["tok_group"]
+    assert 1 <= g <= plan["tok_tiles"]
+    assert g == plan["tok_tiles"] or g * t * k <= 48 << 20
+
+
+def test_gemm_plan_rejects_bad_queries():
+    for args in ((0, 2048, [64]), (4, 100, [64]), (4, 2048, [0]), (4, 2048, [64, 64, 64, 64])):
+        with pytest.raises(nat.W4A4Error):
+            nat.gemm_plan(*args)
+    with pytest.raises(nat.W4A4Error, match="unknown GEMM variant"):
+        nat.gemm_plan(4, 2048, [64], variant=9)
+
+
 def test_ops_refuse_cpu_tensors():
     from pi05_pytorch_fast_b200.w4a4 import extension as ext
 
