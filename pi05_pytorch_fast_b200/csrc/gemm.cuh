@@ -24,11 +24,11 @@
 //    straight into TMEM, where the MMA reads its A operand.  The unpacked
 //    weights never touch shared memory, which leaves the shared-memory
 //    bandwidth to the TMA writes and the MMA's reads of the token operand.
-//  * one thread of warp 1 issues tcgen05.mma (A from TMEM, B = tokens from
+//  * warp 1 runs the MMA loop (warp-uniform control flow and operands) and
+//    one elected lane issues tcgen05.mma (A from TMEM, B = tokens from
 //    shared memory) into one of two TMEM accumulators (double buffered, so
 //    the epilogue of a tile overlaps the mainloop of the next) and frees each
-//    step with ONE tcgen05.commit: the issuing thread has ~400 cycles of MMA
-//    time per step to spend, so its loop carries no warp syncs or divisions.
+//    step with ONE tcgen05.commit.
 //  * warps 10-17 (epilogue, two per TMEM lane quarter taking alternate
 //    16-column chunks) read the accumulator with tcgen05.ld, divide by 16
 //    (exact), apply the token and weight scales in fp32, round to fp16 and
