@@ -115,6 +115,9 @@ def _ops_exist() -> bool:
 
 # The op library; kept alive for the life of the process.
 _library = None
+# Raising stubs, registered while the C++ op library is not built; dropped
+# before that library registers the real bodies.
+_stub_library = None
 _ops_loaded = False
 
 # name, schema arguments / returns, fake implementation
@@ -145,8 +148,11 @@ def _load_ops() -> bool:
     """Loads the C++ op bodies (csrc/torch_ops.cpp, registered under
     CompositeExplicitAutograd) if the library is built; they replace the
     not-built stubs."""
-    global _ops_loaded
+    global _ops_loaded, _stub_library
     if not _ops_loaded and os.path.isfile(OPS_LIB_PATH):
+        if _stub_library is not None:
+            _stub_library._destroy()
+            _stub_library = None
         torch.ops.load_library(OPS_LIB_PATH)
         _ops_loaded = True
     return _ops_loaded
@@ -159,7 +165,7 @@ def _register_custom_op() -> None:
     bodies are C++ (_w4a4_ops.so): checks, output allocation and the call
     into libw4a4_sm100.so cost about 2 us of host time per op.  Without that
     library every op raises."""
-    global _op_registered, _library
+    global _op_registered, _library, _stub_library
     if _op_registered:
         return
     if _ops_exist():
@@ -174,8 +180,9 @@ def _register_custom_op() -> None:
     _library = lib
     _op_registered = True
     if not _load_ops():
+        _stub_library = torch.library.Library("pi05_w4a4", "IMPL")
         for name, _, _ in _OPS:
-            lib.impl(name, _not_built, "CompositeExplicitAutograd")
+            _stub_library.impl(name, _not_built, "CompositeExplicitAutograd")
 
 
 _register_custom_op()

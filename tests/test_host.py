@@ -173,6 +173,39 @@ def test_op_bodies_come_from_the_cpp_op_library():
         assert "torch_ops.cpp" in line, table
 
 
+def test_ops_raise_when_the_op_library_is_not_built(tmp_path):
+    """A package copy without _w4a4_ops.so registers raising stubs (no CPU
+    fallback); building and loading the library afterwards in the same
+    process replaces them without a duplicate-kernel registration."""
+    import shutil
+    import subprocess
+    import sys
+
+    pkg = os.path.join(ROOT, "pi05_pytorch_fast_b200")
+    shutil.copytree(pkg, tmp_path / "pi05_pytorch_fast_b200",
+                    ignore=shutil.ignore_patterns("_w4a4_ops.so", "__pycache__", "csrc"))
+    script = (
+        "import os, shutil, torch\n"
+        "from pi05_pytorch_fast_b200.w4a4 import extension as ext\n"
+        "try:\n"
+        "    torch.ops.pi05_w4a4.int4_gemm(torch.zeros(1, 8, dtype=torch.float16),"
+        " torch.zeros(1, 2, dtype=torch.int32))\n"
+        "    raise SystemExit('stub did not raise')\n"
+        "except RuntimeError as e:\n"
+        "    assert 'is not built' in str(e), e\n"
+        f"shutil.copy({os.path.join(pkg, '_w4a4_ops.so')!r}, ext.OPS_LIB_PATH)\n"
+        "ext.preload()\n"
+        "table = torch._C._dispatch_dump('pi05_w4a4::int4_gemm')\n"
+        "line = next(l for l in table.splitlines() if l.startswith('CompositeExplicitAutograd'))\n"
+        "assert 'torch_ops.cpp' in line, table\n"
+        "print('ok')\n")
+    env = dict(os.environ, PYTHONPATH=str(tmp_path))
+    r = subprocess.run([sys.executable, "-c", script], cwd=tmp_path, env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+    assert "Overriding a previously registered kernel" not in r.stderr, r.stderr
+
+
 def test_op_library_uses_the_shared_cxx_runtime():
     """_w4a4_ops.so must take libstdc++ from libstdc++.so.6, like torch: a
     second, statically linked C++ runtime in it makes every exception torch
