@@ -230,6 +230,64 @@ def time_device(fn, steps: int, warmup: int, dist_on: bool, device) -> float:
     return ms
 
 
+def time_e2e(x_host, layers, steps: int, warmup: int, dist_on: bool, device) -> float:
+    """ms per step of the prefix pass through the public ops, with every
+    step's input copied in from pinned host memory and its output copied back
+    inside the timed region. The copies run on a copy stream with two device
+    input buffers and two pinned output buffers, so step i+1's input copy and
+    step i's output copy overlap the neighbouring steps' compute, as a serving
+    loop would run them. Events on the compute stream, barrier + sync both
+    sides, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    compute = torch.cuda.current_stream(device)
+    copy = torch.cuda.Stream(device)
+    x_dev = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
+    y_host = [torch.empty(x_host.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    h2d = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
+
+    def run(n: int, after=None):
+        with torch.cuda.stream(copy):
+            if after is not None:
+                copy.wait_event(after)
+            x_dev[0].copy_(x_host, non_blocking=True)
+            h2d[0].record(copy)
+        for i in range(n):
+            b = i & 1
+            if i + 1 < n:
+                with torch.cuda.stream(copy):
+                    if i >= 1:
+                        copy.wait_event(used[b ^ 1])  # step i-1 has read x_dev[b^1]
+                    x_dev[b ^ 1].copy_(x_host, non_blocking=True)
+                    h2d[b ^ 1].record(copy)
+            compute.wait_event(h2d[b])
+            y = prefix_forward(x_dev[b], layers)
+            used[b].record(compute)
+            y.record_stream(copy)
+            with torch.cuda.stream(copy):
+                copy.wait_event(used[b])
+                y_host[b].copy_(y, non_blocking=True)
+        compute.wait_stream(copy)
+
+    run(warmup)
+    torch.cuda.synchronize(device)
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(compute)
+    run(steps, after=start)
+    end.record(compute)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / steps
+    if dist_on:
+        dist.barrier()
+        ms = max_over_ranks(ms, device)
+    return ms
+
+
 def max_over_ranks(value: float, device) -> float:
     """The largest of every rank's `value` (the step time of the slowest
     rank); every rank must call it at the same point."""
@@ -323,16 +381,8 @@ def run_ours(args, rank, world, local_rank, dist_on):
 
     # --- end to end through the public ops: pinned host in/out every step
     x_host = synthetic_prefix(m, device, seed=200 + rank).cpu().pin_memory()
-    y_host = torch.empty((m, HIDDEN), dtype=torch.float16).pin_memory()
-    x_dev = torch.empty((m, HIDDEN), dtype=torch.float16, device=device)
-
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        y = prefix_forward(x_dev, layers)
-        y_host.copy_(y, non_blocking=True)
-
     e2e_steps = max(5, min(args.steps, 50))
-    ms_e2e = time_device(e2e_step, e2e_steps, max(3, args.warmup), dist_on, device)
+    ms_e2e = time_e2e(x_host, layers, e2e_steps, max(3, args.warmup), dist_on, device)
 
     # --- roofline of the dominant kernel: the gate/up GEMM (one launch, two
     # weights) cycling over the layers so weights always come from HBM.
@@ -415,9 +465,10 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "value": job_throughput(ms_e2e, args.batch, world),
             "unit": UNIT,
             "h2d_bytes_per_step": int(x_host.numel() * 2),
-            "d2h_bytes_per_step": int(y_host.numel() * 2),
-            "mode": "eager torch.ops.pi05_w4a4 calls, pinned host input copied in and output "
-                    "copied out inside the timed region",
+            "d2h_bytes_per_step": int(x_host.numel() * 2),
+            "mode": "eager torch.ops.pi05_w4a4 calls; every step's pinned-host input copy and "
+                    "result copy inside the timed region, on a copy stream, double buffered so "
+                    "they overlap the neighbouring steps' compute",
             "steps": e2e_steps,
         },
         "roofline": {
