@@ -588,7 +588,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // j % 2 == r (j indexes this warp's chunks half + 2j) and pushes its
         // partial sums of the others into the partner's token ring, which is
         // idle once the partner's MMAs are done.  Exchange area of a warp:
-        // chunk j at [j][32 lanes][16 int32]; ceil(T / 32) chunks per warp.
+        // chunk j at [j][4 quads][32 lanes][4 int32] (a warp's 16-byte stores and
+        // loads cover 512 contiguous bytes: no bank conflicts); ceil(T / 32)
+        // chunks per warp.
         const int xstride = ((p.tok_tile / 16 + 1) / 2) * kXchgChunkBytes;
         const uint32_t xarea = smem_addr(tok_ring) + ew * xstride;
         const uint32_t peer = rank ^ 1u;
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive_remote(mapa_shared(bar_xready, peer));
         const bool free = warp_all(mbar_wait_bounded_cl(bar_xready, 0, abort_flag, err,
                                                         kErrWaitAccum, limit));
-        const uint32_t dst0 = mapa_shared(xarea, peer) + lane * 64;
+        const uint32_t dst0 = mapa_shared(xarea, peer) + lane * 16;
         bool released = false;
         const auto release_once = [&] {
           if (!released) release();
@@ -607,7 +609,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (free) {
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              st_shared_cluster_v4(dst0 + j * kXchgChunkBytes + 16 * q, acc[4 * q],
+              st_shared_cluster_v4(dst0 + j * kXchgChunkBytes + 512 * q, acc[4 * q],
                                    acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
           }
           return false;
@@ -620,10 +622,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                release_once, [&](uint32_t (&acc)[16], int j) -> bool {
           if (!got) return true;
           const uint4* src = reinterpret_cast<const uint4*>(tok_ring + ew * xstride +
-                                                            j * kXchgChunkBytes + lane * 64);
+                                                            j * kXchgChunkBytes + lane * 16);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const uint4 v = src[q];
+            const uint4 v = src[32 * q];
             acc[4 * q] += v.x;
             acc[4 * q + 1] += v.y;
             acc[4 * q + 2] += v.z;
