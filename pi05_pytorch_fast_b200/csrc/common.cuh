@@ -164,25 +164,22 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-// 16-byte store to shared memory given by its shared::cluster address (may
-// be another CTA's of the cluster: distributed shared memory).
-__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
-                                                     uint32_t c, uint32_t d) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a),
-               "r"(b), "r"(c), "r"(d)
-               : "memory");
+// 16-byte store into the shared memory of a CTA of the cluster (cluster_addr,
+// may be remote) that, once performed, reports its 16 bytes on that CTA's
+// mbarrier (cluster_bar) as completed transaction bytes.  The receiver's wait
+// on that barrier then covers the data: no release fence on this side.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
+                                            uint32_t c, uint32_t d, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(cluster_bar)
+      : "memory");
 }
-// Arrive on an mbarrier given by its shared::cluster address (may be remote),
-// releasing this thread's prior writes at cluster scope: what a partner that
-// reads data this thread stored into its shared memory needs.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-// The same arrival with the default (CTA-scope) release: a pure signal, for
-// when the waiting side needs no generic-memory data from this thread (TMEM
-// stores are ordered by tcgen05.wait::st and tcgen05.fence::before_thread_sync
-// instead).  A cluster-scope release costs ~0.7 us here; this one does not.
+// Arrive on an mbarrier given by its shared::cluster address (may be remote)
+// with the default (CTA-scope) release: a pure signal, for when the waiting
+// side needs no generic-memory data from this thread (TMEM stores are ordered
+// by tcgen05.wait::st and tcgen05.fence::before_thread_sync instead).  A
+// cluster-scope release costs ~0.7 us here; this one does not.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }

@@ -34,8 +34,10 @@
 //    (exact), apply the token and weight scales in fp32, round to fp16 and
 //    transpose 16x32 blocks through shared memory into 16-byte row stores.
 //  * SPLIT = true (split-K): the two CTAs of a cluster run the two K halves
-//    of one tile; rank 1 pushes its int32 partial sums into rank 0's idle
-//    ring through distributed shared memory, and rank 0's epilogue adds them.
+//    of one tile; each pushes the int32 partial sums of the half of the tile
+//    its partner writes out into the partner's idle ring (distributed shared
+//    memory, st.async with transaction bytes on the partner's barrier), then
+//    adds the partner's sums to its own half and writes that half.
 // TMEM map (512 columns): accumulators at [0, T) and [T, 2T) for a token tile
 // of T columns, then A stages of 32 columns (128 K-bytes per row) up to 512.
 #pragma once
@@ -302,9 +304,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const auto bar_accfull = [&](int b) { return smem_addr(bars + 3 * kMaxStages + b); };
   const auto bar_accempty = [&](int b) { return smem_addr(bars + 3 * kMaxStages + 2 + b); };
   const uint32_t bar_drain = smem_addr(bars + 3 * kMaxStages + 4);
-  // split-K: xready (rank 1) rank 0's MMAs are done, its token ring is free
-  // (one arrival per rank-0 epilogue warp); xfull[w] (rank 0) the partner
-  // warp's partial sums landed (32 lane arrivals).
+  // split-K: xready the partner's MMAs are done, its token ring is free (one
+  // arrival per partner epilogue warp); xfull[w] the partner warp's partial
+  // sums landed (this warp's arrival with the expected bytes, then the
+  // transaction bytes of the partner's st.async pushes).
   const auto bar_xfull = [&](int w) { return smem_addr(bars + 3 * kMaxStages + 5 + w); };
   const uint32_t bar_xready = smem_addr(bars + 3 * kMaxStages + 5 + kEpiWarps);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(bar_drain, 1);
     if (SPLIT) {
-      for (int w = 0; w < kEpiWarps; ++w) mbar_init(bar_xfull(w), 32);
+      for (int w = 0; w < kEpiWarps; ++w) mbar_init(bar_xfull(w), 1);
       mbar_init(bar_xready, kEpiWarps);
     }
     *abort_flag = 0;
@@ -594,11 +597,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int xstride = ((p.tok_tile / 16 + 1) / 2) * kXchgChunkBytes;
         const uint32_t xarea = smem_addr(tok_ring) + ew * xstride;
         const uint32_t peer = rank ^ 1u;
+        // The partner's pushes into our ring complete bytes on xfull[ew]: arm it
+        // with the bytes of the chunks this warp writes (j = rank, rank + 2, ...).
+        if (lane == 0) {
+          const int all = ((((c.rows + 15) & ~15) >> 4) - half + 1) >> 1;
+          const int mine = all > static_cast<int>(rank) ? (all - static_cast<int>(rank) + 1) / 2 : 0;
+          mbar_arrive_expect_tx(bar_xfull(ew), static_cast<uint32_t>(mine * kXchgChunkBytes));
+        }
         // our MMAs are done: our ring is free for the partner's sums
         if (lane == 0) mbar_arrive_remote(mapa_shared(bar_xready, peer));
         const bool free = warp_all(mbar_wait_bounded_cl(bar_xready, 0, abort_flag, err,
                                                         kErrWaitAccum, limit));
         const uint32_t dst0 = mapa_shared(xarea, peer) + lane * 16;
+        const uint32_t peer_xfull = mapa_shared(bar_xfull(ew), peer);
         bool released = false;
         const auto release_once = [&] {
           if (!released) release();
@@ -609,13 +620,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (free) {
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              st_shared_cluster_v4(dst0 + j * kXchgChunkBytes + 512 * q, acc[4 * q],
-                                   acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+              st_async_v4(dst0 + j * kXchgChunkBytes + 512 * q, acc[4 * q], acc[4 * q + 1],
+                          acc[4 * q + 2], acc[4 * q + 3], peer_xfull);
           }
           return false;
         }, static_cast<int>(peer), 2);
-        // every lane's stores are ordered before its arrival (release, cluster scope)
-        mbar_arrive_cluster(mapa_shared(bar_xfull(ew), peer));
         const bool got = warp_all(mbar_wait_bounded_cl(bar_xfull(ew), 0, abort_flag, err,
                                                        kErrWaitAccum, limit));
         epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
