@@ -383,8 +383,13 @@ GemmPlan choose_plan(int64_t m, int w_tiles, int k_steps, int sms, int variant) 
       const int64_t workers = split ? sms / 2 : sms;
       const int64_t waves = (tiles + workers - 1) / workers;
       const double steps = split ? k_steps / 2 : k_steps;
+      // split-K adds the partial-sum exchange (~12 per token column) and a
+      // per-cluster cost measured on B200 (~45 per cluster: 16-step GEMMs
+      // at 64 clusters ran 1.5 us slower than at 32 with the same per-CTA
+      // work, and lost to no split from ~60 clusters on).
       const double cost = static_cast<double>(waves) *
-                          (steps * (330.0 + 1.5 * tile) + 2000.0 + (split ? 12.0 * tile : 0.0));
+                          (steps * (330.0 + 1.5 * tile) + 2000.0 +
+                           (split ? 12.0 * tile + 45.0 * static_cast<double>(tiles) : 0.0));
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
         best = {tile, split != 0};
