@@ -46,10 +46,11 @@ METRIC = "W4A4 prefix-LM ms per 776-tok prefix; GEMM int TOPS; obs/s at 1/2/4/8 
 UNIT = "obs/s (776-token W4A4 prefixes per second)"
 HIDDEN, INTER, N_Q, N_KV = 2048, 16384, 2048, 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch at
-# M=776, from one `ncu --set full` capture of `bench.py --case gateup` (cold
-# L2; most of the fp16 output is still in L2 when the kernel ends, so writes
-# read low).  Re-captured whenever the GEMM changes.
-GATE_UP_DRAM_BYTES = 35_334_912 + 5_386_752
+# M=776 (the CTA-pair kernel, which the default variant picks for it), from
+# one `ncu --set full` capture of `bench.py --case gateup` (cold L2; most of
+# the fp16 output is still in L2 when the kernel ends, so writes read low).
+# Re-captured whenever the GEMM changes.
+GATE_UP_DRAM_BYTES = 35_335_424 + 7_729_408
 
 
 def parse_args():
@@ -472,7 +473,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "steps": e2e_steps,
         },
         "roofline": {
-            "kernel": "w4a4_gemm_kernel<fragment-major> (gate+up, one launch)",
+            "kernel": "w4a4_gemm_pair_kernel<fragment-major> (gate+up, one launch on CTA pairs)",
             "bound": "tensor",
             "achieved": gu_tops,
             "peak": int8_peak,

@@ -150,7 +150,8 @@ int w4a4_device_error(uint32_t* bits, int32_t clear);
 int w4a4_set_wait_limit_ns(uint64_t limit_ns);
 
 /* GEMM kernel variant for launches after this call (W4A4_GEMM_*; default
- * W4A4_GEMM_SINGLE_CTA).  Split-K runs a tile's two K halves on the two CTAs
+ * W4A4_GEMM_SINGLE_CTA, which also runs fragment-major GEMMs of 768 or more
+ * tokens on the CTA pair).  Split-K runs a tile's two K halves on the two CTAs
  * of a cluster and adds the partial sums through distributed shared memory.
  * All variants give bit-identical results.  Process-wide; the environment
  * variable W4A4_GEMM_PAIR=1 sets the initial value to W4A4_GEMM_CTA_PAIR.  No
@@ -158,12 +159,14 @@ int w4a4_set_wait_limit_ns(uint64_t limit_ns);
 int w4a4_set_gemm_variant(int32_t variant);
 
 /* Test hook (host only, no GPU needed): the launch shape w4a4_gemm would use
- * for m tokens, K = k and n_weights weights of n[i] rows on `sms` SMs with
- * GEMM variant `variant`.  out[6] receives the token tile, split-K (0/1), the
- * grid size, the number of token tiles, the token tiles per rasterisation
- * group and the number of weight tiles.  No counterpart in the reference. */
+ * for m tokens, K = k and n_weights weights of n[i] rows in weight layout
+ * `layout` (W4A4_LAYOUT_*) on `sms` SMs with GEMM variant `variant`.  out[6]
+ * receives the token tile, split-K (0/1), the grid size, the number of token
+ * tiles, the token tiles per rasterisation group and the number of weight
+ * tiles (of 256 rows when the CTA pair runs).  No counterpart in the
+ * reference. */
 int w4a4_gemm_plan(int64_t m, int32_t k, int32_t n_weights, const int32_t* n, int32_t sms,
-                   int32_t variant, int32_t* out);
+                   int32_t variant, int32_t layout, int32_t* out);
 
 /* Test hook: launches one CTA that waits on a barrier nobody arrives at, with
  * the given limit; the kernel must give up, set its error bit and return. */

@@ -91,7 +91,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_set_wait_limit_ns.argtypes = [c_u64]
     lib.w4a4_set_gemm_variant.argtypes = [c_i32]
     lib.w4a4_gemm_plan.argtypes = [c_i64, c_i32, c_i32, ctypes.POINTER(c_i32), c_i32, c_i32,
-                                   ctypes.POINTER(c_i32)]
+                                   c_i32, ctypes.POINTER(c_i32)]
     lib.w4a4_selftest_wait_timeout.argtypes = [c_u64, vp]
     lib.w4a4_version.argtypes = []
     for name in EXPORTED_SYMBOLS:
@@ -145,11 +145,12 @@ def set_gemm_variant(variant: int) -> None:
     check(lib().w4a4_set_gemm_variant(int(variant)))
 
 
-def gemm_plan(m: int, k: int, ns, sms: int = 148, variant: int = GEMM_SINGLE_CTA) -> dict:
+def gemm_plan(m: int, k: int, ns, sms: int = 148, variant: int = GEMM_SINGLE_CTA,
+              layout: int = LAYOUT_ROW_MAJOR) -> dict:
     """The launch shape w4a4_gemm would choose (host computation, no GPU)."""
     n_arr = (ctypes.c_int32 * len(ns))(*ns)
     out = (ctypes.c_int32 * 6)()
-    check(lib().w4a4_gemm_plan(m, k, len(ns), n_arr, sms, variant, out))
+    check(lib().w4a4_gemm_plan(m, k, len(ns), n_arr, sms, variant, layout, out))
     return {"tok_tile": out[0], "split": bool(out[1]), "grid": out[2], "tok_tiles": out[3],
             "tok_group": out[4], "w_tiles": out[5]}
 

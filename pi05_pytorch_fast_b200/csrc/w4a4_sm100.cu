@@ -485,7 +485,17 @@ std::atomic<int> g_gemm_variant{[] {
   return (e && e[0] == '1') ? W4A4_GEMM_CTA_PAIR : W4A4_GEMM_SINGLE_CTA;
 }()};
 
-bool use_pair_kernel() { return g_gemm_variant.load() == W4A4_GEMM_CTA_PAIR; }
+// The default variant runs fragment-major GEMMs (gate/up) of at least
+// kPairMinRows tokens on the CTA pair: its token tile is split over two SMs,
+// which halves each SM's token traffic.  Measured on the prefix pass: 2.144 vs
+// 2.157 ms per 776-token prefix and 13.3 vs 13.7 ms per 8-prefix step,
+// bit-identical; below ~200 tokens the single-CTA kernel is faster.
+constexpr int64_t kPairMinRows = 768;
+bool use_pair_kernel(int variant, int layout, int64_t m) {
+  return variant == W4A4_GEMM_CTA_PAIR ||
+         (variant == W4A4_GEMM_SINGLE_CTA && layout == W4A4_LAYOUT_FRAGMENT_MAJOR &&
+          m >= kPairMinRows);
+}
 
 
 int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
@@ -511,7 +521,8 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   if (int e = current_device(&dev)) return e;
   if (int e = sm_count(dev, &sms)) return e;
 
-  const bool pair = use_pair_kernel();
+  const int variant = g_gemm_variant.load();
+  const bool pair = use_pair_kernel(variant, layout, m);
   const int rows_per_wtile = pair ? 2 * kBlockW : kBlockW;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -542,7 +553,7 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
   const int k_steps = (k + kBlockK - 1) / kBlockK;
-  const LaunchShape ls = launch_shape(m, w_tiles, k, sms, pair, g_gemm_variant.load());
+  const LaunchShape ls = launch_shape(m, w_tiles, k, sms, pair, variant);
   const int tok_tile = ls.tok_tile;
   const bool split = ls.split;
   if (int e = make_map_2d(&p.tmap_tok, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, m, k, kBlockK,
@@ -735,14 +746,16 @@ int w4a4_device_error(uint32_t* bits, int32_t clear) {
 }
 
 int w4a4_gemm_plan(int64_t m, int32_t k, int32_t n_weights, const int32_t* n, int32_t sms,
-                   int32_t variant, int32_t* out) {
+                   int32_t variant, int32_t layout, int32_t* out) {
   if (m <= 0 || k <= 0 || k % 64 != 0 || sms < 2 || !n || !out)
     return fail(W4A4_ERR_INVALID, "invalid plan query");
   if (n_weights < 1 || n_weights > kMaxSegments)
     return fail(W4A4_ERR_INVALID, "n_weights must be 1..%d, got %d", kMaxSegments, n_weights);
   if (variant < W4A4_GEMM_SINGLE_CTA || variant > W4A4_GEMM_SPLIT_K)
     return fail(W4A4_ERR_INVALID, "unknown GEMM variant %d", variant);
-  const bool pair = variant == W4A4_GEMM_CTA_PAIR;
+  if (layout != W4A4_LAYOUT_ROW_MAJOR && layout != W4A4_LAYOUT_FRAGMENT_MAJOR)
+    return fail(W4A4_ERR_INVALID, "unknown weight layout %d", layout);
+  const bool pair = use_pair_kernel(variant, layout, m);
   const int rows_per_wtile = pair ? 2 * kBlockW : kBlockW;
   int w_tiles = 0;
   for (int i = 0; i < n_weights; ++i) {

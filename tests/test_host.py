@@ -80,18 +80,38 @@ def test_gemm_variant_selection_validated():
 
 # The launch plans of the prefix's GEMMs at M = 776 on 148 SMs (as the ncu
 # launch list shows them): q/k/v, o, gate/up, down.
+# gate/up (fragment-major, 776 tokens) runs on the CTA pair: 128 weight tiles
+# of 256 rows.
 PREFIX_PLANS = [
-    ("qkv", 776, 2048, [2048, 256, 256], dict(tok_tile=112, split=False, grid=140, tok_group=7)),
-    ("o", 776, 2048, [2048], dict(tok_tile=96, split=False, grid=144, tok_group=9)),
-    ("gate/up", 776, 2048, [16384, 16384], dict(tok_tile=208, split=False, grid=148, tok_group=4)),
-    ("down", 776, 16384, [2048], dict(tok_tile=208, split=True, grid=128, tok_group=4)),
+    ("qkv", 776, 2048, [2048, 256, 256], nat.LAYOUT_ROW_MAJOR,
+     dict(tok_tile=112, split=False, grid=140, tok_group=7, w_tiles=20)),
+    ("o", 776, 2048, [2048], nat.LAYOUT_ROW_MAJOR,
+     dict(tok_tile=96, split=False, grid=144, tok_group=9, w_tiles=16)),
+    ("gate/up", 776, 2048, [16384, 16384], nat.LAYOUT_FRAGMENT_MAJOR,
+     dict(tok_tile=208, split=False, grid=148, tok_group=4, w_tiles=128)),
+    ("down", 776, 16384, [2048], nat.LAYOUT_ROW_MAJOR,
+     dict(tok_tile=208, split=True, grid=128, tok_group=4, w_tiles=16)),
 ]
 
 
-@pytest.mark.parametrize("name,m,k,ns,want", PREFIX_PLANS)
-def test_prefix_gemm_plans(name, m, k, ns, want):
-    plan = nat.gemm_plan(m, k, ns)
+@pytest.mark.parametrize("name,m,k,ns,layout,want", PREFIX_PLANS)
+def test_prefix_gemm_plans(name, m, k, ns, layout, want):
+    plan = nat.gemm_plan(m, k, ns, layout=layout)
     assert {key: plan[key] for key in want} == want, (name, plan)
+
+
+def test_default_variant_pairs_only_large_fragment_major_gemms():
+    """The default variant runs fragment-major GEMMs of 768 or more tokens on
+    the CTA pair (256-row weight tiles, no split-K) and everything else on
+    single CTAs."""
+    ns = [16384, 16384]
+    assert nat.gemm_plan(767, 2048, ns, layout=nat.LAYOUT_FRAGMENT_MAJOR)["w_tiles"] == 256
+    big = nat.gemm_plan(768, 2048, ns, layout=nat.LAYOUT_FRAGMENT_MAJOR)
+    assert big["w_tiles"] == 128 and not big["split"] and big["grid"] % 2 == 0
+    assert nat.gemm_plan(6208, 2048, ns, layout=nat.LAYOUT_ROW_MAJOR)["w_tiles"] == 256
+    for v in (nat.GEMM_NO_SPLIT, nat.GEMM_SPLIT_K):
+        assert nat.gemm_plan(6208, 2048, ns, variant=v,
+                             layout=nat.LAYOUT_FRAGMENT_MAJOR)["w_tiles"] == 256
 
 
 @pytest.mark.parametrize("m", [1, 15, 16, 17, 208, 209, 640, 768, 776, 6208, 24832])
@@ -99,13 +119,18 @@ def test_prefix_gemm_plans(name, m, k, ns, want):
                                   (16384, [2048]), (1024, [384, 128]), (64, [24])])
 @pytest.mark.parametrize("variant", [nat.GEMM_SINGLE_CTA, nat.GEMM_CTA_PAIR, nat.GEMM_NO_SPLIT,
                                      nat.GEMM_SPLIT_K])
-def test_gemm_plan_invariants(m, k, ns, variant):
+@pytest.mark.parametrize("layout", [nat.LAYOUT_ROW_MAJOR, nat.LAYOUT_FRAGMENT_MAJOR])
+def test_gemm_plan_invariants(m, k, ns, variant, layout):
     """Whatever the shape, the plan covers every token with at most 208-token
     MMA tiles, launches no more CTAs than SMs (pairs and split-K clusters: an
     even grid, one tile per cluster for split-K), splits K only into two even
     halves, and groups token tiles so one group's codes stay within ~48 MB."""
     sms = 148
-    plan = nat.gemm_plan(m, k, ns, sms=sms, variant=variant)
+    plan = nat.gemm_plan(m, k, ns, sms=sms, variant=variant, layout=layout)
+    pair = variant == nat.GEMM_CTA_PAIR or (
+        variant == nat.GEMM_SINGLE_CTA and layout == nat.LAYOUT_FRAGMENT_MAJOR and m >= 768)
+    rows = 256 if pair else 128
+    assert plan["w_tiles"] == sum(-(-n // rows) for n in ns)
     t = plan["tok_tile"]
     assert t % 16 == 0 and 16 <= t <= 208
     assert plan["tok_tiles"] == -(-m // t)
@@ -113,11 +138,11 @@ def test_gemm_plan_invariants(m, k, ns, variant):
     assert 1 <= plan["grid"] <= sms
     k_steps = -(-k // 128)
     if plan["split"]:
-        assert variant != nat.GEMM_NO_SPLIT and variant != nat.GEMM_CTA_PAIR
+        assert variant != nat.GEMM_NO_SPLIT and not pair
         assert k_steps % 2 == 0 and plan["grid"] == 2 * total <= sms
     elif variant == nat.GEMM_SPLIT_K:
         assert k_steps % 2 == 1 or k_steps < 2 or total > sms // 2  # could not split
-    if variant == nat.GEMM_CTA_PAIR:
+    if pair:
         assert plan["grid"] % 2 == 0
     g = plan["tok_group"]
     assert 1 <= g <= plan["tok_tiles"]
@@ -130,6 +155,8 @@ def test_gemm_plan_rejects_bad_queries():
             nat.gemm_plan(*args)
     with pytest.raises(nat.W4A4Error, match="unknown GEMM variant"):
         nat.gemm_plan(4, 2048, [64], variant=9)
+    with pytest.raises(nat.W4A4Error, match="unknown weight layout"):
+        nat.gemm_plan(4, 2048, [64], layout=7)
 
 
 def test_ops_refuse_cpu_tensors():
