@@ -1,30 +1,33 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 W4A4 prefix-LM GEMM path.
+"""Benchmark of the B200 W4A4 prefix LM (BASELINE config 2 / 3).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--batch B] [--prefix M]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
-One step = the W4A4 work of the Gemma-2B prefix LM for one 776-token robot
-observation prefix (the metric's "776-tok prefix"):
-18 layers x {int4_gemm3 q/k/v (2048 -> 2048+256+256), int4_gemm o_proj
-(2048 -> 2048), int4_gemm2_tiled gate/up (2048 -> 2 x 16384, fragment-major
-weights), int4_gemm down_proj (16384 -> 2048)}, every op = one fused
-Hadamard+INT4 activation quant + one tensor-core GEMM launch.  The ops are
-chained (q -> o_proj input, o -> gate/up input, gate -> down input, down ->
-next layer) so each consumes the previous op's output as in the model; the
-attention / GeGLU glue between them is not part of this path.  Weights are
-random-init N(0, 1/sqrt(K)) packed with the reference's format; activations
-are synthetic N(0, 1) with 1% outlier channels x20.  The 18 layers' weights
-(~1 GB) stream through HBM every step, far more than the 126 MB L2, so no
-L2 flush is needed between steps.
+One step = the full 18-layer W4A4 prefix-LM forward (PaliGemma's Gemma-2B,
+fp16, every projection W4A4) of B robot-observation prefixes of M tokens per
+GPU: per layer residual add + RMSNorm + Hadamard/INT4 quant, the fused q/k/v
+GEMM, RoPE, bidirectional attention over the prefix with its padding mask,
+quant + o_proj GEMM, residual add + RMSNorm + quant, the gate/up GEMM, GeGLU +
+quant, the down GEMM; then the final residual add + norm.  The prefix is
+config 2's: 256 + 256 + 64 image-token embeddings ~ N(0, 1) and M - 576
+language tokens, 52 of them real.  Weights are random-init N(0, 0.02) (norm
+weights N(0, 0.1)) packed in the reference's format; there is no dataset.
+The 18 layers' ~1 GB of packed weights stream through HBM every step, far
+more than the 126 MB L2, so no L2 flush is needed between steps.
 
 Printed JSON (rank 0): ``value`` = prefixes/s of the whole job measured on
-the device (CUDA graph of the 72 ops, inputs resident), ``e2e`` = the same
-through the public torch ops with pinned-host input/output copies in the
-timed region, ``roofline`` = the gate/up GEMM (61% of the prefix's ops)
-against the int8 tensor peak, ``cpu_baseline`` = the CPU oracle port.
-With N > 1, every rank runs its own observations (data parallel, weak
-scaling); the step time is the max over ranks.
+the device (CUDA graph of the forward, inputs resident), ``e2e`` = the same
+through the model's public entry point with pinned-host inputs copied in and
+the final hidden states copied out inside the timed region, ``roofline`` =
+the gate/up GEMM (61 % of the prefix's integer ops) against the int8 tensor
+peak, ``kernels`` = every kernel of a layer timed alone, ``w4a4_ops`` = the
+72 W4A4 ops of a prefix chained without the glue (the path of the
+pi05_w4a4 custom ops), ``cpu_baseline`` = the CPU oracle port of the
+reference's int4_gemm_ref.  With N > 1, every rank runs its own
+observations (data parallel, weak scaling); the step time is the max over
+ranks.
 """
 
 from __future__ import annotations
@@ -43,40 +46,48 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "W4A4 prefix-LM ms per 776-tok prefix; GEMM int TOPS; obs/s at 1/2/4/8 B200"
-UNIT = "obs/s (776-token W4A4 prefixes per second)"
+UNIT = "obs/s (776-token W4A4 prefix-LM forwards per second)"
 HIDDEN, INTER, N_Q, N_KV = 2048, 16384, 2048, 256
+N_IMG = 576  # 256 + 256 + 64 image tokens
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch at
 # M=776 (the CTA-pair kernel, which the default variant picks for it), from
 # one `ncu --set full` capture of `bench.py --case gateup` (cold L2; most of
 # the fp16 output is still in L2 when the kernel ends, so writes read low).
-# Re-captured whenever the GEMM changes.
 GATE_UP_DRAM_BYTES = 35_335_424 + 7_729_408
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=1, help="observations per GPU per step")
-    ap.add_argument("--prefix", type=int, default=776, help="tokens per observation prefix")
+    ap.add_argument("--prefix", type=int, default=776, help="tokens per observation prefix (>= 628)")
     ap.add_argument("--layers", type=int, default=18)
     ap.add_argument("--staging", choices=("fp16", "fp32"), default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timings")
     ap.add_argument("--roofline-reps", type=int, default=20)
-    ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k"),
-                    default=None, help="run one op 3 times at the bench shape and exit "
-                                       "(a small, self-contained case for ncu)")
+    ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k",
+                                       "normquant", "geglu", "forward"),
+                    default=None, help="run one op (or one forward) 3 times at the bench shape and "
+                                       "exit (a small, self-contained case for ncu)")
     return ap.parse_args()
 
 
 # ----------------------------------------------------------------------------- helpers
 def ops_per_prefix(m: int, layers: int) -> float:
-    """Algorithmic integer ops (2 per MAC) of one prefix's GEMMs."""
+    """Algorithmic integer ops (2 per MAC) of one prefix's W4A4 GEMMs."""
     per_layer = 2 * m * HIDDEN * (N_Q + 2 * N_KV) + 2 * m * HIDDEN * HIDDEN \
         + 2 * m * HIDDEN * 2 * INTER + 2 * m * INTER * HIDDEN
     return float(per_layer * layers)
+
+
+def quant_bytes(m: int, k: int) -> int:
+    """Algorithmic bytes of one activation quant: fp16 in, packed INT4
+    codes (K/2 bytes a row) and an fp32 scale out: 2MK + MK/2 + 4M."""
+    return 2 * m * k + m * k // 2 + 4 * m
 
 
 def measured_peaks() -> dict:
@@ -153,37 +164,15 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(mhz)}
 
 
-# ----------------------------------------------------------------------------- model
-def build_layers(n_layers: int, device, seed: int):
-    """Packed weights of n_layers Gemma-2B decoder layers in the layouts the
-    reference's loader produces (rows padded to K/8+8; gate/up fragment-major)."""
-    import torch
-
-    from pi05_pytorch_fast_b200.w4a4.pack import pack_linear_weight, preshuffle_wmma_weight
-
-    gen = torch.Generator(device=device).manual_seed(seed)
-
-    def packed(n, k, pad=True):
-        w = torch.randn(n, k, device=device, generator=gen) * (1.0 / math.sqrt(k))
-        p = pack_linear_weight(w, device=device)
-        return torch.nn.functional.pad(p, (0, 7)) if pad else p
-
-    layers = []
-    for _ in range(n_layers):
-        qkv = packed(N_Q + 2 * N_KV, HIDDEN)
-        layers.append({
-            "q": qkv[:N_Q].contiguous(), "k": qkv[N_Q:N_Q + N_KV].contiguous(),
-            "v": qkv[N_Q + N_KV:].contiguous(),
-            "o": packed(HIDDEN, HIDDEN),
-            "gate": preshuffle_wmma_weight(packed(INTER, HIDDEN, pad=False), HIDDEN),
-            "up": preshuffle_wmma_weight(packed(INTER, HIDDEN, pad=False), HIDDEN),
-            "down": packed(HIDDEN, INTER),
-        })
-    return layers
+# ----------------------------------------------------------------------------- the W4A4 op chain
+def layer_weights(lw) -> dict:
+    return {"q": lw.q, "k": lw.k, "v": lw.v, "o": lw.o, "gate": lw.gate, "up": lw.up, "down": lw.down}
 
 
-def prefix_forward(x, layers):
-    """The 72 W4A4 ops of one prefix pass, chained through their outputs."""
+def w4a4_op_chain(x, layers):
+    """The 72 pi05_w4a4 ops of one prefix pass chained through their outputs
+    (q -> o_proj input, o -> gate/up input, gate -> down input, down -> next
+    layer), without the glue between them."""
     import torch
 
     ops = torch.ops.pi05_w4a4
@@ -195,12 +184,12 @@ def prefix_forward(x, layers):
     return x
 
 
-def synthetic_prefix(rows: int, device, seed: int):
+def synthetic_activations(rows: int, k: int, device, seed: int):
     import torch
 
     gen = torch.Generator(device=device).manual_seed(seed)
-    x = torch.randn(rows, HIDDEN, device=device, generator=gen)
-    ch = torch.randperm(HIDDEN, device=device, generator=gen)[: HIDDEN // 100]
+    x = torch.randn(rows, k, device=device, generator=gen)
+    ch = torch.randperm(k, device=device, generator=gen)[: k // 100]
     x[:, ch] *= 20
     return x.half()
 
@@ -231,45 +220,48 @@ def time_device(fn, steps: int, warmup: int, dist_on: bool, device) -> float:
     return ms
 
 
-def time_e2e(x_host, layers, steps: int, warmup: int, dist_on: bool, device) -> float:
-    """ms per step of the prefix pass through the public ops, with every
-    step's input copied in from pinned host memory and its output copied back
-    inside the timed region. The copies run on a copy stream with two device
-    input buffers and two pinned output buffers, so step i+1's input copy and
-    step i's output copy overlap the neighbouring steps' compute, as a serving
-    loop would run them. Events on the compute stream, barrier + sync both
-    sides, max over ranks."""
+def time_e2e(graphs, emb_host, pad_host, steps: int, warmup: int, dist_on: bool, device) -> float:
+    """ms per step of the forward through GraphedPrefixLM with every step's
+    inputs (embeddings and pad mask) copied in from pinned host memory and its
+    final hidden states copied back, inside the timed region.  The copies run
+    on a copy stream and two graph instances (each with its own static
+    inputs and outputs) alternate, so step i+1's input copy and step i's
+    output copy overlap the neighbouring steps' compute, as a serving loop
+    runs them.  Events on the compute stream, barrier + sync both sides, max
+    over ranks."""
     import torch
     import torch.distributed as dist
 
     compute = torch.cuda.current_stream(device)
     copy = torch.cuda.Stream(device)
-    x_dev = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
-    y_host = [torch.empty(x_host.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
-    h2d = [torch.cuda.Event() for _ in range(2)]
-    used = [torch.cuda.Event() for _ in range(2)]
+    out_host = [torch.empty(g.out.hidden.shape, dtype=torch.float16).pin_memory() for g in graphs]
+    h2d = [torch.cuda.Event() for _ in graphs]
+    done = [torch.cuda.Event() for _ in graphs]
+    d2h = [torch.cuda.Event() for _ in graphs]
 
-    def run(n: int, after=None):
+    def load(b, after):
         with torch.cuda.stream(copy):
             if after is not None:
                 copy.wait_event(after)
-            x_dev[0].copy_(x_host, non_blocking=True)
-            h2d[0].record(copy)
+            graphs[b].embeds.copy_(emb_host, non_blocking=True)
+            graphs[b].pad.copy_(pad_host, non_blocking=True)
+            h2d[b].record(copy)
+
+    def run(n: int, after=None):
+        load(0, after)
         for i in range(n):
             b = i & 1
             if i + 1 < n:
-                with torch.cuda.stream(copy):
-                    if i >= 1:
-                        copy.wait_event(used[b ^ 1])  # step i-1 has read x_dev[b^1]
-                    x_dev[b ^ 1].copy_(x_host, non_blocking=True)
-                    h2d[b ^ 1].record(copy)
+                load(b ^ 1, done[b ^ 1] if i >= 1 else None)  # step i-1 has consumed its inputs
             compute.wait_event(h2d[b])
-            y = prefix_forward(x_dev[b], layers)
-            used[b].record(compute)
-            y.record_stream(copy)
+            if i >= 2:
+                compute.wait_event(d2h[b])  # step i-2's output has been copied out
+            graphs[b].replay()
+            done[b].record(compute)
             with torch.cuda.stream(copy):
-                copy.wait_event(used[b])
-                y_host[b].copy_(y, non_blocking=True)
+                copy.wait_event(done[b])
+                out_host[b].copy_(graphs[b].out.hidden, non_blocking=True)
+                d2h[b].record(copy)
         compute.wait_stream(copy)
 
     run(warmup)
@@ -307,6 +299,34 @@ def job_throughput(ms_per_step: float, per_rank_prefixes: int, world: int) -> fl
     return per_rank_prefixes * world / (ms_per_step * 1e-3)
 
 
+def graph_ms(fn, reps: int, dist_on: bool, device, per_graph: int = 1) -> float:
+    """ms per call of fn, captured `per_graph` times in one CUDA graph."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    fn()
+    torch.cuda.synchronize(device)
+    with torch.cuda.graph(g):
+        for _ in range(per_graph):
+            fn()
+    ms = time_device(g.replay, reps, 3, dist_on, device) / per_graph
+    del g
+    return ms
+
+
+# ----------------------------------------------------------------------------- CPU reference
+def set_host_threads(n: int) -> int:
+    """All BLAS / OpenMP pools to n threads, whatever OMP_NUM_THREADS a
+    launcher (torchrun sets 1) left behind."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n)
+    except Exception:  # noqa: BLE001 - threadpoolctl is optional
+        pass
+    return n
+
+
 def oracle_layer(m: int, staging: str):
     """One decoder layer's W4A4 ops through the CPU oracle port (numpy; exact
     integer products in fp32 BLAS), with weights in the reference's layouts:
@@ -332,107 +352,67 @@ def oracle_layer(m: int, staging: str):
     return run
 
 
-def cpu_baseline_sample(m: int, staging: str, layers: int) -> dict:
+def cpu_baseline_sample(m: int, staging: str, layers: int, batch: int) -> dict:
     """The CPU oracle port timed on this host for ONE decoder layer at M=m
     (median of 3), scaled to the prefix's layers.  A reported baseline only."""
+    cores = set_host_threads(os.cpu_count() or 1)
     run = oracle_layer(m, staging)
     times = []
     for _ in range(3):
         t0 = time.perf_counter()
         run()
         times.append(time.perf_counter() - t0)
-    per_prefix = statistics.median(times) * layers
-    return {"value": 1.0 / per_prefix, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+    per_step = statistics.median(times) * layers
+    return {"value": batch / per_step, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"1 decoder layer's W4A4 ops (qkv, o, gate, up, down) at M={m}, median of 3, "
                       f"x{layers} layers; numpy oracle port of int4_gemm_ref (BLAS threads = cores, "
-                      "elementwise numpy on 1 thread)",
-            "ms_per_prefix": per_prefix * 1e3}
+                      "elementwise numpy on 1 thread); the glue (norms, attention, GeGLU) not included",
+            "ms_per_prefix": per_step * 1e3 / batch}
 
 
 # ----------------------------------------------------------------------------- arms
 def run_ours(args, rank, world, local_rank, dist_on):
     import torch
 
+    from pi05_pytorch_fast_b200 import _native as nat
+    from pi05_pytorch_fast_b200 import prefix_lm as plm
     from pi05_pytorch_fast_b200.w4a4 import extension as ext
 
     if args.staging:
         os.environ["PI05_W4A4_STAGING"] = args.staging
-    staging = os.environ.get("PI05_W4A4_STAGING", "fp16")
+    staging_name = os.environ.get("PI05_W4A4_STAGING", "fp16")
+    staging = nat.STAGING_FP32 if staging_name == "fp32" else nat.STAGING_FP16
+    if args.prefix < N_IMG + 52:
+        raise SystemExit(f"--prefix must be >= {N_IMG + 52} (576 image tokens + 52 real language tokens)")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     ext.preload()
+    cfg = plm.PrefixLMConfig(layers=args.layers)
+    model = plm.W4A4PrefixLM.random(cfg, device, seed=1234, staging=staging)
+    lang = args.prefix - N_IMG
+    embeds, pad = plm.synthetic_prefix(args.batch, lang_tokens=lang, device=device, seed=100 + rank)
     m = args.batch * args.prefix
-    layers = build_layers(args.layers, device, seed=1234)
-    x_static = synthetic_prefix(m, device, seed=100 + rank)
     torch.cuda.synchronize(device)
 
-    # --- CUDA graph of the whole prefix pass (device-resident inputs)
-    side = torch.cuda.Stream(device)
-    side.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(side):
-        for _ in range(2):
-            prefix_forward(x_static, layers)
-    torch.cuda.current_stream(device).wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        y_static = prefix_forward(x_static, layers)
-    with ClockSampler(local_rank) as clocks:
-        ms = time_device(graph.replay, args.steps, args.warmup, dist_on, device)
-    launches_per_step = args.layers * 4 * 2
+    # --- the forward as one CUDA graph, inputs resident on the device
+    with torch.no_grad():
+        graphs = [plm.GraphedPrefixLM(model, args.batch, args.prefix) for _ in range(2)]
+        graphs[0].run(embeds, pad)
+        with ClockSampler(local_rank) as clocks:
+            ms = time_device(graphs[0].replay, args.steps, args.warmup, dist_on, device)
 
-    # --- end to end through the public ops: pinned host in/out every step
-    x_host = synthetic_prefix(m, device, seed=200 + rank).cpu().pin_memory()
-    e2e_steps = max(5, min(args.steps, 50))
-    ms_e2e = time_e2e(x_host, layers, e2e_steps, max(3, args.warmup), dist_on, device)
+        # --- end to end: pinned host inputs in, final hidden states out, every step
+        emb_host = plm.synthetic_prefix(args.batch, lang_tokens=lang, seed=200 + rank)[0].pin_memory()
+        pad_host = pad.cpu().pin_memory()
+        e2e_steps = max(5, min(args.steps, 50))
+        ms_e2e = time_e2e(graphs, emb_host, pad_host, e2e_steps, max(3, args.warmup), dist_on, device)
+        del graphs
 
-    # --- roofline of the dominant kernel: the gate/up GEMM (one launch, two
-    # weights) cycling over the layers so weights always come from HBM.
-    codes, scales = ext.quantize(x_static, fmt="gemm")
-    ga = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(ga):
-        for lw in layers:
-            ext.gemm_from_codes(codes, scales, [lw["gate"], lw["up"]], fragment_major=True)
-    ms_gu = time_device(ga.replay, args.roofline_reps, 3, dist_on, device) / len(layers)
-    gu_ops = 2.0 * m * 2 * INTER * HIDDEN
-    gu_tops = gu_ops / (ms_gu * 1e-3) / 1e12
-    # quant kernel at K = 16384 (HBM-bound)
-    h16 = torch.randn(m, INTER, device=device).half()
-    gq = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gq):
-        for _ in range(10):
-            ext.quantize(h16, fmt="gemm")
-    ms_q = time_device(gq.replay, args.roofline_reps, 3, dist_on, device) / 10
-    q_bytes = 2 * m * INTER + m * INTER + 4 * m
-    # quant kernel at K = 2048 (the q/k/v, o and gate/up inputs)
-    gq2 = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gq2):
-        for _ in range(10):
-            ext.quantize(x_static, fmt="gemm")
-    ms_q2 = time_device(gq2.replay, args.roofline_reps, 3, dist_on, device) / 10
-    q2_bytes = 2 * m * HIDDEN + m * HIDDEN + 4 * m
-    # the other GEMMs of a layer, each cycled over the layers' weights
-    codes16, scales16 = ext.quantize(h16, fmt="gemm")
-    other = {
-        "gemm_qkv": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]]),
-                     2.0 * m * (N_Q + 2 * N_KV) * HIDDEN),
-        "gemm_o": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["o"]]), 2.0 * m * HIDDEN * HIDDEN),
-        "gemm_down": (lambda lw: ext.gemm_from_codes(codes16, scales16, [lw["down"]]),
-                      2.0 * m * HIDDEN * INTER),
-    }
-    gemm_ms = {}
-    for name, (fn, _) in other.items():
-        gg = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gg):
-            for lw in layers:
-                fn(lw)
-        gemm_ms[name] = time_device(gg.replay, args.roofline_reps, 3, dist_on, device) / len(layers)
-        del gg
-    del graph, ga, gq, gq2
-    torch.cuda.synchronize(device)
+        # --- the 72 W4A4 ops alone (the pi05_w4a4 op path), one CUDA graph
+        lws = [layer_weights(lw) for lw in model.layers]
+        x_static = synthetic_activations(m, HIDDEN, device, seed=100 + rank)
+        ms_ops = graph_ms(lambda: w4a4_op_chain(x_static, lws), max(5, args.steps // 4), dist_on, device)
 
-    peaks = measured_peaks()
-    int8_peak = 2.0 * peaks["bf16_tflops"]
-    total_ops = ops_per_prefix(m, args.layers)
     result = {
         "metric": METRIC,
         "value": job_throughput(ms, args.batch, world),
@@ -441,80 +421,158 @@ def run_ours(args, rank, world, local_rank, dist_on):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": ms,
-        "ms_per_prefix": ms / args.batch,
-        "gemm_int_tops": total_ops / (ms * 1e-3) / 1e12,
+        "prefix_lm_ms": ms / args.batch,
+        "gemm_int_tops": ops_per_prefix(m, args.layers) / (ms * 1e-3) / 1e12,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "int4 codes x int4 codes -> int32 (tcgen05 kind::i8), fp16 in/out",
-        "data": "synthetic: random-init N(0,1/sqrt(K)) weights in the reference's packed format; "
-                "N(0,1) activations with 1% outlier channels x20",
+        "dtype": "int4 codes x int4 codes -> int32 (tcgen05 kind::i8) for every projection; "
+                 "fp16 activations, glue and attention",
+        "data": "synthetic: random-init weights N(0,0.02) packed in the reference's format, norm weights "
+                "N(0,0.1); prefix = 576 image-token embeddings N(0,1) + language tokens (52 real ids, "
+                "rest padding) as config 2 builds it",
         "config": {
-            "workload": f"config 2 W4A4 path: {args.layers} Gemma-2B layers x (int4_gemm3 qkv, int4_gemm o, "
-                        f"int4_gemm2_tiled gate/up, int4_gemm down), prefix M={args.prefix}, "
-                        f"{args.batch} observation(s) per GPU per step",
+            "workload": f"config 2: full {args.layers}-layer W4A4 Gemma-2B prefix-LM forward, prefix "
+                        f"M={args.prefix} tokens, {args.batch} observation(s) per GPU per step",
             "rows_per_gpu": m,
             "layers": args.layers,
-            "staging": staging,
+            "staging": staging_name,
+            "staging_parity": "fp32: pinned to the reference's golden vectors; fp16: the HIP kernel's "
+                              "rounding, parity unpinned (no reference output exists for it)",
             "parallelism": f"dp{world} (independent observations per GPU, no collective in the step)",
             "l2": "working set ~1.0 GB of packed weights per step >> 126 MB L2 (no flush needed)",
-            "timing": "CUDA graph replay of the 144 launches, CUDA events, max over ranks",
+            "timing": "CUDA graph replay of the whole forward, CUDA events, max over ranks",
         },
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": model.launches_per_forward() * args.steps,
+        "gpu_launches_note": "kernels of libw4a4_sm100.so per timed region (10 per layer + the final "
+                             "norm); the attention and cos/sin glue are PyTorch kernels, not counted",
         "clocks": clocks.summary(),
         "e2e": {
             "value": job_throughput(ms_e2e, args.batch, world),
             "unit": UNIT,
-            "h2d_bytes_per_step": int(x_host.numel() * 2),
-            "d2h_bytes_per_step": int(x_host.numel() * 2),
-            "mode": "eager torch.ops.pi05_w4a4 calls; every step's pinned-host input copy and "
-                    "result copy inside the timed region, on a copy stream, double buffered so "
-                    "they overlap the neighbouring steps' compute",
+            "h2d_bytes_per_step": int(emb_host.numel() * 2 + pad_host.numel()),
+            "d2h_bytes_per_step": int(emb_host.numel() * 2),
+            "mode": "GraphedPrefixLM.run semantics: every step's pinned-host embeddings and pad mask "
+                    "copied in and its final hidden states copied out inside the timed region, on a "
+                    "copy stream, two graph instances alternating so copies overlap compute",
             "steps": e2e_steps,
         },
+        "w4a4_ops": {
+            "ms_per_prefix": ms_ops / args.batch,
+            "obs_per_s": job_throughput(ms_ops, args.batch, 1),
+            "what": "the 72 pi05_w4a4 ops of a prefix (int4_gemm3, int4_gemm, int4_gemm2_tiled, "
+                    "int4_gemm x 18) chained without the glue, one CUDA graph, torch op path",
+        },
+    }
+    if not args.no_kernels:
+        result.update(kernel_figures(args, model, m, staging, dist_on, device))
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the reference's CPU path is int4_gemm_ref: fp32 FWHT staging
+        result["cpu_baseline"] = cpu_baseline_sample(m, "fp32", args.layers, args.batch)
+    return result
+
+
+def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> dict:
+    """Every kernel of a layer timed alone (CUDA graphs cycling over the
+    layers' weights, so weights come from HBM), with roofline fractions."""
+    import torch
+
+    from pi05_pytorch_fast_b200 import _native as nat
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    lib = nat.lib()
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    hbm = peaks["hbm_gbs"]
+    reps = args.roofline_reps
+    x = synthetic_activations(m, HIDDEN, device, seed=7)
+    h = synthetic_activations(m, INTER, device, seed=8)
+    codes, scales = ext.quantize(x, fmt="gemm", staging=staging)
+    codes16, scales16 = ext.quantize(h, fmt="gemm", staging=staging)
+    lws = [layer_weights(lw) for lw in model.layers]
+    out: dict = {}
+
+    def cycle(fn):
+        return lambda: [fn(lw) for lw in lws]
+
+    gemms = {
+        "gemm_qkv": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]]),
+                     2.0 * m * (N_Q + 2 * N_KV) * HIDDEN),
+        "gemm_o": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["o"]]), 2.0 * m * HIDDEN * HIDDEN),
+        "gemm_gateup": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["gate"], lw["up"]],
+                                                       fragment_major=True),
+                        2.0 * m * 2 * INTER * HIDDEN),
+        "gemm_down": (lambda lw: ext.gemm_from_codes(codes16, scales16, [lw["down"]]),
+                      2.0 * m * HIDDEN * INTER),
+    }
+    for name, (fn, ops) in gemms.items():
+        t = graph_ms(cycle(fn), reps, dist_on, device, per_graph=1) / len(lws)
+        out[name] = {"ms": t, "tops": ops / (t * 1e-3) / 1e12, "frac": ops / (t * 1e-3) / 1e12 / int8_peak}
+
+    def bw(name, fn, nbytes, note):
+        t = graph_ms(fn, reps, dist_on, device, per_graph=10)
+        gbs = nbytes / (t * 1e-3) / 1e9
+        out[name] = {"ms": t, "gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "bytes": nbytes, "note": note}
+
+    for sname, st in (("", staging), ("_fp32", nat.STAGING_FP32)):
+        if sname and st == staging:
+            continue
+        bw("quant_k2048" + sname, lambda st=st: ext.quantize(x, fmt="gemm", staging=st),
+           quant_bytes(m, HIDDEN), "2MK + MK/2 + 4M algorithmic bytes (packed codes); 4.0 MB at M=776, "
+                                   "L2-resident, launch-latency bound")
+        bw("quant_k16384" + sname, lambda st=st: ext.quantize(h, fmt="gemm", staging=st),
+           quant_bytes(m, INTER), "2MK + MK/2 + 4M algorithmic bytes (packed codes); repeated on one "
+                                  "input, mostly L2-resident as in the forward")
+    gate = synthetic_activations(m, INTER, device, seed=9)
+    up = synthetic_activations(m, INTER, device, seed=10)
+    gain = torch.ones(HIDDEN, dtype=torch.float32, device=device)
+    xo = torch.empty_like(x)
+    cb = torch.empty((m, INTER), dtype=torch.int8, device=device)
+    sb = torch.empty((m,), dtype=torch.float32, device=device)
+    stream = lambda: torch.cuda.current_stream(device).cuda_stream  # noqa: E731
+
+    def geglu():
+        nat.check(lib.w4a4_geglu_quant(gate.data_ptr(), up.data_ptr(), m, INTER, INTER, staging,
+                                       nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), None, INTER, stream()))
+
+    def normq():
+        nat.check(lib.w4a4_rmsnorm_quant(x.data_ptr(), HIDDEN, h.data_ptr(), INTER, gain.data_ptr(), 1e-6,
+                                         xo.data_ptr(), HIDDEN, None, HIDDEN, m, HIDDEN, staging,
+                                         nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), stream()))
+
+    bw("geglu_quant_k16384", geglu, 2 * 2 * m * INTER + m * INTER // 2 + 4 * m,
+       "gate + up fp16 in, packed codes + scale out; replaces F.gelu(gate)*up and the down_proj quant")
+    bw("rmsnorm_quant_k2048", normq, 3 * 2 * m * HIDDEN + m * HIDDEN // 2 + 4 * m,
+       "x + delta in, x out (residual), packed codes + scale out; replaces add, RMSNorm and quant")
+    gu = out["gemm_gateup"]
+    return {
         "roofline": {
             "kernel": "w4a4_gemm_pair_kernel<fragment-major> (gate+up, one launch on CTA pairs)",
             "bound": "tensor",
-            "achieved": gu_tops,
+            "achieved": gu["tops"],
             "peak": int8_peak,
             "unit": "TFLOP/s",
             "op_kind": "int8 tensor ops (1 MAC = 2 ops); peak = 2 x bf16 dense "
                        f"({peaks['_source']}: {peaks['bf16_tflops']} TFLOP/s), the i8:f16 rate ratio",
-            "frac": gu_tops / int8_peak,
+            "frac": gu["frac"],
             "traffic": GATE_UP_DRAM_BYTES,
-            "ms_per_launch": ms_gu,
-            "algorithmic_ops_per_launch": gu_ops,
+            "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M=776",
+            "ms_per_launch": gu["ms"],
+            "algorithmic_ops_per_launch": 2.0 * m * 2 * INTER * HIDDEN,
         },
-        "kernels": {
-            "gemm_gateup": {"ms": ms_gu, "tops": gu_tops, "frac": gu_tops / int8_peak},
-            **{name: {"ms": gemm_ms[name], "tops": ops / (gemm_ms[name] * 1e-3) / 1e12,
-                      "frac": ops / (gemm_ms[name] * 1e-3) / 1e12 / int8_peak}
-               for name, (_, ops) in other.items()},
-            "quant_k16384": {"ms": ms_q, "gbs": q_bytes / (ms_q * 1e-3) / 1e9,
-                             "peak_gbs": peaks["hbm_gbs"],
-                             "frac": q_bytes / (ms_q * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                             "note": "38 MB per launch, repeated on one input: mostly L2-resident, "
-                                     "as in the prefix pass (the gate/up output feeds it)"},
-            "quant_k2048": {"ms": ms_q2, "gbs": q2_bytes / (ms_q2 * 1e-3) / 1e9,
-                            "peak_gbs": peaks["hbm_gbs"],
-                            "frac": q2_bytes / (ms_q2 * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                            "note": "4.8 MB per launch: fits in L2, launch-latency bound"},
-        },
+        "kernels": out,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        # the reference's CPU path is int4_gemm_ref: fp32 FWHT staging
-        result["cpu_baseline"] = cpu_baseline_sample(m, "fp32", args.layers)
-    return result
 
 
 def run_reference(args, rank, world):
     """The reference's CPU implementation of the path (this repo's oracle port
     of int4_gemm_ref; the reference itself is Python + HIP and cannot run
-    here), timed on the host cores.  Rank 0 only."""
+    here), timed on the host cores.  Rank 0 only; BLAS on every core."""
     import numpy as np
 
     if rank != 0:
         return None
+    cores = set_host_threads(os.cpu_count() or 1)
     staging = "fp32"  # int4_gemm_ref's arithmetic (pack.py:113-145)
     m = args.batch * args.prefix
     one_layer = oracle_layer(m, staging)
@@ -532,7 +590,7 @@ def run_reference(args, rank, world):
     t_layer = (time.perf_counter() - t0) / steps
     value = 1.0 / (t_layer * args.layers) * args.batch
     sample = (f"each step = 1 decoder layer's W4A4 ops at M={m} (q/k/v as one N=2560 GEMM), "
-              f"scaled x{args.layers} layers; numpy oracle port of int4_gemm_ref")
+              f"scaled x{args.layers} layers; numpy oracle port of int4_gemm_ref, {cores} BLAS threads")
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": t_layer * 1e3,
@@ -540,8 +598,9 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int32 codes in fp32 BLAS (exact), fp16 out", "data": "synthetic",
         "config": {"workload": f"config 2 W4A4 path, {args.layers} layers, prefix M={args.prefix}, "
-                               f"{args.batch} observation(s)", "rows": m, "staging": staging},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                               f"{args.batch} observation(s); one CPU process for the whole job",
+                   "rows": m, "staging": staging},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "numpy": np.__version__,
@@ -549,21 +608,33 @@ def run_reference(args, rank, world):
 
 
 def run_case(args):
-    """One op of one layer, 3 launches, for profiling (no timing, no JSON)."""
+    """One op (or one forward) of one layer, 3 launches, for profiling (no
+    timing, no JSON)."""
     import torch
 
+    from pi05_pytorch_fast_b200 import _native as nat
+    from pi05_pytorch_fast_b200 import prefix_lm as plm
     from pi05_pytorch_fast_b200.w4a4 import extension as ext
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     if args.staging:
         os.environ["PI05_W4A4_STAGING"] = args.staging
+    staging = nat.STAGING_FP32 if os.environ.get("PI05_W4A4_STAGING", "fp16") == "fp32" else nat.STAGING_FP16
     m = args.batch * args.prefix
-    lw = build_layers(1, device, seed=1234)[0]
-    x = synthetic_prefix(m, device, seed=100)
-    h = torch.randn(m, INTER, device=device).half()
+    layers = 1 if args.case != "forward" else args.layers
+    model = plm.W4A4PrefixLM.random(plm.PrefixLMConfig(layers=layers), device, seed=1234, staging=staging)
+    lw = layer_weights(model.layers[0])
+    x = synthetic_activations(m, HIDDEN, device, seed=100)
+    h = synthetic_activations(m, INTER, device, seed=101)
     codes, scales = ext.quantize(x, fmt="gemm")
     codes_h, scales_h = ext.quantize(h, fmt="gemm")
+    lib = nat.lib()
+    st = torch.cuda.current_stream(device).cuda_stream
+    cb = torch.empty((m, INTER), dtype=torch.int8, device=device)
+    sb = torch.empty((m,), dtype=torch.float32, device=device)
+    gain = torch.ones(HIDDEN, dtype=torch.float32, device=device)
+    embeds, pad = plm.synthetic_prefix(args.batch, lang_tokens=args.prefix - N_IMG, device=device)
     for _ in range(3):
         if args.case == "qkv":
             ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]])
@@ -577,6 +648,16 @@ def run_case(args):
             ext.quantize(x, fmt="gemm")
         elif args.case == "quant16k":
             ext.quantize(h, fmt="gemm")
+        elif args.case == "geglu":
+            nat.check(lib.w4a4_geglu_quant(h.data_ptr(), h.data_ptr(), m, INTER, INTER, staging,
+                                           nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), None, INTER, st))
+        elif args.case == "normquant":
+            nat.check(lib.w4a4_rmsnorm_quant(x.data_ptr(), HIDDEN, None, HIDDEN, gain.data_ptr(), 1e-6,
+                                             None, HIDDEN, None, HIDDEN, m, HIDDEN, staging,
+                                             nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), st))
+        elif args.case == "forward":
+            with torch.no_grad():
+                model.forward(embeds, pad)
     torch.cuda.synchronize(device)
     print(f"case {args.case} done (M={m})")
 

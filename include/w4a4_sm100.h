@@ -17,6 +17,8 @@
  *                                                             -> w4a4_int4_gemm
  *   pi05_fast/w4a4/apply.py:68-69             row padding     -> w4a4_pad_rows
  *   pi05_fast/w4a4/csrc/int4_gemm.cu:487-501  TORCH_CHECK text-> w4a4_last_error
+ *   pi05_fast/w4a4/apply.py:126-191           layer glue      -> w4a4_rmsnorm_quant,
+ *                                                                w4a4_geglu_quant, w4a4_rope
  */
 #ifndef W4A4_SM100_H_
 #define W4A4_SM100_H_
@@ -129,6 +131,44 @@ int w4a4_int4_gemm(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rot
 int w4a4_int4_gemm_noalloc(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
                            int32_t staging, int32_t n_weights, const w4a4_weight* weights,
                            void* const* y, void* stream);
+
+/* ---- prefix-LM layer glue fused with the quant that follows it ----
+ * The reference runs this glue as PyTorch ops between its pi05_w4a4 calls
+ * (pi05_fast/w4a4/apply.py:126-191 over transformers' GemmaDecoderLayer:
+ * input_layernorm / post_attention_layernorm, the residual adds,
+ * apply_rotary_pos_emb, act_fn(gate) * up). */
+
+/* Residual add + Gemma RMSNorm + activation quant of K = 2048 rows.
+ * Replaces `residual + hidden_states`, GemmaRMSNorm.forward and the
+ * following quantize_x (int4_gemm.cu:496-531) of the q/k/v and gate/up
+ * inputs.  Per row: s = fl16(x + delta) (delta may be NULL: s = x), written
+ * to x_out when not NULL (x_out may equal x); h = fl16(s * rsqrt(mean(s^2)
+ * + eps) * gain) in fp32 (gain = 1 + weight, fp32 [k], 16-byte aligned),
+ * written to h_out when not NULL; when codes is not NULL, the codes and row
+ * scale of h exactly as w4a4_quant(h, rotate = 1, staging, codes_format)
+ * computes them.  codes == NULL is the norm alone (then h_out is required).
+ * Rows: 16-byte aligned, strides >= k and multiples of 8 elements. */
+int w4a4_rmsnorm_quant(const void* x, int64_t ldx, const void* delta, int64_t ldd,
+                       const float* gain, float eps, void* x_out, int64_t ldo, void* h_out,
+                       int64_t ldh, int64_t m, int32_t k, int32_t staging, int32_t codes_format,
+                       void* codes, float* row_scale, void* stream);
+
+/* GeGLU + activation quant of the down_proj input (K = 16384).  Replaces
+ * `act_fn(gate) * up` (apply.py:138, F.gelu(approximate="tanh") on fp16)
+ * and the following quantize_x.  h = fl16(fl16(gelu_tanh(gate)) * up), the
+ * rounding of PyTorch's eager CUDA ops; its codes and row scale exactly as
+ * w4a4_quant(h, rotate = 1, staging, codes_format) computes them; h itself
+ * is written to h_out when not NULL.  gate and up share the row stride ld. */
+int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int64_t ld,
+                     int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                     void* h_out, int64_t ldh, void* stream);
+
+/* Rotary position embedding of `heads` heads of width 256 in each of m rows
+ * (apply_rotary_pos_emb: q * cos + rotate_half(q) * sin, each product and
+ * the sum rounded to fp16).  cos_t / sin_t: fp16 [m, 256], row stride 256.
+ * out may equal x. */
+int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
+              const void* sin_t, int64_t m, int32_t heads, void* stream);
 
 /* Copy a row-major packed weight [n, src_row_words] into [n, dst_row_words]
  * (dst_row_words >= src_row_words), zero-filling the new words: the

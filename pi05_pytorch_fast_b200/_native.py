@@ -40,6 +40,9 @@ EXPORTED_SYMBOLS = (
     "w4a4_gemm_accumulators",
     "w4a4_int4_gemm",
     "w4a4_int4_gemm_noalloc",
+    "w4a4_rmsnorm_quant",
+    "w4a4_geglu_quant",
+    "w4a4_rope",
     "w4a4_pad_rows",
     "w4a4_last_error",
     "w4a4_device_error",
@@ -85,6 +88,10 @@ def _declare(lib: ctypes.CDLL) -> None:
                                    ctypes.POINTER(W4A4Weight), ctypes.POINTER(vp), vp, vp, vp]
     lib.w4a4_int4_gemm_noalloc.argtypes = [vp, c_i64, c_i32, c_i64, c_i32, c_i32, c_i32,
                                            ctypes.POINTER(W4A4Weight), ctypes.POINTER(vp), vp]
+    lib.w4a4_rmsnorm_quant.argtypes = [vp, c_i64, vp, c_i64, vp, ctypes.c_float, vp, c_i64, vp,
+                                       c_i64, c_i64, c_i32, c_i32, c_i32, vp, vp, vp]
+    lib.w4a4_geglu_quant.argtypes = [vp, vp, c_i64, c_i32, c_i64, c_i32, c_i32, vp, vp, vp, c_i64, vp]
+    lib.w4a4_rope.argtypes = [vp, c_i64, vp, c_i64, vp, vp, c_i64, c_i32, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]

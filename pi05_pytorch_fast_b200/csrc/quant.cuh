@@ -56,6 +56,46 @@ __device__ __forceinline__ void load8_half_as_float(const __half* p, float (&v)[
   }
 }
 
+// GeGLU of the Gemma MLP as PyTorch's eager CUDA ops round it
+// (F.gelu(gate, approximate="tanh") * up on fp16 tensors): the tanh-form
+// GELU 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) in fp32 with the
+// constants rounded to fp32, x^3 as (x x) x, the inner sum as one fused
+// multiply-add, rounded to fp16; then the fp16 product with up (the exact
+// fp32 product of two fp16 values, rounded once).  tanhf is CUDA's.
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  constexpr float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  constexpr float kKappa = 0.044715f;
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ __half geglu_half(__half g, __half u) {
+  const __half gl = __float2half_rn(gelu_tanh_f32(__half2float(g)));
+  return __float2half_rn(__fmul_rn(__half2float(gl), __half2float(u)));
+}
+
+// Eight fp16 GeGLU values from 16-byte vectors of gate and up.
+__device__ __forceinline__ uint4 geglu8(const uint4 g, const uint4 u) {
+  uint4 r;
+  const __half* gh = reinterpret_cast<const __half*>(&g);
+  const __half* uh = reinterpret_cast<const __half*>(&u);
+  __half* rh = reinterpret_cast<__half*>(&r);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) rh[j] = geglu_half(gh[j], uh[j]);
+  return r;
+}
+
+__device__ __forceinline__ void half8_to_float(const uint4 raw, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
 // Packed fp32 pairs: elements (2i, 2i + 1) of a vector go through the
 // sm_100 two-lane fp32 instructions (add / fma .rn.f32x2), each lane rounded
 // exactly like the scalar instruction.  a - b is fma(b, -1, a): the product is
@@ -344,32 +384,32 @@ __device__ __forceinline__ float cross_warp_stages<4, float>(const float (&x)[4]
   return (w & 2) ? __fsub_rn(a, b) : __fadd_rn(a, b);
 }
 
-// K = 1024 / 2048: one CTA of K / 16 threads (2 or 4 warps) per row, so a
-// 776-row activation is resident in one wave at ~21 warps per SM with short
-// per-thread dependency chains.  Thread (w, l) holds elements
-// 512 w + 256 c + 8 l + j (c = 0, 1; j = 0..7): index bits 0-2 are in a
-// vector, 3-7 across lanes, bit 8 across the thread's two vectors and bits 9
-// and up across the row's warps, whose stages (the last, as in the
-// reference's ascending order) go through one shared-memory exchange.
+// Shared memory of the row-split K <= 2048 quant: the cross-warp exchange
+// and the per-warp amax.
+template <int LOGK, bool FP16>
+struct RowSplitSmem {
+  static constexpr int NW = (1 << LOGK) / 512;
+  uint4 xchg[NW][2][32][FP16 ? 1 : 2];
+  float warp_amax[NW];
+};
+
+// The FWHT + codes of one K = 1024 / 2048 row held by a CTA of K / 16
+// threads: thread (warp, lane) holds elements 512 warp + 256 c + 8 lane + j
+// (c = 0, 1; j = 0..7) of the row in v, as fp32 copies of fp16 values.
+// Index bits 0-2 are in a vector, 3-7 across lanes, bit 8 across the
+// thread's two vectors and bits 9 and up across the row's warps, whose
+// stages (the last, as in the reference's ascending order) go through one
+// shared-memory exchange.  Writes the row's codes and row scale.
 template <int LOGK, bool FP16, int MODE>
-__global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
-    const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
-    float* __restrict__ row_scale, float inv_sqrt_k) {
+__device__ __forceinline__ void fwht_quant_row_split(float (&v)[2][8], RowSplitSmem<LOGK, FP16>& sm,
+                                                     int warp, int lane, long long row,
+                                                     void* __restrict__ codes,
+                                                     float* __restrict__ row_scale,
+                                                     float inv_sqrt_k) {
   constexpr int K = 1 << LOGK;
   constexpr int NW = K / 512;      // warps per row (2 or 4)
   constexpr int RBITS = LOGK - 8;  // log2(K / 256): stages kept in fp32
   static_assert(RBITS <= 3, "fp32 stages must stay inside a vector");
-  __shared__ __align__(16) uint4 xchg[NW][2][32][FP16 ? 1 : 2];
-  __shared__ float warp_amax[NW];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long row = blockIdx.x;
-  pdl_launch_dependents();
-  pdl_wait();  // x is the previous kernel's output
-  if (row >= m) return;
-  float v[2][8];
-  const __half* xr = x + row * ldx + 512 * warp + 8 * lane;
-#pragma unroll
-  for (int c = 0; c < 2; ++c) load8_half_as_float(xr + 256 * c, v[c]);
   fwht_f32_bits<2, 0, RBITS>(v, lane);
   float mx = 0.f;
   if constexpr (FP16) {
@@ -377,14 +417,14 @@ __global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
     pack_half2<2>(v, h);
     fwht_h2_bits<2, RBITS, 9>(h, lane);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) xchg[warp][c][lane][0] = *reinterpret_cast<const uint4*>(h[c]);
+    for (int c = 0; c < 2; ++c) sm.xchg[warp][c][lane][0] = *reinterpret_cast<const uint4*>(h[c]);
     __syncthreads();
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       __half2 all[4][NW];
 #pragma unroll
       for (int u = 0; u < NW; ++u) {
-        const uint4 q = xchg[u][c][lane][0];
+        const uint4 q = sm.xchg[u][c][lane][0];
         const __half2* qh = reinterpret_cast<const __half2*>(&q);
 #pragma unroll
         for (int i = 0; i < 4; ++i) all[i][u] = qh[i];
@@ -399,10 +439,10 @@ __global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
     fwht_f32_bits<2, RBITS, 9>(v, lane);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
-      xchg[warp][c][lane][0] = make_uint4(__float_as_uint(v[c][0]), __float_as_uint(v[c][1]),
-                                          __float_as_uint(v[c][2]), __float_as_uint(v[c][3]));
-      xchg[warp][c][lane][1] = make_uint4(__float_as_uint(v[c][4]), __float_as_uint(v[c][5]),
-                                          __float_as_uint(v[c][6]), __float_as_uint(v[c][7]));
+      sm.xchg[warp][c][lane][0] = make_uint4(__float_as_uint(v[c][0]), __float_as_uint(v[c][1]),
+                                             __float_as_uint(v[c][2]), __float_as_uint(v[c][3]));
+      sm.xchg[warp][c][lane][1] = make_uint4(__float_as_uint(v[c][4]), __float_as_uint(v[c][5]),
+                                             __float_as_uint(v[c][6]), __float_as_uint(v[c][7]));
     }
     __syncthreads();
 #pragma unroll
@@ -410,7 +450,7 @@ __global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
       float all[8][NW];
 #pragma unroll
       for (int u = 0; u < NW; ++u) {
-        const uint4 q0 = xchg[u][c][lane][0], q1 = xchg[u][c][lane][1];
+        const uint4 q0 = sm.xchg[u][c][lane][0], q1 = sm.xchg[u][c][lane][1];
         all[0][u] = __uint_as_float(q0.x); all[1][u] = __uint_as_float(q0.y);
         all[2][u] = __uint_as_float(q0.z); all[3][u] = __uint_as_float(q0.w);
         all[4][u] = __uint_as_float(q1.x); all[5][u] = __uint_as_float(q1.y);
@@ -424,27 +464,50 @@ __global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
     }
   }
   mx = warp_max(mx);
-  if (lane == 0) warp_amax[warp] = mx;
+  if (lane == 0) sm.warp_amax[warp] = mx;
   __syncthreads();
-  mx = warp_amax[0];
+  mx = sm.warp_amax[0];
 #pragma unroll
-  for (int u = 1; u < NW; ++u) mx = fmaxf(mx, warp_amax[u]);
+  for (int u = 1; u < NW; ++u) mx = fmaxf(mx, sm.warp_amax[u]);
   const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
   const float rs = __frcp_rn(sdiv);
-  if (threadIdx.x == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+  if (warp == 0 && lane == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
 #pragma unroll
   for (int c = 0; c < 2; ++c)
     store_codes8<MODE>(codes, row * K + 512 * warp + 256 * c + 8 * lane, v[c], sdiv, rs);
+}
+
+// K = 1024 / 2048: one CTA of K / 16 threads (2 or 4 warps) per row, so a
+// 776-row activation is resident in one wave at ~21 warps per SM with short
+// per-thread dependency chains (layout: fwht_quant_row_split).
+template <int LOGK, bool FP16, int MODE>
+__global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
+    const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
+    float* __restrict__ row_scale, float inv_sqrt_k) {
+  __shared__ RowSplitSmem<LOGK, FP16> sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // x is the previous kernel's output
+  if (row >= m) return;
+  float v[2][8];
+  const __half* xr = x + row * ldx + 512 * warp + 8 * lane;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) load8_half_as_float(xr + 256 * c, v[c]);
+  fwht_quant_row_split<LOGK, FP16, MODE>(v, sm, warp, lane, row, codes, row_scale, inv_sqrt_k);
 }
 
 // K = 16384: one 256-thread CTA per row.  Phase 1: warp w transforms its
 // 2048-element slice (index bits 0-10) in registers.  Phase 2: after a
 // shared-memory transpose, thread (c, l) = (warp, lane) holds the 8 slices'
 // values at offsets 256c + 8l + j and finishes bits 11-13 in registers.
-template <bool FP16, int MODE>
+// GEGLU: the row is gelu_tanh(x) * up (x = the gate), formed as it is
+// loaded (geglu8) and, when h_out is not null, also written there.
+template <bool FP16, int MODE, bool GEGLU = false>
 __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
-    float* __restrict__ row_scale, float inv_sqrt_k) {
+    float* __restrict__ row_scale, float inv_sqrt_k, const __half* __restrict__ up = nullptr,
+    long long ldu = 0, __half* __restrict__ h_out = nullptr, long long ldh = 0) {
   constexpr int K = 16384;
   constexpr int RBITS = 6;  // log2(16384 / 256)
   extern __shared__ __align__(16) unsigned char quant_smem[];
@@ -458,8 +521,18 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
   float v[8][8];
   {
     const __half* xr = x + row * ldx + 2048 * warp + 8 * lane;
+    if constexpr (GEGLU) {
+      const __half* ur = up + row * ldu + 2048 * warp + 8 * lane;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) load8_half_as_float(xr + 256 * c, v[c]);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 h8 = geglu8(ld_nc_v4(xr + 256 * c), ld_nc_v4(ur + 256 * c));
+        if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 2048 * warp + 8 * lane + 256 * c) = h8;
+        half8_to_float(h8, v[c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) load8_half_as_float(xr + 256 * c, v[c]);
+    }
     fwht_f32_bits<8, 0, RBITS>(v, lane);
     if constexpr (FP16) {
       __half2 h[8][4];
@@ -551,16 +624,23 @@ constexpr int kQ16RowBytes = 16384 * 2;
 constexpr int kQ16Smem = kQ16RowBytes + 1024;
 constexpr int kQ16CtasPerSm = 3;
 
+// GEGLU: two row buffers (gate, up), both loaded by TMA.
+constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
+
 // One CTA per row (the block scheduler hands rows to SMs as CTAs finish,
 // which balanced the 776-row prefix better than persistent CTAs with a
 // prefetched second row: 17.1 vs 18.6 us).  One thread loads the row with
 // TMA (a 3-D map {64, 256, M} of 128-byte lines, 128-byte swizzle).  The
 // swizzle puts 16-byte chunk c of line u at chunk c ^ (u & 7): thread u
 // reads its line (elements 64u .. 64u + 63) without bank conflicts.
-template <int MODE>
+// GEGLU: xmap is the gate and umap the up projection (same shape); the row
+// quantised is gelu_tanh(gate) * up, formed in phase A (geglu8) and, when
+// h_out is not null, written there too.  Otherwise umap is unused.
+template <int MODE, bool GEGLU = false>
 __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
     const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
-    float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns) {
+    float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns,
+    const __grid_constant__ CUtensorMap umap, __half* __restrict__ h_out, long long ldh) {
   constexpr int K = 16384;
   extern __shared__ unsigned char quant_smem[];
   __shared__ float warp_amax[kQuantThreads / 32];
@@ -581,8 +661,9 @@ __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp
   pdl_wait();  // x is the previous kernel's output
   if (row >= m) return;
   if (u == 0) {
-    mbar_arrive_expect_tx(bar_a, kQ16RowBytes);
+    mbar_arrive_expect_tx(bar_a, GEGLU ? 2 * kQ16RowBytes : kQ16RowBytes);
     tma_load_3d(smem_addr(base), &xmap, 0, 0, static_cast<int>(row), bar_a);
+    if constexpr (GEGLU) tma_load_3d(smem_addr(base + kQ16RowBytes), &umap, 0, 0, static_cast<int>(row), bar_a);
   }
   if (!mbar_wait_bounded(bar_a, 0, &abort_flag, &g_w4a4_device_error, kErrWaitTma, limit_ns))
     return;
@@ -593,7 +674,11 @@ __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp
     float v[8][8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const uint4 raw = buf[8 * u + (c ^ (u & 7))];
+      uint4 raw = buf[8 * u + (c ^ (u & 7))];
+      if constexpr (GEGLU) {
+        raw = geglu8(raw, buf[2048 + 8 * u + (c ^ (u & 7))]);
+        if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 64 * u + 8 * c) = raw;
+      }
       const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {

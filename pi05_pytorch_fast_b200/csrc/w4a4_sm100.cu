@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
+#include "layer.cuh"
 #include "quant.cuh"
 
 // Scratch of w4a4_int4_gemm_noalloc: the intermediate activation codes and
@@ -109,7 +110,7 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 // ------------------------------------------------------------- device info
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
-unsigned g_attr_done[kMaxDevices];  // bit per kernel whose smem attribute is set
+uint64_t g_attr_done[kMaxDevices];  // bit per kernel whose smem attribute is set
 std::mutex g_dev_mu;
 
 int current_device(int* dev) {
@@ -130,7 +131,7 @@ int sm_count(int dev, int* out) {
 }
 
 template <class Kernel>
-int ensure_smem_attr(int dev, unsigned bit, Kernel kernel, int bytes) {
+int ensure_smem_attr(int dev, uint64_t bit, Kernel kernel, int bytes) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
   if (!(g_attr_done[dev] & bit)) {
     W4A4_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
@@ -334,10 +335,13 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
         }
         err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE>, dim3(grid),
                                              dim3(kQuantThreads), kQ16Smem, stream, 1, xmap, m, codes,
-                                             row_scale, isk, g_wait_limit_ns.load()));
+                                             row_scale, isk, g_wait_limit_ns.load(), xmap,
+                                             static_cast<__half*>(nullptr), 0ll));
       } else
         err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<F, MODE>, dim3(grid), dim3(kQuantThreads),
-                                             smem, stream, 1, xh, ldx, m, codes, row_scale, isk));
+                                             smem, stream, 1, xh, ldx, m, codes, row_scale, isk,
+                                             static_cast<const __half*>(nullptr), 0ll,
+                                             static_cast<__half*>(nullptr), 0ll));
     });
   } else {
     dispatch([&](auto, auto mode) {
@@ -347,6 +351,167 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
     });
   }
   if (err_code) return err_code;
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+// ------------------------------------------------------------- layer glue
+int check_codes_format(int32_t codes_format) {
+  if (codes_format != W4A4_CODES_INT8 && codes_format != W4A4_CODES_PACKED &&
+      codes_format != W4A4_CODES_GEMM)
+    return fail(W4A4_ERR_INVALID, "unknown codes format %d", codes_format);
+  return W4A4_OK;
+}
+
+// Calls launch(std::integral_constant<bool, FP16>, std::integral_constant<int, MODE>)
+// for the runtime staging and codes format.
+template <typename Launch>
+void dispatch_staging_format(bool fp16, int32_t codes_format, Launch&& launch) {
+  const auto by_mode = [&](auto fp16_tag) {
+    constexpr bool F = decltype(fp16_tag)::value;
+    switch (codes_format) {
+      case W4A4_CODES_PACKED: launch(std::integral_constant<bool, F>{}, std::integral_constant<int, kCodesPacked>{}); break;
+      case W4A4_CODES_GEMM: launch(std::integral_constant<bool, F>{}, std::integral_constant<int, kCodesGemm>{}); break;
+      default: launch(std::integral_constant<bool, F>{}, std::integral_constant<int, kCodesInt8>{}); break;
+    }
+  };
+  if (fp16) by_mode(std::true_type{});
+  else by_mode(std::false_type{});
+}
+
+int launch_rmsnorm_quant(const void* x, int64_t ldx, const void* delta, int64_t ldd, const float* gain,
+                         float eps, void* x_out, int64_t ldo, void* h_out, int64_t ldh, int64_t m,
+                         int32_t k, int32_t staging, int32_t codes_format, void* codes,
+                         float* row_scale, cudaStream_t stream) {
+  if (k != kNormK) return fail(W4A4_ERR_UNSUPPORTED, "rmsnorm_quant supports K = %d only, got %d", kNormK, k);
+  if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative, got %lld", (long long)m);
+  if (staging != W4A4_STAGING_FP16 && staging != W4A4_STAGING_FP32)
+    return fail(W4A4_ERR_INVALID, "unknown staging mode %d", staging);
+  if (int e = check_codes_format(codes_format)) return e;
+  if (!codes && !h_out) return fail(W4A4_ERR_INVALID, "rmsnorm_quant needs codes or h_out");
+  if (codes && !row_scale) return fail(W4A4_ERR_INVALID, "codes need a row_scale output");
+  if (m == 0) return ok();
+  if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large: %lld", (long long)m);
+  if (!x || !gain) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  const auto row_ok = [&](const void* p, int64_t ld) {
+    return !p || (aligned(p, 16) && ld >= k && ld % 8 == 0);
+  };
+  if (!row_ok(x, ldx) || !row_ok(delta, ldd) || !row_ok(x_out, ldo) || !row_ok(h_out, ldh))
+    return fail(W4A4_ERR_INVALID,
+                "rows must be 16-byte aligned with a stride >= K and a multiple of 8 elements");
+  if (!aligned(gain, 16)) return fail(W4A4_ERR_INVALID, "gain pointer must be 16-byte aligned");
+  if (codes && !aligned(codes, 8)) return fail(W4A4_ERR_INVALID, "codes pointer must be 8-byte aligned");
+  const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* dh = static_cast<const __half*>(delta);
+  __half* xo = static_cast<__half*>(x_out);
+  __half* ho = static_cast<__half*>(h_out);
+  int err_code = W4A4_OK;
+  const dim3 grid(static_cast<unsigned>(m)), block(kNormThreads);
+  const auto go = [&](auto kernel) {
+    err_code = cuda_status(launch_kernel(kernel, grid, block, 0, stream, 1, xh, ldx, dh, ldd, gain, eps,
+                                         xo, ldo, ho, ldh, m, codes, row_scale, isk));
+  };
+  if (!codes) {  // the norm alone (staging and codes format unused)
+    if (delta) go(rmsnorm_quant_kernel<true, false, true, kCodesInt8>);
+    else go(rmsnorm_quant_kernel<false, false, true, kCodesInt8>);
+  } else {
+    dispatch_staging_format(staging == W4A4_STAGING_FP16, codes_format, [&](auto f, auto mode) {
+      constexpr bool F = decltype(f)::value;
+      constexpr int MODE = decltype(mode)::value;
+      if (delta) go(rmsnorm_quant_kernel<true, true, F, MODE>);
+      else go(rmsnorm_quant_kernel<false, true, F, MODE>);
+    });
+  }
+  if (err_code) return err_code;
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int launch_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int64_t ld,
+                       int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                       void* h_out, int64_t ldh, cudaStream_t stream) {
+  if (k != 16384)
+    return fail(W4A4_ERR_UNSUPPORTED, "geglu_quant supports K = 16384 only, got %d", k);
+  if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative, got %lld", (long long)m);
+  if (staging != W4A4_STAGING_FP16 && staging != W4A4_STAGING_FP32)
+    return fail(W4A4_ERR_INVALID, "unknown staging mode %d", staging);
+  if (int e = check_codes_format(codes_format)) return e;
+  if (m == 0) return ok();
+  if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large: %lld", (long long)m);
+  if (!gate || !up || !codes || !row_scale) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (!aligned(gate, 16) || !aligned(up, 16) || ld < k || ld % 8 != 0)
+    return fail(W4A4_ERR_INVALID,
+                "gate/up rows must be 16-byte aligned with a stride >= K and a multiple of 8 elements");
+  if (h_out && (!aligned(h_out, 16) || ldh < k || ldh % 8 != 0))
+    return fail(W4A4_ERR_INVALID, "h_out rows must be 16-byte aligned with a stride >= K, multiple of 8");
+  if (!aligned(codes, 8)) return fail(W4A4_ERR_INVALID, "codes pointer must be 8-byte aligned");
+  int dev;
+  if (int e = current_device(&dev)) return e;
+  const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
+  const unsigned grid = static_cast<unsigned>(m);
+  __half* ho = static_cast<__half*>(h_out);
+  int err_code = W4A4_OK;
+  dispatch_staging_format(staging == W4A4_STAGING_FP16, codes_format, [&](auto f, auto mode) {
+    constexpr bool F = decltype(f)::value;
+    constexpr int MODE = decltype(mode)::value;
+    if constexpr (F) {
+      CUtensorMap gmap, umap;
+      const uint64_t dims[3] = {64, 256, static_cast<uint64_t>(m)};
+      const uint64_t strides[2] = {128, static_cast<uint64_t>(ld) * 2};
+      const uint32_t box[3] = {64, 256, 1};
+      if (int e = make_map(&gmap, gate, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B)) {
+        err_code = e;
+        return;
+      }
+      if (int e = make_map(&umap, up, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B)) {
+        err_code = e;
+        return;
+      }
+      if (int e = ensure_smem_attr(dev, 1ull << (32 + MODE), quant_rot_16k_fp16_kernel<MODE, true>,
+                                   kQ16SmemGeglu)) {
+        err_code = e;
+        return;
+      }
+      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, true>, dim3(grid),
+                                           dim3(kQuantThreads), kQ16SmemGeglu, stream, 1, gmap, m, codes,
+                                           row_scale, isk, g_wait_limit_ns.load(), umap, ho, ldh));
+    } else {
+      const int smem = 16384 * 4;
+      if (int e = ensure_smem_attr(dev, 1ull << (36 + MODE), quant_rot_16k_kernel<false, MODE, true>, smem)) {
+        err_code = e;
+        return;
+      }
+      err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<false, MODE, true>, dim3(grid),
+                                           dim3(kQuantThreads), smem, stream, 1,
+                                           static_cast<const __half*>(gate), ld, m, codes, row_scale, isk,
+                                           static_cast<const __half*>(up), ld, ho, ldh));
+    }
+  });
+  if (err_code) return err_code;
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int launch_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
+                const void* sin_t, int64_t m, int32_t heads, cudaStream_t stream) {
+  if (m < 0 || heads <= 0) return fail(W4A4_ERR_INVALID, "invalid rope shape: m=%lld heads=%d", (long long)m, heads);
+  if (m == 0) return ok();
+  if (!x || !out || !cos_t || !sin_t) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  const int64_t width = static_cast<int64_t>(heads) * kRopeHeadDim;
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(cos_t, 16) || !aligned(sin_t, 16) ||
+      ldx < width || ldo < width || ldx % 8 || ldo % 8)
+    return fail(W4A4_ERR_INVALID,
+                "rope rows must be 16-byte aligned with strides >= heads * 256, multiples of 8");
+  const int64_t threads = m * heads * (kRopeHeadDim / 16);
+  const int64_t blocks = (threads + 255) / 256;
+  if (blocks > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "rope: too many rows");
+  W4A4_CUDA_TRY(launch_kernel(rope_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
+                              static_cast<const __half*>(x), ldx, static_cast<__half*>(out), ldo,
+                              static_cast<const __half*>(cos_t), static_cast<const __half*>(sin_t), m,
+                              heads));
   W4A4_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -708,6 +873,26 @@ int w4a4_int4_gemm_noalloc(const void* x, int64_t m, int32_t k, int64_t ldx, int
   float* scales = nullptr;
   if (int e = noalloc_buffers(&codes, &scales)) return e;
   return w4a4_int4_gemm(x, m, k, ldx, rotate, staging, n_weights, weights, y, codes, scales, stream);
+}
+
+int w4a4_rmsnorm_quant(const void* x, int64_t ldx, const void* delta, int64_t ldd,
+                       const float* gain, float eps, void* x_out, int64_t ldo, void* h_out,
+                       int64_t ldh, int64_t m, int32_t k, int32_t staging, int32_t codes_format,
+                       void* codes, float* row_scale, void* stream) {
+  return launch_rmsnorm_quant(x, ldx, delta, ldd, gain, eps, x_out, ldo, h_out, ldh, m, k, staging,
+                              codes_format, codes, row_scale, static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int64_t ld,
+                     int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                     void* h_out, int64_t ldh, void* stream) {
+  return launch_geglu_quant(gate, up, m, k, ld, staging, codes_format, codes, row_scale, h_out, ldh,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
+              const void* sin_t, int64_t m, int32_t heads, void* stream) {
+  return launch_rope(x, ldx, out, ldo, cos_t, sin_t, m, heads, static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,

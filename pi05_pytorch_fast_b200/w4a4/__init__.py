@@ -1,4 +1,10 @@
-"""B200 W4A4 path behind the reference's ``pi05_fast.w4a4`` interface."""
+"""B200 W4A4 ops behind the reference's ``pi05_fast.w4a4`` op interface.
+
+Importing registers the five ``pi05_w4a4::*`` custom ops on the sm_100a
+kernels.  The reference's own model glue (``pi05_fast/w4a4/linear.py``,
+``apply.py``) then runs unmodified on them; this package's own caller of
+the path is ``pi05_pytorch_fast_b200.prefix_lm``.
+"""
 
 from .extension import (
     int4_gemm,
@@ -8,14 +14,9 @@ from .extension import (
     int4_gemm_tiled,
     preload,
 )
-from .linear import W4A4Linear
 from .pack import pack_linear_weight, preshuffle_wmma_weight
-from .apply import apply_w4a4_from_dir, maybe_apply_w4a4_from_env
 
 __all__ = [
-    "W4A4Linear",
-    "apply_w4a4_from_dir",
-    "maybe_apply_w4a4_from_env",
     "pack_linear_weight",
     "preshuffle_wmma_weight",
     "int4_gemm",

@@ -1,0 +1,199 @@
+"""GPU parity of the fused prefix-LM layer kernels (w4a4_rmsnorm_quant,
+w4a4_geglu_quant, w4a4_rope), called through the C ABI.
+
+The glue each kernel fuses is floating-point PyTorch in the reference
+(pi05_fast/w4a4/apply.py:126-191 over transformers' Gemma layer), so its
+check is PyTorch's own eager CUDA result on the same GPU:
+
+* GeGLU (F.gelu(gate, approximate="tanh") * up) and RoPE
+  (apply_rotary_pos_emb): bit-exact;
+* the residual add: bit-exact; GemmaRMSNorm: within one fp16 ulp (the mean
+  of squares is summed in another order), almost always equal;
+* the codes and row scales that follow: bit-exact against the CPU oracle fed
+  the kernel's own normalised / GeGLU values (written to h_out).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import w4a4_oracle as orc
+from pi05_pytorch_fast_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+STAGINGS = {"fp16": nat.STAGING_FP16, "fp32": nat.STAGING_FP32}
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_device_errors():
+    nat.device_error(clear=True)
+    yield
+    assert nat.device_error(clear=True) == 0, "a kernel's bounded wait ran out"
+
+
+def _stream():
+    return torch.cuda.current_stream(DEV).cuda_stream
+
+
+def geglu_quant(gate, up, staging, h_out=True):
+    m, k = gate.shape
+    codes = torch.empty((m, k), dtype=torch.int8, device=DEV)
+    scales = torch.empty((m,), dtype=torch.float32, device=DEV)
+    h = torch.empty_like(gate) if h_out else None
+    nat.check(nat.lib().w4a4_geglu_quant(gate.data_ptr(), up.data_ptr(), m, k, gate.stride(0),
+                                         staging, nat.CODES_INT8, codes.data_ptr(), scales.data_ptr(),
+                                         h.data_ptr() if h is not None else None, k, _stream()))
+    return codes, scales, h
+
+
+def rmsnorm_quant(x, delta, gain, eps, staging, quant=True, x_out=None):
+    m, k = x.shape
+    h = torch.empty_like(x)
+    codes = torch.empty((m, k), dtype=torch.int8, device=DEV) if quant else None
+    scales = torch.empty((m,), dtype=torch.float32, device=DEV) if quant else None
+    nat.check(nat.lib().w4a4_rmsnorm_quant(
+        x.data_ptr(), x.stride(0), delta.data_ptr() if delta is not None else None, k,
+        gain.data_ptr(), eps, x_out.data_ptr() if x_out is not None else None, k, h.data_ptr(), k,
+        m, k, staging, nat.CODES_INT8, codes.data_ptr() if quant else None,
+        scales.data_ptr() if quant else None, _stream()))
+    return h, codes, scales
+
+
+def assert_half_equal(a: torch.Tensor, b: torch.Tensor):
+    """Bit-exact fp16 equality, NaN payloads aside."""
+    a16 = a.view(torch.int16).cpu().numpy()
+    b16 = b.view(torch.int16).cpu().numpy()
+    both_nan = torch.isnan(a).cpu().numpy() & torch.isnan(b).cpu().numpy()
+    bad = (a16 != b16) & ~both_nan
+    assert not bad.any(), f"{int(bad.sum())} of {bad.size} values differ; first at {np.argwhere(bad)[:3]}"
+
+
+def assert_codes_match_oracle(h: torch.Tensor, codes, scales, staging):
+    qa, sa = orc.quant_activation(h.cpu().numpy(), rotate=True, staging=staging)
+    np.testing.assert_array_equal(codes.cpu().numpy(), qa)
+    np.testing.assert_array_equal(scales.cpu().numpy().view(np.int32), sa.view(np.int32))
+
+
+# ----------------------------------------------------------------------------- GeGLU
+def test_gelu_of_every_finite_fp16_value_matches_torch():
+    """gelu_tanh(x) for all 63,488 finite fp16 x (up = 1, so h = fl16(gelu))."""
+    bits = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16)
+    vals = bits.view(torch.float16)
+    vals = vals[torch.isfinite(vals)]
+    k = 16384
+    m = -(-vals.numel() // k)
+    gate = torch.zeros(m * k, dtype=torch.float16)
+    gate[: vals.numel()] = vals
+    gate = gate.view(m, k).to(DEV)
+    up = torch.ones_like(gate)
+    _, _, h = geglu_quant(gate, up, nat.STAGING_FP16)
+    ref = F.gelu(gate, approximate="tanh")
+    torch.cuda.synchronize()
+    assert_half_equal(h, ref)
+
+
+@pytest.mark.parametrize("staging", list(STAGINGS))
+@pytest.mark.parametrize("m", [1, 5, 776])
+def test_geglu_quant_matches_torch_and_oracle(staging, m):
+    gen = torch.Generator(device=DEV).manual_seed(11 + m)
+    gate = (torch.randn(m, 16384, device=DEV, generator=gen) * 1.5).half()
+    up = torch.randn(m, 16384, device=DEV, generator=gen).half()
+    codes, scales, h = geglu_quant(gate, up, STAGINGS[staging])
+    ref = F.gelu(gate, approximate="tanh") * up
+    torch.cuda.synchronize()
+    assert_half_equal(h, ref)
+    assert_codes_match_oracle(ref, codes, scales, staging)
+
+
+def test_geglu_quant_without_h_out_gives_the_same_codes():
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    gate = torch.randn(64, 16384, device=DEV, generator=gen).half()
+    up = torch.randn(64, 16384, device=DEV, generator=gen).half()
+    c1, s1, _ = geglu_quant(gate, up, nat.STAGING_FP16)
+    c2, s2, _ = geglu_quant(gate, up, nat.STAGING_FP16, h_out=False)
+    assert torch.equal(c1, c2) and torch.equal(s1, s2)
+
+
+# ----------------------------------------------------------------------------- RMSNorm
+def gemma_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """transformers' GemmaRMSNorm.forward (fp32 math, (1 + w) gain, cast back)."""
+    xf = x.float()
+    out = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (out * (1.0 + weight.float())).type_as(x)
+
+
+@pytest.mark.parametrize("staging", list(STAGINGS))
+@pytest.mark.parametrize("with_delta", [False, True])
+@pytest.mark.parametrize("m", [1, 3, 776])
+def test_rmsnorm_quant_matches_torch_and_oracle(staging, with_delta, m):
+    gen = torch.Generator(device=DEV).manual_seed(5 * m + with_delta)
+    x = (torch.randn(m, 2048, device=DEV, generator=gen) * 3).half()
+    x[:, :20] *= 20  # outlier channels
+    delta = torch.randn(m, 2048, device=DEV, generator=gen).half() if with_delta else None
+    w = (torch.randn(2048, device=DEV, generator=gen) * 0.1).half()
+    gain = (1.0 + w.float()).contiguous()
+    eps = 1e-6
+    x_out = torch.empty_like(x)
+    h, codes, scales = rmsnorm_quant(x, delta, gain, eps, STAGINGS[staging], x_out=x_out)
+    s_ref = x + delta if with_delta else x
+    h_ref = gemma_rmsnorm(s_ref, w, eps)
+    torch.cuda.synchronize()
+    assert_half_equal(x_out, s_ref)
+    d = (h.float() - h_ref.float()).abs()
+    ulp = torch.finfo(torch.float16).eps * h_ref.float().abs().clamp_min(2.0 ** -14)
+    assert bool((d <= ulp).all()), float((d / ulp).max())
+    assert float((d > 0).float().mean()) < 2e-3
+    assert_codes_match_oracle(h, codes, scales, staging)
+
+
+def test_rmsnorm_in_place_residual_and_norm_only():
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn(40, 2048, device=DEV, generator=gen).half()
+    delta = torch.randn(40, 2048, device=DEV, generator=gen).half()
+    w = (torch.randn(2048, device=DEV, generator=gen) * 0.1).half()
+    gain = (1.0 + w.float()).contiguous()
+    s_ref = x + delta
+    h_q, _, _ = rmsnorm_quant(x.clone(), delta, gain, 1e-6, nat.STAGING_FP16)
+    h, _, _ = rmsnorm_quant(x, delta, gain, 1e-6, nat.STAGING_FP16, quant=False, x_out=x)
+    torch.cuda.synchronize()
+    assert_half_equal(x, s_ref)      # x updated in place
+    assert_half_equal(h, h_q)        # the norm alone equals the norm inside the fused kernel
+
+
+# ----------------------------------------------------------------------------- RoPE
+def hf_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, heads: int) -> torch.Tensor:
+    """transformers' apply_rotary_pos_emb on [1, heads, M, 256] (fp16)."""
+    m = x.shape[0]
+    xh = x.view(m, heads, 256).transpose(0, 1).unsqueeze(0)
+    x1, x2 = xh[..., :128], xh[..., 128:]
+    rot = torch.cat((-x2, x1), dim=-1)
+    out = (xh * cos[None, None]) + (rot * sin[None, None])
+    return out.squeeze(0).transpose(0, 1).reshape(m, heads * 256)
+
+
+@pytest.mark.parametrize("heads", [1, 8])
+def test_rope_matches_transformers(heads):
+    m = 776
+    gen = torch.Generator(device=DEV).manual_seed(heads)
+    x = (torch.randn(m, heads * 256, device=DEV, generator=gen) * 2).half()
+    pos = torch.arange(m, device=DEV)
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, 256, 2, dtype=torch.int64).float() / 256))
+    freqs = pos[:, None].float() * inv_freq.to(DEV)[None]
+    emb = torch.cat((freqs, freqs), -1)
+    cos, sin = emb.cos().half().contiguous(), emb.sin().half().contiguous()
+    out = torch.empty_like(x)
+    nat.check(nat.lib().w4a4_rope(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0),
+                                  cos.data_ptr(), sin.data_ptr(), m, heads, _stream()))
+    ref = hf_rope(x, cos, sin, heads)
+    torch.cuda.synchronize()
+    assert_half_equal(out, ref)
+    # in place gives the same
+    nat.check(nat.lib().w4a4_rope(x.data_ptr(), x.stride(0), x.data_ptr(), x.stride(0),
+                                  cos.data_ptr(), sin.data_ptr(), m, heads, _stream()))
+    torch.cuda.synchronize()
+    assert_half_equal(x, ref)

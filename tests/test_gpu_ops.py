@@ -177,16 +177,17 @@ def test_error_messages_match_reference():
         torch.ops.pi05_w4a4.int4_gemm_tiled(torch.randn(2, 2048, device=DEV).half(), p)
 
 
-def test_w4a4_linear_matches_oracle(staging):
-    from pi05_pytorch_fast_b200.w4a4 import W4A4Linear
-
+def test_op_on_fp32_caller_input_matches_oracle(staging):
+    """What the reference's W4A4Linear.forward does around the op
+    (linear.py:50-59): an fp32 caller tensor cast to fp16, the op, the
+    result cast back, plus a bias."""
     lin = torch.nn.Linear(2048, 320, bias=True)
-    mod = W4A4Linear.from_linear(lin).to(DEV)
+    packed = pack_linear_weight(lin.weight)
     x = orc.make_activations(40, 2048, 11)
-    y = mod(to_dev(x).float())  # fp32 in -> fp16 op -> cast back to fp32, + bias
-    assert y.dtype == torch.float32
-    packed = pack_linear_weight(lin.weight).numpy()
-    ref = orc.int4_gemm_ref(x, packed, staging=staging).astype(np.float32) + lin.bias.detach().numpy()
+    xf = to_dev(x).float()
+    y = torch.ops.pi05_w4a4.int4_gemm(xf.half().contiguous(), F.pad(packed, (0, 7)).to(DEV)).float()
+    y = y + lin.bias.detach().to(DEV)
+    ref = orc.int4_gemm_ref(x, packed.numpy(), staging=staging).astype(np.float32) + lin.bias.detach().numpy()
     np.testing.assert_array_equal(to_np(y), ref)
 
 
