@@ -18,7 +18,8 @@
  *   pi05_fast/w4a4/apply.py:68-69             row padding     -> w4a4_pad_rows
  *   pi05_fast/w4a4/csrc/int4_gemm.cu:487-501  TORCH_CHECK text-> w4a4_last_error
  *   pi05_fast/w4a4/apply.py:126-191           layer glue      -> w4a4_rmsnorm_quant,
- *                                                                w4a4_geglu_quant, w4a4_rope
+ *                                                                w4a4_geglu_quant, w4a4_rope,
+ *                                                                w4a4_prefix_attention
  */
 #ifndef W4A4_SM100_H_
 #define W4A4_SM100_H_
@@ -169,6 +170,27 @@ int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int
  * out may equal x. */
 int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
               const void* sin_t, int64_t m, int32_t heads, void* stream);
+
+/* Bidirectional prefix attention with one shared key/value head (Gemma-2B:
+ * 8 query heads, 1 kv head, head_dim 256) on the tensor cores.  Replaces
+ * the reference's eager attention (apply.py:170-188, transformers'
+ * eager_attention_forward) under lerobot's prefix mask: query i of
+ * observation b sees key j iff key_valid[b, i] and key_valid[b, j]; a query
+ * with key_valid 0 averages all seq values (its all-masked fp32 softmax is
+ * uniform).  Scores in fp32 (scale 1/16 = 256^-0.5), softmax in fp32,
+ * probabilities rounded to fp16 for the P V product, fp32 accumulation.
+ *   q          fp16 [batch * seq, ldq], heads x 256 per row (after RoPE)
+ *   k, v       fp16 [batch * seq, ldk / ldv], 256 per row (k after RoPE)
+ *   key_valid  uint8 [batch, seq] (1 = real token)
+ *   kv_len     int32 [batch]: every key at or past kv_len[b] is padding
+ *   vt_scratch fp16 [batch, 256, W4A4_ATTN_VT_STRIDE(seq)]: V transposed
+ *   out        fp16 [batch * seq, ldo], heads x 256 per row
+ * heads must divide 128; seq <= 4096.  Two launches (V transpose, attention). */
+#define W4A4_ATTN_VT_STRIDE(seq) ((((int64_t)(seq)) + 7) / 8 * 8)
+int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                          int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
+                          int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
+                          void* stream);
 
 /* Copy a row-major packed weight [n, src_row_words] into [n, dst_row_words]
  * (dst_row_words >= src_row_words), zero-filling the new words: the

@@ -30,6 +30,7 @@ GEMM_SINGLE_CTA = 0
 GEMM_CTA_PAIR = 1
 GEMM_NO_SPLIT = 2
 GEMM_SPLIT_K = 3
+ATTN_MAX_SEQ = 4096
 NOALLOC_MAX_ROWS = 65536
 NOALLOC_MAX_CODES = 16 * 1024 * 1024
 
@@ -43,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "w4a4_rmsnorm_quant",
     "w4a4_geglu_quant",
     "w4a4_rope",
+    "w4a4_prefix_attention",
     "w4a4_pad_rows",
     "w4a4_last_error",
     "w4a4_device_error",
@@ -92,6 +94,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                        c_i64, c_i64, c_i32, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_geglu_quant.argtypes = [vp, vp, c_i64, c_i32, c_i64, c_i32, c_i32, vp, vp, vp, c_i64, vp]
     lib.w4a4_rope.argtypes = [vp, c_i64, vp, c_i64, vp, vp, c_i64, c_i32, vp]
+    lib.w4a4_prefix_attention.argtypes = [vp, c_i64, vp, c_i64, vp, c_i64, vp, vp, c_i32, c_i32, c_i32,
+                                          vp, vp, c_i64, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]
@@ -160,6 +164,11 @@ def gemm_plan(m: int, k: int, ns, sms: int = 148, variant: int = GEMM_SINGLE_CTA
     check(lib().w4a4_gemm_plan(m, k, len(ns), n_arr, sms, variant, layout, out))
     return {"tok_tile": out[0], "split": bool(out[1]), "grid": out[2], "tok_tiles": out[3],
             "tok_group": out[4], "w_tiles": out[5]}
+
+
+def attn_vt_stride(seq: int) -> int:
+    """Row stride (elements) of the V^T scratch of w4a4_prefix_attention."""
+    return (seq + 7) // 8 * 8
 
 
 def weights_array(descs) -> ctypes.Array:

@@ -1,0 +1,444 @@
+// Prefix attention of the Gemma-2B prefix LM on the sm_100a tensor cores
+// (tcgen05.mma kind::f16, fp32 accumulators in TMEM).
+//
+// Replaces the reference's eager attention over the prefix
+// (pi05_fast/w4a4/apply.py:170-188: transformers' eager_attention_forward,
+// 8 query heads sharing 1 key/value head, head_dim 256) with the padding mask
+// of a bidirectional prefix: query i sees key j iff both are real tokens; a
+// padded query sees no key, so its softmax is uniform over all L keys (the
+// result of the all-masked row in the reference's fp32 softmax).
+//
+// Design (one CTA per 128 (token, head) rows of one observation):
+//  * the CTA's rows are `128 / heads` consecutive tokens x all heads, so every
+//    row shares the one key/value head: Q is one 64 KB TMA load (4-D map
+//    {d, head, token, batch}, 128-byte swizzle), K and V^T stream in blocks
+//    of 64 keys through a two-stage ring (32 KB each);
+//  * warp 1 issues S = Q K^T (M = 128, N = 64, 16 MMAs of K = 16 over d) into
+//    one of two TMEM score buffers, and O += P V^T (M = 128, N = 256, 4 MMAs of
+//    K = 16 keys) with P read from TMEM (the A operand of the TS form);
+//  * warps 2-5 (one per TMEM lane quarter, thread = row) run the softmax:
+//    pass 1 reads each score block once for the row max and sum; pass 2
+//    recomputes the block, writes p = exp(s - max) as fp16 into TMEM for the
+//    PV MMA; then they scale O by 1 / sum and store fp16 rows;
+//  * key blocks past the last real key are skipped for tiles of real queries;
+//  * every wait is bounded (the device error word, an abort flag, teardown
+//    that drains its copies and MMAs and frees TMEM).
+// Softmax is base 2: s2 = acc * (scale * log2 e), p = exp2(s2 - max2).
+#pragma once
+
+#include "common.cuh"
+
+namespace w4a4 {
+
+constexpr int kAttnRows = 128;            // UMMA M: (token, head) rows of a CTA
+constexpr int kAttnHeadDim = 256;
+constexpr int kAttnKeyBlock = 64;         // keys per pipeline step (UMMA N of S)
+constexpr int kAttnMaxKeys = 4096;        // longest prefix (key-mask words in shared memory)
+constexpr int kAttnSlices = kAttnHeadDim / 64;                     // 128-byte rows of 64 fp16
+constexpr int kAttnQBytes = kAttnRows * kAttnHeadDim * 2;          // 64 KB
+constexpr int kAttnKBytes = kAttnKeyBlock * kAttnHeadDim * 2;      // 32 KB
+constexpr int kAttnVBytes = kAttnHeadDim * kAttnKeyBlock * 2;      // 32 KB
+constexpr int kAttnStages = 2;
+constexpr int kAttnThreads = 192;                                  // 6 warps
+constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 1;      // q, k/v full/empty, s/p full/free, o
+constexpr int kAttnSmem = kAttnQBytes + kAttnStages * (kAttnKBytes + kAttnVBytes) +
+                          kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + 1024;
+// TMEM columns: O [0, 256), S buffers at 256 and 320 (64 each), P buffers at
+// 384 and 416 (32 columns: 64 fp16 per row).
+constexpr uint32_t kAttnTmemCols = 512;
+constexpr uint32_t kAttnOCol = 0, kAttnSCol = 256, kAttnPCol = 384;
+
+struct alignas(64) AttnParams {
+  CUtensorMap tmap_q;   // fp16 {256 d, heads, L, B}, box {64, heads, 128 / heads, 1}, SW128
+  CUtensorMap tmap_k;   // fp16 {256 d, L, B}, box {64, 64, 1}, SW128
+  CUtensorMap tmap_vt;  // fp16 {L, 256 d, B} (V transposed per observation), box {64, 256, 1}, SW128
+  const uint8_t* key_valid;  // [B, L]: 1 = real token
+  const int* kv_len;         // [B]: keys past this index are all padding
+  __half* out;               // [B * L, ldo], row (b, t) columns head * 256 + d
+  long long ldo;
+  int seq;
+  int heads;
+  float scale_log2;          // head_dim^-0.5 * log2(e)
+  unsigned long long wait_limit_ns;
+};
+
+// Instruction descriptor of tcgen05.mma.kind::f16: D = f32, A and B fp16,
+// both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4)                                  // D format: F32
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, fp16 x fp16 -> fp32, K = 16.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, fp16 x fp16 -> fp32, K = 16: A is
+// M rows in TMEM lanes, 16 fp16 in 8 consecutive 32-bit columns.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 4-D tiled bulk tensor load global -> shared (x innermost, in elements).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int x, int y, int z,
+                                            int w, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_half2_bits(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    prefix_attention_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t attn_smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_smem = base;                                   // [4 slices][128 rows][128 B]
+  uint8_t* k_ring = base + kAttnQBytes;                     // [2][4 slices][64 rows][128 B]
+  uint8_t* v_ring = k_ring + kAttnStages * kAttnKBytes;     // [2][256 rows][128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(v_ring + kAttnStages * kAttnVBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kAttnNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* nkb_slot = reinterpret_cast<int*>(tmem_slot + 2);
+  unsigned long long* kmask = reinterpret_cast<unsigned long long*>(tmem_slot + 4);  // 8-byte aligned
+
+  const auto bar_q = [&] { return smem_addr(bars); };
+  const auto bar_kfull = [&](int s) { return smem_addr(bars + 1 + s); };
+  const auto bar_kempty = [&](int s) { return smem_addr(bars + 3 + s); };
+  const auto bar_vfull = [&](int s) { return smem_addr(bars + 5 + s); };
+  const auto bar_vempty = [&](int s) { return smem_addr(bars + 7 + s); };
+  const auto bar_sfull = [&](int s) { return smem_addr(bars + 9 + s); };
+  const auto bar_sfree = [&](int s) { return smem_addr(bars + 11 + s); };
+  const auto bar_pfull = [&](int s) { return smem_addr(bars + 13 + s); };
+  const auto bar_pfree = [&](int s) { return smem_addr(bars + 15 + s); };
+  const uint32_t bar_o = smem_addr(bars + 17);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int L = p.seq;
+  const int tpt = kAttnRows / p.heads;  // tokens per tile
+  const int t0 = blockIdx.x * tpt;
+  unsigned* err = &g_w4a4_device_error;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (L < 1 || L > kAttnMaxKeys || p.heads < 1 || kAttnRows % p.heads != 0) {
+    if (threadIdx.x == 0) atomicOr(&g_w4a4_device_error, kErrBadParams);
+    return;
+  }
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q(), 1);
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(bar_kfull(s), 1);
+      mbar_init(bar_kempty(s), 1);
+      mbar_init(bar_vfull(s), 1);
+      mbar_init(bar_vempty(s), 1);
+      mbar_init(bar_sfull(s), 1);
+      mbar_init(bar_sfree(s), 4);
+      mbar_init(bar_pfull(s), 4);
+      mbar_init(bar_pfree(s), 1);
+    }
+    mbar_init(bar_o, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tmap_q);
+    tma_prefetch_desc(&p.tmap_k);
+    tma_prefetch_desc(&p.tmap_vt);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), kAttnTmemCols);
+    tmem_relinquish();
+  }
+  pdl_wait();  // q, k, v and the masks are earlier kernels' outputs
+  // Key blocks to visit: up to the last real key, or all of them when a
+  // padded (or past-the-end) query row is in the tile (uniform over L keys).
+  if (threadIdx.x == 0) {
+    bool pad_row = false;
+    for (int t = t0; t < t0 + tpt; ++t) pad_row |= (t >= L) || !p.key_valid[static_cast<long long>(b) * L + t];
+    const int kv = pad_row ? L : max(0, min(L, p.kv_len[b]));
+    *nkb_slot = (kv + kAttnKeyBlock - 1) / kAttnKeyBlock;
+  }
+  // 64-bit masks of the real keys of every block (warps 2-5)
+  if (warp >= 2) {
+    const int nblk = (L + kAttnKeyBlock - 1) / kAttnKeyBlock;
+    for (int kb = warp - 2; kb < nblk; kb += 4) {
+      const int j0 = kb * kAttnKeyBlock + lane, j1 = j0 + 32;
+      const bool v0 = j0 < L && p.key_valid[static_cast<long long>(b) * L + j0];
+      const bool v1 = j1 < L && p.key_valid[static_cast<long long>(b) * L + j1];
+      const unsigned lo = __ballot_sync(0xffffffffu, v0), hi = __ballot_sync(0xffffffffu, v1);
+      if (lane == 0) kmask[kb] = static_cast<unsigned long long>(hi) << 32 | lo;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nkb = *nkb_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (lane 0)
+    if (lane == 0 && nkb > 0) {
+      mbar_arrive_expect_tx(bar_q(), kAttnQBytes);
+      for (int s = 0; s < kAttnSlices; ++s)
+        tma_load_4d(smem_addr(q_smem + s * (kAttnQBytes / kAttnSlices)), &p.tmap_q, 64 * s, 0, t0, b,
+                    bar_q());
+      int nk = 0, nv = 0;
+      bool alive = true;
+      // K blocks for pass 1 (0 .. nkb-1) then pass 2 (again), V blocks in pass 2.
+      for (int g = 0; alive && g < 2 * nkb; ++g) {
+        const int slot = g & 1;
+        if (g >= kAttnStages &&
+            !mbar_wait_bounded(bar_kempty(slot), ((g >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit)) {
+          alive = false;
+          break;
+        }
+        const int kb = g < nkb ? g : g - nkb;
+        mbar_arrive_expect_tx(bar_kfull(slot), kAttnKBytes);
+        for (int s = 0; s < kAttnSlices; ++s)
+          tma_load_3d(smem_addr(k_ring + slot * kAttnKBytes + s * (kAttnKBytes / kAttnSlices)), &p.tmap_k,
+                      64 * s, kb * kAttnKeyBlock, b, bar_kfull(slot));
+        ++nk;
+        if (g >= nkb) {
+          const int vslot = kb & 1;
+          if (kb >= kAttnStages &&
+              !mbar_wait_bounded(bar_vempty(vslot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty,
+                                 limit)) {
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_vfull(vslot), kAttnVBytes);
+          tma_load_3d(smem_addr(v_ring + vslot * kAttnVBytes), &p.tmap_vt, kb * kAttnKeyBlock, 0, b,
+                      bar_vfull(vslot));
+          ++nv;
+        }
+      }
+      // Drain: no copy may still be in flight at exit.
+      volatile int no_abort = 0;
+      mbar_wait_bounded(bar_q(), 0, &no_abort, err, kErrWaitDrain, limit);
+      for (int i = 0; i < kAttnStages && i < nk; ++i) {
+        const int last = i + ((nk - 1 - i) / kAttnStages) * kAttnStages;
+        mbar_wait_bounded(bar_kfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
+      }
+      for (int i = 0; i < kAttnStages && i < nv; ++i) {
+        const int last = i + ((nv - 1 - i) / kAttnStages) * kAttnStages;
+        mbar_wait_bounded(bar_vfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (one elected lane)
+    const bool issuer = elect_one();
+    const uint32_t idesc_s = idesc_f16(kAttnRows, kAttnKeyBlock);
+    const uint32_t idesc_o = idesc_f16(kAttnRows, kAttnHeadDim);
+    const uint64_t qdesc = smem_desc_sw128(smem_addr(q_smem));
+    bool alive = nkb > 0 && warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit));
+    // S(g) for score block g (g < nkb: pass 1, else pass 2 of block g - nkb)
+    const auto issue_s = [&](int g) -> bool {
+      const int slot = g & 1;
+      bool ok = mbar_wait_bounded(bar_kfull(slot), (g >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+      if (ok && g >= 2)
+        ok = mbar_wait_bounded(bar_sfree(slot), ((g >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
+      if (!warp_all(ok)) return false;
+      tc_fence_after();
+      const uint64_t kdesc = smem_desc_sw128(smem_addr(k_ring + slot * kAttnKBytes));
+      if (issuer) {
+#pragma unroll
+        for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>((kk & 3) * 2);
+          umma_f16_ss(tmem_base + kAttnSCol + slot * kAttnKeyBlock,
+                      qdesc + static_cast<uint64_t>((kk >> 2) * (kAttnQBytes / kAttnSlices) >> 4) + off,
+                      kdesc + static_cast<uint64_t>((kk >> 2) * (kAttnKBytes / kAttnSlices) >> 4) + off,
+                      idesc_s, kk > 0);
+        }
+        umma_commit(bar_kempty(slot));
+        umma_commit(bar_sfull(slot));
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int g = 0; alive && g < nkb; ++g) alive = issue_s(g);
+    if (alive) alive = issue_s(nkb);
+    for (int kb = 0; alive && kb < nkb; ++kb) {
+      if (kb + 1 < nkb && !(alive = issue_s(nkb + kb + 1))) break;
+      const int slot = kb & 1;
+      bool ok = mbar_wait_bounded(bar_vfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+      if (ok) ok = mbar_wait_bounded(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
+      if (!warp_all(ok)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t vdesc = smem_desc_sw128(smem_addr(v_ring + slot * kAttnVBytes));
+      if (issuer) {
+#pragma unroll
+        for (int kk = 0; kk < kAttnKeyBlock / 16; ++kk)
+          umma_f16_ts(tmem_base + kAttnOCol, tmem_base + kAttnPCol + slot * 32 + 8 * kk,
+                      vdesc + static_cast<uint64_t>(kk * 2), idesc_o, (kb | kk) != 0);
+        umma_commit(bar_vempty(slot));
+        umma_commit(bar_pfree(slot));
+      }
+      __syncwarp();
+    }
+    // Every MMA of this CTA has completed once this commit arrives (also
+    // after an abort: the epilogue's bounded wait then gives up or passes).
+    if (issuer && nkb > 0) umma_commit(bar_o);
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax + epilogue (warps 2-5)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                // this thread's row (TMEM lane)
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int tok = t0 + r / p.heads, head = r % p.heads;
+    const bool q_real = tok < L && p.key_valid[static_cast<long long>(b) * L + tok];
+    float m = -INFINITY, l = 0.f;
+    bool alive = nkb > 0;
+    // masked scores of block kb, this row: real query -> real keys only;
+    // padded query -> every key < L with score 0 (uniform weights)
+    const auto scores = [&](int kb, const uint32_t (&raw)[64], float (&s)[64]) {
+      const unsigned long long km = kmask[kb];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int j = kb * kAttnKeyBlock + c;
+        const bool ok = q_real ? ((km >> c) & 1ull) != 0 : j < L;
+        s[c] = ok ? (q_real ? __fmul_rn(__uint_as_float(raw[c]), p.scale_log2) : 0.f) : -INFINITY;
+      }
+    };
+    const auto load_s = [&](int g, uint32_t (&raw)[64]) -> bool {
+      const int slot = g & 1;
+      if (!warp_all(mbar_wait_bounded(bar_sfull(slot), (g >> 1) & 1, abort_flag, err, kErrWaitAccum, limit)))
+        return false;
+      tc_fence_after();
+      const uint32_t t = tmem_base + lane_addr + kAttnSCol + slot * kAttnKeyBlock;
+      tmem_ld_32x32b_x16(t, *reinterpret_cast<uint32_t(*)[16]>(&raw[0]));
+      tmem_ld_32x32b_x16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&raw[16]));
+      tmem_ld_32x32b_x16(t + 32, *reinterpret_cast<uint32_t(*)[16]>(&raw[32]));
+      tmem_ld_32x32b_x16(t + 48, *reinterpret_cast<uint32_t(*)[16]>(&raw[48]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree(slot));
+      return true;
+    };
+    // pass 1: row max and sum
+    for (int g = 0; alive && g < nkb; ++g) {
+      uint32_t raw[64];
+      float s[64];
+      if (!(alive = load_s(g, raw))) break;
+      scores(g, raw, s);
+      float bm = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) bm = fmaxf(bm, s[c]);
+      const float mn = fmaxf(m, bm);
+      if (mn != -INFINITY) {
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) sum += exp2f(s[c] - mn);
+        l = l * exp2f(m - mn) + sum;
+        m = mn;
+      }
+    }
+    // pass 2: p = exp2(s - m) as fp16 into TMEM for the PV MMA
+    for (int kb = 0; alive && kb < nkb; ++kb) {
+      uint32_t raw[64];
+      float s[64];
+      if (!(alive = load_s(nkb + kb, raw))) break;
+      scores(kb, raw, s);
+      uint32_t pw[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = m == -INFINITY ? 0.f : exp2f(s[2 * c] - m);
+        const float p1 = m == -INFINITY ? 0.f : exp2f(s[2 * c + 1] - m);
+        pw[c] = pack_half2_bits(p0, p1);
+      }
+      const int slot = kb & 1;
+      if (kb >= 2 && !warp_all(mbar_wait_bounded(bar_pfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err,
+                                                  kErrWaitAccum, limit))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      tmem_st_32x32b_x32(tmem_base + lane_addr + kAttnPCol + slot * 32, pw);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_pfull(slot));
+    }
+    // epilogue: O / l -> fp16 rows
+    if (alive && warp_all(mbar_wait_bounded(bar_o, 0, abort_flag, err, kErrWaitAccum, limit))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim;
+      const bool store = tok < L;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kAttnHeadDim; c0 += 16) {
+        uint32_t o[16];
+        tmem_ld_32x32b_x16(tmem_base + lane_addr + kAttnOCol + c0, o);
+        tmem_ld_wait();
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          w[i] = pack_half2_bits(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+        if (store) {
+          *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every MMA has completed (bar_o, or the issuer's last
+  // commits when it gave up) before TMEM is freed
+  if (warp == 1 && nkb > 0) {
+    volatile int no_abort = 0;
+    mbar_wait_bounded(bar_o, 0, &no_abort, err, kErrWaitDrain, limit);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kAttnTmemCols);
+  }
+}
+
+// V [B * L, ldv] (rows of 256) -> V^T per observation [B][256][ldt]: the
+// B operand of the PV MMA must be K-major (keys contiguous).  64 x 64 tiles
+// through shared memory.
+__global__ void __launch_bounds__(256) transpose_v_kernel(const __half* __restrict__ v, long long ldv,
+                                                          __half* __restrict__ vt, long long ldt, int seq) {
+  __shared__ __half tile[64][66];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.z, j0 = blockIdx.x * 64, d0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+  for (int j = ty; j < 64; j += 4) {
+    const int key = j0 + j;
+    tile[j][tx] = key < seq ? v[(static_cast<long long>(b) * seq + key) * ldv + d0 + tx] : __float2half(0.f);
+  }
+  __syncthreads();
+  for (int d = ty; d < 64; d += 4) {
+    const int key = j0 + tx;
+    if (key < ldt) vt[(static_cast<long long>(b) * kAttnHeadDim + d0 + d) * ldt + key] = tile[tx][d];
+  }
+}
+
+}  // namespace w4a4

@@ -101,7 +101,13 @@ struct alignas(64) GemmSegment {
   int n;                    // weight rows of this matrix
   int tile_begin;           // first global weight-tile index of this matrix
   int vec_store;            // 1: y is 16-byte aligned and n % 8 == 0
+  int wide_k;               // 1: K > kMagicMaxK, acc / 16 may reach 2^22 (exact int -> float)
 };
+
+// Up to this K, |acc / 16| <= 7 * 8 * K < 2^22 and the epilogue converts it
+// to fp32 with the magic-number trick; beyond it, with cvt.rn.f32.s32 (the
+// reference's (float)acc, correct for any int32).
+constexpr int kMagicMaxK = 65536;
 
 struct alignas(64) GemmParams {
   CUtensorMap tmap_tok;     // int8 codes [M, K] in GEMM byte order: box {128, tok_tile}, SW128
@@ -190,10 +196,17 @@ __device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const Til
     }
 #pragma unroll
     for (int i = 0; i < 16; i += 2) {
-      // acc / 16 as fp32, exactly: |acc / 16| < 2^22, so adding it to the
-      // integer bits of 1.5 * 2^23 and subtracting that value is exact.
-      const float a0 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
-      const float a1 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
+      // acc / 16 as fp32: for K <= kMagicMaxK |acc / 16| < 2^22, so adding it
+      // to the integer bits of 1.5 * 2^23 and subtracting that value is
+      // exact; wider K rounds it like (float)acc (uniform branch).
+      float a0, a1;
+      if (!seg.wide_k) {
+        a0 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
+        a1 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
+      } else {
+        a0 = __int2float_rn(static_cast<int32_t>(acc[i]) >> 4);
+        a1 = __int2float_rn(static_cast<int32_t>(acc[i + 1]) >> 4);
+      }
       const __half2 h = __floats2half2_rn(__fmul_rn(__fmul_rn(a0, t[i]), sw),
                                           __fmul_rn(__fmul_rn(a1, t[i + 1]), sw));
       stage[i * 32 + lane] = __low2half(h);

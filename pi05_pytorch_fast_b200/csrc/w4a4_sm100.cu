@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -21,12 +22,17 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
+#include "attention.cuh"
 #include "layer.cuh"
 #include "quant.cuh"
 
 // Scratch of w4a4_int4_gemm_noalloc: the intermediate activation codes and
 // row scales, as file-scope device arrays (one copy per device, shared by
-// every call on it; no allocation of any kind).
+// every call on it; no allocation of any kind).  Calls on one stream are
+// ordered only because every kernel that writes this scratch (the quants)
+// executes griddepcontrol.wait (pdl_wait) before its first store: under
+// programmatic dependent launch the previous call's GEMM may still be
+// reading the codes when the next quant starts.
 __device__ __align__(256) int8_t g_w4a4_noalloc_codes[W4A4_NOALLOC_MAX_CODES];
 __device__ __align__(256) float g_w4a4_noalloc_scales[W4A4_NOALLOC_MAX_ROWS];
 
@@ -162,8 +168,8 @@ EncodeTiledFn encode_fn() {
 
 struct MapKey {
   uintptr_t ptr;
-  uint64_t d[3], stride[2];
-  uint32_t box[3];
+  uint64_t d[4], stride[3];
+  uint32_t box[4];
   int rank, dtype, swizzle;
   bool operator==(const MapKey& o) const {
     return ptr == o.ptr && rank == o.rank && dtype == o.dtype && swizzle == o.swizzle &&
@@ -174,22 +180,35 @@ struct MapKey {
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     uint64_t h = k.ptr * 0x9E3779B97F4A7C15ull;
-    for (uint64_t v : {k.d[0], k.d[1], k.d[2], k.stride[0], k.stride[1],
+    for (uint64_t v : {k.d[0], k.d[1], k.d[2], k.d[3], k.stride[0], k.stride[1], k.stride[2],
                        static_cast<uint64_t>(k.box[0]) << 32 | k.box[1],
-                       static_cast<uint64_t>(k.box[2]) << 32 | static_cast<uint64_t>(k.rank),
+                       static_cast<uint64_t>(k.box[2]) << 32 | k.box[3],
+                       static_cast<uint64_t>(k.rank),
                        static_cast<uint64_t>(k.dtype) << 8 | static_cast<uint64_t>(k.swizzle)})
       h = (h ^ v) * 0x100000001B3ull;
     return static_cast<size_t>(h);
   }
 };
 std::mutex g_map_mu;
-std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+// Two caches: long-lived maps (packed weights, read by every call of a layer)
+// and per-call maps (activations and codes, whose pointers and row counts
+// change from call to call).  Each is bounded; when a cache is full its
+// oldest entry is evicted (insertion order), so a stream of new activation
+// shapes never pushes the weight maps out.
+struct MapCache {
+  std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
+  std::deque<MapKey> order;
+  size_t capacity;
+};
+MapCache g_weight_maps{{}, {}, 8192};
+MapCache g_call_maps{{}, {}, 1024};
 
-// Tiled tensor map of rank 2 or 3, cached by its parameters: dims[0]
+// Tiled tensor map of rank 2 to 4, cached by its parameters: dims[0]
 // innermost (elements), strides_bytes[i] the byte stride of dims[i + 1].
 int make_map(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int rank,
              const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-             CUtensorMapSwizzle swizzle) {
+             CUtensorMapSwizzle swizzle, bool weight = false) {
+  MapCache& cache = weight ? g_weight_maps : g_call_maps;
   MapKey key{};
   key.ptr = reinterpret_cast<uintptr_t>(ptr);
   key.rank = rank;
@@ -202,16 +221,17 @@ int make_map(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int r
   }
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
-    auto it = g_maps.find(key);
-    if (it != g_maps.end()) {
+    auto it = cache.maps.find(key);
+    if (it != cache.maps.end()) {
       *out = it->second;
       return W4A4_OK;
     }
   }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(W4A4_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-  cuuint64_t cdims[3], cstrides[2];
-  cuuint32_t cbox[3], estr[3] = {1, 1, 1};
+  if (rank < 1 || rank > 4) return fail(W4A4_ERR_INVALID, "tensor map rank %d", rank);
+  cuuint64_t cdims[4], cstrides[3];
+  cuuint32_t cbox[4], estr[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     cdims[i] = dims[i];
     cbox[i] = box[i];
@@ -223,12 +243,18 @@ int make_map(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int r
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(W4A4_ERR_CUDA,
-                "cuTensorMapEncodeTiled failed (%d): rank %d, dims {%llu, %llu, %llu}, box {%u, %u, %u}",
+                "cuTensorMapEncodeTiled failed (%d): rank %d, dims {%llu, %llu, %llu, %llu}, box {%u, %u, %u, %u}",
                 static_cast<int>(r), rank, (unsigned long long)key.d[0], (unsigned long long)key.d[1],
-                (unsigned long long)key.d[2], key.box[0], key.box[1], key.box[2]);
+                (unsigned long long)key.d[2], (unsigned long long)key.d[3], key.box[0], key.box[1],
+                key.box[2], key.box[3]);
   std::lock_guard<std::mutex> lk(g_map_mu);
-  if (g_maps.size() > 4096) g_maps.clear();
-  g_maps.emplace(key, map);
+  if (cache.maps.emplace(key, map).second) {
+    cache.order.push_back(key);
+    while (cache.maps.size() > cache.capacity) {
+      cache.maps.erase(cache.order.front());
+      cache.order.pop_front();
+    }
+  }
   *out = map;
   return W4A4_OK;
 }
@@ -236,10 +262,10 @@ int make_map(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int r
 // 2-D tiled tensor map: dim0 innermost (elements), dim1 rows, row stride in bytes.
 int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, uint64_t d0,
                 uint64_t d1, uint64_t stride_bytes, uint32_t b0, uint32_t b1,
-                CUtensorMapSwizzle swizzle) {
+                CUtensorMapSwizzle swizzle, bool weight = false) {
   const uint64_t dims[2] = {d0, d1};
   const uint32_t box[2] = {b0, b1};
-  return make_map(out, ptr, dtype, 2, dims, &stride_bytes, box, swizzle);
+  return make_map(out, ptr, dtype, 2, dims, &stride_bytes, box, swizzle, weight);
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -516,12 +542,85 @@ int launch_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* 
   return ok();
 }
 
+// ------------------------------------------------------------- attention
+int64_t attn_vt_stride(int32_t seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
+
+int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                     int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
+                     int32_t seq, int32_t heads, void* vt, void* out, int64_t ldo, cudaStream_t stream) {
+  if (batch < 0 || seq < 0) return fail(W4A4_ERR_INVALID, "invalid attention shape: batch %d, seq %d", batch, seq);
+  if (heads < 1 || heads > kAttnRows || kAttnRows % heads != 0)
+    return fail(W4A4_ERR_UNSUPPORTED, "attention: heads must divide %d, got %d", kAttnRows, heads);
+  if (seq > kAttnMaxKeys)
+    return fail(W4A4_ERR_UNSUPPORTED, "attention: prefix of %d tokens exceeds %d", seq, kAttnMaxKeys);
+  if (batch == 0 || seq == 0) return ok();
+  if (!q || !k || !v || !key_valid || !kv_len || !vt || !out)
+    return fail(W4A4_ERR_INVALID, "null pointer argument");
+  const int64_t width = static_cast<int64_t>(heads) * kAttnHeadDim;
+  const auto rows_ok = [](const void* ptr, int64_t ld, int64_t w) {
+    return aligned(ptr, 16) && ld >= w && ld % 8 == 0;
+  };
+  if (!rows_ok(q, ldq, width) || !rows_ok(out, ldo, width) || !rows_ok(k, ldk, kAttnHeadDim) ||
+      !rows_ok(v, ldv, kAttnHeadDim) || !aligned(vt, 16))
+    return fail(W4A4_ERR_INVALID,
+                "attention rows must be 16-byte aligned with strides >= their width and multiples of 8");
+  int dev;
+  if (int e = current_device(&dev)) return e;
+  const int64_t ldt = attn_vt_stride(seq);
+  const __half* vh = static_cast<const __half*>(v);
+  __half* vth = static_cast<__half*>(vt);
+  W4A4_CUDA_TRY(launch_kernel(transpose_v_kernel,
+                              dim3(static_cast<unsigned>((ldt + 63) / 64), kAttnHeadDim / 64,
+                                   static_cast<unsigned>(batch)),
+                              dim3(256), 0, stream, 1, vh, ldv, vth, ldt, seq));
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  {
+    const uint64_t dims[4] = {kAttnHeadDim, static_cast<uint64_t>(heads), static_cast<uint64_t>(seq),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t strides[3] = {kAttnHeadDim * 2, static_cast<uint64_t>(ldq) * 2,
+                                 static_cast<uint64_t>(ldq) * 2 * static_cast<uint64_t>(seq)};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(heads), static_cast<uint32_t>(kAttnRows / heads), 1};
+    if (int e = make_map(&p.tmap_q, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+  }
+  {
+    const uint64_t dims[3] = {kAttnHeadDim, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldk) * 2,
+                                 static_cast<uint64_t>(ldk) * 2 * static_cast<uint64_t>(seq)};
+    const uint32_t box[3] = {64, kAttnKeyBlock, 1};
+    if (int e = make_map(&p.tmap_k, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(seq), kAttnHeadDim, static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldt) * 2,
+                                 static_cast<uint64_t>(ldt) * 2 * kAttnHeadDim};
+    const uint32_t box[3] = {kAttnKeyBlock, kAttnHeadDim, 1};
+    if (int e = make_map(&p.tmap_vt, vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+  }
+  p.key_valid = key_valid;
+  p.kv_len = kv_len;
+  p.out = static_cast<__half*>(out);
+  p.ldo = ldo;
+  p.seq = seq;
+  p.heads = heads;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kAttnHeadDim)));
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  if (int e = ensure_smem_attr(dev, 1ull << 40, prefix_attention_kernel, kAttnSmem)) return e;
+  const int tpt = kAttnRows / heads;
+  W4A4_CUDA_TRY(launch_kernel(prefix_attention_kernel,
+                              dim3(static_cast<unsigned>((seq + tpt - 1) / tpt), static_cast<unsigned>(batch)),
+                              dim3(kAttnThreads), kAttnSmem, stream, 1, p));
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 // ------------------------------------------------------------- GEMM
-// Token-tile width for the persistent GEMM.  The tile count T is chosen to
-// minimise ceil(tiles / SMs) * (tile + kTileOverhead): the busiest CTA's tile
-// count times a per-tile cost in which the overhead term models the work that
-// does not scale with the tile (streaming and unpacking the 128-row weight
-// operand).  Tiles are multiples of 16 (the UMMA N granularity).
 // Tile width and split-K for the single-CTA kernel.  A K step of a tile of
 // t tokens costs about 330 + 1.5 t SM cycles (per-step traces on B200: the
 // MMA issue loop, ~480 at t = 96 and ~640 at t = 208), a tile about 2000
@@ -565,6 +664,11 @@ GemmPlan choose_plan(int64_t m, int w_tiles, int k_steps, int sms, int variant) 
   return best;
 }
 
+// Token-tile width for the CTA-pair kernel (no split-K).  The tile count T
+// is chosen to minimise ceil(tiles / workers) * (tile + kTileOverhead): the
+// busiest pair's tile count times a per-tile cost in which the overhead term
+// models the work that does not scale with the tile (streaming and unpacking
+// the weight operand).  Tiles are multiples of 16 (the UMMA N granularity).
 int choose_tok_tile(int64_t m, int w_tiles, int sms) {
   constexpr int kTileOverhead = 64;
   int best_tile = 16;
@@ -618,6 +722,8 @@ LaunchShape launch_shape(int64_t m, int w_tiles, int32_t k, int sms, bool pair, 
   return ls;
 }
 
+constexpr int32_t kMaxGemmK = 1 << 21;
+
 int check_weight(const w4a4_weight& w, int32_t k, int idx) {
   if (!w.data) return fail(W4A4_ERR_INVALID, "packed W %d: null data pointer", idx);
   if (w.n <= 0) return fail(W4A4_ERR_INVALID, "packed W %d: N must be positive, got %d", idx, w.n);
@@ -641,10 +747,10 @@ int check_weight(const w4a4_weight& w, int32_t k, int idx) {
   return W4A4_OK;
 }
 
-// The single-CTA kernel is the default; W4A4_GEMM_PAIR=1 (or
-// w4a4_set_gemm_variant) selects the CTA-pair (cta_group::2) kernel, which is
-// bit-identical but measured slower on the prefix workload (4.41 vs 3.62 ms
-// per 776-token prefix).
+// The GEMM variant of later launches: W4A4_GEMM_SINGLE_CTA (the default,
+// see use_pair_kernel for the shapes it still sends to CTA pairs), or a
+// forced variant from w4a4_set_gemm_variant / W4A4_GEMM_PAIR=1 (CTA pairs
+// for every shape).  All variants are bit-identical.
 std::atomic<int> g_gemm_variant{[] {
   const char* e = std::getenv("W4A4_GEMM_PAIR");
   return (e && e[0] == '1') ? W4A4_GEMM_CTA_PAIR : W4A4_GEMM_SINGLE_CTA;
@@ -667,6 +773,9 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
                 const w4a4_weight* weights, void* const* y, cudaStream_t stream,
                 bool acc_out = false) {
   if (k <= 0 || k % 64 != 0) return fail(W4A4_ERR_INVALID, "K must be a multiple of 64, got %d", k);
+  // the tensor cores accumulate 16 x sum(qa * qw), |.| <= 16 * 7 * 8 * K, in int32
+  if (k > kMaxGemmK)
+    return fail(W4A4_ERR_UNSUPPORTED, "K = %d exceeds %d (int32 accumulator range)", k, kMaxGemmK);
   if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative");
   if (n_weights < 1 || n_weights > kMaxSegments)
     return fail(W4A4_ERR_INVALID, "n_weights must be 1..%d, got %d", kMaxSegments, n_weights);
@@ -698,7 +807,7 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     if (layout == W4A4_LAYOUT_ROW_MAJOR) {
       if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT32, k / 8, w.n,
                               static_cast<uint64_t>(w.row_words) * 4, kBlockK / 8, kBlockW,
-                              CU_TENSOR_MAP_SWIZZLE_64B))
+                              CU_TENSOR_MAP_SWIZZLE_64B, true))
         return e;
       s.scale = reinterpret_cast<const float*>(w.data + k / 8);
       s.scale_stride = w.row_words;
@@ -706,7 +815,7 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
       if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT32,
                               static_cast<uint64_t>(w.n) * 2, k / 16,
                               static_cast<uint64_t>(w.n) * 8, 2 * kBlockW, kBlockK / 16,
-                              CU_TENSOR_MAP_SWIZZLE_NONE))
+                              CU_TENSOR_MAP_SWIZZLE_NONE, true))
         return e;
       s.scale = reinterpret_cast<const float*>(w.data + static_cast<int64_t>(w.n) * (k / 8));
       s.scale_stride = 1;
@@ -715,6 +824,7 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     s.n = w.n;
     s.tile_begin = w_tiles;
     s.vec_store = (!acc_out && w.n % 8 == 0 && aligned(y[i], 16)) ? 1 : 0;
+    s.wide_k = k > kMagicMaxK ? 1 : 0;
     w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
   const int k_steps = (k + kBlockK - 1) / kBlockK;
@@ -893,6 +1003,14 @@ int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int
 int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
               const void* sin_t, int64_t m, int32_t heads, void* stream) {
   return launch_rope(x, ldx, out, ldo, cos_t, sin_t, m, heads, static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                          int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
+                          int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
+                          void* stream) {
+  return launch_attention(q, ldq, k, ldk, v, ldv, key_valid, kv_len, batch, seq, heads, vt_scratch, out,
+                          ldo, static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,

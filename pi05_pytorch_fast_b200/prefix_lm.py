@@ -9,8 +9,9 @@ C ABI instead of modules:
 
 * one preallocated workspace per token count, so a forward allocates
   nothing and captures into one CUDA graph;
-* per layer, nine launches: residual add + RMSNorm + quant (one kernel),
-  the q/k/v GEMM (one launch, three weights), RoPE, attention, quant + o_proj
+* per layer, twelve launches, all of this library: residual add + RMSNorm +
+  quant (one kernel), the q/k/v GEMM (one launch, three weights), RoPE of q
+  and of k, the V transpose and the tensor-core attention, quant + o_proj
   GEMM, residual add + RMSNorm + quant, the gate/up GEMM, GeGLU + quant (one
   kernel), the down GEMM; the residual add of each sublayer is folded into
   the next norm;
@@ -124,11 +125,17 @@ def layer_from_packed(packed: dict, prefix: str, input_norm: torch.Tensor, post_
         input_gain=_gain(input_norm, device), post_gain=_gain(post_norm, device))
 
 
-def rope_inv_freq(cfg: PrefixLMConfig) -> torch.Tensor:
+def rope_inv_freq(cfg: PrefixLMConfig, fp16_buffer: bool = True) -> torch.Tensor:
     """Rotary inverse frequencies as transformers' default rope computes them
-    (fp32 on the CPU: 1 / theta ** (arange(0, d, 2) / d))."""
+    (fp32 on the CPU: 1 / theta ** (arange(0, d, 2) / d)).  With
+    ``fp16_buffer`` they are rounded through fp16, as in the reference's fp16
+    prefix LM: its cast converts every floating parameter AND buffer of the
+    language model, the rotary ``inv_freq`` included
+    (pi05_fast/rocm_pi05_optim.py:136-154), and the rotary embedding then
+    computes positions x inv_freq.float()."""
     exps = torch.arange(0, cfg.head_dim, 2, dtype=torch.int64).to(dtype=torch.float) / cfg.head_dim
-    return 1.0 / (cfg.rope_theta ** exps)
+    inv = 1.0 / (cfg.rope_theta ** exps)
+    return inv.half().float() if fp16_buffer else inv
 
 
 def prefix_positions_and_mask(pad_mask: torch.Tensor):
@@ -143,30 +150,13 @@ def prefix_positions_and_mask(pad_mask: torch.Tensor):
     return pos, mask
 
 
-def attention_eager(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor,
-                    cfg: PrefixLMConfig, batch: int, seq: int) -> torch.Tensor:
-    """Eager attention in fp16 as transformers' eager_attention_forward rounds
-    it: scores = fl16(fl16(q k^T) * scale) + mask (fp32), softmax in fp32,
-    probabilities rounded to fp16, fl16(p v).  q [B*L, H*D], k/v [B*L, D]."""
-    h, d = cfg.heads, cfg.head_dim
-    qh = q.view(batch, seq, h, d).transpose(1, 2)
-    kh = k.view(batch, seq, cfg.kv_heads, d).transpose(1, 2)
-    vh = v.view(batch, seq, cfg.kv_heads, d).transpose(1, 2)
-    rep = h // cfg.kv_heads
-    kh = kh[:, :, None].expand(batch, cfg.kv_heads, rep, seq, d).reshape(batch, h, seq, d)
-    vh = vh[:, :, None].expand(batch, cfg.kv_heads, rep, seq, d).reshape(batch, h, seq, d)
-    w = torch.matmul(qh, kh.transpose(2, 3)) * (d ** -0.5)
-    w = torch.softmax(w + mask, dim=-1, dtype=torch.float32).to(q.dtype)
-    o = torch.matmul(w, vh)
-    return o.transpose(1, 2).reshape(batch * seq, h * d)
-
-
 class _Workspace:
     """Every intermediate of one forward at `rows` tokens, allocated once."""
 
-    def __init__(self, cfg: PrefixLMConfig, rows: int, device, trace: bool):
+    def __init__(self, cfg: PrefixLMConfig, batch: int, seq: int, device, trace: bool):
         f16 = dict(dtype=torch.float16, device=device)
         e = torch.empty
+        rows = batch * seq
         self.rows = rows
         self.x = e((rows, cfg.hidden), **f16)            # residual stream
         self.codes = e((rows, cfg.intermediate), dtype=torch.int8, device=device)
@@ -181,6 +171,10 @@ class _Workspace:
         self.out = e((rows, cfg.hidden), **f16)
         self.cos = e((rows, cfg.head_dim), **f16)
         self.sin = e((rows, cfg.head_dim), **f16)
+        # attention: V transposed per observation, the key mask, real-key spans
+        self.vt = e((batch, cfg.head_dim, nat.attn_vt_stride(seq)), **f16)
+        self.key_valid = e((batch, seq), dtype=torch.uint8, device=device)
+        self.kv_len = e((batch,), dtype=torch.int32, device=device)
         # debug copies of the quantised activations (traces only)
         self.h = e((rows, cfg.hidden), **f16) if trace else None
         self.h_mlp = e((rows, cfg.intermediate), **f16) if trace else None
@@ -202,7 +196,7 @@ class W4A4PrefixLM:
     W4A4_STAGING_*; fp16 = the reference HIP kernel's)."""
 
     def __init__(self, cfg: PrefixLMConfig, layers: list[PackedLayer], final_norm: torch.Tensor,
-                 device, staging: int = nat.STAGING_FP16):
+                 device, staging: int = nat.STAGING_FP16, inv_freq: torch.Tensor | None = None):
         if cfg.hidden != 2048 or cfg.intermediate != 16384 or cfg.head_dim != 256:
             raise ValueError("the fused layer kernels are built for Gemma-2B shapes "
                              "(hidden 2048, MLP 16384, head_dim 256)")
@@ -211,7 +205,9 @@ class W4A4PrefixLM:
         self.device = torch.device(device)
         self.final_gain = _gain(final_norm, self.device)
         self.staging = staging
-        self.inv_freq = rope_inv_freq(cfg).to(self.device)
+        # the rotary table: the model's own inv_freq buffer when one is given,
+        # else the fp16 LM's (rope_inv_freq)
+        self.inv_freq = (rope_inv_freq(cfg) if inv_freq is None else inv_freq.detach().float()).to(self.device)
         self._ws: dict = {}
         self._lib = nat.lib()
 
@@ -219,7 +215,8 @@ class W4A4PrefixLM:
     @classmethod
     def from_gemma(cls, model, device, staging: int = nat.STAGING_FP16) -> "W4A4PrefixLM":
         """From a transformers GemmaModel (or anything with .layers / .norm of
-        Gemma decoder layers): packs every projection."""
+        Gemma decoder layers): packs every projection; RoPE uses the model's
+        own rotary inv_freq buffer (fp16 once the model is cast to fp16)."""
         cfg = PrefixLMConfig.from_gemma(model.config)
         layers = []
         for layer in model.layers:
@@ -230,7 +227,9 @@ class W4A4PrefixLM:
             layers.append(pack_layer({n: w.detach() for n, w in lin.items()},
                                      layer.input_layernorm.weight, layer.post_attention_layernorm.weight,
                                      device))
-        return cls(cfg, layers, model.norm.weight, device, staging)
+        rot = getattr(model, "rotary_emb", None)
+        inv_freq = getattr(rot, "inv_freq", None)
+        return cls(cfg, layers, model.norm.weight, device, staging, inv_freq=inv_freq)
 
     @classmethod
     def random(cls, cfg: PrefixLMConfig, device, seed: int = 0, std: float = 0.02,
@@ -283,10 +282,10 @@ class W4A4PrefixLM:
         return cls(cfg, layers, norms["norm"], device, staging)
 
     # ------------------------------------------------------------- forward
-    def workspace(self, rows: int, trace: bool = False) -> _Workspace:
-        key = (rows, trace)
+    def workspace(self, batch: int, seq: int, trace: bool = False) -> _Workspace:
+        key = (batch, seq, trace)
         if key not in self._ws:
-            self._ws[key] = _Workspace(self.cfg, rows, self.device, trace)
+            self._ws[key] = _Workspace(self.cfg, batch, seq, self.device, trace)
         return self._ws[key]
 
     def _stream(self):
@@ -323,9 +322,13 @@ class W4A4PrefixLM:
         if hidden != cfg.hidden or embeds.dtype != torch.float16:
             raise ValueError(f"embeds must be fp16 [B, L, {cfg.hidden}]")
         rows = b * seq
-        ws = self.workspace(rows, trace is not None)
+        ws = self.workspace(b, seq, trace is not None)
         ws.x.copy_(embeds.reshape(rows, hidden))
-        pos, mask = prefix_positions_and_mask(pad_mask)
+        pad = pad_mask.bool()
+        pos = torch.cumsum(pad.to(torch.int64), dim=1) - 1
+        ws.key_valid.copy_(pad)
+        # keys at or past the last real token + 1 are all padding
+        ws.kv_len.copy_((pad * torch.arange(1, seq + 1, device=pad.device)).amax(dim=1))
         freqs = pos.reshape(rows, 1).float() * self.inv_freq[None, :]
         emb = torch.cat((freqs, freqs), dim=-1)
         ws.cos.copy_(emb.cos().half())
@@ -353,7 +356,10 @@ class W4A4PrefixLM:
                                     ws.cos.data_ptr(), ws.sin.data_ptr(), rows, cfg.heads, st))
             nat.check(lib.w4a4_rope(ws.k.data_ptr(), ws.k.stride(0), k_cache.data_ptr(), kv,
                                     ws.cos.data_ptr(), ws.sin.data_ptr(), rows, cfg.kv_heads, st))
-            ws.attn.copy_(attention_eager(ws.q, k_cache, v_cache, mask, cfg, b, seq))
+            nat.check(lib.w4a4_prefix_attention(
+                ws.q.data_ptr(), ws.q.stride(0), k_cache.data_ptr(), kv, v_cache.data_ptr(), kv,
+                ws.key_valid.data_ptr(), ws.kv_len.data_ptr(), b, seq, cfg.heads, ws.vt.data_ptr(),
+                ws.attn.data_ptr(), ws.attn.stride(0), st))
             nat.check(lib.w4a4_quant(ws.attn.data_ptr(), rows, cfg.hidden, cfg.hidden, nat.ROTATE_BY_K,
                                      self.staging, nat.CODES_GEMM, ws.codes.data_ptr(),
                                      ws.scales.data_ptr(), st))
@@ -387,10 +393,11 @@ class W4A4PrefixLM:
     __call__ = forward
 
     def launches_per_forward(self) -> int:
-        """Kernels of this library per forward (the torch glue -- cos/sin,
-        attention -- not counted): per layer 2 norm+quant, 1 quant, 4 GEMMs,
-        2 RoPE, 1 GeGLU+quant; then the final norm."""
-        return 10 * len(self.layers) + 1
+        """Kernels of this library per forward (the torch glue that builds the
+        position / mask tables is not counted): per layer 2 norm+quant, 1
+        quant, 4 GEMMs, 2 RoPE, V transpose + attention, 1 GeGLU+quant; then
+        the final norm."""
+        return 12 * len(self.layers) + 1
 
 
 class GraphedPrefixLM:

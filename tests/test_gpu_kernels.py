@@ -265,3 +265,22 @@ def test_bounded_wait_times_out_and_context_survives():
     y = ext.int4_gemm(to_dev(x), _row_major(p))
     assert_fp16_equal_and_within_tol(to_np(y), orc.int4_gemm_ref(x, p, staging="fp16"))
     assert nat.device_error(clear=True) == 0
+
+
+def test_wide_k_epilogue_matches_float_of_the_accumulator():
+    """K = 131072 without rotation and worst-case codes (7 x -8 per term):
+    |acc| = 7.3 M > 2^22, past the magic-number conversion's exact range; the
+    epilogue must round like the reference's (float)acc."""
+    m, n, k = 16, 128, 131072
+    x = orc.make_activations(m, k, seed=4)
+    x[0] = np.float16(0.5)
+    x[1] = np.float16(-0.5)
+    payload = np.full((n, k // 8), np.int32(-2004318072), dtype=np.int32)  # 0x88888888: every nibble -8
+    payload[n // 2:] = orc.random_packed_weight(n - n // 2, k, 3)[:, : k // 8]
+    scales = np.full((n,), 1e-3, dtype=np.float32)
+    packed = orc.pad_rows(np.concatenate([payload, scales.view(np.int32)[:, None]], axis=1), k // 8 + 8)
+    y = ext.int4_gemm(to_dev(x), to_dev(packed))
+    ref = orc.int4_gemm_ref(x, packed, rotate=False, staging="fp32")
+    assert abs(int(orc.int_accumulate(*[orc.quant_activation(x[:1], rotate=False)[0],
+                                        orc.weight_codes_scales(packed[:1], k)[0]])[0, 0])) > 2 ** 22
+    assert_fp16_equal_and_within_tol(to_np(y), ref)

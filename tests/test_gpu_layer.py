@@ -1,5 +1,6 @@
 """GPU parity of the fused prefix-LM layer kernels (w4a4_rmsnorm_quant,
-w4a4_geglu_quant, w4a4_rope), called through the C ABI.
+w4a4_geglu_quant, w4a4_rope, w4a4_prefix_attention), called through the C
+ABI.
 
 The glue each kernel fuses is floating-point PyTorch in the reference
 (pi05_fast/w4a4/apply.py:126-191 over transformers' Gemma layer), so its
@@ -10,7 +11,12 @@ check is PyTorch's own eager CUDA result on the same GPU:
 * the residual add: bit-exact; GemmaRMSNorm: within one fp16 ulp (the mean
   of squares is summed in another order), almost always equal;
 * the codes and row scales that follow: bit-exact against the CPU oracle fed
-  the kernel's own normalised / GeGLU values (written to h_out).
+  the kernel's own normalised / GeGLU values (written to h_out);
+* attention (fp32 scores and softmax, fp16 probabilities, fp32 P V): against
+  an fp64 evaluation of the same masked attention, its max error must not
+  exceed 1.5 x that of the reference's eager fp16 attention (which rounds the
+  scores and the normalised probabilities to fp16), nor 2e-3 where that one
+  is smaller.
 """
 
 from __future__ import annotations
@@ -197,3 +203,98 @@ def test_rope_matches_transformers(heads):
                                   cos.data_ptr(), sin.data_ptr(), m, heads, _stream()))
     torch.cuda.synchronize()
     assert_half_equal(x, ref)
+
+
+# ----------------------------------------------------------------------------- attention
+def attention_eager_fp16(q, k, v, pad, heads):
+    """transformers' eager_attention_forward in fp16 under lerobot's prefix
+    mask (fp32 additive mask value -2.3819763e38): the reference's rounding."""
+    from pi05_pytorch_fast_b200.prefix_lm import prefix_positions_and_mask
+
+    b, seq = pad.shape
+    _, mask = prefix_positions_and_mask(pad)
+    qh = q.view(b, seq, heads, 256).transpose(1, 2)
+    kh = k.view(b, seq, 1, 256).transpose(1, 2).expand(b, heads, seq, 256)
+    vh = v.view(b, seq, 1, 256).transpose(1, 2).expand(b, heads, seq, 256)
+    w = torch.matmul(qh, kh.transpose(2, 3)) * (256 ** -0.5)
+    w = torch.softmax(w + mask, dim=-1, dtype=torch.float32).to(torch.float16)
+    return torch.matmul(w, vh).transpose(1, 2).reshape(b * seq, heads * 256)
+
+
+def attention_fp64(q, k, v, pad, heads):
+    """The same attention in fp64: real queries over real keys, padded
+    queries uniform over all keys."""
+    b, seq = pad.shape
+    qh = q.view(b, seq, heads, 256).double().transpose(1, 2)
+    kh = k.view(b, seq, 1, 256).double().transpose(1, 2)
+    vh = v.view(b, seq, 1, 256).double().transpose(1, 2)
+    s = (qh @ kh.transpose(2, 3)) / 16.0
+    allowed = pad[:, None, :, None] & pad[:, None, None, :]
+    s = s.masked_fill(~allowed, float("-inf"))
+    s = torch.where((~pad)[:, None, :, None], torch.zeros_like(s), s)
+    return (torch.softmax(s, dim=-1) @ vh).transpose(1, 2).reshape(b * seq, heads * 256)
+
+
+def prefix_attention(q, k, v, pad, heads):
+    b, seq = pad.shape
+    key_valid = pad.to(torch.uint8).contiguous()
+    kv_len = (pad * torch.arange(1, seq + 1, device=DEV)).amax(dim=1).to(torch.int32)
+    vt = torch.empty((b, 256, nat.attn_vt_stride(seq)), dtype=torch.float16, device=DEV)
+    out = torch.full((b * seq, heads * 256), float("nan"), dtype=torch.float16, device=DEV)
+    nat.check(nat.lib().w4a4_prefix_attention(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
+                                              v.data_ptr(), v.stride(0), key_valid.data_ptr(),
+                                              kv_len.data_ptr(), b, seq, heads, vt.data_ptr(),
+                                              out.data_ptr(), out.stride(0), _stream()))
+    return out
+
+
+ATTN_CASES = [  # (batch, seq, real tokens per observation, q scale)
+    (1, 776, [628], 1.0),
+    (1, 776, [628], 4.0),
+    (2, 640, [640, 300], 2.0),
+    (3, 100, [1, 57, 100], 1.0),
+    (1, 1, [1], 1.0),
+    (2, 200, [0, 130], 1.0),
+]
+
+
+@pytest.mark.parametrize("batch,seq,real,qscale", ATTN_CASES)
+def test_prefix_attention_matches_fp64_at_least_as_well_as_eager(batch, seq, real, qscale):
+    heads = 8
+    gen = torch.Generator(device=DEV).manual_seed(seq + batch)
+    q = (torch.randn(batch * seq, heads * 256, device=DEV, generator=gen) * qscale).half()
+    k = torch.randn(batch * seq, 256, device=DEV, generator=gen).half()
+    v = torch.randn(batch * seq, 256, device=DEV, generator=gen).half()
+    pad = torch.zeros(batch, seq, dtype=torch.bool, device=DEV)
+    for i, n in enumerate(real):
+        pad[i, :n] = True
+    out = prefix_attention(q, k, v, pad, heads)
+    truth = attention_fp64(q, k, v, pad, heads)
+    eager = attention_eager_fp16(q, k, v, pad, heads)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(out).all())
+    rows = pad.reshape(-1)  # real queries; padded ones are checked below
+    err = (out.double() - truth).abs()
+    err_eager = (eager.double() - truth).abs()
+    if rows.any():
+        e, e_ref = float(err[rows].max()), float(err_eager[rows].max())
+        print(f"attention max |err|: kernel {e:.2e}, eager fp16 {e_ref:.2e}")
+        assert e <= max(1.5 * e_ref, 2e-3), (e, e_ref)
+    # padded queries: the mean of all seq values of their observation
+    if (~rows).any():
+        assert float(err[~rows].max()) <= 2e-3
+
+
+def test_prefix_attention_rows_are_independent_of_the_batch():
+    """An observation's output does not depend on the others in the batch."""
+    heads, seq = 8, 776
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    q = torch.randn(2 * seq, heads * 256, device=DEV, generator=gen).half()
+    k = torch.randn(2 * seq, 256, device=DEV, generator=gen).half()
+    v = torch.randn(2 * seq, 256, device=DEV, generator=gen).half()
+    pad = torch.ones(2, seq, dtype=torch.bool, device=DEV)
+    pad[:, 628:] = False
+    both = prefix_attention(q, k, v, pad, heads)
+    second = prefix_attention(q[seq:].contiguous(), k[seq:].contiguous(), v[seq:].contiguous(), pad[1:], heads)
+    torch.cuda.synchronize()
+    assert torch.equal(both[seq:].view(torch.int16), second.view(torch.int16))

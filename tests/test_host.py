@@ -392,14 +392,18 @@ def test_rope_tables_match_transformers_rotary_embedding():
     cfg = plm.PrefixLMConfig()
     hf = GemmaRotaryEmbedding(GemmaConfig(hidden_size=2048, num_attention_heads=8, num_key_value_heads=1,
                                           head_dim=256))
-    assert torch.equal(hf.inv_freq, plm.rope_inv_freq(cfg))
+    assert torch.equal(hf.inv_freq, plm.rope_inv_freq(cfg, fp16_buffer=False))
     pad = torch.ones(1, 776, dtype=torch.bool)
     pad[0, 628:] = False
     pos, _ = plm.prefix_positions_and_mask(pad)
-    cos_hf, sin_hf = hf(torch.empty(1, 776, 2048, dtype=torch.float16), pos)
-    freqs = pos.reshape(-1, 1).float() * plm.rope_inv_freq(cfg)[None, :]
-    emb = torch.cat((freqs, freqs), dim=-1)
-    assert torch.equal(emb.cos().half(), cos_hf[0]) and torch.equal(emb.sin().half(), sin_hf[0])
+    x = torch.empty(1, 776, 2048, dtype=torch.float16)
+    for fp16_buffer in (False, True):
+        if fp16_buffer:  # the reference's fp16 LM cast (buffers included)
+            hf.inv_freq.data = hf.inv_freq.data.half()
+        cos_hf, sin_hf = hf(x, pos)
+        freqs = pos.reshape(-1, 1).float() * plm.rope_inv_freq(cfg, fp16_buffer)[None, :]
+        emb = torch.cat((freqs, freqs), dim=-1)
+        assert torch.equal(emb.cos().half(), cos_hf[0]) and torch.equal(emb.sin().half(), sin_hf[0])
 
 
 def test_synthetic_prefix_layout():
@@ -410,3 +414,18 @@ def test_synthetic_prefix_layout():
     assert pad.shape == (2, 776) and int(pad.sum()) == 2 * 628 and not bool(pad[:, 628:].any())
     emb2, _ = plm.synthetic_prefix(1, lang_tokens=64, seed=3)
     assert emb2.shape == (1, 640, 2048)
+
+
+def test_attention_argument_validation_without_gpu():
+    lib = nat.lib()
+    fake = 0x1000
+    args = lambda **kw: [kw.get("q", fake), kw.get("ldq", 2048), fake, 256, fake, 256, fake, fake,  # noqa: E731
+                         kw.get("batch", 1), kw.get("seq", 776), kw.get("heads", 8), fake, fake,
+                         kw.get("ldo", 2048), None]
+    assert "heads must divide 128" in _err(lib.w4a4_prefix_attention(*args(heads=3)))
+    assert "exceeds 4096" in _err(lib.w4a4_prefix_attention(*args(seq=5000)))
+    assert "16-byte aligned" in _err(lib.w4a4_prefix_attention(*args(q=fake + 2)))
+    assert "16-byte aligned" in _err(lib.w4a4_prefix_attention(*args(ldq=1000)))
+    assert "invalid attention shape" in _err(lib.w4a4_prefix_attention(*args(batch=-1)))
+    assert lib.w4a4_prefix_attention(*args(batch=0)) == nat.W4A4_OK
+    assert nat.attn_vt_stride(776) == 776 and nat.attn_vt_stride(100) == 104
