@@ -70,7 +70,7 @@ def parse_args():
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timings")
     ap.add_argument("--roofline-reps", type=int, default=20)
     ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k",
-                                       "normquant", "geglu", "forward"),
+                                       "normquant", "geglu", "attn", "forward"),
                     default=None, help="run one op (or one forward) 3 times at the bench shape and "
                                        "exit (a small, self-contained case for ncu)")
     return ap.parse_args()
@@ -635,6 +635,10 @@ def run_case(args):
     sb = torch.empty((m,), dtype=torch.float32, device=device)
     gain = torch.ones(HIDDEN, dtype=torch.float32, device=device)
     embeds, pad = plm.synthetic_prefix(args.batch, lang_tokens=args.prefix - N_IMG, device=device)
+    if args.case == "attn":  # the forward's key mask and spans
+        with torch.no_grad():
+            model.forward(embeds, pad)
+        torch.cuda.synchronize(device)
     for _ in range(3):
         if args.case == "qkv":
             ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]])
@@ -655,6 +659,12 @@ def run_case(args):
             nat.check(lib.w4a4_rmsnorm_quant(x.data_ptr(), HIDDEN, None, HIDDEN, gain.data_ptr(), 1e-6,
                                              None, HIDDEN, None, HIDDEN, m, HIDDEN, staging,
                                              nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), st))
+        elif args.case == "attn":
+            ws = model.workspace(args.batch, args.prefix)
+            nat.check(lib.w4a4_prefix_attention(
+                x.data_ptr(), HIDDEN, h.data_ptr(), INTER, h.data_ptr() + 2 * 256, INTER,
+                ws.key_valid.data_ptr(), ws.kv_len.data_ptr(), args.batch, args.prefix, 8,
+                ws.vt.data_ptr(), ws.attn.data_ptr(), HIDDEN, st))
         elif args.case == "forward":
             with torch.no_grad():
                 model.forward(embeds, pad)

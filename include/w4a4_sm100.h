@@ -171,6 +171,26 @@ int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int
 int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
               const void* sin_t, int64_t m, int32_t heads, void* stream);
 
+/* ---- N-sharded gate/up (tensor-parallel MLP over P GPUs) ----
+ * No counterpart in the reference, which runs on one GPU: a rank holding a
+ * column shard [M, N/P] of gate and up forms its part of h with w4a4_geglu,
+ * the ranks exchange row blocks (an all-to-all, NCCL), and each rank
+ * quantises its complete rows straight from the P received segments with
+ * w4a4_quant_segments. */
+
+/* h = fl16(fl16(gelu_tanh(gate)) * up) elementwise over [m, n] (n a multiple
+ * of 8; the rounding of w4a4_geglu_quant and of PyTorch's eager ops). */
+int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
+               int64_t ldh, void* stream);
+
+/* w4a4_quant of K = 16384 rows (rotated) whose elements are stored as
+ * K / seg segments: element e of row r at x + (e / seg) * seg_stride +
+ * r * ld + e % seg (seg a multiple of 64 dividing K; ld >= seg; seg_stride >=
+ * m * ld).  Codes and scales are those w4a4_quant gives the contiguous rows. */
+int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_t ld,
+                        int64_t seg_stride, int32_t staging, int32_t codes_format, void* codes,
+                        float* row_scale, void* stream);
+
 /* Bidirectional prefix attention with one shared key/value head (Gemma-2B:
  * 8 query heads, 1 kv head, head_dim 256) on the tensor cores.  Replaces
  * the reference's eager attention (apply.py:170-188, transformers'

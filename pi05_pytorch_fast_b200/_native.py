@@ -45,6 +45,8 @@ EXPORTED_SYMBOLS = (
     "w4a4_geglu_quant",
     "w4a4_rope",
     "w4a4_prefix_attention",
+    "w4a4_geglu",
+    "w4a4_quant_segments",
     "w4a4_pad_rows",
     "w4a4_last_error",
     "w4a4_device_error",
@@ -96,6 +98,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_rope.argtypes = [vp, c_i64, vp, c_i64, vp, vp, c_i64, c_i32, vp]
     lib.w4a4_prefix_attention.argtypes = [vp, c_i64, vp, c_i64, vp, c_i64, vp, vp, c_i32, c_i32, c_i32,
                                           vp, vp, c_i64, vp]
+    lib.w4a4_geglu.argtypes = [vp, vp, c_i64, c_i32, c_i64, vp, c_i64, vp]
+    lib.w4a4_quant_segments.argtypes = [vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]

@@ -16,17 +16,19 @@
 //  * warp 1 issues S = Q K^T (M = 128, N = 64, 16 MMAs of K = 16 over d) into
 //    one of two TMEM score buffers, and O += P V^T (M = 128, N = 256, 4 MMAs of
 //    K = 16 keys) with P read from TMEM (the A operand of the TS form);
-//  * warps 2-5 (one per TMEM lane quarter, thread = row) run the softmax:
-//    pass 1 reads each score block once for the row max and sum; pass 2
-//    recomputes the block, writes p = exp(s - max) as fp16 into TMEM for the
-//    PV MMA; then they scale O by 1 / sum and store fp16 rows;
+//  * warps 2-5 (one per TMEM lane quarter, thread = row) run an online
+//    softmax in one pass: p = exp2(s - m) as fp16 into TMEM for the PV MMA,
+//    with the running max m moved (and O rescaled in TMEM) only when a block
+//    exceeds it by more than 2^8; then they scale O by 1 / sum and store fp16
+//    rows;
 //  * key blocks past the last real key are skipped for tiles of real queries;
 //  * every wait is bounded (the device error word, an abort flag, teardown
 //    that drains its copies and MMAs and frees TMEM).
-// Softmax is base 2: s2 = acc * (scale * log2 e), p = exp2(s2 - max2).
+// Softmax is base 2: s2 = acc * (scale * log2 e), p = exp2(s2 - m).
 #pragma once
 
 #include "common.cuh"
+#include "quant.cuh"
 
 namespace w4a4 {
 
@@ -93,13 +95,22 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-// 4-D tiled bulk tensor load global -> shared (x innermost, in elements).
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int x, int y, int z,
-                                            int w, uint32_t bar) {
+// 2^x with the MUFU instruction (ex2.approx.ftz.f32: relative error about
+// 2^-22, flushes subnormal results; exp2(-inf) = +0).  The probabilities it
+// produces are rounded to fp16 for the P V product, far coarser.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 32 lanes x 16 consecutive 32-bit columns from registers.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 
@@ -202,45 +213,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int s = 0; s < kAttnSlices; ++s)
         tma_load_4d(smem_addr(q_smem + s * (kAttnQBytes / kAttnSlices)), &p.tmap_q, 64 * s, 0, t0, b,
                     bar_q());
-      int nk = 0, nv = 0;
-      bool alive = true;
-      // K blocks for pass 1 (0 .. nkb-1) then pass 2 (again), V blocks in pass 2.
-      for (int g = 0; alive && g < 2 * nkb; ++g) {
-        const int slot = g & 1;
-        if (g >= kAttnStages &&
-            !mbar_wait_bounded(bar_kempty(slot), ((g >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit)) {
-          alive = false;
+      int n = 0;
+      // key block kb: K into k slot kb % 2, V^T into v slot kb % 2
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int slot = kb & 1;
+        if (kb >= kAttnStages &&
+            !mbar_wait_bounded(bar_kempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
           break;
-        }
-        const int kb = g < nkb ? g : g - nkb;
         mbar_arrive_expect_tx(bar_kfull(slot), kAttnKBytes);
         for (int s = 0; s < kAttnSlices; ++s)
           tma_load_3d(smem_addr(k_ring + slot * kAttnKBytes + s * (kAttnKBytes / kAttnSlices)), &p.tmap_k,
                       64 * s, kb * kAttnKeyBlock, b, bar_kfull(slot));
-        ++nk;
-        if (g >= nkb) {
-          const int vslot = kb & 1;
-          if (kb >= kAttnStages &&
-              !mbar_wait_bounded(bar_vempty(vslot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty,
-                                 limit)) {
-            alive = false;
-            break;
-          }
-          mbar_arrive_expect_tx(bar_vfull(vslot), kAttnVBytes);
-          tma_load_3d(smem_addr(v_ring + vslot * kAttnVBytes), &p.tmap_vt, kb * kAttnKeyBlock, 0, b,
-                      bar_vfull(vslot));
-          ++nv;
+        if (kb >= kAttnStages &&
+            !mbar_wait_bounded(bar_vempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit)) {
+          // the K copy of this block is in flight: account for it in the drain
+          volatile int no_abort = 0;
+          mbar_wait_bounded(bar_kfull(slot), (kb >> 1) & 1, &no_abort, err, kErrWaitDrain, limit);
+          break;
         }
+        mbar_arrive_expect_tx(bar_vfull(slot), kAttnVBytes);
+        tma_load_3d(smem_addr(v_ring + slot * kAttnVBytes), &p.tmap_vt, kb * kAttnKeyBlock, 0, b,
+                    bar_vfull(slot));
+        ++n;
       }
       // Drain: no copy may still be in flight at exit.
       volatile int no_abort = 0;
       mbar_wait_bounded(bar_q(), 0, &no_abort, err, kErrWaitDrain, limit);
-      for (int i = 0; i < kAttnStages && i < nk; ++i) {
-        const int last = i + ((nk - 1 - i) / kAttnStages) * kAttnStages;
+      for (int i = 0; i < kAttnStages && i < n; ++i) {
+        const int last = i + ((n - 1 - i) / kAttnStages) * kAttnStages;
         mbar_wait_bounded(bar_kfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
-      }
-      for (int i = 0; i < kAttnStages && i < nv; ++i) {
-        const int last = i + ((nv - 1 - i) / kAttnStages) * kAttnStages;
         mbar_wait_bounded(bar_vfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
       }
     }
@@ -252,34 +253,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t idesc_o = idesc_f16(kAttnRows, kAttnHeadDim);
     const uint64_t qdesc = smem_desc_sw128(smem_addr(q_smem));
     bool alive = nkb > 0 && warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit));
-    // S(g) for score block g (g < nkb: pass 1, else pass 2 of block g - nkb)
-    const auto issue_s = [&](int g) -> bool {
-      const int slot = g & 1;
-      bool ok = mbar_wait_bounded(bar_kfull(slot), (g >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
-      if (ok && g >= 2)
-        ok = mbar_wait_bounded(bar_sfree(slot), ((g >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
+    // S(kb) = Q K(kb)^T into score buffer kb % 2
+    const auto issue_s = [&](int kb) -> bool {
+      const int slot = kb & 1;
+      bool ok = mbar_wait_bounded(bar_kfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+      if (ok && kb >= 2)
+        ok = mbar_wait_bounded(bar_sfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
       if (!warp_all(ok)) return false;
       tc_fence_after();
       const uint64_t kdesc = smem_desc_sw128(smem_addr(k_ring + slot * kAttnKBytes));
-      if (issuer) {
+      // warp-uniform loop, one lane issues (a loop inside a one-lane branch
+      // issues several times slower)
 #pragma unroll
-        for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>((kk & 3) * 2);
+      for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
+        const uint64_t off = static_cast<uint64_t>((kk & 3) * 2);
+        if (issuer)
           umma_f16_ss(tmem_base + kAttnSCol + slot * kAttnKeyBlock,
                       qdesc + static_cast<uint64_t>((kk >> 2) * (kAttnQBytes / kAttnSlices) >> 4) + off,
                       kdesc + static_cast<uint64_t>((kk >> 2) * (kAttnKBytes / kAttnSlices) >> 4) + off,
                       idesc_s, kk > 0);
-        }
+      }
+      if (issuer) {
         umma_commit(bar_kempty(slot));
         umma_commit(bar_sfull(slot));
       }
       __syncwarp();
       return true;
     };
-    for (int g = 0; alive && g < nkb; ++g) alive = issue_s(g);
-    if (alive) alive = issue_s(nkb);
+    if (alive) alive = issue_s(0);
     for (int kb = 0; alive && kb < nkb; ++kb) {
-      if (kb + 1 < nkb && !(alive = issue_s(nkb + kb + 1))) break;
+      if (kb + 1 < nkb && !(alive = issue_s(kb + 1))) break;
       const int slot = kb & 1;
       bool ok = mbar_wait_bounded(bar_vfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
       if (ok) ok = mbar_wait_bounded(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
@@ -289,11 +292,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       tc_fence_after();
       const uint64_t vdesc = smem_desc_sw128(smem_addr(v_ring + slot * kAttnVBytes));
-      if (issuer) {
 #pragma unroll
-        for (int kk = 0; kk < kAttnKeyBlock / 16; ++kk)
+      for (int kk = 0; kk < kAttnKeyBlock / 16; ++kk)
+        if (issuer)
           umma_f16_ts(tmem_base + kAttnOCol, tmem_base + kAttnPCol + slot * 32 + 8 * kk,
                       vdesc + static_cast<uint64_t>(kk * 2), idesc_o, (kb | kk) != 0);
+      if (issuer) {
         umma_commit(bar_vempty(slot));
         umma_commit(bar_pfree(slot));
       }
@@ -305,72 +309,94 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------ softmax + epilogue (warps 2-5)
+    // Online softmax in one pass, base 2 (s2 = acc * scale * log2 e): the
+    // row's running max m only moves up when a block's max exceeds it by
+    // more than kRescaleLog2, and then O (TMEM) and l are rescaled by
+    // exp2(m_old - m_new) once the previous P V MMA has completed; otherwise
+    // p = exp2(s2 - m) <= 2^kRescaleLog2 is kept unnormalised (fp16 holds it).
+    constexpr float kRescaleLog2 = 8.f;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;                // this thread's row (TMEM lane)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int tok = t0 + r / p.heads, head = r % p.heads;
     const bool q_real = tok < L && p.key_valid[static_cast<long long>(b) * L + tok];
+    const float scale = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool alive = nkb > 0;
-    // masked scores of block kb, this row: real query -> real keys only;
-    // padded query -> every key < L with score 0 (uniform weights)
-    const auto scores = [&](int kb, const uint32_t (&raw)[64], float (&s)[64]) {
-      const unsigned long long km = kmask[kb];
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int j = kb * kAttnKeyBlock + c;
-        const bool ok = q_real ? ((km >> c) & 1ull) != 0 : j < L;
-        s[c] = ok ? (q_real ? __fmul_rn(__uint_as_float(raw[c]), p.scale_log2) : 0.f) : -INFINITY;
+    for (int kb = 0; alive && kb < nkb; ++kb) {
+      const int slot = kb & 1;
+      if (!warp_all(mbar_wait_bounded(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
+        alive = false;
+        break;
       }
-    };
-    const auto load_s = [&](int g, uint32_t (&raw)[64]) -> bool {
-      const int slot = g & 1;
-      if (!warp_all(mbar_wait_bounded(bar_sfull(slot), (g >> 1) & 1, abort_flag, err, kErrWaitAccum, limit)))
-        return false;
       tc_fence_after();
-      const uint32_t t = tmem_base + lane_addr + kAttnSCol + slot * kAttnKeyBlock;
-      tmem_ld_32x32b_x16(t, *reinterpret_cast<uint32_t(*)[16]>(&raw[0]));
-      tmem_ld_32x32b_x16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&raw[16]));
-      tmem_ld_32x32b_x16(t + 32, *reinterpret_cast<uint32_t(*)[16]>(&raw[32]));
-      tmem_ld_32x32b_x16(t + 48, *reinterpret_cast<uint32_t(*)[16]>(&raw[48]));
-      tmem_ld_wait();
+      uint32_t raw[64];
+      {
+        const uint32_t t = tmem_base + lane_addr + kAttnSCol + slot * kAttnKeyBlock;
+        tmem_ld_32x32b_x16(t, *reinterpret_cast<uint32_t(*)[16]>(&raw[0]));
+        tmem_ld_32x32b_x16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&raw[16]));
+        tmem_ld_32x32b_x16(t + 32, *reinterpret_cast<uint32_t(*)[16]>(&raw[32]));
+        tmem_ld_32x32b_x16(t + 48, *reinterpret_cast<uint32_t(*)[16]>(&raw[48]));
+        tmem_ld_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sfree(slot));
-      return true;
-    };
-    // pass 1: row max and sum
-    for (int g = 0; alive && g < nkb; ++g) {
-      uint32_t raw[64];
-      float s[64];
-      if (!(alive = load_s(g, raw))) break;
-      scores(g, raw, s);
-      float bm = -INFINITY;
+      // real query: its real keys; padded query: every key < L, score 0
+      const int j0 = kb * kAttnKeyBlock;
+      const unsigned long long vm =
+          q_real ? kmask[kb]
+                 : (L - j0 >= 64 ? ~0ull : ((1ull << (L - j0)) - 1ull));
+      const unsigned vlo = static_cast<unsigned>(vm), vhi = static_cast<unsigned>(vm >> 32);
+      float bmax = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) bm = fmaxf(bm, s[c]);
-      const float mn = fmaxf(m, bm);
-      if (mn != -INFINITY) {
-        float sum = 0.f;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) sum += exp2f(s[c] - mn);
-        l = l * exp2f(m - mn) + sum;
-        m = mn;
+      for (int c = 0; c < 64; ++c) {
+        const float v = q_real ? __uint_as_float(raw[c]) : 0.f;
+        const bool ok = ((c < 32 ? vlo >> c : vhi >> (c - 32)) & 1u) != 0;
+        raw[c] = __float_as_uint(ok ? v : -INFINITY);
+        bmax = fmaxf(bmax, ok ? v : -INFINITY);
       }
-    }
-    // pass 2: p = exp2(s - m) as fp16 into TMEM for the PV MMA
-    for (int kb = 0; alive && kb < nkb; ++kb) {
-      uint32_t raw[64];
-      float s[64];
-      if (!(alive = load_s(nkb + kb, raw))) break;
-      scores(kb, raw, s);
+      bmax *= scale;  // scale > 0: the max of scaled scores
+      float f = 1.f;  // rescale of the previous O and l
+      const bool grow = bmax > m + kRescaleLog2;  // false while the block is all masked
+      if (grow) {
+        f = m == -INFINITY ? 0.f : ex2_approx(m - bmax);
+        m = bmax;
+        l *= f;
+      }
+      if (__any_sync(0xffffffffu, grow && f != 0.f) && kb >= 1) {
+        // O holds P V of earlier blocks: wait for the last of them, rescale
+        // this warp's rows (whole-warp TMEM access; others multiply by 1)
+        if (!warp_all(mbar_wait_bounded(bar_pfree((kb - 1) & 1), ((kb - 1) >> 1) & 1, abort_flag, err,
+                                        kErrWaitAccum, limit))) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < kAttnHeadDim; c0 += 16) {
+          uint32_t o[16];
+          const uint32_t t = tmem_base + lane_addr + kAttnOCol + c0;
+          tmem_ld_32x32b_x16(t, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st_32x32b_x16(t, o);
+        }
+        tmem_st_wait();
+      }
+      // p = exp2(s2 - m) as fp16 pairs, l += sum p (masked: exp2(-inf) = 0)
+      const float nm = m == -INFINITY ? 0.f : -m;
       uint32_t pw[32];
+      float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float p0 = m == -INFINITY ? 0.f : exp2f(s[2 * c] - m);
-        const float p1 = m == -INFINITY ? 0.f : exp2f(s[2 * c + 1] - m);
+        const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(raw[2 * c]), scale, nm));
+        const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(raw[2 * c + 1]), scale, nm));
+        sum += p0 + p1;
         pw[c] = pack_half2_bits(p0, p1);
       }
-      const int slot = kb & 1;
+      l += sum;
       if (kb >= 2 && !warp_all(mbar_wait_bounded(bar_pfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err,
                                                   kErrWaitAccum, limit))) {
         alive = false;
@@ -421,23 +447,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // V [B * L, ldv] (rows of 256) -> V^T per observation [B][256][ldt]: the
-// B operand of the PV MMA must be K-major (keys contiguous).  64 x 64 tiles
-// through shared memory.
+// B operand of the PV MMA must be K-major (keys contiguous).  A CTA moves a
+// 64-key x 64-d tile through shared memory with 16-byte loads and stores;
+// keys in [seq, ldt) are written as zeros.
 __global__ void __launch_bounds__(256) transpose_v_kernel(const __half* __restrict__ v, long long ldv,
                                                           __half* __restrict__ vt, long long ldt, int seq) {
-  __shared__ __half tile[64][66];
+  __shared__ __align__(16) __half tile[64][72];  // 144-byte rows: 16-byte aligned, staggered banks
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.z, j0 = blockIdx.x * 64, d0 = blockIdx.y * 64;
-  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
-  for (int j = ty; j < 64; j += 4) {
-    const int key = j0 + j;
-    tile[j][tx] = key < seq ? v[(static_cast<long long>(b) * seq + key) * ldv + d0 + tx] : __float2half(0.f);
+  const int t = threadIdx.x, c = t & 7;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int j = (t >> 3) + 32 * h;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (j0 + j < seq)
+      val = ld_nc_v4(v + (static_cast<long long>(b) * seq + j0 + j) * ldv + d0 + 8 * c);
+    *reinterpret_cast<uint4*>(&tile[j][8 * c]) = val;
   }
   __syncthreads();
-  for (int d = ty; d < 64; d += 4) {
-    const int key = j0 + tx;
-    if (key < ldt) vt[(static_cast<long long>(b) * kAttnHeadDim + d0 + d) * ldt + key] = tile[tx][d];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int d = (t >> 3) + 32 * h;
+    if (j0 + 8 * c >= ldt) continue;
+    uint4 out;
+    __half* oh = reinterpret_cast<__half*>(&out);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) oh[i] = tile[8 * c + i][d];
+    *reinterpret_cast<uint4*>(vt + (static_cast<long long>(b) * kAttnHeadDim + d0 + d) * ldt + j0 + 8 * c) = out;
   }
 }
 

@@ -274,6 +274,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// 4-D tiled bulk tensor load global -> shared (x innermost, in elements).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int x, int y, int z,
+                                            int w, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
 // 2-D tile load for a CTA pair (tcgen05 cta_group::2): the data lands in this
 // CTA's shared memory, the transaction bytes are counted on the mbarrier at
 // the same offset in the pair's even (leader) CTA.

@@ -89,6 +89,24 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(
     fwht_quant_row_split<11, FP16, MODE>(v, sm, warp, lane, row, codes, row_scale, inv_sqrt_k);
 }
 
+// GeGLU alone, h = fl16(fl16(gelu_tanh(gate)) * up) over [m, n] (n a
+// multiple of 8): the MLP of a rank that holds a column shard of gate/up,
+// whose rows are completed by an exchange before they are quantised.
+__global__ void __launch_bounds__(256) geglu_kernel(const __half* __restrict__ gate,
+                                                    const __half* __restrict__ up, long long ld,
+                                                    __half* __restrict__ h, long long ldh, long long m,
+                                                    int n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int vpr = n / 8;
+  const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (idx >= m * vpr) return;
+  const long long row = idx / vpr;
+  const int c = static_cast<int>(idx - row * vpr) * 8;
+  *reinterpret_cast<uint4*>(h + row * ldh + c) =
+      geglu8(ld_nc_v4(gate + row * ld + c), ld_nc_v4(up + row * ld + c));
+}
+
 // Rotary embedding of `heads` heads of width 256 per row: element d < 128
 // pairs with d + 128.  cos / sin are fp16 [m, 256] tables (row stride 256),
 // the per-position values transformers' rotary embedding produces.  One

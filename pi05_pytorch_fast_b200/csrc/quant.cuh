@@ -503,11 +503,14 @@ __global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
 // values at offsets 256c + 8l + j and finishes bits 11-13 in registers.
 // GEGLU: the row is gelu_tanh(x) * up (x = the gate), formed as it is
 // loaded (geglu8) and, when h_out is not null, also written there.
-template <bool FP16, int MODE, bool GEGLU = false>
+// SEGMENTED: the row is stored as segments of `seg` elements (a multiple of
+// 8), segment s of row r at x + s * seg_stride + r * ldx.
+template <bool FP16, int MODE, bool GEGLU = false, bool SEGMENTED = false>
 __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, const __half* __restrict__ up = nullptr,
-    long long ldu = 0, __half* __restrict__ h_out = nullptr, long long ldh = 0) {
+    long long ldu = 0, __half* __restrict__ h_out = nullptr, long long ldh = 0, int seg = 0,
+    long long seg_stride = 0) {
   constexpr int K = 16384;
   constexpr int RBITS = 6;  // log2(16384 / 256)
   extern __shared__ __align__(16) unsigned char quant_smem[];
@@ -528,6 +531,13 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
         const uint4 h8 = geglu8(ld_nc_v4(xr + 256 * c), ld_nc_v4(ur + 256 * c));
         if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 2048 * warp + 8 * lane + 256 * c) = h8;
         half8_to_float(h8, v[c]);
+      }
+    } else if constexpr (SEGMENTED) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int e = 2048 * warp + 256 * c + 8 * lane;
+        const int sgi = e / seg;
+        load8_half_as_float(x + sgi * seg_stride + row * ldx + (e - sgi * seg), v[c]);
       }
     } else {
 #pragma unroll
@@ -636,7 +646,10 @@ constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
 // GEGLU: xmap is the gate and umap the up projection (same shape); the row
 // quantised is gelu_tanh(gate) * up, formed in phase A (geglu8) and, when
 // h_out is not null, written there too.  Otherwise umap is unused.
-template <int MODE, bool GEGLU = false>
+// SEGMENTED: xmap is 4-D {64, lines per segment, M, segments} (a row stored
+// as several segments, each a [M, seg] matrix: the layout an all-to-all of
+// column shards delivers), read with one box per row; same smem layout.
+template <int MODE, bool GEGLU = false, bool SEGMENTED = false>
 __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
     const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns,
@@ -662,7 +675,10 @@ __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp
   if (row >= m) return;
   if (u == 0) {
     mbar_arrive_expect_tx(bar_a, GEGLU ? 2 * kQ16RowBytes : kQ16RowBytes);
-    tma_load_3d(smem_addr(base), &xmap, 0, 0, static_cast<int>(row), bar_a);
+    if constexpr (SEGMENTED)
+      tma_load_4d(smem_addr(base), &xmap, 0, 0, static_cast<int>(row), 0, bar_a);
+    else
+      tma_load_3d(smem_addr(base), &xmap, 0, 0, static_cast<int>(row), bar_a);
     if constexpr (GEGLU) tma_load_3d(smem_addr(base + kQ16RowBytes), &umap, 0, 0, static_cast<int>(row), bar_a);
   }
   if (!mbar_wait_bounded(bar_a, 0, &abort_flag, &g_w4a4_device_error, kErrWaitTma, limit_ns))

@@ -367,7 +367,7 @@ int launch_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotat
         err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<F, MODE>, dim3(grid), dim3(kQuantThreads),
                                              smem, stream, 1, xh, ldx, m, codes, row_scale, isk,
                                              static_cast<const __half*>(nullptr), 0ll,
-                                             static_cast<__half*>(nullptr), 0ll));
+                                             static_cast<__half*>(nullptr), 0ll, 0, 0ll));
     });
   } else {
     dispatch([&](auto, auto mode) {
@@ -513,7 +513,89 @@ int launch_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, i
       err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<false, MODE, true>, dim3(grid),
                                            dim3(kQuantThreads), smem, stream, 1,
                                            static_cast<const __half*>(gate), ld, m, codes, row_scale, isk,
-                                           static_cast<const __half*>(up), ld, ho, ldh));
+                                           static_cast<const __half*>(up), ld, ho, ldh, 0, 0ll));
+    }
+  });
+  if (err_code) return err_code;
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int launch_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
+                 int64_t ldh, cudaStream_t stream) {
+  if (m < 0 || n <= 0 || n % 8 != 0)
+    return fail(W4A4_ERR_INVALID, "geglu: invalid shape m=%lld n=%d (n a positive multiple of 8)", (long long)m, n);
+  if (m == 0) return ok();
+  if (!gate || !up || !h) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (!aligned(gate, 16) || !aligned(up, 16) || !aligned(h, 16) || ld < n || ldh < n || ld % 8 || ldh % 8)
+    return fail(W4A4_ERR_INVALID, "geglu rows must be 16-byte aligned with strides >= n, multiples of 8");
+  const int64_t blocks = (m * (n / 8) + 255) / 256;
+  if (blocks > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "geglu: too many rows");
+  W4A4_CUDA_TRY(launch_kernel(geglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
+                              static_cast<const __half*>(gate), static_cast<const __half*>(up), ld,
+                              static_cast<__half*>(h), ldh, m, n));
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int launch_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_t ld,
+                          int64_t seg_stride, int32_t staging, int32_t codes_format, void* codes,
+                          float* row_scale, cudaStream_t stream) {
+  if (k != 16384)
+    return fail(W4A4_ERR_UNSUPPORTED, "quant_segments supports K = 16384 only, got %d", k);
+  if (seg < 64 || seg % 64 != 0 || k % seg != 0 || k / seg > 256)
+    return fail(W4A4_ERR_INVALID, "segment width %d must be a multiple of 64 dividing K = %d", seg, k);
+  if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative, got %lld", (long long)m);
+  if (staging != W4A4_STAGING_FP16 && staging != W4A4_STAGING_FP32)
+    return fail(W4A4_ERR_INVALID, "unknown staging mode %d", staging);
+  if (int e = check_codes_format(codes_format)) return e;
+  if (m == 0) return ok();
+  if (m > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "M too large: %lld", (long long)m);
+  if (!x || !codes || !row_scale) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (!aligned(x, 16) || ld < seg || ld % 8 != 0 || seg_stride % 8 != 0 || seg_stride < ld * m)
+    return fail(W4A4_ERR_INVALID,
+                "segments must be 16-byte aligned [M, seg] blocks: stride >= seg and a multiple of 8, "
+                "segment stride >= M x stride and a multiple of 8");
+  if (!aligned(codes, 8)) return fail(W4A4_ERR_INVALID, "codes pointer must be 8-byte aligned");
+  int dev;
+  if (int e = current_device(&dev)) return e;
+  const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
+  const unsigned grid = static_cast<unsigned>(m);
+  int err_code = W4A4_OK;
+  dispatch_staging_format(staging == W4A4_STAGING_FP16, codes_format, [&](auto f, auto mode) {
+    constexpr bool F = decltype(f)::value;
+    constexpr int MODE = decltype(mode)::value;
+    if constexpr (F) {
+      CUtensorMap xmap;
+      const uint64_t dims[4] = {64, static_cast<uint64_t>(seg / 64), static_cast<uint64_t>(m),
+                                static_cast<uint64_t>(k / seg)};
+      const uint64_t strides[3] = {128, static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(seg_stride) * 2};
+      const uint32_t box[4] = {64, static_cast<uint32_t>(seg / 64), 1, static_cast<uint32_t>(k / seg)};
+      if (int e = make_map(&xmap, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B)) {
+        err_code = e;
+        return;
+      }
+      if (int e = ensure_smem_attr(dev, 1ull << (44 + MODE), quant_rot_16k_fp16_kernel<MODE, false, true>,
+                                   kQ16Smem)) {
+        err_code = e;
+        return;
+      }
+      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, false, true>, dim3(grid),
+                                           dim3(kQuantThreads), kQ16Smem, stream, 1, xmap, m, codes,
+                                           row_scale, isk, g_wait_limit_ns.load(), xmap,
+                                           static_cast<__half*>(nullptr), 0ll));
+    } else {
+      const int smem = 16384 * 4;
+      if (int e = ensure_smem_attr(dev, 1ull << (48 + MODE), quant_rot_16k_kernel<false, MODE, false, true>,
+                                   smem)) {
+        err_code = e;
+        return;
+      }
+      err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<false, MODE, false, true>, dim3(grid),
+                                           dim3(kQuantThreads), smem, stream, 1, static_cast<const __half*>(x),
+                                           ld, m, codes, row_scale, isk, static_cast<const __half*>(nullptr),
+                                           0ll, static_cast<__half*>(nullptr), 0ll, seg, seg_stride));
     }
   });
   if (err_code) return err_code;
@@ -1011,6 +1093,18 @@ int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk
                           void* stream) {
   return launch_attention(q, ldq, k, ldk, v, ldv, key_valid, kv_len, batch, seq, heads, vt_scratch, out,
                           ldo, static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
+               int64_t ldh, void* stream) {
+  return launch_geglu(gate, up, m, n, ld, h, ldh, static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_t ld,
+                        int64_t seg_stride, int32_t staging, int32_t codes_format, void* codes,
+                        float* row_scale, void* stream) {
+  return launch_quant_segments(x, m, k, seg, ld, seg_stride, staging, codes_format, codes, row_scale,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,

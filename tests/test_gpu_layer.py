@@ -12,7 +12,8 @@ check is PyTorch's own eager CUDA result on the same GPU:
   of squares is summed in another order), almost always equal;
 * the codes and row scales that follow: bit-exact against the CPU oracle fed
   the kernel's own normalised / GeGLU values (written to h_out);
-* attention (fp32 scores and softmax, fp16 probabilities, fp32 P V): against
+* attention (fp32 scores, one-pass online softmax, fp16 probabilities, fp32
+  P V): against
   an fp64 evaluation of the same masked attention, its max error must not
   exceed 1.5 x that of the reference's eager fp16 attention (which rounds the
   scores and the normalised probabilities to fp16), nor 2e-3 where that one
@@ -251,6 +252,7 @@ def prefix_attention(q, k, v, pad, heads):
 ATTN_CASES = [  # (batch, seq, real tokens per observation, q scale)
     (1, 776, [628], 1.0),
     (1, 776, [628], 4.0),
+    (1, 776, [628], 8.0),  # scores spread enough that later key blocks raise the row max (O rescaled)
     (2, 640, [640, 300], 2.0),
     (3, 100, [1, 57, 100], 1.0),
     (1, 1, [1], 1.0),
@@ -298,3 +300,25 @@ def test_prefix_attention_rows_are_independent_of_the_batch():
     second = prefix_attention(q[seq:].contiguous(), k[seq:].contiguous(), v[seq:].contiguous(), pad[1:], heads)
     torch.cuda.synchronize()
     assert torch.equal(both[seq:].view(torch.int16), second.view(torch.int16))
+
+
+def test_prefix_attention_rescales_when_a_late_key_dominates():
+    """The dominant key of every query sits in the last real key block, so
+    the running max jumps there and O is rescaled in TMEM."""
+    heads, seq = 8, 640
+    gen = torch.Generator(device=DEV).manual_seed(2)
+    q = torch.randn(seq, heads * 256, device=DEV, generator=gen).half()
+    k = (torch.randn(seq, 256, device=DEV, generator=gen) * 0.1).half()
+    v = torch.randn(seq, 256, device=DEV, generator=gen).half()
+    # key 600 aligned with every head's query direction: score ~ 3 * |q| * ...
+    qmean = q.float().view(seq, heads, 256).mean(dim=(0, 1))
+    k[600] = (qmean / qmean.norm() * 60).half()
+    pad = torch.ones(1, seq, dtype=torch.bool, device=DEV)
+    out = prefix_attention(q, k, v, pad, heads)
+    truth = attention_fp64(q, k, v, pad, heads)
+    eager = attention_eager_fp16(q, k, v, pad, heads)
+    torch.cuda.synchronize()
+    e = float((out.double() - truth).abs().max())
+    e_ref = float((eager.double() - truth).abs().max())
+    print(f"late-max attention: kernel {e:.2e}, eager fp16 {e_ref:.2e}")
+    assert e <= max(1.5 * e_ref, 2e-3)
