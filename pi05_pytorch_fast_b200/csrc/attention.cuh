@@ -181,21 +181,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_relinquish();
   }
   pdl_wait();  // q, k, v and the masks are earlier kernels' outputs
+  const uint8_t* kv_row = p.key_valid + static_cast<long long>(b) * L;
   // Key blocks to visit: up to the last real key, or all of them when a
   // padded (or past-the-end) query row is in the tile (uniform over L keys).
-  if (threadIdx.x == 0) {
+  // One load per lane (tpt <= 128 tokens: up to 4 per lane), then a vote.
+  if (warp == 0) {
     bool pad_row = false;
-    for (int t = t0; t < t0 + tpt; ++t) pad_row |= (t >= L) || !p.key_valid[static_cast<long long>(b) * L + t];
-    const int kv = pad_row ? L : max(0, min(L, p.kv_len[b]));
-    *nkb_slot = (kv + kAttnKeyBlock - 1) / kAttnKeyBlock;
+#pragma unroll
+    for (int i = 0; i < kAttnRows / 32; ++i) {
+      const int t = t0 + lane + 32 * i;
+      if (lane + 32 * i < tpt) pad_row |= t >= L || !kv_row[t];
+    }
+    const int kv_len = p.kv_len[b];
+    pad_row = __any_sync(0xffffffffu, pad_row);
+    if (lane == 0) *nkb_slot = ((pad_row ? L : max(0, min(L, kv_len))) + kAttnKeyBlock - 1) / kAttnKeyBlock;
   }
-  // 64-bit masks of the real keys of every block (warps 2-5)
+  // 64-bit masks of the real keys of every block (warps 2-5; the loads of a
+  // warp's blocks are independent and issued together)
   if (warp >= 2) {
     const int nblk = (L + kAttnKeyBlock - 1) / kAttnKeyBlock;
+#pragma unroll 4
     for (int kb = warp - 2; kb < nblk; kb += 4) {
       const int j0 = kb * kAttnKeyBlock + lane, j1 = j0 + 32;
-      const bool v0 = j0 < L && p.key_valid[static_cast<long long>(b) * L + j0];
-      const bool v1 = j1 < L && p.key_valid[static_cast<long long>(b) * L + j1];
+      const bool v0 = j0 < L && kv_row[j0];
+      const bool v1 = j1 < L && kv_row[j1];
       const unsigned lo = __ballot_sync(0xffffffffu, v0), hi = __ballot_sync(0xffffffffu, v1);
       if (lane == 0) kmask[kb] = static_cast<unsigned long long>(hi) << 32 | lo;
     }
@@ -218,14 +227,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int slot = kb & 1;
         if (kb >= kAttnStages &&
-            !mbar_wait_bounded(bar_kempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
+            !mbar_wait_spin(bar_kempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
           break;
         mbar_arrive_expect_tx(bar_kfull(slot), kAttnKBytes);
         for (int s = 0; s < kAttnSlices; ++s)
           tma_load_3d(smem_addr(k_ring + slot * kAttnKBytes + s * (kAttnKBytes / kAttnSlices)), &p.tmap_k,
                       64 * s, kb * kAttnKeyBlock, b, bar_kfull(slot));
         if (kb >= kAttnStages &&
-            !mbar_wait_bounded(bar_vempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit)) {
+            !mbar_wait_spin(bar_vempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit)) {
           // the K copy of this block is in flight: account for it in the drain
           volatile int no_abort = 0;
           mbar_wait_bounded(bar_kfull(slot), (kb >> 1) & 1, &no_abort, err, kErrWaitDrain, limit);
@@ -256,9 +265,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // S(kb) = Q K(kb)^T into score buffer kb % 2
     const auto issue_s = [&](int kb) -> bool {
       const int slot = kb & 1;
-      bool ok = mbar_wait_bounded(bar_kfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+      bool ok = mbar_wait_spin(bar_kfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
       if (ok && kb >= 2)
-        ok = mbar_wait_bounded(bar_sfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
+        ok = mbar_wait_spin(bar_sfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
       if (!warp_all(ok)) return false;
       tc_fence_after();
       const uint64_t kdesc = smem_desc_sw128(smem_addr(k_ring + slot * kAttnKBytes));
@@ -284,8 +293,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int kb = 0; alive && kb < nkb; ++kb) {
       if (kb + 1 < nkb && !(alive = issue_s(kb + 1))) break;
       const int slot = kb & 1;
-      bool ok = mbar_wait_bounded(bar_vfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
-      if (ok) ok = mbar_wait_bounded(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
+      bool ok = mbar_wait_spin(bar_vfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+      if (ok) ok = mbar_wait_spin(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
       if (!warp_all(ok)) {
         alive = false;
         break;
@@ -325,7 +334,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool alive = nkb > 0;
     for (int kb = 0; alive && kb < nkb; ++kb) {
       const int slot = kb & 1;
-      if (!warp_all(mbar_wait_bounded(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
+      if (!warp_all(mbar_wait_spin(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
         alive = false;
         break;
       }
@@ -348,15 +357,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           q_real ? kmask[kb]
                  : (L - j0 >= 64 ? ~0ull : ((1ull << (L - j0)) - 1ull));
       const unsigned vlo = static_cast<unsigned>(vm), vhi = static_cast<unsigned>(vm >> 32);
-      float bmax = -INFINITY;
+      float bm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // 4 chains: ILP
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const float v = q_real ? __uint_as_float(raw[c]) : 0.f;
         const bool ok = ((c < 32 ? vlo >> c : vhi >> (c - 32)) & 1u) != 0;
-        raw[c] = __float_as_uint(ok ? v : -INFINITY);
-        bmax = fmaxf(bmax, ok ? v : -INFINITY);
+        const float mv = ok ? v : -INFINITY;
+        raw[c] = __float_as_uint(mv);
+        bm4[c & 3] = fmaxf(bm4[c & 3], mv);
       }
-      bmax *= scale;  // scale > 0: the max of scaled scores
+      // scale > 0: the max of the scaled scores
+      const float bmax = fmaxf(fmaxf(bm4[0], bm4[1]), fmaxf(bm4[2], bm4[3])) * scale;
       float f = 1.f;  // rescale of the previous O and l
       const bool grow = bmax > m + kRescaleLog2;  // false while the block is all masked
       if (grow) {
@@ -367,7 +378,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (__any_sync(0xffffffffu, grow && f != 0.f) && kb >= 1) {
         // O holds P V of earlier blocks: wait for the last of them, rescale
         // this warp's rows (whole-warp TMEM access; others multiply by 1)
-        if (!warp_all(mbar_wait_bounded(bar_pfree((kb - 1) & 1), ((kb - 1) >> 1) & 1, abort_flag, err,
+        if (!warp_all(mbar_wait_spin(bar_pfree((kb - 1) & 1), ((kb - 1) >> 1) & 1, abort_flag, err,
                                         kErrWaitAccum, limit))) {
           alive = false;
           break;
@@ -388,16 +399,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // p = exp2(s2 - m) as fp16 pairs, l += sum p (masked: exp2(-inf) = 0)
       const float nm = m == -INFINITY ? 0.f : -m;
       uint32_t pw[32];
-      float sum = 0.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(raw[2 * c]), scale, nm));
         const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(raw[2 * c + 1]), scale, nm));
-        sum += p0 + p1;
+        s4[c & 3] += p0 + p1;
         pw[c] = pack_half2_bits(p0, p1);
       }
-      l += sum;
-      if (kb >= 2 && !warp_all(mbar_wait_bounded(bar_pfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err,
+      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      if (kb >= 2 && !warp_all(mbar_wait_spin(bar_pfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err,
                                                   kErrWaitAccum, limit))) {
         alive = false;
         break;

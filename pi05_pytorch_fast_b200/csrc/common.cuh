@@ -122,6 +122,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// Bounded wait for hand-offs that are normally a few hundred cycles away: it
+// polls try_wait without a suspend hint (a sleeping waiter can wake long after
+// the phase completes) and reads the clock every 64 polls.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned* err, unsigned err_bit, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicOr(err, err_bit);
+        return false;
+      }
+    }
+  }
+}
+
 // The same bounded wait for single-thread issue loops: the first try_wait is
 // inlined and the bounded sleeping loop lives out of line, which keeps the
 // issuer's hot path short (an inlined slow path costs it ~100 cycles a step).

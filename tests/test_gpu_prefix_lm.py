@@ -3,14 +3,13 @@
 * Every W4A4 op inside a real two-layer forward at M = 776 is bit-exact
   against the CPU oracle fed the same activation: the codes, the row scales
   and the fp16 outputs of q/k/v, o_proj, gate/up and down_proj.
-* The whole forward agrees with the reference's own composition -- stock
-  transformers Gemma decoder layers (eager attention, fp16) whose seven
-  projections are the oracle's W4A4 emulation -- on the real tokens' final
-  hidden states.  The two runs round their glue differently (a fused RMSNorm
-  summing in another order, another attention kernel schedule), and a
-  one-ulp difference in an fp16 activation can move an INT4 code by one
-  step, so the check is a tolerance: max |diff| <= 3e-2 x RMS and mean
-  |diff| <= 2e-3 x RMS.
+* The fused composition IS transformers' Gemma decoder layer: run through
+  the stock layers with the same primitives swapped in, the final hidden
+  states are bit-identical.
+* Against the stock layers with the reference's eager fp16 attention and the
+  oracle's projections, the final hidden states differ by no more than two
+  variants of that reference differ from each other (an INT4 code moves one
+  step when its fp16 input moves one ulp, so no two roundings agree closely).
 * The CUDA-graph replay equals the eager forward bit for bit.
 """
 
@@ -110,18 +109,73 @@ class OracleLinear(torch.nn.Module):
         return torch.from_numpy(y).to(x.device)
 
 
-def reference_forward(hf, model: plm.W4A4PrefixLM, embeds, pad, staging: str):
-    """transformers' Gemma layers (stock forward: RMSNorm, RoPE, eager
-    attention, GeGLU MLP, residuals) with every projection replaced by the
-    oracle over the packed weights ``model`` uses."""
-    for layer, lw in zip(hf.layers, model.layers):
-        a, m = layer.self_attn, layer.mlp
-        a.q_proj, a.k_proj, a.v_proj, a.o_proj = (OracleLinear(w, "row", staging)
-                                                  for w in (lw.q, lw.k, lw.v, lw.o))
-        m.gate_proj = OracleLinear(lw.gate, "fragment", staging)
-        m.up_proj = OracleLinear(lw.up, "fragment", staging)
-        m.down_proj = OracleLinear(lw.down, "row", staging)
+class OpLinear(torch.nn.Module):
+    """A projection through the pi05_w4a4 torch ops (what the reference's
+    W4A4Linear calls), on the same packed weight."""
+
+    def __init__(self, packed: torch.Tensor, fragment: bool):
+        super().__init__()
+        self.packed, self.fragment = packed, fragment
+
+    def forward(self, x):
+        op = torch.ops.pi05_w4a4.int4_gemm_tiled if self.fragment else torch.ops.pi05_w4a4.int4_gemm
+        return op(x.contiguous(), self.packed)
+
+
+class LibRMSNorm(torch.nn.Module):
+    """GemmaRMSNorm through the library's norm kernel (w4a4_rmsnorm_quant
+    without the quant): the norm the runner's fused kernels compute."""
+
+    def __init__(self, weight: torch.Tensor, eps: float):
+        super().__init__()
+        self.gain = (1.0 + weight.detach().float()).contiguous()
+        self.eps = eps
+
+    def forward(self, x):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        h = torch.empty_like(x2)
+        nat.check(nat.lib().w4a4_rmsnorm_quant(
+            x2.data_ptr(), x2.stride(0), None, 0, self.gain.data_ptr(), self.eps, None, 0, h.data_ptr(),
+            h.stride(0), x2.shape[0], x2.shape[1], 0, nat.CODES_INT8, None, None,
+            torch.cuda.current_stream().cuda_stream))
+        return h.view_as(x)
+
+
+def library_attention(pad):
+    """transformers attention function running the library's prefix
+    attention kernel under the prefix mask of ``pad``."""
+    def attn(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
+        b, h, seq, d = query.shape
+        q = query.transpose(1, 2).reshape(b * seq, h * d).contiguous()
+        k = key.transpose(1, 2).reshape(b * seq, d).contiguous()
+        v = value.transpose(1, 2).reshape(b * seq, d).contiguous()
+        kvalid = pad.to(torch.uint8).contiguous()
+        kv_len = (pad * torch.arange(1, seq + 1, device=pad.device)).amax(dim=1).to(torch.int32)
+        vt = torch.empty((b, d, nat.attn_vt_stride(seq)), dtype=torch.float16, device=q.device)
+        out = torch.empty_like(q)
+        nat.check(nat.lib().w4a4_prefix_attention(
+            q.data_ptr(), q.stride(0), k.data_ptr(), d, v.data_ptr(), d, kvalid.data_ptr(), kv_len.data_ptr(),
+            b, seq, h, vt.data_ptr(), out.data_ptr(), out.stride(0), torch.cuda.current_stream().cuda_stream))
+        return out.view(b, seq, h, d), None
+    return attn
+
+
+def eager_fp32_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
+    """transformers' eager attention evaluated in fp32, rounded to fp16 once."""
+    from transformers.models.gemma.modeling_gemma import repeat_kv
+
+    k = repeat_kv(key, module.num_key_value_groups).float()
+    v = repeat_kv(value, module.num_key_value_groups).float()
+    w = torch.matmul(query.float(), k.transpose(2, 3)) * module.scaling + attention_mask
+    w = torch.softmax(w, dim=-1, dtype=torch.float32)
+    return torch.matmul(w, v).transpose(1, 2).contiguous().half(), None
+
+
+def hf_forward(hf, embeds, pad, attn_impl: str):
+    """Stock transformers Gemma decoder layers (input norm, attention with
+    RoPE, residual, post-attention norm, GeGLU MLP, residual) and final norm."""
     pos, mask = plm.prefix_positions_and_mask(pad)
+    hf.config._attn_implementation = attn_impl
     hidden = embeds
     cos_sin = hf.rotary_emb(hidden, pos)
     for layer in hf.layers:
@@ -131,24 +185,69 @@ def reference_forward(hf, model: plm.W4A4PrefixLM, embeds, pad, staging: str):
     return hf.norm(hidden)
 
 
-def test_forward_matches_transformers_layers_with_oracle_projections():
+def install_projections(hf, model: plm.W4A4PrefixLM, make):
+    for layer, lw in zip(hf.layers, model.layers):
+        a, m = layer.self_attn, layer.mlp
+        a.q_proj, a.k_proj, a.v_proj, a.o_proj = (make(w, False) for w in (lw.q, lw.k, lw.v, lw.o))
+        m.gate_proj, m.up_proj = make(lw.gate, True), make(lw.up, True)
+        m.down_proj = make(lw.down, False)
+
+
+def test_fused_forward_equals_transformers_layers_on_the_same_primitives():
+    """The runner's fused composition is exactly transformers' Gemma decoder
+    layer (the reference's _fused_attn_forward / _fused_mlp_forward), bit for
+    bit, once both use the same primitives: the pi05_w4a4 ops for the seven
+    projections, this library's norm and attention kernels; RoPE, GeGLU and
+    the residual adds stay transformers' / PyTorch's own (the fused kernels
+    round them identically)."""
+    from transformers import AttentionInterface
+
+    hf = small_gemma(2, seed=3)
+    model = plm.W4A4PrefixLM.from_gemma(hf, DEV)
+    embeds, pad = plm.synthetic_prefix(1, device=DEV, seed=4)
+    with torch.no_grad():
+        ours = model.forward(embeds, pad).hidden.clone()
+        install_projections(hf, model, lambda w, frag: OpLinear(w, frag))
+        for layer in hf.layers:
+            layer.input_layernorm = LibRMSNorm(layer.input_layernorm.weight, 1e-6)
+            layer.post_attention_layernorm = LibRMSNorm(layer.post_attention_layernorm.weight, 1e-6)
+        hf.norm = LibRMSNorm(hf.norm.weight, 1e-6)
+        AttentionInterface.register("w4a4_prefix_test", library_attention(pad))
+        ref = hf_forward(hf, embeds, pad, "w4a4_prefix_test")
+    torch.cuda.synchronize()
+    assert torch.equal(ours.view(torch.int16), ref.view(torch.int16))
+
+
+def test_forward_stays_within_the_references_own_rounding_spread():
+    """Against the stock composition with the reference's eager fp16
+    attention and the oracle's W4A4 projections: INT4 activation codes move
+    by one step when an fp16 input moves by one ulp, so any two correct
+    roundings of this model differ visibly.  The runner's distance from the
+    eager-fp16 reference must stay within 2x the distance between two
+    reference variants (eager attention in fp16 vs in fp32)."""
+    from transformers import AttentionInterface
+
     hf = small_gemma(2, seed=3)
     staging = "fp32"  # the reference's CPU emulation arithmetic, pinned to its golden vectors
     model = plm.W4A4PrefixLM.from_gemma(hf, DEV, staging=STAGINGS[staging])
     embeds, pad = plm.synthetic_prefix(1, device=DEV, seed=4)
     with torch.no_grad():
-        ours = model.forward(embeds, pad).hidden
-        ref = reference_forward(hf, model, embeds, pad, staging)
+        ours = model.forward(embeds, pad).hidden.clone()
+        install_projections(hf, model, lambda w, frag: OracleLinear(w, "fragment" if frag else "row", staging))
+        ref16 = hf_forward(hf, embeds, pad, "eager")
+        AttentionInterface.register("eager_fp32_test", eager_fp32_attention)
+        ref32 = hf_forward(hf, embeds, pad, "eager_fp32_test")
     torch.cuda.synchronize()
     real = pad[0]
-    a = ours[0][real].float()
-    b = ref[0][real].float()
-    rms = float(b.pow(2).mean().sqrt())
-    diff = (a - b).abs()
-    print(f"final hidden: rms {rms:.4f}, max |diff| / rms {float(diff.max()) / rms:.2e}, "
-          f"mean |diff| / rms {float(diff.mean()) / rms:.2e}, equal {float((diff == 0).float().mean()):.4f}")
-    assert float(diff.max()) <= 3e-2 * rms
-    assert float(diff.mean()) <= 2e-3 * rms
+    a, r16, r32 = (t[0][real].float() for t in (ours, ref16, ref32))
+    rms = float(r16.pow(2).mean().sqrt())
+    ours_d = (a - r16).abs()
+    spread = (r32 - r16).abs()
+    print(f"final hidden vs eager-fp16 reference: ours mean {float(ours_d.mean()) / rms:.2e} "
+          f"max {float(ours_d.max()) / rms:.2e}; fp32-attention reference mean "
+          f"{float(spread.mean()) / rms:.2e} max {float(spread.max()) / rms:.2e}")
+    assert float(ours_d.mean()) <= 2.0 * float(spread.mean()) + 1e-4 * rms
+    assert float(ours_d.max()) <= 2.0 * float(spread.max()) + 1e-3 * rms
 
 
 def test_graph_replay_equals_eager_forward(gemma2):
