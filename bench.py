@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--staging", choices=("fp16", "fp32"), default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timings")
+    ap.add_argument("--shard-mlp", action="store_true",
+                    help="with N > 1: every rank runs the SAME observations and holds 1/N of gate/up "
+                         "(tensor-parallel MLP, NCCL all-to-all + all-gather; strong scaling)")
     ap.add_argument("--roofline-reps", type=int, default=20)
     ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k",
                                        "normquant", "geglu", "attn", "forward"),
@@ -376,6 +379,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
 
     from pi05_pytorch_fast_b200 import _native as nat
     from pi05_pytorch_fast_b200 import prefix_lm as plm
+    from pi05_pytorch_fast_b200.shard import MlpShard, exchange_row_blocks, gather_row_blocks
     from pi05_pytorch_fast_b200.w4a4 import extension as ext
 
     if args.staging:
@@ -388,9 +392,13 @@ def run_ours(args, rank, world, local_rank, dist_on):
     torch.cuda.set_device(device)
     ext.preload()
     cfg = plm.PrefixLMConfig(layers=args.layers)
-    model = plm.W4A4PrefixLM.random(cfg, device, seed=1234, staging=staging)
+    sharded = args.shard_mlp and world > 1
+    shard = MlpShard(rank, world) if sharded else None
+    model = plm.W4A4PrefixLM.random(cfg, device, seed=1234, staging=staging, shard=shard)
     lang = args.prefix - N_IMG
-    embeds, pad = plm.synthetic_prefix(args.batch, lang_tokens=lang, device=device, seed=100 + rank)
+    # data parallel: each rank its own observations; sharded: the same ones on every rank
+    in_seed = 100 if sharded else 100 + rank
+    embeds, pad = plm.synthetic_prefix(args.batch, lang_tokens=lang, device=device, seed=in_seed)
     m = args.batch * args.prefix
     torch.cuda.synchronize(device)
 
@@ -402,20 +410,35 @@ def run_ours(args, rank, world, local_rank, dist_on):
             ms = time_device(graphs[0].replay, args.steps, args.warmup, dist_on, device)
 
         # --- end to end: pinned host inputs in, final hidden states out, every step
-        emb_host = plm.synthetic_prefix(args.batch, lang_tokens=lang, seed=200 + rank)[0].pin_memory()
+        emb_host = plm.synthetic_prefix(args.batch, lang_tokens=lang,
+                                        seed=200 if sharded else 200 + rank)[0].pin_memory()
         pad_host = pad.cpu().pin_memory()
         e2e_steps = max(5, min(args.steps, 50))
         ms_e2e = time_e2e(graphs, emb_host, pad_host, e2e_steps, max(3, args.warmup), dist_on, device)
         del graphs
 
         # --- the 72 W4A4 ops alone (the pi05_w4a4 op path), one CUDA graph
-        lws = [layer_weights(lw) for lw in model.layers]
-        x_static = synthetic_activations(m, HIDDEN, device, seed=100 + rank)
-        ms_ops = graph_ms(lambda: w4a4_op_chain(x_static, lws), max(5, args.steps // 4), dist_on, device)
+        ms_ops = None
+        coll_ms = None
+        if not sharded:
+            lws = [layer_weights(lw) for lw in model.layers]
+            x_static = synthetic_activations(m, HIDDEN, device, seed=100 + rank)
+            ms_ops = graph_ms(lambda: w4a4_op_chain(x_static, lws), max(5, args.steps // 4), dist_on, device)
+        else:
+            # the step's collectives alone: per layer the all-to-all of the
+            # GeGLU shards and the all-gather of the down_proj rows
+            ws = model.workspace(args.batch, args.prefix)
 
+            def collectives():
+                for _ in model.layers:
+                    exchange_row_blocks(ws.h_part, ws.h_recv, shard)
+                    gather_row_blocks(ws.down_part, ws.down, shard)
+            coll_ms = time_device(collectives, max(5, args.steps // 4), 3, dist_on, device)
+
+    job_obs = 1 if sharded else world  # observation sets the job runs per step, per rank's batch
     result = {
         "metric": METRIC,
-        "value": job_throughput(ms, args.batch, world),
+        "value": job_throughput(ms, args.batch, job_obs),
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
@@ -424,7 +447,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
         "prefix_lm_ms": ms / args.batch,
         "gemm_int_tops": ops_per_prefix(m, args.layers) / (ms * 1e-3) / 1e12,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if sharded else "weak",
         "vs_baseline": None,
         "dtype": "int4 codes x int4 codes -> int32 (tcgen05 kind::i8) for every projection; "
                  "fp16 activations, glue and attention",
@@ -439,7 +462,10 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "staging": staging_name,
             "staging_parity": "fp32: pinned to the reference's golden vectors; fp16: the HIP kernel's "
                               "rounding, parity unpinned (no reference output exists for it)",
-            "parallelism": f"dp{world} (independent observations per GPU, no collective in the step)",
+            "parallelism": (f"tp{world} MLP (N-sharded gate/up; per layer an NCCL all-to-all of the GeGLU "
+                            "shards and an all-gather of the down_proj rows; attention replicated)")
+                           if sharded else
+                           f"dp{world} (independent observations per GPU, no collective in the step)",
             "l2": "working set ~1.0 GB of packed weights per step >> 126 MB L2 (no flush needed)",
             "timing": "CUDA graph replay of the whole forward, CUDA events, max over ranks",
         },
@@ -448,7 +474,7 @@ def run_ours(args, rank, world, local_rank, dist_on):
                              "norm); the attention and cos/sin glue are PyTorch kernels, not counted",
         "clocks": clocks.summary(),
         "e2e": {
-            "value": job_throughput(ms_e2e, args.batch, world),
+            "value": job_throughput(ms_e2e, args.batch, job_obs),
             "unit": UNIT,
             "h2d_bytes_per_step": int(emb_host.numel() * 2 + pad_host.numel()),
             "d2h_bytes_per_step": int(emb_host.numel() * 2),
@@ -457,14 +483,19 @@ def run_ours(args, rank, world, local_rank, dist_on):
                     "copy stream, two graph instances alternating so copies overlap compute",
             "steps": e2e_steps,
         },
-        "w4a4_ops": {
+    }
+    if ms_ops is not None:
+        result["w4a4_ops"] = {
             "ms_per_prefix": ms_ops / args.batch,
             "obs_per_s": job_throughput(ms_ops, args.batch, 1),
             "what": "the 72 pi05_w4a4 ops of a prefix (int4_gemm3, int4_gemm, int4_gemm2_tiled, "
                     "int4_gemm x 18) chained without the glue, one CUDA graph, torch op path",
-        },
-    }
-    if not args.no_kernels:
+        }
+    if coll_ms is not None:
+        result["collectives"] = {"ms_per_step": coll_ms, "share_of_step": coll_ms / ms,
+                                 "what": "the step's NCCL all-to-alls and all-gathers timed alone "
+                                         "(max over ranks)"}
+    if not args.no_kernels and not sharded:
         result.update(kernel_figures(args, model, m, staging, dist_on, device))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # the reference's CPU path is int4_gemm_ref: fp32 FWHT staging

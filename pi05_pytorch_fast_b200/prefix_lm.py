@@ -34,6 +34,7 @@ from pathlib import Path
 import torch
 
 from . import _native as nat
+from .shard import MlpShard, exchange_row_blocks, gather_row_blocks
 from .w4a4 import pack as wpack
 
 # lerobot's pi05 mask value for disallowed attention pairs (fp32 additive).
@@ -95,9 +96,16 @@ def _fragment_major(packed: torch.Tensor, k: int) -> torch.Tensor:
     return wpack.preshuffle_wmma_weight(packed, k).contiguous()
 
 
-def pack_layer(lin: dict, input_norm: torch.Tensor, post_norm: torch.Tensor, device) -> PackedLayer:
+def pack_layer(lin: dict, input_norm: torch.Tensor, post_norm: torch.Tensor, device,
+               shard: MlpShard | None = None) -> PackedLayer:
     """PackedLayer from fp weights {q, k, v, o, gate, up, down: [N, K]} (packed on
-    ``device`` in fp32, bit-identical to the reference's CPU pack)."""
+    ``device`` in fp32, bit-identical to the reference's CPU pack).  With a
+    shard, gate/up keep only this rank's rows (each row packs on its own, so
+    packing the slice equals slicing the pack)."""
+    if shard is not None and shard.world > 1:
+        lin = dict(lin)
+        cols = shard.cols(lin["gate"].shape[0])
+        lin["gate"], lin["up"] = lin["gate"][cols], lin["up"][cols]
     p = {n: wpack.pack_linear_weight(w, device=device) for n, w in lin.items()}
     return PackedLayer(
         q=_row_major(p["q"]), k=_row_major(p["k"]), v=_row_major(p["v"]), o=_row_major(p["o"]),
@@ -153,11 +161,12 @@ def prefix_positions_and_mask(pad_mask: torch.Tensor):
 class _Workspace:
     """Every intermediate of one forward at `rows` tokens, allocated once."""
 
-    def __init__(self, cfg: PrefixLMConfig, batch: int, seq: int, device, trace: bool):
+    def __init__(self, cfg: PrefixLMConfig, batch: int, seq: int, device, trace: bool, world: int = 1):
         f16 = dict(dtype=torch.float16, device=device)
         e = torch.empty
         rows = batch * seq
         self.rows = rows
+        mlp = cfg.intermediate // world  # gate/up columns held here
         self.x = e((rows, cfg.hidden), **f16)            # residual stream
         self.codes = e((rows, cfg.intermediate), dtype=torch.int8, device=device)
         self.scales = e((rows,), dtype=torch.float32, device=device)
@@ -165,9 +174,13 @@ class _Workspace:
         self.k = e((rows, cfg.kv_heads * cfg.head_dim), **f16)
         self.attn = e((rows, cfg.heads * cfg.head_dim), **f16)
         self.o = e((rows, cfg.hidden), **f16)
-        self.gate = e((rows, cfg.intermediate), **f16)
-        self.up = e((rows, cfg.intermediate), **f16)
+        self.gate = e((rows, mlp), **f16)
+        self.up = e((rows, mlp), **f16)
         self.down = e((rows, cfg.hidden), **f16)
+        if world > 1:  # the sharded MLP's exchange buffers
+            self.h_part = e((rows, mlp), **f16)            # GeGLU of this rank's columns
+            self.h_recv = e((world, rows // world, mlp), **f16)  # this rank's rows, by source rank
+            self.down_part = e((rows // world, cfg.hidden), **f16)
         self.out = e((rows, cfg.hidden), **f16)
         self.cos = e((rows, cfg.head_dim), **f16)
         self.sin = e((rows, cfg.head_dim), **f16)
@@ -196,7 +209,8 @@ class W4A4PrefixLM:
     W4A4_STAGING_*; fp16 = the reference HIP kernel's)."""
 
     def __init__(self, cfg: PrefixLMConfig, layers: list[PackedLayer], final_norm: torch.Tensor,
-                 device, staging: int = nat.STAGING_FP16, inv_freq: torch.Tensor | None = None):
+                 device, staging: int = nat.STAGING_FP16, inv_freq: torch.Tensor | None = None,
+                 shard: MlpShard | None = None):
         if cfg.hidden != 2048 or cfg.intermediate != 16384 or cfg.head_dim != 256:
             raise ValueError("the fused layer kernels are built for Gemma-2B shapes "
                              "(hidden 2048, MLP 16384, head_dim 256)")
@@ -208,12 +222,17 @@ class W4A4PrefixLM:
         # the rotary table: the model's own inv_freq buffer when one is given,
         # else the fp16 LM's (rope_inv_freq)
         self.inv_freq = (rope_inv_freq(cfg) if inv_freq is None else inv_freq.detach().float()).to(self.device)
+        # the N-sharded gate/up over several GPUs (shard.py), or None
+        self.shard = shard if shard is not None and shard.world > 1 else None
+        if self.shard is not None and staging != nat.STAGING_FP16:
+            raise ValueError("the sharded MLP quantises its segmented rows with fp16 staging only")
         self._ws: dict = {}
         self._lib = nat.lib()
 
     # ------------------------------------------------------------- builders
     @classmethod
-    def from_gemma(cls, model, device, staging: int = nat.STAGING_FP16) -> "W4A4PrefixLM":
+    def from_gemma(cls, model, device, staging: int = nat.STAGING_FP16,
+                   shard: MlpShard | None = None) -> "W4A4PrefixLM":
         """From a transformers GemmaModel (or anything with .layers / .norm of
         Gemma decoder layers): packs every projection; RoPE uses the model's
         own rotary inv_freq buffer (fp16 once the model is cast to fp16)."""
@@ -226,16 +245,18 @@ class W4A4PrefixLM:
                    "down": m.down_proj.weight}
             layers.append(pack_layer({n: w.detach() for n, w in lin.items()},
                                      layer.input_layernorm.weight, layer.post_attention_layernorm.weight,
-                                     device))
+                                     device, shard))
         rot = getattr(model, "rotary_emb", None)
         inv_freq = getattr(rot, "inv_freq", None)
-        return cls(cfg, layers, model.norm.weight, device, staging, inv_freq=inv_freq)
+        return cls(cfg, layers, model.norm.weight, device, staging, inv_freq=inv_freq, shard=shard)
 
     @classmethod
     def random(cls, cfg: PrefixLMConfig, device, seed: int = 0, std: float = 0.02,
-               norm_std: float = 0.1, staging: int = nat.STAGING_FP16) -> "W4A4PrefixLM":
+               norm_std: float = 0.1, staging: int = nat.STAGING_FP16,
+               shard: MlpShard | None = None) -> "W4A4PrefixLM":
         """Random-init weights N(0, std), norm weights N(0, norm_std), drawn
-        and packed on the device (config 2's random-init model)."""
+        and packed on the device (config 2's random-init model; every rank of
+        a shard draws the same weights and keeps its gate/up rows)."""
         gen = torch.Generator(device=device).manual_seed(seed)
 
         def w(n, k):
@@ -251,8 +272,8 @@ class W4A4PrefixLM:
                    "v": w(cfg.kv_heads * hd, cfg.hidden), "o": w(cfg.hidden, cfg.heads * hd),
                    "gate": w(cfg.intermediate, cfg.hidden), "up": w(cfg.intermediate, cfg.hidden),
                    "down": w(cfg.hidden, cfg.intermediate)}
-            layers.append(pack_layer(lin, nw(), nw(), device))
-        return cls(cfg, layers, nw(), device, staging)
+            layers.append(pack_layer(lin, nw(), nw(), device, shard))
+        return cls(cfg, layers, nw(), device, staging, shard=shard)
 
     @classmethod
     def from_packed_dir(cls, pack_dir, norms: dict, cfg: PrefixLMConfig, device,
@@ -285,7 +306,10 @@ class W4A4PrefixLM:
     def workspace(self, batch: int, seq: int, trace: bool = False) -> _Workspace:
         key = (batch, seq, trace)
         if key not in self._ws:
-            self._ws[key] = _Workspace(self.cfg, batch, seq, self.device, trace)
+            world = self.shard.world if self.shard is not None else 1
+            if (batch * seq) % world:
+                raise ValueError(f"{batch * seq} token rows do not split over {world} ranks")
+            self._ws[key] = _Workspace(self.cfg, batch, seq, self.device, trace, world)
         return self._ws[key]
 
     def _stream(self):
@@ -373,15 +397,18 @@ class W4A4PrefixLM:
             if trace is not None:
                 trace.append(("gateup", li, ws.h.clone(), self._codes(ws, rows, hid).clone(), ws.scales.clone(),
                               (ws.gate.clone(), ws.up.clone())))
-            h_mlp = ws.h_mlp if trace is not None else None
-            nat.check(lib.w4a4_geglu_quant(
-                ws.gate.data_ptr(), ws.up.data_ptr(), rows, cfg.intermediate, cfg.intermediate,
-                self.staging, nat.CODES_GEMM, ws.codes.data_ptr(), ws.scales.data_ptr(),
-                h_mlp.data_ptr() if h_mlp is not None else None, cfg.intermediate, st))
-            self._gemm(ws, rows, inter, [lw.down], [ws.down], fragment=False)
-            if trace is not None:
-                trace.append(("down", li, ws.h_mlp.clone(), self._codes(ws, rows, inter).clone(), ws.scales.clone(),
-                              (ws.down.clone(),)))
+            if self.shard is not None:
+                self._sharded_mlp_tail(ws, rows, lw)
+            else:
+                h_mlp = ws.h_mlp if trace is not None else None
+                nat.check(lib.w4a4_geglu_quant(
+                    ws.gate.data_ptr(), ws.up.data_ptr(), rows, cfg.intermediate, cfg.intermediate,
+                    self.staging, nat.CODES_GEMM, ws.codes.data_ptr(), ws.scales.data_ptr(),
+                    h_mlp.data_ptr() if h_mlp is not None else None, cfg.intermediate, st))
+                self._gemm(ws, rows, inter, [lw.down], [ws.down], fragment=False)
+                if trace is not None:
+                    trace.append(("down", li, ws.h_mlp.clone(), self._codes(ws, rows, inter).clone(),
+                                  ws.scales.clone(), (ws.down.clone(),)))
             delta = ws.down
         # final residual add + norm
         nat.check(lib.w4a4_rmsnorm_quant(
@@ -390,14 +417,30 @@ class W4A4PrefixLM:
             cfg.hidden, self.staging, nat.CODES_GEMM, None, None, st))
         return out
 
+    def _sharded_mlp_tail(self, ws: _Workspace, rows: int, lw: PackedLayer) -> None:
+        """GeGLU of this rank's gate/up columns, the row-block exchange, the
+        quant of this rank's complete rows from their segments, down_proj on
+        them, and the all-gather of the results (shard.py)."""
+        sh, cfg, st = self.shard, self.cfg, self._stream()
+        part = cfg.intermediate // sh.world
+        mine = rows // sh.world
+        nat.check(self._lib.w4a4_geglu(ws.gate.data_ptr(), ws.up.data_ptr(), rows, part, part,
+                                       ws.h_part.data_ptr(), part, st))
+        exchange_row_blocks(ws.h_part, ws.h_recv, sh)
+        nat.check(self._lib.w4a4_quant_segments(ws.h_recv.data_ptr(), mine, cfg.intermediate, part, part,
+                                                mine * part, self.staging, nat.CODES_GEMM,
+                                                ws.codes.data_ptr(), ws.scales.data_ptr(), st))
+        self._gemm(ws, mine, cfg.intermediate, [lw.down], [ws.down_part], fragment=False)
+        gather_row_blocks(ws.down_part, ws.down, sh)
+
     __call__ = forward
 
     def launches_per_forward(self) -> int:
         """Kernels of this library per forward (the torch glue that builds the
         position / mask tables is not counted): per layer 2 norm+quant, 1
-        quant, 4 GEMMs, 2 RoPE, V transpose + attention, 1 GeGLU+quant; then
-        the final norm."""
-        return 12 * len(self.layers) + 1
+        quant, 4 GEMMs, 2 RoPE, V transpose + attention, 1 GeGLU+quant (the
+        sharded MLP: GeGLU, then the segment quant); then the final norm."""
+        return (12 + (1 if self.shard is not None else 0)) * len(self.layers) + 1
 
 
 class GraphedPrefixLM:
