@@ -536,24 +536,9 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
         "gemm_down": (lambda lw: ext.gemm_from_codes(codes16, scales16, [lw["down"]]),
                       2.0 * m * HIDDEN * INTER),
     }
-    import ctypes
-
-    gu_out = [torch.empty((m, INTER), dtype=torch.float16, device=device) for _ in range(2)]
-    gu_ptrs = nat.pointer_array([o.data_ptr() for o in gu_out])
-    gelu_act = (ctypes.c_int32 * 2)(nat.ACT_GELU_TANH, nat.ACT_NONE)
-
-    def gateup_act(lw):
-        descs = nat.weights_array([(w.data_ptr(), int(w.shape[0]), int(w.shape[1]), nat.LAYOUT_FRAGMENT_MAJOR)
-                                   for w in (lw["gate"], lw["up"])])
-        nat.check(lib.w4a4_gemm_act(codes.data_ptr(), scales.data_ptr(), m, HIDDEN, 2, descs, gu_ptrs, gelu_act,
-                                    torch.cuda.current_stream(device).cuda_stream))
-
-    gemms["gemm_gateup_gelu"] = (gateup_act, 2.0 * m * 2 * INTER * HIDDEN)
     for name, (fn, ops) in gemms.items():
         t = graph_ms(cycle(fn), reps, dist_on, device, per_graph=1) / len(lws)
         out[name] = {"ms": t, "tops": ops / (t * 1e-3) / 1e12, "frac": ops / (t * 1e-3) / 1e12 / int8_peak}
-    out["gemm_gateup_gelu"]["note"] = ("the forward's gate/up launch: GELU of the gate applied in the "
-                                       "epilogue (w4a4_gemm_act)")
 
     def bw(name, fn, nbytes, note):
         t = graph_ms(fn, reps, dist_on, device, per_graph=10)
@@ -578,7 +563,7 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
     stream = lambda: torch.cuda.current_stream(device).cuda_stream  # noqa: E731
 
     def geglu():
-        nat.check(lib.w4a4_geglu_quant(gate.data_ptr(), up.data_ptr(), m, INTER, INTER, 1, staging,
+        nat.check(lib.w4a4_geglu_quant(gate.data_ptr(), up.data_ptr(), m, INTER, INTER, staging,
                                        nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), None, INTER, stream()))
 
     def normq():
@@ -587,8 +572,7 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
                                          nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), stream()))
 
     bw("geglu_quant_k16384", geglu, 2 * 2 * m * INTER + m * INTER // 2 + 4 * m,
-       "gate (already activated by the gate/up GEMM epilogue) + up fp16 in, packed codes + scale out; "
-       "replaces gelu(gate)*up and the down_proj quant")
+       "gate + up fp16 in, packed codes + scale out; replaces F.gelu(gate)*up and the down_proj quant")
     bw("rmsnorm_quant_k2048", normq, 3 * 2 * m * HIDDEN + m * HIDDEN // 2 + 4 * m,
        "x + delta in, x out (residual), packed codes + scale out; replaces add, RMSNorm and quant")
     gu = out["gemm_gateup"]
@@ -700,7 +684,7 @@ def run_case(args):
         elif args.case == "quant16k":
             ext.quantize(h, fmt="gemm")
         elif args.case == "geglu":
-            nat.check(lib.w4a4_geglu_quant(h.data_ptr(), h.data_ptr(), m, INTER, INTER, 1, staging,
+            nat.check(lib.w4a4_geglu_quant(h.data_ptr(), h.data_ptr(), m, INTER, INTER, staging,
                                            nat.CODES_GEMM, cb.data_ptr(), sb.data_ptr(), None, INTER, st))
         elif args.case == "normquant":
             nat.check(lib.w4a4_rmsnorm_quant(x.data_ptr(), HIDDEN, None, HIDDEN, gain.data_ptr(), 1e-6,

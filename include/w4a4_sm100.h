@@ -103,18 +103,6 @@ int w4a4_quant(const void* x, int64_t m, int32_t k, int64_t ldx, int32_t rotate,
 int w4a4_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
               int32_t n_weights, const w4a4_weight* weights, void* const* y, void* stream);
 
-/* activations of w4a4_gemm_act, per weight */
-#define W4A4_ACT_NONE 0
-#define W4A4_ACT_GELU_TANH 1 /* y = fl16(gelu_tanh(fl16(result))): F.gelu(approximate="tanh") on the fp16 output */
-
-/* w4a4_gemm with an activation applied to each weight's fp16 output in the
- * epilogue (act[i], W4A4_ACT_*): the gate of the GeGLU MLP (apply.py:138,
- * act_fn(gate)) leaves the GEMM already activated, rounded exactly as
- * PyTorch's eager gelu rounds the fp16 gate.  No counterpart in the
- * reference, which applies act_fn as a separate op. */
-int w4a4_gemm_act(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
-                  const w4a4_weight* weights, void* const* y, const int32_t* act, void* stream);
-
 /* Test hook: the same GEMM, but writes the raw int32 accumulators
  * acc[i] = int32 [m, weights[i].n] (sum_k qa*qw, before any scaling) so
  * tests can check them bit-exactly; row scales are not used. */
@@ -171,12 +159,10 @@ int w4a4_rmsnorm_quant(const void* x, int64_t ldx, const void* delta, int64_t ld
  * and the following quantize_x.  h = fl16(fl16(gelu_tanh(gate)) * up), the
  * rounding of PyTorch's eager CUDA ops; its codes and row scale exactly as
  * w4a4_quant(h, rotate = 1, staging, codes_format) computes them; h itself
- * is written to h_out when not NULL.  gate and up share the row stride ld.
- * gate_activated = 1: the gate already holds fl16(gelu_tanh(gate)) (from
- * w4a4_gemm_act), so h = fl16(gate * up). */
+ * is written to h_out when not NULL.  gate and up share the row stride ld. */
 int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int64_t ld,
-                     int32_t gate_activated, int32_t staging, int32_t codes_format, void* codes,
-                     float* row_scale, void* h_out, int64_t ldh, void* stream);
+                     int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                     void* h_out, int64_t ldh, void* stream);
 
 /* Rotary position embedding of `heads` heads of width 256 in each of m rows
  * (apply_rotary_pos_emb: q * cos + rotate_half(q) * sin, each product and
@@ -193,10 +179,9 @@ int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* co
  * w4a4_quant_segments. */
 
 /* h = fl16(fl16(gelu_tanh(gate)) * up) elementwise over [m, n] (n a multiple
- * of 8; the rounding of w4a4_geglu_quant and of PyTorch's eager ops);
- * gate_activated = 1: h = fl16(gate * up). */
-int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld,
-               int32_t gate_activated, void* h, int64_t ldh, void* stream);
+ * of 8; the rounding of w4a4_geglu_quant and of PyTorch's eager ops). */
+int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
+               int64_t ldh, void* stream);
 
 /* w4a4_quant of K = 16384 rows (rotated) whose elements are stored as
  * K / seg segments: element e of row r at x + (e / seg) * seg_stride +

@@ -30,8 +30,6 @@ GEMM_SINGLE_CTA = 0
 GEMM_CTA_PAIR = 1
 GEMM_NO_SPLIT = 2
 GEMM_SPLIT_K = 3
-ACT_NONE = 0
-ACT_GELU_TANH = 1
 ATTN_MAX_SEQ = 4096
 NOALLOC_MAX_ROWS = 65536
 NOALLOC_MAX_CODES = 16 * 1024 * 1024
@@ -40,7 +38,6 @@ NOALLOC_MAX_CODES = 16 * 1024 * 1024
 EXPORTED_SYMBOLS = (
     "w4a4_quant",
     "w4a4_gemm",
-    "w4a4_gemm_act",
     "w4a4_gemm_accumulators",
     "w4a4_int4_gemm",
     "w4a4_int4_gemm_noalloc",
@@ -89,8 +86,6 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_quant.argtypes = [vp, c_i64, c_i32, c_i64, c_i32, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_gemm.argtypes = [vp, vp, c_i64, c_i32, c_i32, ctypes.POINTER(W4A4Weight),
                               ctypes.POINTER(vp), vp]
-    lib.w4a4_gemm_act.argtypes = [vp, vp, c_i64, c_i32, c_i32, ctypes.POINTER(W4A4Weight),
-                                  ctypes.POINTER(vp), vp, vp]
     lib.w4a4_gemm_accumulators.argtypes = [vp, c_i64, c_i32, c_i32, ctypes.POINTER(W4A4Weight),
                                            ctypes.POINTER(vp), vp]
     lib.w4a4_int4_gemm.argtypes = [vp, c_i64, c_i32, c_i64, c_i32, c_i32, c_i32,
@@ -99,12 +94,11 @@ def _declare(lib: ctypes.CDLL) -> None:
                                            ctypes.POINTER(W4A4Weight), ctypes.POINTER(vp), vp]
     lib.w4a4_rmsnorm_quant.argtypes = [vp, c_i64, vp, c_i64, vp, ctypes.c_float, vp, c_i64, vp,
                                        c_i64, c_i64, c_i32, c_i32, c_i32, vp, vp, vp]
-    lib.w4a4_geglu_quant.argtypes = [vp, vp, c_i64, c_i32, c_i64, c_i32, c_i32, c_i32, vp, vp, vp, c_i64,
-                                     vp]
+    lib.w4a4_geglu_quant.argtypes = [vp, vp, c_i64, c_i32, c_i64, c_i32, c_i32, vp, vp, vp, c_i64, vp]
     lib.w4a4_rope.argtypes = [vp, c_i64, vp, c_i64, vp, vp, c_i64, c_i32, vp]
     lib.w4a4_prefix_attention.argtypes = [vp, c_i64, vp, c_i64, vp, c_i64, vp, vp, c_i32, c_i32, c_i32,
                                           vp, vp, c_i64, vp]
-    lib.w4a4_geglu.argtypes = [vp, vp, c_i64, c_i32, c_i64, c_i32, vp, c_i64, vp]
+    lib.w4a4_geglu.argtypes = [vp, vp, c_i64, c_i32, c_i64, vp, c_i64, vp]
     lib.w4a4_quant_segments.argtypes = [vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]

@@ -39,22 +39,6 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-// The tanh-form GELU as PyTorch's eager CUDA kernel computes it for an fp16
-// input (F.gelu(x, approximate="tanh")): 0.5 x (1 + tanh(sqrt(2/pi) (x +
-// 0.044715 x^3))) in fp32 with the constants rounded to fp32, x^3 as (x x) x,
-// the inner sum as one fused multiply-add, rounded to fp16.  tanhf is
-// CUDA's.  Checked bit for bit against torch on every finite fp16 input.
-__device__ __forceinline__ float gelu_tanh_f32(float x) {
-  constexpr float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-  constexpr float kKappa = 0.044715f;
-  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-__device__ __forceinline__ __half gelu_half(__half x) {
-  return __float2half_rn(gelu_tanh_f32(__half2float(x)));
-}
-
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

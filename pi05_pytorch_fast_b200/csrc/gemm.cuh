@@ -102,7 +102,6 @@ struct alignas(64) GemmSegment {
   int tile_begin;           // first global weight-tile index of this matrix
   int vec_store;            // 1: y is 16-byte aligned and n % 8 == 0
   int wide_k;               // 1: K > kMagicMaxK, acc / 16 may reach 2^22 (exact int -> float)
-  int act;                  // 1: y = gelu_half(fp16 result) (the GeGLU gate, see gelu_half)
 };
 
 // Up to this K, |acc / 16| <= 7 * 8 * K < 2^22 and the epilogue converts it
@@ -208,9 +207,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const Til
         a0 = __int2float_rn(static_cast<int32_t>(acc[i]) >> 4);
         a1 = __int2float_rn(static_cast<int32_t>(acc[i + 1]) >> 4);
       }
-      __half2 h = __floats2half2_rn(__fmul_rn(__fmul_rn(a0, t[i]), sw),
-                                    __fmul_rn(__fmul_rn(a1, t[i + 1]), sw));
-      if (seg.act) h = __halves2half2(gelu_half(__low2half(h)), gelu_half(__high2half(h)));
+      const __half2 h = __floats2half2_rn(__fmul_rn(__fmul_rn(a0, t[i]), sw),
+                                          __fmul_rn(__fmul_rn(a1, t[i + 1]), sw));
       stage[i * 32 + lane] = __low2half(h);
       stage[(i + 1) * 32 + lane] = __high2half(h);
     }

@@ -92,7 +92,6 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(
 // GeGLU alone, h = fl16(fl16(gelu_tanh(gate)) * up) over [m, n] (n a
 // multiple of 8): the MLP of a rank that holds a column shard of gate/up,
 // whose rows are completed by an exchange before they are quantised.
-template <bool PREACT>
 __global__ void __launch_bounds__(256) geglu_kernel(const __half* __restrict__ gate,
                                                     const __half* __restrict__ up, long long ld,
                                                     __half* __restrict__ h, long long ldh, long long m,
@@ -105,7 +104,7 @@ __global__ void __launch_bounds__(256) geglu_kernel(const __half* __restrict__ g
   const long long row = idx / vpr;
   const int c = static_cast<int>(idx - row * vpr) * 8;
   *reinterpret_cast<uint4*>(h + row * ldh + c) =
-      geglu8<PREACT>(ld_nc_v4(gate + row * ld + c), ld_nc_v4(up + row * ld + c));
+      geglu8(ld_nc_v4(gate + row * ld + c), ld_nc_v4(up + row * ld + c));
 }
 
 // Rotary embedding of `heads` heads of width 256 per row: element d < 128

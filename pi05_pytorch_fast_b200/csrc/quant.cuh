@@ -57,25 +57,32 @@ __device__ __forceinline__ void load8_half_as_float(const __half* p, float (&v)[
 }
 
 // GeGLU of the Gemma MLP as PyTorch's eager CUDA ops round it
-// (F.gelu(gate, approximate="tanh") * up on fp16 tensors): gelu_half
-// (common.cuh), then the fp16 product with up (the exact fp32 product of two
-// fp16 values, rounded once).  PREACT: the gate already went through
-// gelu_half (in the GEMM epilogue), only the product remains.
-template <bool PREACT = false>
+// (F.gelu(gate, approximate="tanh") * up on fp16 tensors): the tanh-form
+// GELU 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) in fp32 with the
+// constants rounded to fp32, x^3 as (x x) x, the inner sum as one fused
+// multiply-add, rounded to fp16; then the fp16 product with up (the exact
+// fp32 product of two fp16 values, rounded once).  tanhf is CUDA's.
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  constexpr float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  constexpr float kKappa = 0.044715f;
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
 __device__ __forceinline__ __half geglu_half(__half g, __half u) {
-  const __half gl = PREACT ? g : gelu_half(g);
+  const __half gl = __float2half_rn(gelu_tanh_f32(__half2float(g)));
   return __float2half_rn(__fmul_rn(__half2float(gl), __half2float(u)));
 }
 
 // Eight fp16 GeGLU values from 16-byte vectors of gate and up.
-template <bool PREACT = false>
 __device__ __forceinline__ uint4 geglu8(const uint4 g, const uint4 u) {
   uint4 r;
   const __half* gh = reinterpret_cast<const __half*>(&g);
   const __half* uh = reinterpret_cast<const __half*>(&u);
   __half* rh = reinterpret_cast<__half*>(&r);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) rh[j] = geglu_half<PREACT>(gh[j], uh[j]);
+  for (int j = 0; j < 8; ++j) rh[j] = geglu_half(gh[j], uh[j]);
   return r;
 }
 
@@ -494,12 +501,11 @@ __global__ void __launch_bounds__((1 << LOGK) / 16) quant_rot_warp_kernel(
 // 2048-element slice (index bits 0-10) in registers.  Phase 2: after a
 // shared-memory transpose, thread (c, l) = (warp, lane) holds the 8 slices'
 // values at offsets 256c + 8l + j and finishes bits 11-13 in registers.
-// GEGLU (1, or 2 for a gate already activated): the row is gelu_tanh(x) *
-// up (x = the gate), formed as it is loaded (geglu8) and, when h_out is not
-// null, also written there.
+// GEGLU: the row is gelu_tanh(x) * up (x = the gate), formed as it is
+// loaded (geglu8) and, when h_out is not null, also written there.
 // SEGMENTED: the row is stored as segments of `seg` elements (a multiple of
 // 8), segment s of row r at x + s * seg_stride + r * ldx.
-template <bool FP16, int MODE, int GEGLU = 0, bool SEGMENTED = false>
+template <bool FP16, int MODE, bool GEGLU = false, bool SEGMENTED = false>
 __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
     const __half* __restrict__ x, long long ldx, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, const __half* __restrict__ up = nullptr,
@@ -522,7 +528,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
       const __half* ur = up + row * ldu + 2048 * warp + 8 * lane;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint4 h8 = geglu8<GEGLU == 2>(ld_nc_v4(xr + 256 * c), ld_nc_v4(ur + 256 * c));
+        const uint4 h8 = geglu8(ld_nc_v4(xr + 256 * c), ld_nc_v4(ur + 256 * c));
         if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 2048 * warp + 8 * lane + 256 * c) = h8;
         half8_to_float(h8, v[c]);
       }
@@ -643,7 +649,7 @@ constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
 // SEGMENTED: xmap is 4-D {64, lines per segment, M, segments} (a row stored
 // as several segments, each a [M, seg] matrix: the layout an all-to-all of
 // column shards delivers), read with one box per row; same smem layout.
-template <int MODE, int GEGLU = 0, bool SEGMENTED = false>
+template <int MODE, bool GEGLU = false, bool SEGMENTED = false>
 __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
     const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns,
@@ -686,7 +692,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp
     for (int c = 0; c < 8; ++c) {
       uint4 raw = buf[8 * u + (c ^ (u & 7))];
       if constexpr (GEGLU) {
-        raw = geglu8<GEGLU == 2>(raw, buf[2048 + 8 * u + (c ^ (u & 7))]);
+        raw = geglu8(raw, buf[2048 + 8 * u + (c ^ (u & 7))]);
         if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 64 * u + 8 * c) = raw;
       }
       const __half2* hp = reinterpret_cast<const __half2*>(&raw);

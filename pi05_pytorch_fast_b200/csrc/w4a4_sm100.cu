@@ -455,10 +455,8 @@ int launch_rmsnorm_quant(const void* x, int64_t ldx, const void* delta, int64_t 
 }
 
 int launch_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int64_t ld,
-                       int32_t gate_activated, int32_t staging, int32_t codes_format, void* codes,
-                       float* row_scale, void* h_out, int64_t ldh, cudaStream_t stream) {
-  if (gate_activated != 0 && gate_activated != 1)
-    return fail(W4A4_ERR_INVALID, "gate_activated must be 0 or 1, got %d", gate_activated);
+                       int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                       void* h_out, int64_t ldh, cudaStream_t stream) {
   if (k != 16384)
     return fail(W4A4_ERR_UNSUPPORTED, "geglu_quant supports K = 16384 only, got %d", k);
   if (m < 0) return fail(W4A4_ERR_INVALID, "M must be non-negative, got %lld", (long long)m);
@@ -498,30 +496,24 @@ int launch_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, i
         err_code = e;
         return;
       }
-      const auto go = [&](auto kernel, uint64_t bit) {
-        if (int e = ensure_smem_attr(dev, bit, kernel, kQ16SmemGeglu)) {
-          err_code = e;
-          return;
-        }
-        err_code = cuda_status(launch_kernel(kernel, dim3(grid), dim3(kQuantThreads), kQ16SmemGeglu, stream, 1,
-                                             gmap, m, codes, row_scale, isk, g_wait_limit_ns.load(), umap, ho,
-                                             ldh));
-      };
-      if (gate_activated) go(quant_rot_16k_fp16_kernel<MODE, 2>, 1ull << (52 + MODE));
-      else go(quant_rot_16k_fp16_kernel<MODE, 1>, 1ull << (32 + MODE));
+      if (int e = ensure_smem_attr(dev, 1ull << (32 + MODE), quant_rot_16k_fp16_kernel<MODE, true>,
+                                   kQ16SmemGeglu)) {
+        err_code = e;
+        return;
+      }
+      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, true>, dim3(grid),
+                                           dim3(kQuantThreads), kQ16SmemGeglu, stream, 1, gmap, m, codes,
+                                           row_scale, isk, g_wait_limit_ns.load(), umap, ho, ldh));
     } else {
       const int smem = 16384 * 4;
-      const auto go = [&](auto kernel, uint64_t bit) {
-        if (int e = ensure_smem_attr(dev, bit, kernel, smem)) {
-          err_code = e;
-          return;
-        }
-        err_code = cuda_status(launch_kernel(kernel, dim3(grid), dim3(kQuantThreads), smem, stream, 1,
-                                             static_cast<const __half*>(gate), ld, m, codes, row_scale, isk,
-                                             static_cast<const __half*>(up), ld, ho, ldh, 0, 0ll));
-      };
-      if (gate_activated) go(quant_rot_16k_kernel<false, MODE, 2>, 1ull << (56 + MODE));
-      else go(quant_rot_16k_kernel<false, MODE, 1>, 1ull << (36 + MODE));
+      if (int e = ensure_smem_attr(dev, 1ull << (36 + MODE), quant_rot_16k_kernel<false, MODE, true>, smem)) {
+        err_code = e;
+        return;
+      }
+      err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<false, MODE, true>, dim3(grid),
+                                           dim3(kQuantThreads), smem, stream, 1,
+                                           static_cast<const __half*>(gate), ld, m, codes, row_scale, isk,
+                                           static_cast<const __half*>(up), ld, ho, ldh, 0, 0ll));
     }
   });
   if (err_code) return err_code;
@@ -529,10 +521,8 @@ int launch_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, i
   return ok();
 }
 
-int launch_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld,
-                 int32_t gate_activated, void* h, int64_t ldh, cudaStream_t stream) {
-  if (gate_activated != 0 && gate_activated != 1)
-    return fail(W4A4_ERR_INVALID, "gate_activated must be 0 or 1, got %d", gate_activated);
+int launch_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
+                 int64_t ldh, cudaStream_t stream) {
   if (m < 0 || n <= 0 || n % 8 != 0)
     return fail(W4A4_ERR_INVALID, "geglu: invalid shape m=%lld n=%d (n a positive multiple of 8)", (long long)m, n);
   if (m == 0) return ok();
@@ -541,8 +531,7 @@ int launch_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t
     return fail(W4A4_ERR_INVALID, "geglu rows must be 16-byte aligned with strides >= n, multiples of 8");
   const int64_t blocks = (m * (n / 8) + 255) / 256;
   if (blocks > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "geglu: too many rows");
-  W4A4_CUDA_TRY(launch_kernel(gate_activated ? geglu_kernel<true> : geglu_kernel<false>,
-                              dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
+  W4A4_CUDA_TRY(launch_kernel(geglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
                               static_cast<const __half*>(gate), static_cast<const __half*>(up), ld,
                               static_cast<__half*>(h), ldh, m, n));
   W4A4_CUDA_TRY(cudaGetLastError());
@@ -587,23 +576,23 @@ int launch_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int6
         err_code = e;
         return;
       }
-      if (int e = ensure_smem_attr(dev, 1ull << (44 + MODE), quant_rot_16k_fp16_kernel<MODE, 0, true>,
+      if (int e = ensure_smem_attr(dev, 1ull << (44 + MODE), quant_rot_16k_fp16_kernel<MODE, false, true>,
                                    kQ16Smem)) {
         err_code = e;
         return;
       }
-      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, 0, true>, dim3(grid),
+      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, false, true>, dim3(grid),
                                            dim3(kQuantThreads), kQ16Smem, stream, 1, xmap, m, codes,
                                            row_scale, isk, g_wait_limit_ns.load(), xmap,
                                            static_cast<__half*>(nullptr), 0ll));
     } else {
       const int smem = 16384 * 4;
-      if (int e = ensure_smem_attr(dev, 1ull << (48 + MODE), quant_rot_16k_kernel<false, MODE, 0, true>,
+      if (int e = ensure_smem_attr(dev, 1ull << (48 + MODE), quant_rot_16k_kernel<false, MODE, false, true>,
                                    smem)) {
         err_code = e;
         return;
       }
-      err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<false, MODE, 0, true>, dim3(grid),
+      err_code = cuda_status(launch_kernel(quant_rot_16k_kernel<false, MODE, false, true>, dim3(grid),
                                            dim3(kQuantThreads), smem, stream, 1, static_cast<const __half*>(x),
                                            ld, m, codes, row_scale, isk, static_cast<const __half*>(nullptr),
                                            0ll, static_cast<__half*>(nullptr), 0ll, seg, seg_stride));
@@ -864,7 +853,7 @@ bool use_pair_kernel(int variant, int layout, int64_t m) {
 
 int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
                 const w4a4_weight* weights, void* const* y, cudaStream_t stream,
-                bool acc_out = false, const int32_t* act = nullptr) {
+                bool acc_out = false) {
   if (k <= 0 || k % 64 != 0) return fail(W4A4_ERR_INVALID, "K must be a multiple of 64, got %d", k);
   // the tensor cores accumulate 16 x sum(qa * qw), |.| <= 16 * 7 * 8 * K, in int32
   if (k > kMaxGemmK)
@@ -879,8 +868,6 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
       return fail(W4A4_ERR_INVALID, "all weights of one call must share a layout");
     if (int e = check_weight(weights[i], k, i)) return e;
     if (m > 0 && !y[i]) return fail(W4A4_ERR_INVALID, "output %d is null", i);
-    if (act && act[i] != W4A4_ACT_NONE && act[i] != W4A4_ACT_GELU_TANH)
-      return fail(W4A4_ERR_INVALID, "unknown activation %d for weight %d", act[i], i);
   }
   if (m == 0) return ok();
   if (!codes || (!row_scale && !acc_out)) return fail(W4A4_ERR_INVALID, "null codes/scale pointer");
@@ -920,7 +907,6 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     s.tile_begin = w_tiles;
     s.vec_store = (!acc_out && w.n % 8 == 0 && aligned(y[i], 16)) ? 1 : 0;
     s.wide_k = k > kMagicMaxK ? 1 : 0;
-    s.act = (act && !acc_out) ? act[i] : W4A4_ACT_NONE;
     w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
   const int k_steps = (k + kBlockK - 1) / kBlockK;
@@ -1043,12 +1029,6 @@ int w4a4_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k, i
                      static_cast<cudaStream_t>(stream));
 }
 
-int w4a4_gemm_act(const void* codes, const float* row_scale, int64_t m, int32_t k, int32_t n_weights,
-                  const w4a4_weight* weights, void* const* y, const int32_t* act, void* stream) {
-  return launch_gemm(codes, row_scale, m, k, n_weights, weights, y, static_cast<cudaStream_t>(stream),
-                     false, act);
-}
-
 int w4a4_gemm_accumulators(const void* codes, int64_t m, int32_t k, int32_t n_weights,
                            const w4a4_weight* weights, int32_t* const* acc, void* stream) {
   return launch_gemm(codes, nullptr, m, k, n_weights, weights,
@@ -1096,10 +1076,10 @@ int w4a4_rmsnorm_quant(const void* x, int64_t ldx, const void* delta, int64_t ld
 }
 
 int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int64_t ld,
-                     int32_t gate_activated, int32_t staging, int32_t codes_format, void* codes,
-                     float* row_scale, void* h_out, int64_t ldh, void* stream) {
-  return launch_geglu_quant(gate, up, m, k, ld, gate_activated, staging, codes_format, codes, row_scale,
-                            h_out, ldh, static_cast<cudaStream_t>(stream));
+                     int32_t staging, int32_t codes_format, void* codes, float* row_scale,
+                     void* h_out, int64_t ldh, void* stream) {
+  return launch_geglu_quant(gate, up, m, k, ld, staging, codes_format, codes, row_scale, h_out, ldh,
+                            static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
@@ -1115,9 +1095,9 @@ int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk
                           ldo, static_cast<cudaStream_t>(stream));
 }
 
-int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld,
-               int32_t gate_activated, void* h, int64_t ldh, void* stream) {
-  return launch_geglu(gate, up, m, n, ld, gate_activated, h, ldh, static_cast<cudaStream_t>(stream));
+int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
+               int64_t ldh, void* stream) {
+  return launch_geglu(gate, up, m, n, ld, h, ldh, static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_t ld,

@@ -26,7 +26,6 @@ are ``cumsum(pad_mask) - 1``.
 
 from __future__ import annotations
 
-import ctypes
 import json
 import math
 from dataclasses import dataclass, field
@@ -316,14 +315,13 @@ class W4A4PrefixLM:
     def _stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def _gemm(self, ws: _Workspace, rows: int, k: int, weights, outs, fragment: bool, act=None) -> None:
+    def _gemm(self, ws: _Workspace, rows: int, k: int, weights, outs, fragment: bool) -> None:
         layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment else nat.LAYOUT_ROW_MAJOR
         descs = nat.weights_array([(w.data_ptr(), int(w.shape[0]), int(w.shape[1]), layout)
                                    for w in weights])
         ptrs = nat.pointer_array([o.data_ptr() for o in outs])
-        acts = None if act is None else (ctypes.c_int32 * len(act))(*act)
-        nat.check(self._lib.w4a4_gemm_act(ws.codes.data_ptr(), ws.scales.data_ptr(), rows, k,
-                                          len(weights), descs, ptrs, acts, self._stream()))
+        nat.check(self._lib.w4a4_gemm(ws.codes.data_ptr(), ws.scales.data_ptr(), rows, k,
+                                      len(weights), descs, ptrs, self._stream()))
 
     @staticmethod
     def _codes(ws: _Workspace, rows: int, k: int) -> torch.Tensor:
@@ -395,19 +393,16 @@ class W4A4PrefixLM:
                               (ws.o.clone(),)))
             # --- MLP block (the attention output is added inside the norm)
             self._norm_quant(ws, rows, ws.o, lw.post_gain, trace)
-            if trace is not None:  # the plain GEMM outputs, for the trace
-                self._gemm(ws, rows, hid, [lw.gate, lw.up], [ws.gate, ws.up], fragment=True)
+            self._gemm(ws, rows, hid, [lw.gate, lw.up], [ws.gate, ws.up], fragment=True)
+            if trace is not None:
                 trace.append(("gateup", li, ws.h.clone(), self._codes(ws, rows, hid).clone(), ws.scales.clone(),
                               (ws.gate.clone(), ws.up.clone())))
-            # the gate leaves the GEMM activated: act_fn(gate), rounded as torch's gelu rounds it
-            self._gemm(ws, rows, hid, [lw.gate, lw.up], [ws.gate, ws.up], fragment=True,
-                       act=(nat.ACT_GELU_TANH, nat.ACT_NONE))
             if self.shard is not None:
                 self._sharded_mlp_tail(ws, rows, lw)
             else:
                 h_mlp = ws.h_mlp if trace is not None else None
                 nat.check(lib.w4a4_geglu_quant(
-                    ws.gate.data_ptr(), ws.up.data_ptr(), rows, cfg.intermediate, cfg.intermediate, 1,
+                    ws.gate.data_ptr(), ws.up.data_ptr(), rows, cfg.intermediate, cfg.intermediate,
                     self.staging, nat.CODES_GEMM, ws.codes.data_ptr(), ws.scales.data_ptr(),
                     h_mlp.data_ptr() if h_mlp is not None else None, cfg.intermediate, st))
                 self._gemm(ws, rows, inter, [lw.down], [ws.down], fragment=False)
@@ -429,7 +424,7 @@ class W4A4PrefixLM:
         sh, cfg, st = self.shard, self.cfg, self._stream()
         part = cfg.intermediate // sh.world
         mine = rows // sh.world
-        nat.check(self._lib.w4a4_geglu(ws.gate.data_ptr(), ws.up.data_ptr(), rows, part, part, 1,
+        nat.check(self._lib.w4a4_geglu(ws.gate.data_ptr(), ws.up.data_ptr(), rows, part, part,
                                        ws.h_part.data_ptr(), part, st))
         exchange_row_blocks(ws.h_part, ws.h_recv, sh)
         nat.check(self._lib.w4a4_quant_segments(ws.h_recv.data_ptr(), mine, cfg.intermediate, part, part,

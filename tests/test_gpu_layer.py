@@ -22,8 +22,6 @@ check is PyTorch's own eager CUDA result on the same GPU:
 
 from __future__ import annotations
 
-import ctypes
-
 import numpy as np
 import pytest
 import torch
@@ -49,15 +47,14 @@ def _stream():
     return torch.cuda.current_stream(DEV).cuda_stream
 
 
-def geglu_quant(gate, up, staging, h_out=True, gate_activated=0):
+def geglu_quant(gate, up, staging, h_out=True):
     m, k = gate.shape
     codes = torch.empty((m, k), dtype=torch.int8, device=DEV)
     scales = torch.empty((m,), dtype=torch.float32, device=DEV)
     h = torch.empty_like(gate) if h_out else None
     nat.check(nat.lib().w4a4_geglu_quant(gate.data_ptr(), up.data_ptr(), m, k, gate.stride(0),
-                                         gate_activated, staging, nat.CODES_INT8, codes.data_ptr(),
-                                         scales.data_ptr(), h.data_ptr() if h is not None else None, k,
-                                         _stream()))
+                                         staging, nat.CODES_INT8, codes.data_ptr(), scales.data_ptr(),
+                                         h.data_ptr() if h is not None else None, k, _stream()))
     return codes, scales, h
 
 
@@ -118,43 +115,6 @@ def test_geglu_quant_matches_torch_and_oracle(staging, m):
     torch.cuda.synchronize()
     assert_half_equal(h, ref)
     assert_codes_match_oracle(ref, codes, scales, staging)
-
-
-@pytest.mark.parametrize("staging", list(STAGINGS))
-def test_geglu_quant_with_an_activated_gate(staging):
-    """gate_activated = 1: the gate holds gelu(gate) already (the GEMM
-    epilogue's activation); the same h, codes and scales result."""
-    gen = torch.Generator(device=DEV).manual_seed(21)
-    gate = (torch.randn(96, 16384, device=DEV, generator=gen) * 1.5).half()
-    up = torch.randn(96, 16384, device=DEV, generator=gen).half()
-    c1, s1, h1 = geglu_quant(gate, up, STAGINGS[staging])
-    c2, s2, h2 = geglu_quant(F.gelu(gate, approximate="tanh"), up, STAGINGS[staging], gate_activated=1)
-    torch.cuda.synchronize()
-    assert_half_equal(h1, h2)
-    assert torch.equal(c1, c2) and torch.equal(s1, s2)
-
-
-def test_gemm_epilogue_gelu_matches_torch():
-    """w4a4_gemm_act with W4A4_ACT_GELU_TANH on one of two weights: that
-    output is F.gelu(approximate="tanh") of the plain GEMM output, bit for
-    bit; the other output is unchanged."""
-    from pi05_pytorch_fast_b200.w4a4 import extension as ext
-
-    gen = torch.Generator().manual_seed(8)
-    x = (torch.randn(200, 2048, generator=gen)).half().to(DEV)
-    ws = [orc.preshuffle_wmma_weight(orc.random_packed_weight(512, 2048, s), 2048) for s in (3, 4)]
-    ws = [torch.from_numpy(w).to(DEV) for w in ws]
-    codes, scales = ext.quantize(x, fmt="gemm")
-    plain = ext.gemm_from_codes(codes, scales, ws, fragment_major=True)
-    ys = [torch.empty_like(p) for p in plain]
-    descs = nat.weights_array([(w.data_ptr(), int(w.shape[0]), int(w.shape[1]), nat.LAYOUT_FRAGMENT_MAJOR)
-                               for w in ws])
-    act = (ctypes.c_int32 * 2)(nat.ACT_GELU_TANH, nat.ACT_NONE)
-    nat.check(nat.lib().w4a4_gemm_act(codes.data_ptr(), scales.data_ptr(), 200, 2048, 2, descs,
-                                      nat.pointer_array([y.data_ptr() for y in ys]), act, _stream()))
-    torch.cuda.synchronize()
-    assert_half_equal(ys[0], F.gelu(plain[0], approximate="tanh"))
-    assert_half_equal(ys[1], plain[1])
 
 
 def test_geglu_quant_without_h_out_gives_the_same_codes():

@@ -354,20 +354,18 @@ def test_layer_glue_argument_validation_without_gpu():
                                                             None, 0, 4, 2048, 0, 2, fake, fake, None))
     assert "staging" in _err(lib.w4a4_rmsnorm_quant(fake, 2048, None, 0, fake, 1e-6, None, 0, None, 0,
                                                     4, 2048, 9, 2, fake, fake, None))
-    assert "K = 16384" in _err(lib.w4a4_geglu_quant(fake, fake, 4, 2048, 2048, 0, 0, 2, fake, fake, None, 0,
+    assert "K = 16384" in _err(lib.w4a4_geglu_quant(fake, fake, 4, 2048, 2048, 0, 2, fake, fake, None, 0,
                                                     None))
-    assert "16-byte aligned" in _err(lib.w4a4_geglu_quant(fake + 2, fake, 4, 16384, 16384, 0, 0, 2, fake, fake,
+    assert "16-byte aligned" in _err(lib.w4a4_geglu_quant(fake + 2, fake, 4, 16384, 16384, 0, 2, fake, fake,
                                                           None, 0, None))
-    assert "gate_activated" in _err(lib.w4a4_geglu_quant(fake, fake, 4, 16384, 16384, 2, 0, 2, fake, fake,
-                                                         None, 0, None))
-    assert "codes format" in _err(lib.w4a4_geglu_quant(fake, fake, 4, 16384, 16384, 0, 0, 7, fake, fake,
+    assert "codes format" in _err(lib.w4a4_geglu_quant(fake, fake, 4, 16384, 16384, 0, 7, fake, fake,
                                                        None, 0, None))
     assert "rope rows" in _err(lib.w4a4_rope(fake, 100, fake, 256, fake, fake, 4, 1, None))
     assert "invalid rope shape" in _err(lib.w4a4_rope(fake, 256, fake, 256, fake, fake, 4, 0, None))
     # empty inputs succeed before any device call
     assert lib.w4a4_rmsnorm_quant(None, 2048, None, 0, None, 1e-6, None, 0, fake, 2048, 0, 2048, 0, 2,
                                   None, None, None) == nat.W4A4_OK
-    assert lib.w4a4_geglu_quant(None, None, 0, 16384, 16384, 0, 0, 2, None, None, None, 0, None) == nat.W4A4_OK
+    assert lib.w4a4_geglu_quant(None, None, 0, 16384, 16384, 0, 2, None, None, None, 0, None) == nat.W4A4_OK
     assert lib.w4a4_rope(None, 256, None, 256, None, None, 0, 8, None) == nat.W4A4_OK
 
 
