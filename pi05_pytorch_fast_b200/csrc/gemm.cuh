@@ -101,12 +101,14 @@ struct alignas(64) GemmSegment {
   int n;                    // weight rows of this matrix
   int tile_begin;           // first global weight-tile index of this matrix
   int vec_store;            // 1: y is 16-byte aligned and n % 8 == 0
-  int wide_k;               // 1: K > kMagicMaxK, acc / 16 may reach 2^22 (exact int -> float)
 };
 
 // Up to this K, |acc / 16| <= 7 * 8 * K < 2^22 and the epilogue converts it
-// to fp32 with the magic-number trick; beyond it, with cvt.rn.f32.s32 (the
-// reference's (float)acc, correct for any int32).
+// to fp32 with the magic-number trick; beyond it the host runs the WIDE
+// instantiation, which converts with cvt.rn.f32.s32 (the reference's
+// (float)acc, correct for any int32).  A compile-time variant keeps the hot
+// kernels' code unchanged: extra code in this epilogue slows the whole GEMM
+// (its issue loops share the SM's instruction cache with it).
 constexpr int kMagicMaxK = 65536;
 
 struct alignas(64) GemmParams {
@@ -171,7 +173,7 @@ __device__ __forceinline__ void stage_tile_scales(float* ts, const float* row_sc
 
 // One 16-token chunk of the epilogue for one warp: thread `lane` owns weight
 // row n (its TMEM lane) and acc[i] = 16 * sum_k qa[token c0+i] * qw[n].
-template <bool ACC_OUT>
+template <bool ACC_OUT, bool WIDE = false>
 __device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const TileCoord& c, int n_warp,
                                                int lane, int c0, float sw, const uint32_t (&acc)[16],
                                                __half* stage, const float* ts) {
@@ -198,9 +200,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmSegment& seg, const Til
     for (int i = 0; i < 16; i += 2) {
       // acc / 16 as fp32: for K <= kMagicMaxK |acc / 16| < 2^22, so adding it
       // to the integer bits of 1.5 * 2^23 and subtracting that value is
-      // exact; wider K rounds it like (float)acc (uniform branch).
+      // exact; the WIDE kernel (K > kMagicMaxK) rounds it like (float)acc.
       float a0, a1;
-      if (!seg.wide_k) {
+      if constexpr (!WIDE) {
         a0 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i]) >> 4) + 0x4B400000), 12582912.0f);
         a1 = __fsub_rn(__int_as_float((static_cast<int32_t>(acc[i + 1]) >> 4) + 0x4B400000), 12582912.0f);
       } else {
@@ -243,7 +245,7 @@ struct NoCombine {
   __device__ __forceinline__ bool operator()(uint32_t (&)[16], int) const { return true; }
 };
 
-template <bool ACC_OUT, typename Release, typename Combine = NoCombine>
+template <bool ACC_OUT, typename Release, typename Combine = NoCombine, bool WIDE = false>
 __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const TileCoord& c, int n_warp,
                                               uint32_t tacc, int half, int lane, __half* stage,
                                               const float* ts, Release release,
@@ -267,13 +269,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const Tile
   for (int j = 0; j < my; j += 2) {
     if (j + 1 < my) tmem_ld_32x32b_x16(tacc + col(j + 1), a1);
     if (combine(a0, first + step * j))
-      epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, col(j), sw, a0, stage, ts);
+      epilogue_chunk<ACC_OUT, WIDE>(seg, c, n_warp, lane, col(j), sw, a0, stage, ts);
     if (j + 1 >= my) break;
     tmem_ld_wait();
     if (j + 2 == my) release();
     if (j + 2 < my) tmem_ld_32x32b_x16(tacc + col(j + 2), a0);
     if (combine(a1, first + step * (j + 1)))
-      epilogue_chunk<ACC_OUT>(seg, c, n_warp, lane, col(j + 1), sw, a1, stage, ts);
+      epilogue_chunk<ACC_OUT, WIDE>(seg, c, n_warp, lane, col(j + 1), sw, a1, stage, ts);
     if (j + 2 >= my) break;
     tmem_ld_wait();
     if (j + 3 == my) release();
@@ -291,7 +293,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmSegment& seg, const Tile
 // the partner writes out into the partner's ring (distributed shared memory),
 // then adds the partner's partial sums of its own half (int32, exact) and
 // writes that half.
-template <int LAYOUT, bool ACC_OUT, bool SPLIT>
+// WIDE = true: the K > kMagicMaxK conversion (single-CTA, no split-K only).
+template <int LAYOUT, bool ACC_OUT, bool SPLIT, bool WIDE = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a4_gemm_kernel(const __grid_constant__ GemmParams p) {
   constexpr int RING = kGemmRing;
@@ -597,8 +600,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       };
       const uint32_t tacc = tmem_base + lane_addr + buf * acc_cols;
       if constexpr (!SPLIT) {
-        epilogue_tile<ACC_OUT>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc, half, lane, stage, ts,
-                               release);
+        epilogue_tile<ACC_OUT, decltype(release), NoCombine, WIDE>(p.seg[c.seg], c, c.n0 + quarter * 32, tacc,
+                                                                   half, lane, stage, ts, release);
       } else {
         // Both ranks finish half of the tile: rank r writes the chunks with
         // j % 2 == r (j indexes this warp's chunks half + 2j) and pushes its

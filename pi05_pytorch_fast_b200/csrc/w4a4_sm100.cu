@@ -877,8 +877,10 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   if (int e = current_device(&dev)) return e;
   if (int e = sm_count(dev, &sms)) return e;
 
-  const int variant = g_gemm_variant.load();
-  const bool pair = use_pair_kernel(variant, layout, m);
+  // K > kMagicMaxK: the WIDE single-CTA kernel (exact int -> float of acc / 16)
+  const bool wide = k > kMagicMaxK && !acc_out;
+  const int variant = wide ? W4A4_GEMM_NO_SPLIT : g_gemm_variant.load();
+  const bool pair = !wide && use_pair_kernel(variant, layout, m);
   const int rows_per_wtile = pair ? 2 * kBlockW : kBlockW;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -906,7 +908,6 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
     s.n = w.n;
     s.tile_begin = w_tiles;
     s.vec_store = (!acc_out && w.n % 8 == 0 && aligned(y[i], 16)) ? 1 : 0;
-    s.wide_k = k > kMagicMaxK ? 1 : 0;
     w_tiles += (w.n + rows_per_wtile - 1) / rows_per_wtile;
   }
   const int k_steps = (k + kBlockK - 1) / kBlockK;
@@ -965,7 +966,16 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
                                   gemm_smem_bytes(tok_tile), stream, 1, p));                  \
     }                                                                                         \
   } while (0)
-  if (layout == W4A4_LAYOUT_ROW_MAJOR) {
+  if (wide) {
+    const auto go = [&](auto kernel, uint64_t bit) -> int {
+      if (int e = ensure_smem_attr(dev, bit, kernel, kSmemLimit)) return e;
+      W4A4_CUDA_TRY(launch_kernel(kernel, grid, dim3(kGemmThreads), gemm_smem_bytes(tok_tile), stream, 1, p));
+      return W4A4_OK;
+    };
+    if (int e = layout == W4A4_LAYOUT_ROW_MAJOR ? go(w4a4_gemm_kernel<kRowMajor, false, false, true>, 1ull << 26)
+                                                : go(w4a4_gemm_kernel<kFragmentMajor, false, false, true>, 1ull << 27))
+      return e;
+  } else if (layout == W4A4_LAYOUT_ROW_MAJOR) {
     if (acc_out) W4A4_LAUNCH_GEMM(kRowMajor, true, 4);
     else W4A4_LAUNCH_GEMM(kRowMajor, false, 2);
   } else {
