@@ -470,8 +470,9 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "timing": "CUDA graph replay of the whole forward, CUDA events, max over ranks",
         },
         "gpu_launches": model.launches_per_forward() * args.steps,
-        "gpu_launches_note": "kernels of libw4a4_sm100.so per timed region (10 per layer + the final "
-                             "norm); the attention and cos/sin glue are PyTorch kernels, not counted",
+        "gpu_launches_note": "kernels of libw4a4_sm100.so per timed region (12 per layer + the final "
+                             "norm; 13 per layer with --shard-mlp); the positions / cos-sin tables are a "
+                             "few PyTorch ops per forward, and NCCL's kernels, not counted",
         "clocks": clocks.summary(),
         "e2e": {
             "value": job_throughput(ms_e2e, args.batch, job_obs),

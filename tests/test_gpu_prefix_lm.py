@@ -250,6 +250,50 @@ def test_forward_stays_within_the_references_own_rounding_spread():
     assert float(ours_d.max()) <= 2.0 * float(spread.max()) + 1e-3 * rms
 
 
+def test_model_from_the_references_on_disk_pack(gemma2, tmp_path):
+    """The reference's offline pack (pack_w4a4_prefix.py: packed.safetensors
+    with `{module}.packed` int32 [N, K/8+1] tensors, meta.json with the
+    embedl-int4-gemm-v1 format) loads through from_packed_dir, is repacked
+    once into the GEMM's layouts and gives the same forward as packing the
+    model directly."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from pi05_pytorch_fast_b200.w4a4.pack import pack_linear_weight
+
+    prefix = "paligemma_with_expert.paligemma.model.language_model"
+    tensors, layers, norms = {}, {}, {}
+    for i, layer in enumerate(gemma2.layers):
+        mods = {"self_attn.q_proj": layer.self_attn.q_proj, "self_attn.k_proj": layer.self_attn.k_proj,
+                "self_attn.v_proj": layer.self_attn.v_proj, "self_attn.o_proj": layer.self_attn.o_proj,
+                "mlp.gate_proj": layer.mlp.gate_proj, "mlp.up_proj": layer.mlp.up_proj,
+                "mlp.down_proj": layer.mlp.down_proj}
+        for name, lin in mods.items():
+            key = f"{prefix}.layers.{i}.{name}"
+            tensors[key + ".packed"] = pack_linear_weight(lin.weight).contiguous()
+            layers[key] = {"in_features": lin.in_features, "out_features": lin.out_features,
+                           "rotate": True, "has_bias": False}
+        norms[f"layers.{i}.input_layernorm"] = layer.input_layernorm.weight
+        norms[f"layers.{i}.post_attention_layernorm"] = layer.post_attention_layernorm.weight
+    norms["norm"] = gemma2.norm.weight
+    save_file(tensors, str(tmp_path / "packed.safetensors"))
+    (tmp_path / "meta.json").write_text(json.dumps({"format": "embedl-int4-gemm-v1", "layers": layers}))
+    cfg = plm.PrefixLMConfig.from_gemma(gemma2.config)
+    loaded = plm.W4A4PrefixLM.from_packed_dir(tmp_path, norms, cfg, DEV)
+    direct = plm.W4A4PrefixLM.from_gemma(gemma2, DEV)
+    assert torch.equal(loaded.layers[0].gate, direct.layers[0].gate)
+    assert torch.equal(loaded.layers[1].q, direct.layers[1].q)
+    embeds, pad = plm.synthetic_prefix(1, device=DEV, seed=9)
+    with torch.no_grad():
+        a = loaded.forward(embeds, pad).hidden.clone()
+        b = direct.forward(embeds, pad).hidden.clone()
+    torch.cuda.synchronize()
+    # from_packed_dir has no rotary buffer to read: the fp16 LM's table, as
+    # from_gemma takes from the fp16 model
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
 def test_graph_replay_equals_eager_forward(gemma2):
     model = plm.W4A4PrefixLM.from_gemma(gemma2, DEV)
     embeds, pad = plm.synthetic_prefix(2, device=DEV, seed=7)
