@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--staging", choices=("fp16", "fp32"), default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timings")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config 3: time the forward at prefix M in {640, 768, 776} x batch B in "
+                         "{1, 8, 32, 64} on one GPU, one JSON line per point")
     ap.add_argument("--shard-mlp", action="store_true",
                     help="with N > 1: every rank runs the SAME observations and holds 1/N of gate/up "
                          "(tensor-parallel MLP, NCCL all-to-all + all-gather; strong scaling)")
@@ -525,7 +528,10 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
     out: dict = {}
 
     def cycle(fn):
-        return lambda: [fn(lw) for lw in lws]
+        def run():
+            for lw in lws:  # outputs dropped at once: the graph pool reuses their memory
+                fn(lw)
+        return run
 
     gemms = {
         "gemm_qkv": (lambda lw: ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]]),
@@ -594,6 +600,65 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
         },
         "kernels": out,
     }
+
+
+def run_sweep(args) -> None:
+    """Config 3 on one GPU: the forward at every (prefix, batch) of the
+    sweep, one model, one JSON line per point with its own clock record and
+    the per-GEMM fractions at that row count."""
+    import torch
+
+    from pi05_pytorch_fast_b200 import _native as nat
+    from pi05_pytorch_fast_b200 import prefix_lm as plm
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    ext.preload()
+    staging = nat.STAGING_FP32 if args.staging == "fp32" else nat.STAGING_FP16
+    model = plm.W4A4PrefixLM.random(plm.PrefixLMConfig(layers=args.layers), device, seed=1234,
+                                    staging=staging)
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    lws = [layer_weights(lw) for lw in model.layers]
+    for prefix in (640, 768, 776):
+        for batch in (1, 8, 32, 64):
+            m = batch * prefix
+            embeds, pad = plm.synthetic_prefix(batch, lang_tokens=prefix - N_IMG, device=device, seed=7)
+            steps = max(5, args.steps // batch)
+            with torch.no_grad():
+                g = plm.GraphedPrefixLM(model, batch, prefix)
+                g.run(embeds, pad)
+                with ClockSampler(0) as clocks:
+                    ms = time_device(g.replay, steps, args.warmup, False, device)
+                del g
+                x = synthetic_activations(m, HIDDEN, device, seed=1)
+                h = synthetic_activations(m, INTER, device, seed=2)
+                codes, scales = ext.quantize(x, fmt="gemm", staging=staging)
+                codes16, scales16 = ext.quantize(h, fmt="gemm", staging=staging)
+                fr = {}
+                for name, fn, ops in (
+                        ("qkv", lambda lw: ext.gemm_from_codes(codes, scales, [lw["q"], lw["k"], lw["v"]]),
+                         2.0 * m * (N_Q + 2 * N_KV) * HIDDEN),
+                        ("o", lambda lw: ext.gemm_from_codes(codes, scales, [lw["o"]]), 2.0 * m * HIDDEN * HIDDEN),
+                        ("gateup", lambda lw: ext.gemm_from_codes(codes, scales, [lw["gate"], lw["up"]],
+                                                                  fragment_major=True),
+                         2.0 * m * 2 * INTER * HIDDEN),
+                        ("down", lambda lw: ext.gemm_from_codes(codes16, scales16, [lw["down"]]),
+                         2.0 * m * HIDDEN * INTER)):
+                    def cyc(fn=fn):
+                        for lw in lws:  # outputs dropped at once: the graph pool reuses their memory
+                            fn(lw)
+                    t = graph_ms(cyc, 3, False, device) / len(lws)
+                    fr[name] = {"us": round(t * 1e3, 2), "frac": ops / (t * 1e-3) / 1e12 / int8_peak}
+                del x, h, codes, scales, codes16, scales16
+            model._ws.clear()
+            torch.cuda.empty_cache()
+            print(json.dumps({"sweep": "config 3", "prefix": prefix, "batch": batch, "rows": m,
+                              "ms_per_step": ms, "ms_per_prefix": ms / batch, "obs_per_s": batch / (ms * 1e-3),
+                              "gemm_int_tops": ops_per_prefix(m, args.layers) / (ms * 1e-3) / 1e12,
+                              "gemm_frac_of_int8": fr, "int8_peak_tops": int8_peak,
+                              "clocks": clocks.summary(), "steps": steps}), flush=True)
 
 
 def run_reference(args, rank, world):
@@ -708,6 +773,9 @@ def main():
     args = parse_args()
     if args.case:
         run_case(args)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
