@@ -761,7 +761,7 @@ def run_case(args):
             nat.check(lib.w4a4_prefix_attention(
                 x.data_ptr(), HIDDEN, h.data_ptr(), INTER, h.data_ptr() + 2 * 256, INTER,
                 ws.key_valid.data_ptr(), ws.kv_len.data_ptr(), args.batch, args.prefix, 8,
-                ws.vt.data_ptr(), ws.attn.data_ptr(), HIDDEN, st))
+                ws.vt.data_ptr(), ws.attn.data_ptr(), HIDDEN, None, None, None, 0, st))
         elif args.case == "forward":
             with torch.no_grad():
                 model.forward(embeds, pad)

@@ -164,6 +164,17 @@ int w4a4_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, int
                      int32_t staging, int32_t codes_format, void* codes, float* row_scale,
                      void* h_out, int64_t ldh, void* stream);
 
+/* The per-forward tables of a batch of prefixes from its pad mask (uint8
+ * [batch, seq], 1 = real token): key_valid (a byte copy of the mask),
+ * kv_len[b] = last real token + 1, and the rotary tables cos_t / sin_t fp16
+ * [batch * seq, 2 * half] at position cumsum(pad) - 1: cos / sin of
+ * fl32(pos * inv_freq[i]), i < half, repeated over both halves.  Replaces
+ * the position ids and rotary embedding of the reference's prefix pass
+ * (lerobot's cumsum position ids; transformers' GemmaRotaryEmbedding). */
+int w4a4_prefix_tables(const uint8_t* pad, int32_t batch, int32_t seq, const float* inv_freq,
+                       int32_t half, uint8_t* key_valid, int32_t* kv_len, void* cos_t, void* sin_t,
+                       void* stream);
+
 /* Rotary position embedding of `heads` heads of width 256 in each of m rows
  * (apply_rotary_pos_emb: q * cos + rotate_half(q) * sin, each product and
  * the sum rounded to fp16).  cos_t / sin_t: fp16 [m, 256], row stride 256.
@@ -205,11 +216,18 @@ int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_
  *   kv_len     int32 [batch]: every key at or past kv_len[b] is padding
  *   vt_scratch fp16 [batch, 256, W4A4_ATTN_VT_STRIDE(seq)]: V transposed
  *   out        fp16 [batch * seq, ldo], heads x 256 per row
- * heads must divide 128; seq <= 4096.  Two launches (V transpose, attention). */
+ *   cos_t, sin_t  NULL: q and k are used as given; else fp16 [batch * seq,
+ *              256] rotary tables: q is rotated in place first (w4a4_rope's
+ *              arithmetic) and k is rotated into k_out [batch * seq, ldko]
+ *              (k_out may equal k; it is the KV cache's key rows), which the
+ *              attention then reads
+ * heads must divide 128; seq <= 4096.  Two launches (RoPE + V transpose,
+ * attention). */
 #define W4A4_ATTN_VT_STRIDE(seq) ((((int64_t)(seq)) + 7) / 8 * 8)
-int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                           int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                           int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
+                          const void* cos_t, const void* sin_t, void* k_out, int64_t ldko,
                           void* stream);
 
 /* Copy a row-major packed weight [n, src_row_words] into [n, dst_row_words]

@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "w4a4_int4_gemm_noalloc",
     "w4a4_rmsnorm_quant",
     "w4a4_geglu_quant",
+    "w4a4_prefix_tables",
     "w4a4_rope",
     "w4a4_prefix_attention",
     "w4a4_geglu",
@@ -95,9 +96,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_rmsnorm_quant.argtypes = [vp, c_i64, vp, c_i64, vp, ctypes.c_float, vp, c_i64, vp,
                                        c_i64, c_i64, c_i32, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_geglu_quant.argtypes = [vp, vp, c_i64, c_i32, c_i64, c_i32, c_i32, vp, vp, vp, c_i64, vp]
+    lib.w4a4_prefix_tables.argtypes = [vp, c_i32, c_i32, vp, c_i32, vp, vp, vp, vp, vp]
     lib.w4a4_rope.argtypes = [vp, c_i64, vp, c_i64, vp, vp, c_i64, c_i32, vp]
     lib.w4a4_prefix_attention.argtypes = [vp, c_i64, vp, c_i64, vp, c_i64, vp, vp, c_i32, c_i32, c_i32,
-                                          vp, vp, c_i64, vp]
+                                          vp, vp, c_i64, vp, vp, vp, c_i64, vp]
     lib.w4a4_geglu.argtypes = [vp, vp, c_i64, c_i32, c_i64, vp, c_i64, vp]
     lib.w4a4_quant_segments.argtypes = [vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]

@@ -28,6 +28,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "layer.cuh"
 #include "quant.cuh"
 
 namespace w4a4 {
@@ -457,35 +458,78 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
-// V [B * L, ldv] (rows of 256) -> V^T per observation [B][256][ldt]: the
-// B operand of the PV MMA must be K-major (keys contiguous).  A CTA moves a
-// 64-key x 64-d tile through shared memory with 16-byte loads and stores;
-// keys in [seq, ldt) are written as zeros.
-__global__ void __launch_bounds__(256) transpose_v_kernel(const __half* __restrict__ v, long long ldv,
-                                                          __half* __restrict__ vt, long long ldt, int seq) {
-  __shared__ __align__(16) __half tile[64][72];  // 144-byte rows: 16-byte aligned, staggered banks
+// The attention's inputs in one launch, one CTA per 16 tokens of one
+// observation: V [B * L, ldv] (rows of 256) -> V^T per observation
+// [B][256][ldt] (the PV MMA's B operand must be K-major: keys contiguous;
+// keys in [seq, ldt) written as zeros), and, when cos_t is not null, RoPE of
+// q (in place, `heads` heads) and of k (into k_out, which may equal k).
+constexpr int kPrepTokens = 16;
+__global__ void __launch_bounds__(256) attn_prep_kernel(__half* q, long long ldq, const __half* k, long long ldk,
+                                                        __half* k_out, long long ldko,
+                                                        const __half* __restrict__ v, long long ldv,
+                                                        __half* __restrict__ vt, long long ldt,
+                                                        const __half* __restrict__ cos_t,
+                                                        const __half* __restrict__ sin_t, int seq, int heads) {
+  __shared__ __align__(16) __half tile[kPrepTokens][kAttnHeadDim + 8];
   pdl_launch_dependents();
   pdl_wait();
-  const int b = blockIdx.z, j0 = blockIdx.x * 64, d0 = blockIdx.y * 64;
-  const int t = threadIdx.x, c = t & 7;
+  const int b = blockIdx.y, j0 = blockIdx.x * kPrepTokens;
+  const int t = threadIdx.x;
+  const long long row0 = static_cast<long long>(b) * seq + j0;
+  // V rows -> shared memory: 16 keys x 32 vectors
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int j = (t >> 3) + 32 * h;
+    const int i = t + 256 * h, j = i >> 5, c = i & 31;
     uint4 val = make_uint4(0, 0, 0, 0);
-    if (j0 + j < seq)
-      val = ld_nc_v4(v + (static_cast<long long>(b) * seq + j0 + j) * ldv + d0 + 8 * c);
+    if (j0 + j < seq) val = ld_nc_v4(v + (row0 + j) * ldv + 8 * c);
     *reinterpret_cast<uint4*>(&tile[j][8 * c]) = val;
   }
+  if (cos_t) {
+    // k: 16 rows x 16 vectors of 8 pairs, one per thread
+    {
+      const int j = t >> 4, d = 8 * (t & 15);
+      if (j0 + j < seq) {
+        const long long row = row0 + j;
+        uint4 a = *reinterpret_cast<const uint4*>(k + row * ldk + d);
+        uint4 bb = *reinterpret_cast<const uint4*>(k + row * ldk + d + 128);
+        const __half* cr = cos_t + row * kAttnHeadDim;
+        const __half* sr = sin_t + row * kAttnHeadDim;
+        rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)),
+                    __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
+                    __ldg(reinterpret_cast<const uint4*>(sr + d)), __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
+        *reinterpret_cast<uint4*>(k_out + row * ldko + d) = a;
+        *reinterpret_cast<uint4*>(k_out + row * ldko + d + 128) = bb;
+      }
+    }
+    // q: 16 rows x heads x 16 vectors
+    const int nvec = kPrepTokens * heads * 16;
+    for (int i = t; i < nvec; i += 256) {
+      const int j = i / (heads * 16), hv = i - j * heads * 16, head = hv >> 4, d = 8 * (hv & 15);
+      if (j0 + j >= seq) continue;
+      const long long row = row0 + j;
+      __half* qr = q + row * ldq + head * kAttnHeadDim;
+      uint4 a = *reinterpret_cast<const uint4*>(qr + d);
+      uint4 bb = *reinterpret_cast<const uint4*>(qr + d + 128);
+      const __half* cr = cos_t + row * kAttnHeadDim;
+      const __half* sr = sin_t + row * kAttnHeadDim;
+      rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)), __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
+                  __ldg(reinterpret_cast<const uint4*>(sr + d)), __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
+      *reinterpret_cast<uint4*>(qr + d) = a;
+      *reinterpret_cast<uint4*>(qr + d + 128) = bb;
+    }
+  }
   __syncthreads();
+  // V^T: 256 d-rows x 2 vectors of 8 keys
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int d = (t >> 3) + 32 * h;
-    if (j0 + 8 * c >= ldt) continue;
+    const int i = t + 256 * h, d = i >> 1, c = i & 1;
+    const int key = j0 + 8 * c;
+    if (key >= ldt) continue;
     uint4 out;
     __half* oh = reinterpret_cast<__half*>(&out);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) oh[i] = tile[8 * c + i][d];
-    *reinterpret_cast<uint4*>(vt + (static_cast<long long>(b) * kAttnHeadDim + d0 + d) * ldt + j0 + 8 * c) = out;
+    for (int e = 0; e < 8; ++e) oh[e] = tile[8 * c + e][d];
+    *reinterpret_cast<uint4*>(vt + (static_cast<long long>(b) * kAttnHeadDim + d) * ldt + key) = out;
   }
 }
 

@@ -107,6 +107,104 @@ __global__ void __launch_bounds__(256) geglu_kernel(const __half* __restrict__ g
       geglu8(ld_nc_v4(gate + row * ld + c), ld_nc_v4(up + row * ld + c));
 }
 
+// The per-forward tables of a prefix, one CTA of 256 threads per
+// observation: position ids cumsum(pad) - 1 (a block scan), the key mask as
+// bytes, the real-key span (last real token + 1), and the rotary cos / sin
+// tables [L, 2 half] in fp16: cos(fl32(pos * inv_freq[i])) rounded to fp16,
+// duplicated over both halves -- transformers' rotary embedding evaluated for
+// these positions (its product of an fp32 position and an fp32 frequency is
+// one rounding, as here).  CUDA's cosf / sinf.
+constexpr int kTableThreads = 256;
+__global__ void __launch_bounds__(kTableThreads) prefix_tables_kernel(
+    const uint8_t* __restrict__ pad, int seq, const float* __restrict__ inv_freq, int half,
+    uint8_t* __restrict__ key_valid, int* __restrict__ kv_len, __half* __restrict__ cos_t,
+    __half* __restrict__ sin_t) {
+  __shared__ int warp_tot[kTableThreads / 32];
+  __shared__ int span;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const uint8_t* pr = pad + static_cast<long long>(b) * seq;
+  if (t == 0) span = 0;
+  int carry = 0;
+  for (int base = 0; base < seq; base += kTableThreads) {
+    const int i = base + t;
+    const int v = (i < seq && pr[i]) ? 1 : 0;
+    // inclusive scan of v over the block
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    int before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < kTableThreads / 32; ++w) {
+      before += w < warp ? warp_tot[w] : 0;
+      all += warp_tot[w];
+    }
+    const int pos = carry + before + x - 1;
+    carry += all;
+    if (i < seq) {
+      const long long row = static_cast<long long>(b) * seq + i;
+      key_valid[row] = static_cast<uint8_t>(v);
+      if (v) atomicMax(&span, i + 1);
+      const float pf = static_cast<float>(pos);
+      for (int f = 0; f < half; f += 8) {
+        uint4 cv, sv;
+        __half* ch = reinterpret_cast<__half*>(&cv);
+        __half* sh = reinterpret_cast<__half*>(&sv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float a = __fmul_rn(pf, __ldg(inv_freq + f + j));
+          ch[j] = __float2half_rn(cosf(a));
+          sh[j] = __float2half_rn(sinf(a));
+        }
+        __half* cr = cos_t + row * (2 * half);
+        __half* sr = sin_t + row * (2 * half);
+        *reinterpret_cast<uint4*>(cr + f) = cv;
+        *reinterpret_cast<uint4*>(cr + half + f) = cv;
+        *reinterpret_cast<uint4*>(sr + f) = sv;
+        *reinterpret_cast<uint4*>(sr + half + f) = sv;
+      }
+    }
+    __syncthreads();  // warp_tot is rewritten by the next round
+  }
+  if (t == 0) kv_len[b] = span;
+}
+
+// Rotary embedding of 8 pairs (d, d + 128), d = d0 .. d0 + 7, of one head:
+// a = x[d0 ..], b = x[d0 + 128 ..], ca / sa = cos / sin at d0, cb / sb at
+// d0 + 128.  out_a = fl16(fl16(a cos) + fl16(-b sin)), out_b = fl16(fl16(b
+// cos) + fl16(a sin)): transformers' apply_rotary_pos_emb in fp16 (products
+// of two fp16 values are exact in fp32, so each rounds once).
+__device__ __forceinline__ void rope_pairs8(uint4& a, uint4& b, const uint4 ca, const uint4 cb, const uint4 sa,
+                                            const uint4 sb) {
+  const __half* ah = reinterpret_cast<const __half*>(&a);
+  const __half* bh = reinterpret_cast<const __half*>(&b);
+  const __half* cah = reinterpret_cast<const __half*>(&ca);
+  const __half* cbh = reinterpret_cast<const __half*>(&cb);
+  const __half* sah = reinterpret_cast<const __half*>(&sa);
+  const __half* sbh = reinterpret_cast<const __half*>(&sb);
+  uint4 oa, ob;
+  __half* oah = reinterpret_cast<__half*>(&oa);
+  __half* obh = reinterpret_cast<__half*>(&ob);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float x1 = __half2float(ah[j]), x2 = __half2float(bh[j]);
+    const float p1 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(cah[j]))));
+    const float r1 = __half2float(__float2half_rn(__fmul_rn(-x2, __half2float(sah[j]))));
+    const float p2 = __half2float(__float2half_rn(__fmul_rn(x2, __half2float(cbh[j]))));
+    const float r2 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(sbh[j]))));
+    oah[j] = __float2half_rn(__fadd_rn(p1, r1));
+    obh[j] = __float2half_rn(__fadd_rn(p2, r2));
+  }
+  a = oa;
+  b = ob;
+}
+
 // Rotary embedding of `heads` heads of width 256 per row: element d < 128
 // pairs with d + 128.  cos / sin are fp16 [m, 256] tables (row stride 256),
 // the per-position values transformers' rotary embedding produces.  One
@@ -128,35 +226,15 @@ __global__ void __launch_bounds__(256) rope_kernel(const __half* x, long long ld
   const long long row = rh / heads;
   const int d = 8 * vec;
   const __half* xr = x + row * ldx + head * kRopeHeadDim;
-  const uint4 a = *reinterpret_cast<const uint4*>(xr + d);
-  const uint4 b = *reinterpret_cast<const uint4*>(xr + d + 128);
-  const uint4 ca = __ldg(reinterpret_cast<const uint4*>(cos_t + row * kRopeHeadDim + d));
-  const uint4 cb = __ldg(reinterpret_cast<const uint4*>(cos_t + row * kRopeHeadDim + d + 128));
-  const uint4 sa = __ldg(reinterpret_cast<const uint4*>(sin_t + row * kRopeHeadDim + d));
-  const uint4 sb = __ldg(reinterpret_cast<const uint4*>(sin_t + row * kRopeHeadDim + d + 128));
-  const __half* ah = reinterpret_cast<const __half*>(&a);
-  const __half* bh = reinterpret_cast<const __half*>(&b);
-  const __half* cah = reinterpret_cast<const __half*>(&ca);
-  const __half* cbh = reinterpret_cast<const __half*>(&cb);
-  const __half* sah = reinterpret_cast<const __half*>(&sa);
-  const __half* sbh = reinterpret_cast<const __half*>(&sb);
-  uint4 oa, ob;
-  __half* oah = reinterpret_cast<__half*>(&oa);
-  __half* obh = reinterpret_cast<__half*>(&ob);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float x1 = __half2float(ah[j]), x2 = __half2float(bh[j]);
-    // products of two fp16 values are exact in fp32: one rounding each
-    const float p1 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(cah[j]))));
-    const float r1 = __half2float(__float2half_rn(__fmul_rn(-x2, __half2float(sah[j]))));
-    const float p2 = __half2float(__float2half_rn(__fmul_rn(x2, __half2float(cbh[j]))));
-    const float r2 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(sbh[j]))));
-    oah[j] = __float2half_rn(__fadd_rn(p1, r1));
-    obh[j] = __float2half_rn(__fadd_rn(p2, r2));
-  }
+  uint4 a = *reinterpret_cast<const uint4*>(xr + d);
+  uint4 b = *reinterpret_cast<const uint4*>(xr + d + 128);
+  const __half* cr = cos_t + row * kRopeHeadDim;
+  const __half* sr = sin_t + row * kRopeHeadDim;
+  rope_pairs8(a, b, __ldg(reinterpret_cast<const uint4*>(cr + d)), __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
+              __ldg(reinterpret_cast<const uint4*>(sr + d)), __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
   __half* orow = out + row * ldo + head * kRopeHeadDim;
-  *reinterpret_cast<uint4*>(orow + d) = oa;
-  *reinterpret_cast<uint4*>(orow + d + 128) = ob;
+  *reinterpret_cast<uint4*>(orow + d) = a;
+  *reinterpret_cast<uint4*>(orow + d + 128) = b;
 }
 
 }  // namespace w4a4

@@ -634,7 +634,8 @@ constexpr int kQ16RowBytes = 16384 * 2;
 constexpr int kQ16Smem = kQ16RowBytes + 1024;
 constexpr int kQ16CtasPerSm = 3;
 
-// GEGLU: two row buffers (gate, up), both loaded by TMA.
+// GEGLU: two row buffers (gate, up), both loaded by TMA; two CTAs per SM,
+// so the GELU's registers fit without spilling.
 constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
 
 // One CTA per row (the block scheduler hands rows to SMs as CTAs finish,
@@ -650,7 +651,7 @@ constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
 // as several segments, each a [M, seg] matrix: the layout an all-to-all of
 // column shards delivers), read with one box per row; same smem layout.
 template <int MODE, bool GEGLU = false, bool SEGMENTED = false>
-__global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
+__global__ void __launch_bounds__(kQuantThreads, GEGLU ? 2 : kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
     const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns,
     const __grid_constant__ CUtensorMap umap, __half* __restrict__ h_out, long long ldh) {

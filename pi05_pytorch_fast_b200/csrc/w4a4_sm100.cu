@@ -603,6 +603,22 @@ int launch_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int6
   return ok();
 }
 
+int launch_prefix_tables(const uint8_t* pad, int32_t batch, int32_t seq, const float* inv_freq, int32_t half,
+                         uint8_t* key_valid, int32_t* kv_len, void* cos_t, void* sin_t, cudaStream_t stream) {
+  if (batch < 0 || seq < 0 || half <= 0 || half % 8 != 0)
+    return fail(W4A4_ERR_INVALID, "prefix tables: invalid shape batch %d seq %d half %d", batch, seq, half);
+  if (batch == 0 || seq == 0) return ok();
+  if (!pad || !inv_freq || !key_valid || !kv_len || !cos_t || !sin_t)
+    return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (!aligned(cos_t, 16) || !aligned(sin_t, 16))
+    return fail(W4A4_ERR_INVALID, "cos / sin tables must be 16-byte aligned");
+  W4A4_CUDA_TRY(launch_kernel(prefix_tables_kernel, dim3(static_cast<unsigned>(batch)), dim3(kTableThreads), 0,
+                              stream, 1, pad, static_cast<int>(seq), inv_freq, static_cast<int>(half), key_valid,
+                              static_cast<int*>(kv_len), static_cast<__half*>(cos_t), static_cast<__half*>(sin_t)));
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 int launch_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* cos_t,
                 const void* sin_t, int64_t m, int32_t heads, cudaStream_t stream) {
   if (m < 0 || heads <= 0) return fail(W4A4_ERR_INVALID, "invalid rope shape: m=%lld heads=%d", (long long)m, heads);
@@ -627,9 +643,10 @@ int launch_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* 
 // ------------------------------------------------------------- attention
 int64_t attn_vt_stride(int32_t seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
 
-int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                      int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
-                     int32_t seq, int32_t heads, void* vt, void* out, int64_t ldo, cudaStream_t stream) {
+                     int32_t seq, int32_t heads, void* vt, void* out, int64_t ldo, const void* cos_t,
+                     const void* sin_t, void* k_out, int64_t ldko, cudaStream_t stream) {
   if (batch < 0 || seq < 0) return fail(W4A4_ERR_INVALID, "invalid attention shape: batch %d, seq %d", batch, seq);
   if (heads < 1 || heads > kAttnRows || kAttnRows % heads != 0)
     return fail(W4A4_ERR_UNSUPPORTED, "attention: heads must divide %d, got %d", kAttnRows, heads);
@@ -646,15 +663,25 @@ int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, con
       !rows_ok(v, ldv, kAttnHeadDim) || !aligned(vt, 16))
     return fail(W4A4_ERR_INVALID,
                 "attention rows must be 16-byte aligned with strides >= their width and multiples of 8");
+  const bool rope = cos_t != nullptr;
+  if (rope && (!sin_t || !k_out || !aligned(cos_t, 16) || !aligned(sin_t, 16) ||
+               !rows_ok(k_out, ldko, kAttnHeadDim)))
+    return fail(W4A4_ERR_INVALID,
+                "attention RoPE needs 16-byte aligned cos/sin tables and a k_out of rows >= 256, stride a "
+                "multiple of 8");
   int dev;
   if (int e = current_device(&dev)) return e;
   const int64_t ldt = attn_vt_stride(seq);
-  const __half* vh = static_cast<const __half*>(v);
-  __half* vth = static_cast<__half*>(vt);
-  W4A4_CUDA_TRY(launch_kernel(transpose_v_kernel,
-                              dim3(static_cast<unsigned>((ldt + 63) / 64), kAttnHeadDim / 64,
+  W4A4_CUDA_TRY(launch_kernel(attn_prep_kernel,
+                              dim3(static_cast<unsigned>((ldt + kPrepTokens - 1) / kPrepTokens),
                                    static_cast<unsigned>(batch)),
-                              dim3(256), 0, stream, 1, vh, ldv, vth, ldt, seq));
+                              dim3(256), 0, stream, 1, static_cast<__half*>(q), ldq, static_cast<const __half*>(k),
+                              ldk, static_cast<__half*>(rope ? k_out : nullptr), rope ? ldko : 0ll,
+                              static_cast<const __half*>(v), ldv, static_cast<__half*>(vt), ldt,
+                              static_cast<const __half*>(cos_t), static_cast<const __half*>(sin_t), seq, heads));
+  // the keys the attention reads: rotated into k_out, or k as given
+  const void* kr = rope ? k_out : k;
+  const int64_t ldkr = rope ? ldko : ldk;
   AttnParams p;
   std::memset(&p, 0, sizeof(p));
   {
@@ -669,10 +696,10 @@ int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   }
   {
     const uint64_t dims[3] = {kAttnHeadDim, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(ldk) * 2,
-                                 static_cast<uint64_t>(ldk) * 2 * static_cast<uint64_t>(seq)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldkr) * 2,
+                                 static_cast<uint64_t>(ldkr) * 2 * static_cast<uint64_t>(seq)};
     const uint32_t box[3] = {64, kAttnKeyBlock, 1};
-    if (int e = make_map(&p.tmap_k, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
+    if (int e = make_map(&p.tmap_k, kr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B))
       return e;
   }
@@ -1097,12 +1124,12 @@ int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* co
   return launch_rope(x, ldx, out, ldo, cos_t, sin_t, m, heads, static_cast<cudaStream_t>(stream));
 }
 
-int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                           int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                           int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
-                          void* stream) {
+                          const void* cos_t, const void* sin_t, void* k_out, int64_t ldko, void* stream) {
   return launch_attention(q, ldq, k, ldk, v, ldv, key_valid, kv_len, batch, seq, heads, vt_scratch, out,
-                          ldo, static_cast<cudaStream_t>(stream));
+                          ldo, cos_t, sin_t, k_out, ldko, static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
@@ -1115,6 +1142,13 @@ int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_
                         float* row_scale, void* stream) {
   return launch_quant_segments(x, m, k, seg, ld, seg_stride, staging, codes_format, codes, row_scale,
                                static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_prefix_tables(const uint8_t* pad, int32_t batch, int32_t seq, const float* inv_freq,
+                       int32_t half, uint8_t* key_valid, int32_t* kv_len, void* cos_t, void* sin_t,
+                       void* stream) {
+  return launch_prefix_tables(pad, batch, seq, inv_freq, half, key_valid, kv_len, cos_t, sin_t,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,

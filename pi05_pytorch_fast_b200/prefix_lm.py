@@ -9,14 +9,16 @@ C ABI instead of modules:
 
 * one preallocated workspace per token count, so a forward allocates
   nothing and captures into one CUDA graph;
-* per layer, twelve launches, all of this library: residual add + RMSNorm +
+* per layer, ten launches, all of this library: residual add + RMSNorm +
   quant (one kernel), the q/k/v GEMM (one launch, three weights), RoPE of q
-  and of k, the V transpose and the tensor-core attention, quant + o_proj
-  GEMM, residual add + RMSNorm + quant, the gate/up GEMM, GeGLU + quant (one
-  kernel), the down GEMM; the residual add of each sublayer is folded into
-  the next norm;
+  and k with the V transpose (one kernel), the tensor-core attention, quant +
+  o_proj GEMM, residual add + RMSNorm + quant, the gate/up GEMM, GeGLU +
+  quant (one kernel), the down GEMM; the residual add of each sublayer is
+  folded into the next norm;
 * the keys after RoPE and the values of every layer stay in a KV cache, the
-  prefix state the action expert attends to (apply.py:170-171).
+  prefix state the action expert attends to (apply.py:170-171);
+* the positions, key mask and rotary tables come from one kernel per
+  forward (w4a4_prefix_tables).
 
 Attention is bidirectional over the prefix with the padding mask of lerobot's
 ``make_att_2d_masks`` (query i sees key j iff both are real tokens; a padded
@@ -327,10 +329,11 @@ class W4A4PrefixLM:
     def _codes(ws: _Workspace, rows: int, k: int) -> torch.Tensor:
         return ws.codes.view(-1)[: rows * k].view(rows, k)
 
-    def _norm_quant(self, ws: _Workspace, rows: int, delta, gain, trace) -> None:
+    def _norm_quant(self, ws: _Workspace, rows: int, delta, gain, trace, x_in=None) -> None:
         h = ws.h if trace is not None else None
+        src = ws.x if x_in is None else x_in
         nat.check(self._lib.w4a4_rmsnorm_quant(
-            ws.x.data_ptr(), ws.x.stride(0), delta.data_ptr() if delta is not None else None,
+            src.data_ptr(), src.stride(0), delta.data_ptr() if delta is not None else None,
             self.cfg.hidden, gain.data_ptr(), self.cfg.rms_eps, ws.x.data_ptr(), ws.x.stride(0),
             h.data_ptr() if h is not None else None, self.cfg.hidden, rows, self.cfg.hidden,
             self.staging, nat.CODES_GEMM, ws.codes.data_ptr(), ws.scales.data_ptr(), self._stream()))
@@ -347,16 +350,16 @@ class W4A4PrefixLM:
             raise ValueError(f"embeds must be fp16 [B, L, {cfg.hidden}]")
         rows = b * seq
         ws = self.workspace(b, seq, trace is not None)
-        ws.x.copy_(embeds.reshape(rows, hidden))
-        pad = pad_mask.bool()
-        pos = torch.cumsum(pad.to(torch.int64), dim=1) - 1
-        ws.key_valid.copy_(pad)
-        # keys at or past the last real token + 1 are all padding
-        ws.kv_len.copy_((pad * torch.arange(1, seq + 1, device=pad.device)).amax(dim=1))
-        freqs = pos.reshape(rows, 1).float() * self.inv_freq[None, :]
-        emb = torch.cat((freqs, freqs), dim=-1)
-        ws.cos.copy_(emb.cos().half())
-        ws.sin.copy_(emb.sin().half())
+        x_in = embeds.reshape(rows, hidden)
+        if not x_in.is_contiguous():
+            x_in = x_in.contiguous()
+        pad = pad_mask if pad_mask.dtype in (torch.bool, torch.uint8) else pad_mask.bool()
+        pad = pad.contiguous()
+        lib, st = self._lib, self._stream()
+        # positions cumsum(pad) - 1, key mask, real-key spans, rotary tables
+        nat.check(lib.w4a4_prefix_tables(pad.data_ptr(), b, seq, self.inv_freq.data_ptr(),
+                                         cfg.head_dim // 2, ws.key_valid.data_ptr(), ws.kv_len.data_ptr(),
+                                         ws.cos.data_ptr(), ws.sin.data_ptr(), st))
         kv = cfg.kv_heads * cfg.head_dim
         if out is None:
             out = PrefixOutput(hidden=torch.empty_like(embeds),
@@ -364,26 +367,24 @@ class W4A4PrefixLM:
                                      for _ in self.layers],
                                values=[torch.empty((b, seq, kv), dtype=torch.float16, device=self.device)
                                        for _ in self.layers])
-        lib, st = self._lib, self._stream()
         hid, inter = cfg.hidden, cfg.intermediate
         delta = None
         for li, lw in enumerate(self.layers):
             k_cache = out.keys[li].view(rows, kv)
             v_cache = out.values[li].view(rows, kv)
-            # --- attention block
-            self._norm_quant(ws, rows, delta, lw.input_gain, trace)
+            # --- attention block (layer 0's norm reads the embeddings and
+            # starts the residual stream)
+            self._norm_quant(ws, rows, delta, lw.input_gain, trace, x_in=x_in if li == 0 else None)
             self._gemm(ws, rows, hid, [lw.q, lw.k, lw.v], [ws.q, ws.k, v_cache], fragment=False)
             if trace is not None:
                 trace.append(("qkv", li, ws.h.clone(), self._codes(ws, rows, hid).clone(), ws.scales.clone(),
                               (ws.q.clone(), ws.k.clone(), v_cache.clone())))
-            nat.check(lib.w4a4_rope(ws.q.data_ptr(), ws.q.stride(0), ws.q.data_ptr(), ws.q.stride(0),
-                                    ws.cos.data_ptr(), ws.sin.data_ptr(), rows, cfg.heads, st))
-            nat.check(lib.w4a4_rope(ws.k.data_ptr(), ws.k.stride(0), k_cache.data_ptr(), kv,
-                                    ws.cos.data_ptr(), ws.sin.data_ptr(), rows, cfg.kv_heads, st))
+            # RoPE of q (in place) and k (into the KV cache), V^T, then attention
             nat.check(lib.w4a4_prefix_attention(
-                ws.q.data_ptr(), ws.q.stride(0), k_cache.data_ptr(), kv, v_cache.data_ptr(), kv,
+                ws.q.data_ptr(), ws.q.stride(0), ws.k.data_ptr(), ws.k.stride(0), v_cache.data_ptr(), kv,
                 ws.key_valid.data_ptr(), ws.kv_len.data_ptr(), b, seq, cfg.heads, ws.vt.data_ptr(),
-                ws.attn.data_ptr(), ws.attn.stride(0), st))
+                ws.attn.data_ptr(), ws.attn.stride(0), ws.cos.data_ptr(), ws.sin.data_ptr(),
+                k_cache.data_ptr(), kv, st))
             nat.check(lib.w4a4_quant(ws.attn.data_ptr(), rows, cfg.hidden, cfg.hidden, nat.ROTATE_BY_K,
                                      self.staging, nat.CODES_GEMM, ws.codes.data_ptr(),
                                      ws.scales.data_ptr(), st))
@@ -436,11 +437,11 @@ class W4A4PrefixLM:
     __call__ = forward
 
     def launches_per_forward(self) -> int:
-        """Kernels of this library per forward (the torch glue that builds the
-        position / mask tables is not counted): per layer 2 norm+quant, 1
-        quant, 4 GEMMs, 2 RoPE, V transpose + attention, 1 GeGLU+quant (the
-        sharded MLP: GeGLU, then the segment quant); then the final norm."""
-        return (12 + (1 if self.shard is not None else 0)) * len(self.layers) + 1
+        """Kernels of this library per forward: the prefix tables; per layer 2
+        norm+quant, 1 quant, 4 GEMMs, RoPE + V transpose, attention, 1
+        GeGLU+quant (the sharded MLP: GeGLU, then the segment quant); then the
+        final norm.  Nothing else runs on the device."""
+        return (10 + (1 if self.shard is not None else 0)) * len(self.layers) + 2
 
 
 class GraphedPrefixLM:

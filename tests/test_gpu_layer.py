@@ -245,7 +245,7 @@ def prefix_attention(q, k, v, pad, heads):
     nat.check(nat.lib().w4a4_prefix_attention(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
                                               v.data_ptr(), v.stride(0), key_valid.data_ptr(),
                                               kv_len.data_ptr(), b, seq, heads, vt.data_ptr(),
-                                              out.data_ptr(), out.stride(0), _stream()))
+                                              out.data_ptr(), out.stride(0), None, None, None, 0, _stream()))
     return out
 
 
@@ -322,3 +322,68 @@ def test_prefix_attention_rescales_when_a_late_key_dominates():
     e_ref = float((eager.double() - truth).abs().max())
     print(f"late-max attention: kernel {e:.2e}, eager fp16 {e_ref:.2e}")
     assert e <= max(1.5 * e_ref, 2e-3)
+
+
+def test_prefix_attention_with_fused_rope_equals_rope_then_attention():
+    """cos / sin given: q is rotated in place and k into k_out inside the
+    attention's first launch, exactly as w4a4_rope does it, and the attention
+    result is the one of the rotated inputs."""
+    heads, seq, batch = 8, 776, 2
+    gen = torch.Generator(device=DEV).manual_seed(4)
+    q = torch.randn(batch * seq, heads * 256, device=DEV, generator=gen).half()
+    k = torch.randn(batch * seq, 256, device=DEV, generator=gen).half()
+    v = torch.randn(batch * seq, 256, device=DEV, generator=gen).half()
+    pad = torch.ones(batch, seq, dtype=torch.bool, device=DEV)
+    pad[:, 628:] = False
+    pos = (torch.cumsum(pad.long(), 1) - 1).reshape(-1)
+    inv_freq = (1.0 / (10000.0 ** (torch.arange(0, 256, 2, dtype=torch.int64).float() / 256))).half().float()
+    freqs = pos[:, None].float() * inv_freq.to(DEV)[None]
+    emb = torch.cat((freqs, freqs), -1)
+    cos, sin = emb.cos().half().contiguous(), emb.sin().half().contiguous()
+    q_ref, k_ref = hf_rope(q, cos, sin, heads), hf_rope(k, cos, sin, 1)
+    expect = prefix_attention(q_ref.contiguous(), k_ref.contiguous(), v, pad, heads)
+    key_valid = pad.to(torch.uint8).contiguous()
+    kv_len = (pad * torch.arange(1, seq + 1, device=DEV)).amax(dim=1).to(torch.int32)
+    vt = torch.empty((batch, 256, nat.attn_vt_stride(seq)), dtype=torch.float16, device=DEV)
+    out = torch.empty_like(q)
+    k_out = torch.empty_like(k)
+    q2 = q.clone()
+    nat.check(nat.lib().w4a4_prefix_attention(q2.data_ptr(), q2.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
+                                              v.stride(0), key_valid.data_ptr(), kv_len.data_ptr(), batch, seq,
+                                              heads, vt.data_ptr(), out.data_ptr(), out.stride(0), cos.data_ptr(),
+                                              sin.data_ptr(), k_out.data_ptr(), k_out.stride(0), _stream()))
+    torch.cuda.synchronize()
+    assert_half_equal(q2, q_ref)
+    assert_half_equal(k_out, k_ref)
+    assert torch.equal(out.view(torch.int16), expect.view(torch.int16))
+
+
+@pytest.mark.parametrize("seq,fp16_freq", [(776, True), (4096, True), (300, False)])
+def test_prefix_tables_match_torch(seq, fp16_freq):
+    """Positions, key mask, real-key spans and the rotary tables of
+    w4a4_prefix_tables equal PyTorch's evaluation (transformers' rotary
+    embedding: fl32(pos * inv_freq), cos / sin on CUDA, rounded to fp16) bit
+    for bit, over positions up to 4095."""
+    from pi05_pytorch_fast_b200 import prefix_lm as plm
+
+    batch = 3
+    pad = torch.ones(batch, seq, dtype=torch.bool, device=DEV)
+    pad[0, seq // 2:] = False            # trailing padding
+    pad[1, ::7] = False                  # scattered padding
+    pad[2, :] = False                    # no real token
+    inv_freq = plm.rope_inv_freq(plm.PrefixLMConfig(), fp16_buffer=fp16_freq).to(DEV)
+    key_valid = torch.empty(batch, seq, dtype=torch.uint8, device=DEV)
+    kv_len = torch.empty(batch, dtype=torch.int32, device=DEV)
+    cos = torch.empty(batch * seq, 256, dtype=torch.float16, device=DEV)
+    sin = torch.empty_like(cos)
+    nat.check(nat.lib().w4a4_prefix_tables(pad.data_ptr(), batch, seq, inv_freq.data_ptr(), 128,
+                                           key_valid.data_ptr(), kv_len.data_ptr(), cos.data_ptr(),
+                                           sin.data_ptr(), _stream()))
+    pos = torch.cumsum(pad.long(), dim=1) - 1
+    freqs = pos.reshape(-1, 1).float() * inv_freq[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    torch.cuda.synchronize()
+    assert torch.equal(key_valid, pad.to(torch.uint8))
+    assert kv_len.tolist() == (pad * torch.arange(1, seq + 1, device=DEV)).amax(dim=1).tolist()
+    assert_half_equal(cos, emb.cos().half())
+    assert_half_equal(sin, emb.sin().half())

@@ -155,7 +155,8 @@ def library_attention(pad):
         out = torch.empty_like(q)
         nat.check(nat.lib().w4a4_prefix_attention(
             q.data_ptr(), q.stride(0), k.data_ptr(), d, v.data_ptr(), d, kvalid.data_ptr(), kv_len.data_ptr(),
-            b, seq, h, vt.data_ptr(), out.data_ptr(), out.stride(0), torch.cuda.current_stream().cuda_stream))
+            b, seq, h, vt.data_ptr(), out.data_ptr(), out.stride(0), None, None, None, 0,
+            torch.cuda.current_stream().cuda_stream))
         return out.view(b, seq, h, d), None
     return attn
 

@@ -421,11 +421,12 @@ def test_attention_argument_validation_without_gpu():
     fake = 0x1000
     args = lambda **kw: [kw.get("q", fake), kw.get("ldq", 2048), fake, 256, fake, 256, fake, fake,  # noqa: E731
                          kw.get("batch", 1), kw.get("seq", 776), kw.get("heads", 8), fake, fake,
-                         kw.get("ldo", 2048), None]
+                         kw.get("ldo", 2048), kw.get("cos"), fake, None, 256, None]
     assert "heads must divide 128" in _err(lib.w4a4_prefix_attention(*args(heads=3)))
     assert "exceeds 4096" in _err(lib.w4a4_prefix_attention(*args(seq=5000)))
     assert "16-byte aligned" in _err(lib.w4a4_prefix_attention(*args(q=fake + 2)))
     assert "16-byte aligned" in _err(lib.w4a4_prefix_attention(*args(ldq=1000)))
     assert "invalid attention shape" in _err(lib.w4a4_prefix_attention(*args(batch=-1)))
+    assert "RoPE needs" in _err(lib.w4a4_prefix_attention(*args(cos=fake)))
     assert lib.w4a4_prefix_attention(*args(batch=0)) == nat.W4A4_OK
     assert nat.attn_vt_stride(776) == 776 and nat.attn_vt_stride(100) == 104
