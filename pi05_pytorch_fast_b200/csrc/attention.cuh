@@ -16,6 +16,8 @@
 //  * warp 1 issues S = Q K^T (M = 128, N = 64, 16 MMAs of K = 16 over d) into
 //    one of two TMEM score buffers, and O += P V^T (M = 128, N = 256, 4 MMAs of
 //    K = 16 keys) with P read from TMEM (the A operand of the TS form);
+//  * with rotary tables given, warps 2-5 first rotate the Q tile in shared
+//    memory (RoPE) while the first key blocks stream in;
 //  * warps 2-5 (one per TMEM lane quarter, thread = row) run an online
 //    softmax in one pass: p = exp2(s - m) as fp16 into TMEM for the PV MMA,
 //    with the running max m moved (and O rescaled in TMEM) only when a block
@@ -43,7 +45,7 @@ constexpr int kAttnKBytes = kAttnKeyBlock * kAttnHeadDim * 2;      // 32 KB
 constexpr int kAttnVBytes = kAttnHeadDim * kAttnKeyBlock * 2;      // 32 KB
 constexpr int kAttnStages = 2;
 constexpr int kAttnThreads = 192;                                  // 6 warps
-constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 1;      // q, k/v full/empty, s/p full/free, o
+constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 1 + 1;  // q, k/v full/empty, s/p full/free, o, q rotated
 constexpr int kAttnSmem = kAttnQBytes + kAttnStages * (kAttnKBytes + kAttnVBytes) +
                           kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + 1024;
 // TMEM columns: O [0, 256), S buffers at 256 and 320 (64 each), P buffers at
@@ -62,6 +64,8 @@ struct alignas(64) AttnParams {
   int seq;
   int heads;
   float scale_log2;          // head_dim^-0.5 * log2(e)
+  const __half* cos_t;       // null, or rotary tables [B * L, 256]: Q is rotated in shared memory
+  const __half* sin_t;
   unsigned long long wait_limit_ns;
 };
 
@@ -144,6 +148,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const auto bar_pfull = [&](int s) { return smem_addr(bars + 13 + s); };
   const auto bar_pfree = [&](int s) { return smem_addr(bars + 15 + s); };
   const uint32_t bar_o = smem_addr(bars + 17);
+  const uint32_t bar_qrot = smem_addr(bars + 18);  // the softmax warps rotated Q (RoPE) in place
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y;
@@ -171,6 +176,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(bar_pfree(s), 1);
     }
     mbar_init(bar_o, 1);
+    mbar_init(bar_qrot, 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tmap_q);
@@ -263,6 +269,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t idesc_o = idesc_f16(kAttnRows, kAttnHeadDim);
     const uint64_t qdesc = smem_desc_sw128(smem_addr(q_smem));
     bool alive = nkb > 0 && warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit));
+    if (alive && p.cos_t)  // RoPE applied to Q in shared memory by the softmax warps
+      alive = warp_all(mbar_wait_spin(bar_qrot, 0, abort_flag, err, kErrWaitUnpack, limit));
     // S(kb) = Q K(kb)^T into score buffer kb % 2
     const auto issue_s = [&](int kb) -> bool {
       const int slot = kb & 1;
@@ -333,6 +341,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float scale = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool alive = nkb > 0;
+    if (alive && p.cos_t) {
+      // RoPE of the Q tile in place.  Element d of row rr sits in slice d / 64,
+      // 16-byte chunk ((d % 64) / 8) ^ (rr % 8) of the row (128-byte swizzle),
+      // so its partner d + 128 is the same chunk of slice d / 64 + 2.
+      if (!warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit))) {
+        alive = false;
+      } else {
+        const int tq = threadIdx.x - 64;  // 0 .. 127
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int i = tq + 128 * it;    // (row, slice 0/1, chunk)
+          const int rr = i >> 4, sl = (i >> 3) & 1, c = i & 7;
+          const int tk = t0 + rr / p.heads;
+          if (tk >= L) continue;
+          const int off = rr * 128 + ((c ^ (rr & 7)) << 4);
+          uint4* lo = reinterpret_cast<uint4*>(q_smem + sl * (kAttnQBytes / kAttnSlices) + off);
+          uint4* hi = reinterpret_cast<uint4*>(q_smem + (sl + 2) * (kAttnQBytes / kAttnSlices) + off);
+          const int d = 64 * sl + 8 * c;
+          const __half* cr = p.cos_t + (static_cast<long long>(b) * L + tk) * kAttnHeadDim;
+          const __half* sr = p.sin_t + (static_cast<long long>(b) * L + tk) * kAttnHeadDim;
+          uint4 a = *lo, bb = *hi;
+          rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)),
+                      __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
+                      __ldg(reinterpret_cast<const uint4*>(sr + d)),
+                      __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
+          *lo = a;
+          *hi = bb;
+        }
+        fence_proxy_async_smem();  // generic-proxy stores, read next by the MMA (async proxy)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_qrot);
+      }
+    }
     for (int kb = 0; alive && kb < nkb; ++kb) {
       const int slot = kb & 1;
       if (!warp_all(mbar_wait_spin(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
@@ -458,18 +499,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
-// The attention's inputs in one launch, one CTA per 16 tokens of one
-// observation: V [B * L, ldv] (rows of 256) -> V^T per observation
+// The attention's key-side inputs in one launch, one CTA per 16 tokens of
+// one observation: V [B * L, ldv] (rows of 256) -> V^T per observation
 // [B][256][ldt] (the PV MMA's B operand must be K-major: keys contiguous;
 // keys in [seq, ldt) written as zeros), and, when cos_t is not null, RoPE of
-// q (in place, `heads` heads) and of k (into k_out, which may equal k).
+// k into k_out (which may equal k).  Q is rotated by the attention kernel.
 constexpr int kPrepTokens = 16;
-__global__ void __launch_bounds__(256) attn_prep_kernel(__half* q, long long ldq, const __half* k, long long ldk,
-                                                        __half* k_out, long long ldko,
-                                                        const __half* __restrict__ v, long long ldv,
-                                                        __half* __restrict__ vt, long long ldt,
+__global__ void __launch_bounds__(256) attn_prep_kernel(const __half* k, long long ldk, __half* k_out,
+                                                        long long ldko, const __half* __restrict__ v,
+                                                        long long ldv, __half* __restrict__ vt, long long ldt,
                                                         const __half* __restrict__ cos_t,
-                                                        const __half* __restrict__ sin_t, int seq, int heads) {
+                                                        const __half* __restrict__ sin_t, int seq) {
   __shared__ __align__(16) __half tile[kPrepTokens][kAttnHeadDim + 8];
   pdl_launch_dependents();
   pdl_wait();
@@ -500,22 +540,6 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(__half* q, long long ldq
         *reinterpret_cast<uint4*>(k_out + row * ldko + d) = a;
         *reinterpret_cast<uint4*>(k_out + row * ldko + d + 128) = bb;
       }
-    }
-    // q: 16 rows x heads x 16 vectors
-    const int nvec = kPrepTokens * heads * 16;
-    for (int i = t; i < nvec; i += 256) {
-      const int j = i / (heads * 16), hv = i - j * heads * 16, head = hv >> 4, d = 8 * (hv & 15);
-      if (j0 + j >= seq) continue;
-      const long long row = row0 + j;
-      __half* qr = q + row * ldq + head * kAttnHeadDim;
-      uint4 a = *reinterpret_cast<const uint4*>(qr + d);
-      uint4 bb = *reinterpret_cast<const uint4*>(qr + d + 128);
-      const __half* cr = cos_t + row * kAttnHeadDim;
-      const __half* sr = sin_t + row * kAttnHeadDim;
-      rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)), __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
-                  __ldg(reinterpret_cast<const uint4*>(sr + d)), __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
-      *reinterpret_cast<uint4*>(qr + d) = a;
-      *reinterpret_cast<uint4*>(qr + d + 128) = bb;
     }
   }
   __syncthreads();

@@ -107,72 +107,95 @@ __global__ void __launch_bounds__(256) geglu_kernel(const __half* __restrict__ g
       geglu8(ld_nc_v4(gate + row * ld + c), ld_nc_v4(up + row * ld + c));
 }
 
-// The per-forward tables of a prefix, one CTA of 256 threads per
-// observation: position ids cumsum(pad) - 1 (a block scan), the key mask as
-// bytes, the real-key span (last real token + 1), and the rotary cos / sin
-// tables [L, 2 half] in fp16: cos(fl32(pos * inv_freq[i])) rounded to fp16,
-// duplicated over both halves -- transformers' rotary embedding evaluated for
-// these positions (its product of an fp32 position and an fp32 frequency is
-// one rounding, as here).  CUDA's cosf / sinf.
+// The per-forward tables of a batch of prefixes.  CTA (x, b) covers rows
+// [16 x, 16 x + 16) of observation b: it counts the real tokens before its
+// rows (every CTA reads the mask up to its rows: at most 4 KB), scans its 16
+// rows, and writes position ids cumsum(pad) - 1 as the rotary tables cos /
+// sin [L, 2 half] in fp16 -- cos(fl32(pos * inv_freq[i])) rounded to fp16,
+// duplicated over both halves: transformers' rotary embedding for these
+// positions (its product of an fp32 position and an fp32 frequency is one
+// rounding, as here; CUDA's cosf / sinf).  It also copies the key mask as
+// bytes; CTA 0 of each observation writes the real-key span (last real
+// token + 1).
 constexpr int kTableThreads = 256;
+constexpr int kTableRows = 16;
 __global__ void __launch_bounds__(kTableThreads) prefix_tables_kernel(
     const uint8_t* __restrict__ pad, int seq, const float* __restrict__ inv_freq, int half,
     uint8_t* __restrict__ key_valid, int* __restrict__ kv_len, __half* __restrict__ cos_t,
     __half* __restrict__ sin_t) {
-  __shared__ int warp_tot[kTableThreads / 32];
-  __shared__ int span;
+  __shared__ int warp_cnt[kTableThreads / 32];
+  __shared__ int warp_span[kTableThreads / 32];
+  __shared__ int row_pos[kTableRows];
   pdl_launch_dependents();
   pdl_wait();
-  const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int b = blockIdx.y, r0 = blockIdx.x * kTableRows;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const uint8_t* pr = pad + static_cast<long long>(b) * seq;
-  if (t == 0) span = 0;
-  int carry = 0;
-  for (int base = 0; base < seq; base += kTableThreads) {
-    const int i = base + t;
+  // real tokens before r0 (and, for CTA 0, the last real token of the row)
+  const int scan_end = blockIdx.x == 0 ? seq : r0;
+  int cnt = 0, last = 0;
+  for (int i = t; i < scan_end; i += kTableThreads) {
+    const bool v = pr[i] != 0;
+    cnt += (v && i < r0) ? 1 : 0;
+    if (v) last = max(last, i + 1);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+  }
+  if (lane == 0) {
+    warp_cnt[warp] = cnt;
+    warp_span[warp] = last;
+  }
+  __syncthreads();
+  if (t < kTableRows) {
+    int base = 0;
+#pragma unroll
+    for (int w = 0; w < kTableThreads / 32; ++w) base += warp_cnt[w];
+    // scan of this CTA's rows (16 lanes of warp 0)
+    const int i = r0 + t;
     const int v = (i < seq && pr[i]) ? 1 : 0;
-    // inclusive scan of v over the block
     int x = v;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
+    for (int o = 1; o < kTableRows; o <<= 1) {
+      const int y = __shfl_up_sync(0x0000ffffu, x, o);
+      if (t >= o) x += y;
     }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    int before = 0, all = 0;
-#pragma unroll
-    for (int w = 0; w < kTableThreads / 32; ++w) {
-      before += w < warp ? warp_tot[w] : 0;
-      all += warp_tot[w];
-    }
-    const int pos = carry + before + x - 1;
-    carry += all;
-    if (i < seq) {
-      const long long row = static_cast<long long>(b) * seq + i;
-      key_valid[row] = static_cast<uint8_t>(v);
-      if (v) atomicMax(&span, i + 1);
-      const float pf = static_cast<float>(pos);
-      for (int f = 0; f < half; f += 8) {
-        uint4 cv, sv;
-        __half* ch = reinterpret_cast<__half*>(&cv);
-        __half* sh = reinterpret_cast<__half*>(&sv);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float a = __fmul_rn(pf, __ldg(inv_freq + f + j));
-          ch[j] = __float2half_rn(cosf(a));
-          sh[j] = __float2half_rn(sinf(a));
-        }
-        __half* cr = cos_t + row * (2 * half);
-        __half* sr = sin_t + row * (2 * half);
-        *reinterpret_cast<uint4*>(cr + f) = cv;
-        *reinterpret_cast<uint4*>(cr + half + f) = cv;
-        *reinterpret_cast<uint4*>(sr + f) = sv;
-        *reinterpret_cast<uint4*>(sr + half + f) = sv;
-      }
-    }
-    __syncthreads();  // warp_tot is rewritten by the next round
+    row_pos[t] = base + x - 1;
+    if (i < seq) key_valid[static_cast<long long>(b) * seq + i] = static_cast<uint8_t>(v);
   }
-  if (t == 0) kv_len[b] = span;
+  if (blockIdx.x == 0 && t == 0) {
+    int span = 0;
+#pragma unroll
+    for (int w = 0; w < kTableThreads / 32; ++w) span = max(span, warp_span[w]);
+    kv_len[b] = span;
+  }
+  __syncthreads();
+  // rotary tables: 16 rows x half / 8 vectors of 8 frequencies
+  const int nvec = kTableRows * (half / 8);
+  for (int idx = t; idx < nvec; idx += kTableThreads) {
+    const int j = idx / (half / 8), f = 8 * (idx - j * (half / 8));
+    const int i = r0 + j;
+    if (i >= seq) continue;
+    const long long row = static_cast<long long>(b) * seq + i;
+    const float pf = static_cast<float>(row_pos[j]);
+    uint4 cv, sv;
+    __half* ch = reinterpret_cast<__half*>(&cv);
+    __half* sh = reinterpret_cast<__half*>(&sv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = __fmul_rn(pf, __ldg(inv_freq + f + e));
+      ch[e] = __float2half_rn(cosf(a));
+      sh[e] = __float2half_rn(sinf(a));
+    }
+    __half* cr = cos_t + row * (2 * half);
+    __half* sr = sin_t + row * (2 * half);
+    *reinterpret_cast<uint4*>(cr + f) = cv;
+    *reinterpret_cast<uint4*>(cr + half + f) = cv;
+    *reinterpret_cast<uint4*>(sr + f) = sv;
+    *reinterpret_cast<uint4*>(sr + half + f) = sv;
+  }
 }
 
 // Rotary embedding of 8 pairs (d, d + 128), d = d0 .. d0 + 7, of one head:

@@ -612,7 +612,10 @@ int launch_prefix_tables(const uint8_t* pad, int32_t batch, int32_t seq, const f
     return fail(W4A4_ERR_INVALID, "null pointer argument");
   if (!aligned(cos_t, 16) || !aligned(sin_t, 16))
     return fail(W4A4_ERR_INVALID, "cos / sin tables must be 16-byte aligned");
-  W4A4_CUDA_TRY(launch_kernel(prefix_tables_kernel, dim3(static_cast<unsigned>(batch)), dim3(kTableThreads), 0,
+  W4A4_CUDA_TRY(launch_kernel(prefix_tables_kernel,
+                              dim3(static_cast<unsigned>((seq + kTableRows - 1) / kTableRows),
+                                   static_cast<unsigned>(batch)),
+                              dim3(kTableThreads), 0,
                               stream, 1, pad, static_cast<int>(seq), inv_freq, static_cast<int>(half), key_valid,
                               static_cast<int*>(kv_len), static_cast<__half*>(cos_t), static_cast<__half*>(sin_t)));
   W4A4_CUDA_TRY(cudaGetLastError());
@@ -643,7 +646,7 @@ int launch_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* 
 // ------------------------------------------------------------- attention
 int64_t attn_vt_stride(int32_t seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
 
-int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                      int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                      int32_t seq, int32_t heads, void* vt, void* out, int64_t ldo, const void* cos_t,
                      const void* sin_t, void* k_out, int64_t ldko, cudaStream_t stream) {
@@ -675,10 +678,10 @@ int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const voi
   W4A4_CUDA_TRY(launch_kernel(attn_prep_kernel,
                               dim3(static_cast<unsigned>((ldt + kPrepTokens - 1) / kPrepTokens),
                                    static_cast<unsigned>(batch)),
-                              dim3(256), 0, stream, 1, static_cast<__half*>(q), ldq, static_cast<const __half*>(k),
-                              ldk, static_cast<__half*>(rope ? k_out : nullptr), rope ? ldko : 0ll,
+                              dim3(256), 0, stream, 1, static_cast<const __half*>(k), ldk,
+                              static_cast<__half*>(rope ? k_out : nullptr), rope ? ldko : 0ll,
                               static_cast<const __half*>(v), ldv, static_cast<__half*>(vt), ldt,
-                              static_cast<const __half*>(cos_t), static_cast<const __half*>(sin_t), seq, heads));
+                              static_cast<const __half*>(cos_t), static_cast<const __half*>(sin_t), seq));
   // the keys the attention reads: rotated into k_out, or k as given
   const void* kr = rope ? k_out : k;
   const int64_t ldkr = rope ? ldko : ldk;
@@ -719,6 +722,8 @@ int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const voi
   p.seq = seq;
   p.heads = heads;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kAttnHeadDim)));
+  p.cos_t = static_cast<const __half*>(cos_t);
+  p.sin_t = static_cast<const __half*>(sin_t);
   p.wait_limit_ns = g_wait_limit_ns.load();
   if (int e = ensure_smem_attr(dev, 1ull << 40, prefix_attention_kernel, kAttnSmem)) return e;
   const int tpt = kAttnRows / heads;
@@ -1124,7 +1129,7 @@ int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* co
   return launch_rope(x, ldx, out, ldo, cos_t, sin_t, m, heads, static_cast<cudaStream_t>(stream));
 }
 
-int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                           int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                           int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
                           const void* cos_t, const void* sin_t, void* k_out, int64_t ldko, void* stream) {
