@@ -473,9 +473,10 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "timing": "CUDA graph replay of the whole forward, CUDA events, max over ranks",
         },
         "gpu_launches": model.launches_per_forward() * args.steps,
-        "gpu_launches_note": "kernels of libw4a4_sm100.so per timed region (12 per layer + the final "
-                             "norm; 13 per layer with --shard-mlp); the positions / cos-sin tables are a "
-                             "few PyTorch ops per forward, and NCCL's kernels, not counted",
+        "gpu_launches_note": "kernels of libw4a4_sm100.so per timed region: per forward the positions / "
+                             "mask / cos-sin tables, 10 per layer (11 with --shard-mlp) and the final "
+                             "norm; nothing else runs on the device (NCCL's kernels under --shard-mlp "
+                             "not counted)",
         "clocks": clocks.summary(),
         "e2e": {
             "value": job_throughput(ms_e2e, args.batch, job_obs),

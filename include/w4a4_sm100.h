@@ -217,14 +217,14 @@ int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_
  *   vt_scratch fp16 [batch, 256, W4A4_ATTN_VT_STRIDE(seq)]: V transposed
  *   out        fp16 [batch * seq, ldo], heads x 256 per row
  *   cos_t, sin_t  NULL: q and k are used as given; else fp16 [batch * seq,
- *              256] rotary tables: k is rotated into k_out [batch * seq,
- *              ldko] (k_out may equal k; it is the KV cache's key rows),
- *              which the attention then reads, and q is rotated on the fly
- *              (q itself is left as given); w4a4_rope's arithmetic
+ *              256] rotary tables: q is rotated in place and k into k_out
+ *              [batch * seq, ldko] (k_out may equal k; it is the KV cache's
+ *              key rows) in the first launch, with w4a4_rope's arithmetic,
+ *              and the attention reads them
  * heads must divide 128; seq <= 4096.  Two launches (RoPE + V transpose,
  * attention). */
 #define W4A4_ATTN_VT_STRIDE(seq) ((((int64_t)(seq)) + 7) / 8 * 8)
-int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                           int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                           int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
                           const void* cos_t, const void* sin_t, void* k_out, int64_t ldko,

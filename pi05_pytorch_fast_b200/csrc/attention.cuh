@@ -8,7 +8,7 @@
 // padded query sees no key, so its softmax is uniform over all L keys (the
 // result of the all-masked row in the reference's fp32 softmax).
 //
-// Design (one CTA of 10 warps per 128 (token, head) rows of one observation):
+// Design (one CTA per 128 (token, head) rows of one observation):
 //  * the CTA's rows are `128 / heads` consecutive tokens x all heads, so every
 //    row shares the one key/value head: Q is one 64 KB TMA load (4-D map
 //    {d, head, token, batch}, 128-byte swizzle), K and V^T stream in blocks
@@ -16,10 +16,7 @@
 //  * warp 1 issues S = Q K^T (M = 128, N = 64, 16 MMAs of K = 16 over d) into
 //    one of two TMEM score buffers, and O += P V^T (M = 128, N = 256, 4 MMAs of
 //    K = 16 keys) with P read from TMEM (the A operand of the TS form);
-//  * with rotary tables given, warps 2-5 first rotate the Q tile in shared
-//    memory (RoPE) while the first key blocks stream in;
-//  * warps 2-9 (two per TMEM lane quarter, thread = row, each warp half of
-//    a block's columns and of O) run an online
+//  * warps 2-5 (one per TMEM lane quarter, thread = row) run an online
 //    softmax in one pass: p = exp2(s - m) as fp16 into TMEM for the PV MMA,
 //    with the running max m moved (and O rescaled in TMEM) only when a block
 //    exceeds it by more than 2^8; then they scale O by 1 / sum and store fp16
@@ -45,13 +42,10 @@ constexpr int kAttnQBytes = kAttnRows * kAttnHeadDim * 2;          // 64 KB
 constexpr int kAttnKBytes = kAttnKeyBlock * kAttnHeadDim * 2;      // 32 KB
 constexpr int kAttnVBytes = kAttnHeadDim * kAttnKeyBlock * 2;      // 32 KB
 constexpr int kAttnStages = 2;
-constexpr int kAttnSoftmaxWarps = 8;                               // two per TMEM lane quarter
-constexpr int kAttnThreads = 32 * (2 + kAttnSoftmaxWarps);         // 10 warps
-// q, k/v full/empty, s/p full/free, o, q rotated, 4 max-exchange, 4 sum-exchange
-constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 1 + 1 + 4 + 4;
-constexpr int kAttnXchgBytes = 3 * 2 * kAttnRows * 4;  // [block parity 0, 1, final sums][half][row] fp32
+constexpr int kAttnThreads = 192;                                  // 6 warps
+constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 1;      // q, k/v full/empty, s/p full/free, o
 constexpr int kAttnSmem = kAttnQBytes + kAttnStages * (kAttnKBytes + kAttnVBytes) +
-                          kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + kAttnXchgBytes + 1024;
+                          kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + 1024;
 // TMEM columns: O [0, 256), S buffers at 256 and 320 (64 each), P buffers at
 // 384 and 416 (32 columns: 64 fp16 per row).
 constexpr uint32_t kAttnTmemCols = 512;
@@ -68,8 +62,6 @@ struct alignas(64) AttnParams {
   int seq;
   int heads;
   float scale_log2;          // head_dim^-0.5 * log2(e)
-  const __half* cos_t;       // null, or rotary tables [B * L, 256]: Q is rotated in shared memory
-  const __half* sin_t;
   unsigned long long wait_limit_ns;
 };
 
@@ -141,7 +133,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* nkb_slot = reinterpret_cast<int*>(tmem_slot + 2);
   unsigned long long* kmask = reinterpret_cast<unsigned long long*>(tmem_slot + 4);  // 8-byte aligned
-  float* xchg = reinterpret_cast<float*>(kmask + kAttnMaxKeys / 64);  // [3][2][128]
 
   const auto bar_q = [&] { return smem_addr(bars); };
   const auto bar_kfull = [&](int s) { return smem_addr(bars + 1 + s); };
@@ -153,10 +144,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const auto bar_pfull = [&](int s) { return smem_addr(bars + 13 + s); };
   const auto bar_pfree = [&](int s) { return smem_addr(bars + 15 + s); };
   const uint32_t bar_o = smem_addr(bars + 17);
-  const uint32_t bar_qrot = smem_addr(bars + 18);  // the softmax warps rotated Q (RoPE) in place
-  // the two softmax warps of lane quarter q exchange block maxima / final sums
-  const auto bar_xmax = [&](int q) { return smem_addr(bars + 19 + q); };
-  const auto bar_xsum = [&](int q) { return smem_addr(bars + 23 + q); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y;
@@ -179,16 +166,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(bar_vfull(s), 1);
       mbar_init(bar_vempty(s), 1);
       mbar_init(bar_sfull(s), 1);
-      mbar_init(bar_sfree(s), kAttnSoftmaxWarps);
-      mbar_init(bar_pfull(s), kAttnSoftmaxWarps);
+      mbar_init(bar_sfree(s), 4);
+      mbar_init(bar_pfull(s), 4);
       mbar_init(bar_pfree(s), 1);
     }
     mbar_init(bar_o, 1);
-    mbar_init(bar_qrot, kAttnSoftmaxWarps);
-    for (int q = 0; q < 4; ++q) {
-      mbar_init(bar_xmax(q), 2);
-      mbar_init(bar_xsum(q), 2);
-    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tmap_q);
@@ -215,12 +197,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     pad_row = __any_sync(0xffffffffu, pad_row);
     if (lane == 0) *nkb_slot = ((pad_row ? L : max(0, min(L, kv_len))) + kAttnKeyBlock - 1) / kAttnKeyBlock;
   }
-  // 64-bit masks of the real keys of every block (the softmax warps; the
-  // loads of a warp's blocks are independent and issued together)
+  // 64-bit masks of the real keys of every block (warps 2-5; the loads of a
+  // warp's blocks are independent and issued together)
   if (warp >= 2) {
     const int nblk = (L + kAttnKeyBlock - 1) / kAttnKeyBlock;
 #pragma unroll 4
-    for (int kb = warp - 2; kb < nblk; kb += kAttnSoftmaxWarps) {
+    for (int kb = warp - 2; kb < nblk; kb += 4) {
       const int j0 = kb * kAttnKeyBlock + lane, j1 = j0 + 32;
       const bool v0 = j0 < L && kv_row[j0];
       const bool v1 = j1 < L && kv_row[j1];
@@ -281,8 +263,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t idesc_o = idesc_f16(kAttnRows, kAttnHeadDim);
     const uint64_t qdesc = smem_desc_sw128(smem_addr(q_smem));
     bool alive = nkb > 0 && warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit));
-    if (alive && p.cos_t)  // RoPE applied to Q in shared memory by the softmax warps
-      alive = warp_all(mbar_wait_spin(bar_qrot, 0, abort_flag, err, kErrWaitUnpack, limit));
     // S(kb) = Q K(kb)^T into score buffer kb % 2
     const auto issue_s = [&](int kb) -> bool {
       const int slot = kb & 1;
@@ -338,59 +318,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (issuer && nkb > 0) umma_commit(bar_o);
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax + epilogue (warps 2-9)
+    // ------------------------------------------------ softmax + epilogue (warps 2-5)
     // Online softmax in one pass, base 2 (s2 = acc * scale * log2 e): the
     // row's running max m only moves up when a block's max exceeds it by
     // more than kRescaleLog2, and then O (TMEM) and l are rescaled by
     // exp2(m_old - m_new) once the previous P V MMA has completed; otherwise
     // p = exp2(s2 - m) <= 2^kRescaleLog2 is kept unnormalised (fp16 holds it).
-    // Two warps per TMEM lane quarter: `half` 0 takes columns 0-31 of every
-    // score block (and O columns 0-127), half 1 columns 32-63 (O 128-255);
-    // they agree on each block's row max through shared memory, and add
-    // their partial sums at the end.
     constexpr float kRescaleLog2 = 8.f;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;                // this thread's row (TMEM lane)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int tok = t0 + r / p.heads, head = r % p.heads;
-    const bool q_real = tok < L && kv_row[tok];
+    const bool q_real = tok < L && p.key_valid[static_cast<long long>(b) * L + tok];
     const float scale = p.scale_log2;
-    float m = -INFINITY, l = 0.f;  // l: this warp's half of the row sum
+    float m = -INFINITY, l = 0.f;
     bool alive = nkb > 0;
-    if (alive && p.cos_t) {
-      // RoPE of the Q tile in place.  Element d of row rr sits in slice d / 64,
-      // 16-byte chunk ((d % 64) / 8) ^ (rr % 8) of the row (128-byte swizzle),
-      // so its partner d + 128 is the same chunk of slice d / 64 + 2.
-      if (!warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit))) {
-        alive = false;
-      } else {
-        const int tq = threadIdx.x - 64;  // 0 .. 255
-#pragma unroll 4
-        for (int it = 0; it < 8; ++it) {
-          const int i = tq + 256 * it;    // (row, slice 0/1, chunk)
-          const int rr = i >> 4, sl = (i >> 3) & 1, c = i & 7;
-          const int tk = t0 + rr / p.heads;
-          if (tk >= L) continue;
-          const int off = rr * 128 + ((c ^ (rr & 7)) << 4);
-          uint4* lo = reinterpret_cast<uint4*>(q_smem + sl * (kAttnQBytes / kAttnSlices) + off);
-          uint4* hi = reinterpret_cast<uint4*>(q_smem + (sl + 2) * (kAttnQBytes / kAttnSlices) + off);
-          const int d = 64 * sl + 8 * c;
-          const __half* cr = p.cos_t + (static_cast<long long>(b) * L + tk) * kAttnHeadDim;
-          const __half* sr = p.sin_t + (static_cast<long long>(b) * L + tk) * kAttnHeadDim;
-          uint4 a = *lo, bb = *hi;
-          rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)),
-                      __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
-                      __ldg(reinterpret_cast<const uint4*>(sr + d)),
-                      __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
-          *lo = a;
-          *hi = bb;
-        }
-        fence_proxy_async_smem();  // generic-proxy stores, read next by the MMA (async proxy)
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_qrot);
-      }
-    }
     for (int kb = 0; alive && kb < nkb; ++kb) {
       const int slot = kb & 1;
       if (!warp_all(mbar_wait_spin(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
@@ -398,11 +340,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t raw[32];
+      uint32_t raw[64];
       {
-        const uint32_t t = tmem_base + lane_addr + kAttnSCol + slot * kAttnKeyBlock + 32 * half;
+        const uint32_t t = tmem_base + lane_addr + kAttnSCol + slot * kAttnKeyBlock;
         tmem_ld_32x32b_x16(t, *reinterpret_cast<uint32_t(*)[16]>(&raw[0]));
         tmem_ld_32x32b_x16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&raw[16]));
+        tmem_ld_32x32b_x16(t + 32, *reinterpret_cast<uint32_t(*)[16]>(&raw[32]));
+        tmem_ld_32x32b_x16(t + 48, *reinterpret_cast<uint32_t(*)[16]>(&raw[48]));
         tmem_ld_wait();
       }
       tc_fence_before();
@@ -413,25 +357,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const unsigned long long vm =
           q_real ? kmask[kb]
                  : (L - j0 >= 64 ? ~0ull : ((1ull << (L - j0)) - 1ull));
-      const unsigned vh = static_cast<unsigned>(vm >> (32 * half));  // this warp's 32 columns
+      const unsigned vlo = static_cast<unsigned>(vm), vhi = static_cast<unsigned>(vm >> 32);
       float bm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // 4 chains: ILP
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < 64; ++c) {
         const float v = q_real ? __uint_as_float(raw[c]) : 0.f;
-        const float mv = ((vh >> c) & 1u) ? v : -INFINITY;
+        const bool ok = ((c < 32 ? vlo >> c : vhi >> (c - 32)) & 1u) != 0;
+        const float mv = ok ? v : -INFINITY;
         raw[c] = __float_as_uint(mv);
         bm4[c & 3] = fmaxf(bm4[c & 3], mv);
       }
-      // the block max of the row: both halves (scale > 0 commutes with max)
-      float* xm = xchg + (slot * 2) * kAttnRows;  // [half][row] of this block parity
-      xm[half * kAttnRows + r] = fmaxf(fmaxf(bm4[0], bm4[1]), fmaxf(bm4[2], bm4[3]));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_xmax(quarter));
-      if (!warp_all(mbar_wait_spin(bar_xmax(quarter), kb & 1, abort_flag, err, kErrWaitAccum, limit))) {
-        alive = false;
-        break;
-      }
-      const float bmax = fmaxf(xm[r], xm[kAttnRows + r]) * scale;
+      // scale > 0: the max of the scaled scores
+      const float bmax = fmaxf(fmaxf(bm4[0], bm4[1]), fmaxf(bm4[2], bm4[3])) * scale;
       float f = 1.f;  // rescale of the previous O and l
       const bool grow = bmax > m + kRescaleLog2;  // false while the block is all masked
       if (grow) {
@@ -441,18 +378,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       if (__any_sync(0xffffffffu, grow && f != 0.f) && kb >= 1) {
         // O holds P V of earlier blocks: wait for the last of them, rescale
-        // this warp's rows and O half (whole-warp TMEM access; rows that did
-        // not grow multiply by 1)
+        // this warp's rows (whole-warp TMEM access; others multiply by 1)
         if (!warp_all(mbar_wait_spin(bar_pfree((kb - 1) & 1), ((kb - 1) >> 1) & 1, abort_flag, err,
-                                     kErrWaitAccum, limit))) {
+                                        kErrWaitAccum, limit))) {
           alive = false;
           break;
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int c0 = 0; c0 < kAttnHeadDim / 2; c0 += 16) {
+        for (int c0 = 0; c0 < kAttnHeadDim; c0 += 16) {
           uint32_t o[16];
-          const uint32_t t = tmem_base + lane_addr + kAttnOCol + half * (kAttnHeadDim / 2) + c0;
+          const uint32_t t = tmem_base + lane_addr + kAttnOCol + c0;
           tmem_ld_32x32b_x16(t, o);
           tmem_ld_wait();
 #pragma unroll
@@ -463,10 +399,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // p = exp2(s2 - m) as fp16 pairs, l += sum p (masked: exp2(-inf) = 0)
       const float nm = m == -INFINITY ? 0.f : -m;
-      uint32_t pw[16];
+      uint32_t pw[32];
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 32; ++c) {
         const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(raw[2 * c]), scale, nm));
         const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(raw[2 * c + 1]), scale, nm));
         s4[c & 3] += p0 + p1;
@@ -474,35 +410,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
       if (kb >= 2 && !warp_all(mbar_wait_spin(bar_pfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err,
-                                               kErrWaitAccum, limit))) {
+                                                  kErrWaitAccum, limit))) {
         alive = false;
         break;
       }
       tc_fence_after();
-      tmem_st_32x32b_x16(tmem_base + lane_addr + kAttnPCol + slot * 32 + 16 * half, pw);
+      tmem_st_32x32b_x32(tmem_base + lane_addr + kAttnPCol + slot * 32, pw);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull(slot));
     }
-    // epilogue: the row sum of both halves, then this warp's O half / l -> fp16
-    if (alive) {
-      xchg[(4 + half) * kAttnRows + r] = l;  // its own area: the partner may still read block maxima
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_xsum(quarter));
-      alive = warp_all(mbar_wait_spin(bar_xsum(quarter), 0, abort_flag, err, kErrWaitAccum, limit));
-    }
+    // epilogue: O / l -> fp16 rows
     if (alive && warp_all(mbar_wait_bounded(bar_o, 0, abort_flag, err, kErrWaitAccum, limit))) {
       tc_fence_after();
-      const float lt = xchg[4 * kAttnRows + r] + xchg[5 * kAttnRows + r];
-      const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-      __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim +
-                     half * (kAttnHeadDim / 2);
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim;
       const bool store = tok < L;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kAttnHeadDim / 2; c0 += 16) {
+      for (int c0 = 0; c0 < kAttnHeadDim; c0 += 16) {
         uint32_t o[16];
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + kAttnOCol + half * (kAttnHeadDim / 2) + c0, o);
+        tmem_ld_32x32b_x16(tmem_base + lane_addr + kAttnOCol + c0, o);
         tmem_ld_wait();
         uint32_t w[8];
 #pragma unroll
@@ -530,23 +458,61 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
-// The attention's key-side inputs in one launch, one CTA per 16 tokens of
-// one observation: V [B * L, ldv] (rows of 256) -> V^T per observation
-// [B][256][ldt] (the PV MMA's B operand must be K-major: keys contiguous;
-// keys in [seq, ldt) written as zeros), and, when cos_t is not null, RoPE of
-// k into k_out (which may equal k).  Q is rotated by the attention kernel.
+// The attention's inputs in one launch.  CTA (x, b, z) covers tokens
+// [16 x, 16 x + 16) of observation b; z = 0: V [B * L, ldv] (rows of 256)
+// -> V^T per observation [B][256][ldt] (the PV MMA's B operand must be
+// K-major: keys contiguous; keys in [seq, ldt) written as zeros) and, when
+// cos_t is not null, RoPE of k into k_out (which may equal k); z >= 1 (only
+// with cos_t): RoPE of q in place for heads [2 (z - 1), 2 z) -- a grid wide
+// enough that the 3.2 MB of q at a 776-token prefix is not latency bound.
 constexpr int kPrepTokens = 16;
-__global__ void __launch_bounds__(256) attn_prep_kernel(const __half* k, long long ldk, __half* k_out,
-                                                        long long ldko, const __half* __restrict__ v,
-                                                        long long ldv, __half* __restrict__ vt, long long ldt,
+constexpr int kPrepHeadsPerSlice = 2;
+__global__ void __launch_bounds__(256) attn_prep_kernel(__half* q, long long ldq, const __half* k, long long ldk,
+                                                        __half* k_out, long long ldko,
+                                                        const __half* __restrict__ v, long long ldv,
+                                                        __half* __restrict__ vt, long long ldt,
                                                         const __half* __restrict__ cos_t,
-                                                        const __half* __restrict__ sin_t, int seq) {
+                                                        const __half* __restrict__ sin_t, int seq, int heads) {
   __shared__ __align__(16) __half tile[kPrepTokens][kAttnHeadDim + 8];
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.y, j0 = blockIdx.x * kPrepTokens;
   const int t = threadIdx.x;
   const long long row0 = static_cast<long long>(b) * seq + j0;
+  if (blockIdx.z > 0) {
+    // q: 16 rows x 2 heads x 16 vectors of 8 pairs, two per thread, loads first
+    const int h0 = kPrepHeadsPerSlice * (blockIdx.z - 1);
+    uint4 a[2], bb[2], ca[2], cb[2], sa[2], sb[2];
+    bool ok[2];
+    __half* qr[2];
+    int dd[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = t + 256 * u;
+      const int j = i >> 5, head = h0 + ((i >> 4) & 1), d = 8 * (i & 15);
+      ok[u] = j0 + j < seq && head < heads;
+      dd[u] = d;
+      if (!ok[u]) continue;
+      const long long row = row0 + j;
+      qr[u] = q + row * ldq + head * kAttnHeadDim;
+      a[u] = *reinterpret_cast<const uint4*>(qr[u] + d);
+      bb[u] = *reinterpret_cast<const uint4*>(qr[u] + d + 128);
+      const __half* cr = cos_t + row * kAttnHeadDim;
+      const __half* sr = sin_t + row * kAttnHeadDim;
+      ca[u] = __ldg(reinterpret_cast<const uint4*>(cr + d));
+      cb[u] = __ldg(reinterpret_cast<const uint4*>(cr + d + 128));
+      sa[u] = __ldg(reinterpret_cast<const uint4*>(sr + d));
+      sb[u] = __ldg(reinterpret_cast<const uint4*>(sr + d + 128));
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!ok[u]) continue;
+      rope_pairs8(a[u], bb[u], ca[u], cb[u], sa[u], sb[u]);
+      *reinterpret_cast<uint4*>(qr[u] + dd[u]) = a[u];
+      *reinterpret_cast<uint4*>(qr[u] + dd[u] + 128) = bb[u];
+    }
+    return;
+  }
   // V rows -> shared memory: 16 keys x 32 vectors
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -557,20 +523,18 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const __half* k, long lo
   }
   if (cos_t) {
     // k: 16 rows x 16 vectors of 8 pairs, one per thread
-    {
-      const int j = t >> 4, d = 8 * (t & 15);
-      if (j0 + j < seq) {
-        const long long row = row0 + j;
-        uint4 a = *reinterpret_cast<const uint4*>(k + row * ldk + d);
-        uint4 bb = *reinterpret_cast<const uint4*>(k + row * ldk + d + 128);
-        const __half* cr = cos_t + row * kAttnHeadDim;
-        const __half* sr = sin_t + row * kAttnHeadDim;
-        rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)),
-                    __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
-                    __ldg(reinterpret_cast<const uint4*>(sr + d)), __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
-        *reinterpret_cast<uint4*>(k_out + row * ldko + d) = a;
-        *reinterpret_cast<uint4*>(k_out + row * ldko + d + 128) = bb;
-      }
+    const int j = t >> 4, d = 8 * (t & 15);
+    if (j0 + j < seq) {
+      const long long row = row0 + j;
+      uint4 a = *reinterpret_cast<const uint4*>(k + row * ldk + d);
+      uint4 bb = *reinterpret_cast<const uint4*>(k + row * ldk + d + 128);
+      const __half* cr = cos_t + row * kAttnHeadDim;
+      const __half* sr = sin_t + row * kAttnHeadDim;
+      rope_pairs8(a, bb, __ldg(reinterpret_cast<const uint4*>(cr + d)),
+                  __ldg(reinterpret_cast<const uint4*>(cr + d + 128)),
+                  __ldg(reinterpret_cast<const uint4*>(sr + d)), __ldg(reinterpret_cast<const uint4*>(sr + d + 128)));
+      *reinterpret_cast<uint4*>(k_out + row * ldko + d) = a;
+      *reinterpret_cast<uint4*>(k_out + row * ldko + d + 128) = bb;
     }
   }
   __syncthreads();

@@ -646,7 +646,7 @@ int launch_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* 
 // ------------------------------------------------------------- attention
 int64_t attn_vt_stride(int32_t seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
 
-int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                      int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                      int32_t seq, int32_t heads, void* vt, void* out, int64_t ldo, const void* cos_t,
                      const void* sin_t, void* k_out, int64_t ldko, cudaStream_t stream) {
@@ -677,11 +677,14 @@ int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   const int64_t ldt = attn_vt_stride(seq);
   W4A4_CUDA_TRY(launch_kernel(attn_prep_kernel,
                               dim3(static_cast<unsigned>((ldt + kPrepTokens - 1) / kPrepTokens),
-                                   static_cast<unsigned>(batch)),
-                              dim3(256), 0, stream, 1, static_cast<const __half*>(k), ldk,
-                              static_cast<__half*>(rope ? k_out : nullptr), rope ? ldko : 0ll,
-                              static_cast<const __half*>(v), ldv, static_cast<__half*>(vt), ldt,
-                              static_cast<const __half*>(cos_t), static_cast<const __half*>(sin_t), seq));
+                                   static_cast<unsigned>(batch),
+                                   rope ? 1u + static_cast<unsigned>((heads + kPrepHeadsPerSlice - 1) /
+                                                                     kPrepHeadsPerSlice)
+                                        : 1u),
+                              dim3(256), 0, stream, 1, static_cast<__half*>(const_cast<void*>(q)), ldq,
+                              static_cast<const __half*>(k), ldk, static_cast<__half*>(rope ? k_out : nullptr),
+                              rope ? ldko : 0ll, static_cast<const __half*>(v), ldv, static_cast<__half*>(vt), ldt,
+                              static_cast<const __half*>(cos_t), static_cast<const __half*>(sin_t), seq, heads));
   // the keys the attention reads: rotated into k_out, or k as given
   const void* kr = rope ? k_out : k;
   const int64_t ldkr = rope ? ldko : ldk;
@@ -722,8 +725,6 @@ int launch_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   p.seq = seq;
   p.heads = heads;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kAttnHeadDim)));
-  p.cos_t = static_cast<const __half*>(cos_t);
-  p.sin_t = static_cast<const __half*>(sin_t);
   p.wait_limit_ns = g_wait_limit_ns.load();
   if (int e = ensure_smem_attr(dev, 1ull << 40, prefix_attention_kernel, kAttnSmem)) return e;
   const int tpt = kAttnRows / heads;
@@ -1129,7 +1130,7 @@ int w4a4_rope(const void* x, int64_t ldx, void* out, int64_t ldo, const void* co
   return launch_rope(x, ldx, out, ldo, cos_t, sin_t, m, heads, static_cast<cudaStream_t>(stream));
 }
 
-int w4a4_prefix_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                           int64_t ldv, const uint8_t* key_valid, const int32_t* kv_len, int32_t batch,
                           int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
                           const void* cos_t, const void* sin_t, void* k_out, int64_t ldko, void* stream) {

@@ -438,7 +438,7 @@ class W4A4PrefixLM:
 
     def launches_per_forward(self) -> int:
         """Kernels of this library per forward: the prefix tables; per layer 2
-        norm+quant, 1 quant, 4 GEMMs, RoPE + V transpose, attention, 1
+        norm+quant, 1 quant, 4 GEMMs, RoPE of q and k + V transpose, attention, 1
         GeGLU+quant (the sharded MLP: GeGLU, then the segment quant); then the
         final norm.  Nothing else runs on the device."""
         return (10 + (1 if self.shard is not None else 0)) * len(self.layers) + 2

@@ -325,9 +325,9 @@ def test_prefix_attention_rescales_when_a_late_key_dominates():
 
 
 def test_prefix_attention_with_fused_rope_equals_rope_then_attention():
-    """cos / sin given: k is rotated into k_out ahead of the attention and Q
-    inside it (in shared memory), exactly as w4a4_rope rotates them: the
-    result is the attention of the rotated inputs, and q is left as given."""
+    """cos / sin given: q is rotated in place and k into k_out in the
+    attention's first launch, exactly as w4a4_rope rotates them, and the
+    result is the attention of the rotated inputs."""
     heads, seq, batch = 8, 776, 2
     gen = torch.Generator(device=DEV).manual_seed(4)
     q = torch.randn(batch * seq, heads * 256, device=DEV, generator=gen).half()
@@ -353,7 +353,7 @@ def test_prefix_attention_with_fused_rope_equals_rope_then_attention():
                                               heads, vt.data_ptr(), out.data_ptr(), out.stride(0), cos.data_ptr(),
                                               sin.data_ptr(), k_out.data_ptr(), k_out.stride(0), _stream()))
     torch.cuda.synchronize()
-    assert_half_equal(q2, q)
+    assert_half_equal(q2, q_ref)
     assert_half_equal(k_out, k_ref)
     assert torch.equal(out.view(torch.int16), expect.view(torch.int16))
 
