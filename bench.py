@@ -74,6 +74,9 @@ def parse_args():
     ap.add_argument("--shard-mlp", action="store_true",
                     help="with N > 1: every rank runs the SAME observations and holds 1/N of gate/up "
                          "(tensor-parallel MLP, NCCL all-to-all + all-gather; strong scaling)")
+    ap.add_argument("--int8", default="",
+                    help="comma-separated projections (q,k,v,o,gate,up,down) repacked once into the "
+                         "int8 layout (SS CTA-pair GEMM); default: none")
     ap.add_argument("--roofline-reps", type=int, default=20)
     ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k",
                                        "normquant", "geglu", "attn", "forward"),
@@ -398,6 +401,8 @@ def run_ours(args, rank, world, local_rank, dist_on):
     sharded = args.shard_mlp and world > 1
     shard = MlpShard(rank, world) if sharded else None
     model = plm.W4A4PrefixLM.random(cfg, device, seed=1234, staging=staging, shard=shard)
+    if args.int8:
+        model.repack_int8(tuple(args.int8.split(",")))
     lang = args.prefix - N_IMG
     # data parallel: each rank its own observations; sharded: the same ones on every rank
     in_seed = 100 if sharded else 100 + rank
@@ -722,6 +727,8 @@ def run_case(args):
     m = args.batch * args.prefix
     layers = 1 if args.case != "forward" else args.layers
     model = plm.W4A4PrefixLM.random(plm.PrefixLMConfig(layers=layers), device, seed=1234, staging=staging)
+    if args.int8:
+        model.repack_int8(tuple(args.int8.split(",")))
     lw = layer_weights(model.layers[0])
     x = synthetic_activations(m, HIDDEN, device, seed=100)
     h = synthetic_activations(m, INTER, device, seed=101)

@@ -63,6 +63,12 @@ extern "C" {
  *   inside a tensor declared [N, K/8+9] (pack.py:45-68). */
 #define W4A4_LAYOUT_ROW_MAJOR 0
 #define W4A4_LAYOUT_FRAGMENT_MAJOR 1
+/* INT8: either layout repacked once by w4a4_repack_int8 (no reference
+ *   counterpart; the load-time "Blackwell tile order"): int32 [N, K/4+4], a
+ *   row = K int8 values (16 x code, in the GEMM's K byte order), then the
+ *   fp32 scale and three zero words.  Runs on the CTA-pair kernel with both
+ *   MMA operands in shared memory. */
+#define W4A4_LAYOUT_INT8 2
 
 /* variant argument of w4a4_set_gemm_variant */
 #define W4A4_GEMM_SINGLE_CTA 0 /* single-CTA kernel; split-K where the planner finds it faster */
@@ -229,6 +235,13 @@ int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, cons
                           int32_t seq, int32_t heads, void* vt_scratch, void* out, int64_t ldo,
                           const void* cos_t, const void* sin_t, void* k_out, int64_t ldko,
                           void* stream);
+
+/* Repack a packed weight (row-major or fragment-major, as w4a4_gemm takes
+ * it) into W4A4_LAYOUT_INT8: dst int32 [src->n, k/4 + 4], 16-byte aligned.
+ * The GEMM of the repacked weight is bit-identical to that of the packed
+ * one.  No reference counterpart (the reference's pack.py:45-68 repack is
+ * its WMMA fragment order). */
+int w4a4_repack_int8(const w4a4_weight* src, int32_t k, int32_t* dst, void* stream);
 
 /* Copy a row-major packed weight [n, src_row_words] into [n, dst_row_words]
  * (dst_row_words >= src_row_words), zero-filling the new words: the

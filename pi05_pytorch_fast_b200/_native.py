@@ -25,6 +25,7 @@ CODES_PACKED = 1
 CODES_GEMM = 2
 LAYOUT_ROW_MAJOR = 0
 LAYOUT_FRAGMENT_MAJOR = 1
+LAYOUT_INT8 = 2
 ROTATE_BY_K = -1
 GEMM_SINGLE_CTA = 0
 GEMM_CTA_PAIR = 1
@@ -49,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "w4a4_geglu",
     "w4a4_quant_segments",
     "w4a4_pad_rows",
+    "w4a4_repack_int8",
     "w4a4_last_error",
     "w4a4_device_error",
     "w4a4_set_wait_limit_ns",
@@ -103,6 +105,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_geglu.argtypes = [vp, vp, c_i64, c_i32, c_i64, vp, c_i64, vp]
     lib.w4a4_quant_segments.argtypes = [vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
+    lib.w4a4_repack_int8.argtypes = [vp, c_i32, vp, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]
     lib.w4a4_set_wait_limit_ns.argtypes = [c_u64]

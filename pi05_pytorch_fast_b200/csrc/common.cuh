@@ -356,6 +356,18 @@ __device__ __forceinline__ void umma_i8_ts_pair(uint32_t d_tmem, uint32_t a_tmem
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Pair MMA with both operands in shared memory: A = 128 rows in each CTA at
+// the descriptor's address (M = 256 across the pair), B split by N across
+// the pair's shared memory.
+__device__ __forceinline__ void umma_i8_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
 // when all previously issued pair MMAs have completed.
 __device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t cta_mask) {

@@ -62,27 +62,29 @@ __device__ __forceinline__ void load8_half_as_float(const __half* p, float (&v)[
 // constants rounded to fp32, x^3 as (x x) x, the inner sum as one fused
 // multiply-add, rounded to fp16; then the fp16 product with up (the exact
 // fp32 product of two fp16 values, rounded once).  tanhf is CUDA's.
-__device__ __forceinline__ float gelu_tanh_f32(float x) {
-  constexpr float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-  constexpr float kKappa = 0.044715f;
-  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+// Two values at a time: the fp32 arithmetic through the two-lane fp32
+// instructions (each lane rounded as the scalar instruction) and both
+// results rounded to fp16 by one packed conversion.
+__device__ __forceinline__ __half2 gelu_tanh_h2(__half2 g) {
+  const float2 x = __half22float2(g);
+  const float2 x3 = __fmul2_rn(__fmul2_rn(x, x), x);
+  const float2 inner = __fmul2_rn(make_float2(0.7978845608028654f, 0.7978845608028654f),
+                                  __ffma2_rn(make_float2(0.044715f, 0.044715f), x3, x));
+  const float2 t = make_float2(tanhf(inner.x), tanhf(inner.y));
+  const float2 r = __fmul2_rn(__fmul2_rn(make_float2(0.5f, 0.5f), x), __fadd2_rn(make_float2(1.f, 1.f), t));
+  return __floats2half2_rn(r.x, r.y);
 }
 
-__device__ __forceinline__ __half geglu_half(__half g, __half u) {
-  const __half gl = __float2half_rn(gelu_tanh_f32(__half2float(g)));
-  return __float2half_rn(__fmul_rn(__half2float(gl), __half2float(u)));
-}
-
-// Eight fp16 GeGLU values from 16-byte vectors of gate and up.
+// Eight fp16 GeGLU values from 16-byte vectors of gate and up.  The product
+// is the fp16 multiply: the fp32 product of two fp16 values is exact, so
+// rounding it to fp16 once is the correctly rounded fp16 product.
 __device__ __forceinline__ uint4 geglu8(const uint4 g, const uint4 u) {
   uint4 r;
-  const __half* gh = reinterpret_cast<const __half*>(&g);
-  const __half* uh = reinterpret_cast<const __half*>(&u);
-  __half* rh = reinterpret_cast<__half*>(&r);
+  const __half2* gh = reinterpret_cast<const __half2*>(&g);
+  const __half2* uh = reinterpret_cast<const __half2*>(&u);
+  __half2* rh = reinterpret_cast<__half2*>(&r);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) rh[j] = geglu_half(gh[j], uh[j]);
+  for (int i = 0; i < 4; ++i) rh[i] = __hmul2_rn(gelu_tanh_h2(gh[i]), uh[i]);
   return r;
 }
 
@@ -613,9 +615,9 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rot_16k_kernel(
 
 // ---- K = 16384, fp16 staging: every butterfly stage in registers.
 // A row is 2048 16-byte vectors (8 fp16 elements, index bits 0-2 inside a
-// vector); each of the CTA's 256 threads holds 8 of them.  Between phases the
-// vectors move through a shared-memory buffer so that the next three index
-// bits become the thread's vector index c:
+// vector); each of the 256 threads working on a row holds 8 of them.  Between
+// phases the vectors move through a shared-memory buffer so that the next
+// three index bits become the thread's vector index c:
 //   A: vec = 8u + c                      -> element bits 3-5 across c (fp32, with 0-2)
 //   B: vec = (u>>3)<<6 | c<<3 | (u&7)    -> bits 6-8
 //   C: vec = (u>>6)<<9 | c<<6 | (u&63)   -> bits 9-11
@@ -634,9 +636,90 @@ constexpr int kQ16RowBytes = 16384 * 2;
 constexpr int kQ16Smem = kQ16RowBytes + 1024;
 constexpr int kQ16CtasPerSm = 3;
 
-// GEGLU: two row buffers (gate, up), both loaded by TMA; two CTAs per SM,
-// so the GELU's registers fit without spilling.
-constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
+// One row through phases A-D, the amax and the codes, by the 256 threads
+// u = 0..255 of a row group.  base: the group's 1024-byte aligned buffer
+// (the row's 128-byte lines, line u's 16-byte chunk c at chunk c ^ (u & 7)).
+// load(c) gives the fp16 vector c of line u (phase A's input); sync() is the
+// group's barrier; buffer_free() runs once every thread of the group has
+// read the buffer for the last time (phase D's loads).
+template <int MODE, class Load, class Sync, class Free>
+__device__ __forceinline__ void q16k_row(unsigned char* base, int u, long long row, void* __restrict__ codes,
+                                         float* __restrict__ row_scale, float inv_sqrt_k, float* warp_amax,
+                                         Load load, Sync sync, Free buffer_free) {
+  constexpr int K = 16384;
+  const int warp = u >> 5, lane = u & 31;
+  uint4* buf = reinterpret_cast<uint4*>(base);
+  __half2 h[8][4];
+  {
+    // phase A: index bits 0-5 in fp32
+    float v[8][8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 raw = load(c);
+      const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(hp[i]);
+        v[c][2 * i] = f.x;
+        v[c][2 * i + 1] = f.y;
+      }
+    }
+#pragma unroll
+    for (int bb = 0; bb < 3; ++bb) stage_in_vector<8>(v, 1 << bb);
+#pragma unroll
+    for (int bb = 0; bb < 3; ++bb) stage_across_chunks<8>(v, 1 << bb);
+    pack_half2<8>(v, h);
+  }
+  sync();  // every thread has read its line before the buffer is rewritten
+#pragma unroll
+  for (int c = 0; c < 8; ++c) buf[q16k_slot(8 * u + c)] = *reinterpret_cast<const uint4*>(h[c]);
+  sync();
+  // phase B: bits 6-8
+  {
+    const int bq = ((u >> 3) << 6) | (u & 7);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(bq | (c << 3))];
+#pragma unroll
+    for (int bb = 0; bb < 3; ++bb) h2_stage_across_chunks<8>(h, 1 << bb);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) buf[q16k_slot(bq | (c << 3))] = *reinterpret_cast<const uint4*>(h[c]);
+  }
+  sync();
+  // phase C: bits 9-11
+  {
+    const int bq = ((u >> 6) << 9) | (u & 63);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(bq | (c << 6))];
+#pragma unroll
+    for (int bb = 0; bb < 3; ++bb) h2_stage_across_chunks<8>(h, 1 << bb);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) buf[q16k_slot(bq | (c << 6))] = *reinterpret_cast<const uint4*>(h[c]);
+  }
+  sync();
+  // phase D: bits 12-13
+  const auto vec_d = [&](int c) { return ((c & 3) << 9) | ((c >> 2) << 8) | u; };
+#pragma unroll
+  for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(vec_d(c))];
+  h2_stage_across_chunks<8>(h, 1);
+  h2_stage_across_chunks<8>(h, 2);
+  float mx = amax_h2<8>(h);
+  mx = warp_max(mx);
+  if (lane == 0) warp_amax[warp] = mx;
+  sync();
+  buffer_free();
+  mx = warp_amax[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) mx = fmaxf(mx, warp_amax[w]);
+  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
+  const float rs = __frcp_rn(sdiv);
+  if (u == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float v[8];
+    unpack_half2<8>(h[c], v);
+    store_codes8<MODE>(codes, row * K + 8 * vec_d(c), v, sdiv, rs);
+  }
+}
 
 // One CTA per row (the block scheduler hands rows to SMs as CTAs finish,
 // which balanced the 776-row prefix better than persistent CTAs with a
@@ -644,18 +727,23 @@ constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
 // TMA (a 3-D map {64, 256, M} of 128-byte lines, 128-byte swizzle).  The
 // swizzle puts 16-byte chunk c of line u at chunk c ^ (u & 7): thread u
 // reads its line (elements 64u .. 64u + 63) without bank conflicts.
-// GEGLU: xmap is the gate and umap the up projection (same shape); the row
-// quantised is gelu_tanh(gate) * up, formed in phase A (geglu8) and, when
-// h_out is not null, written there too.  Otherwise umap is unused.
 // SEGMENTED: xmap is 4-D {64, lines per segment, M, segments} (a row stored
 // as several segments, each a [M, seg] matrix: the layout an all-to-all of
 // column shards delivers), read with one box per row; same smem layout.
-template <int MODE, bool GEGLU = false, bool SEGMENTED = false>
+// GEGLU: xmap is the gate and umap the up projection (same shape), loaded
+// into two row buffers; the row quantised is gelu_tanh(gate) * up, formed in
+// phase A (geglu8) and, when h_out is not null, written there too; two CTAs
+// per SM so that the GELU's registers fit.  A table of the GELU's 65,536
+// fp16 results in shared memory instead of tanhf was measured slower (32.4
+// vs 31.9 us at M = 776, one persistent CTA of two rows per SM): the kernel
+// is bound by the latency of its row pipeline, not by the GELU's arithmetic.
+constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
+
+template <int MODE, bool SEGMENTED = false, bool GEGLU = false>
 __global__ void __launch_bounds__(kQuantThreads, GEGLU ? 2 : kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
     const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns,
     const __grid_constant__ CUtensorMap umap, __half* __restrict__ h_out, long long ldh) {
-  constexpr int K = 16384;
   extern __shared__ unsigned char quant_smem[];
   __shared__ float warp_amax[kQuantThreads / 32];
   __shared__ __align__(8) uint64_t bar;
@@ -663,7 +751,7 @@ __global__ void __launch_bounds__(kQuantThreads, GEGLU ? 2 : kQ16CtasPerSm) quan
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(quant_smem) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t bar_a = smem_addr(&bar);
-  const int u = threadIdx.x, warp = u >> 5, lane = u & 31;
+  const int u = threadIdx.x;
   const long long row = blockIdx.x;
   if (u == 0) {
     mbar_init(bar_a, 1);
@@ -682,82 +770,23 @@ __global__ void __launch_bounds__(kQuantThreads, GEGLU ? 2 : kQ16CtasPerSm) quan
       tma_load_3d(smem_addr(base), &xmap, 0, 0, static_cast<int>(row), bar_a);
     if constexpr (GEGLU) tma_load_3d(smem_addr(base + kQ16RowBytes), &umap, 0, 0, static_cast<int>(row), bar_a);
   }
-  if (!mbar_wait_bounded(bar_a, 0, &abort_flag, &g_w4a4_device_error, kErrWaitTma, limit_ns))
-    return;
-  uint4* buf = reinterpret_cast<uint4*>(base);
-  __half2 h[8][4];
-  {
-    // phase A: index bits 0-5 in fp32
-    float v[8][8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 raw = buf[8 * u + (c ^ (u & 7))];
-      if constexpr (GEGLU) {
-        raw = geglu8(raw, buf[2048 + 8 * u + (c ^ (u & 7))]);
-        if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 64 * u + 8 * c) = raw;
-      }
-      const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(hp[i]);
-        v[c][2 * i] = f.x;
-        v[c][2 * i + 1] = f.y;
-      }
-    }
-#pragma unroll
-    for (int bb = 0; bb < 3; ++bb) stage_in_vector<8>(v, 1 << bb);
-#pragma unroll
-    for (int bb = 0; bb < 3; ++bb) stage_across_chunks<8>(v, 1 << bb);
-    pack_half2<8>(v, h);
-  }
-  __syncthreads();  // every thread has read its line before the buffer is rewritten
-#pragma unroll
-  for (int c = 0; c < 8; ++c) buf[q16k_slot(8 * u + c)] = *reinterpret_cast<const uint4*>(h[c]);
-  __syncthreads();
-  // phase B: bits 6-8
-  {
-    const int bq = ((u >> 3) << 6) | (u & 7);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(bq | (c << 3))];
-#pragma unroll
-    for (int bb = 0; bb < 3; ++bb) h2_stage_across_chunks<8>(h, 1 << bb);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) buf[q16k_slot(bq | (c << 3))] = *reinterpret_cast<const uint4*>(h[c]);
-  }
-  __syncthreads();
-  // phase C: bits 9-11
-  {
-    const int bq = ((u >> 6) << 9) | (u & 63);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(bq | (c << 6))];
-#pragma unroll
-    for (int bb = 0; bb < 3; ++bb) h2_stage_across_chunks<8>(h, 1 << bb);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) buf[q16k_slot(bq | (c << 6))] = *reinterpret_cast<const uint4*>(h[c]);
-  }
-  __syncthreads();
-  // phase D: bits 12-13
-  const auto vec_d = [&](int c) { return ((c & 3) << 9) | ((c >> 2) << 8) | u; };
-#pragma unroll
-  for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(h[c]) = buf[q16k_slot(vec_d(c))];
-  h2_stage_across_chunks<8>(h, 1);
-  h2_stage_across_chunks<8>(h, 2);
-  float mx = amax_h2<8>(h);
-  mx = warp_max(mx);
-  if (lane == 0) warp_amax[warp] = mx;
-  __syncthreads();
-  mx = warp_amax[0];
-#pragma unroll
-  for (int w = 1; w < kQuantThreads / 32; ++w) mx = fmaxf(mx, warp_amax[w]);
-  const float sdiv = __fadd_rn(__fdiv_rn(mx, 7.0f), 1e-12f);
-  const float rs = __frcp_rn(sdiv);
-  if (u == 0) row_scale[row] = __fmul_rn(sdiv, inv_sqrt_k);
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    float v[8];
-    unpack_half2<8>(h[c], v);
-    store_codes8<MODE>(codes, row * K + 8 * vec_d(c), v, sdiv, rs);
-  }
+  mbar_wait_bounded(bar_a, 0, &abort_flag, &g_w4a4_device_error, kErrWaitTma, limit_ns);
+  __syncthreads();  // a timed-out wait sets abort_flag first: every thread leaves together
+  if (abort_flag) return;
+  const uint4* buf = reinterpret_cast<const uint4*>(base);
+  q16k_row<MODE>(
+      base, u, row, codes, row_scale, inv_sqrt_k, warp_amax,
+      [&](int c) {
+        const int slot = 8 * u + (c ^ (u & 7));
+        if constexpr (GEGLU) {
+          const uint4 r = geglu8(buf[slot], buf[2048 + slot]);
+          if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 64 * u + 8 * c) = r;
+          return r;
+        } else {
+          return buf[slot];
+        }
+      },
+      [] { __syncthreads(); }, [] {});
 }
 
 // Any K (multiple of 64) without rotation: one warp per row, two passes

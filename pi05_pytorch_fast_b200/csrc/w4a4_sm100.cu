@@ -496,12 +496,12 @@ int launch_geglu_quant(const void* gate, const void* up, int64_t m, int32_t k, i
         err_code = e;
         return;
       }
-      if (int e = ensure_smem_attr(dev, 1ull << (32 + MODE), quant_rot_16k_fp16_kernel<MODE, true>,
+      if (int e = ensure_smem_attr(dev, 1ull << (32 + MODE), quant_rot_16k_fp16_kernel<MODE, false, true>,
                                    kQ16SmemGeglu)) {
         err_code = e;
         return;
       }
-      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, true>, dim3(grid),
+      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, false, true>, dim3(grid),
                                            dim3(kQuantThreads), kQ16SmemGeglu, stream, 1, gmap, m, codes,
                                            row_scale, isk, g_wait_limit_ns.load(), umap, ho, ldh));
     } else {
@@ -576,12 +576,12 @@ int launch_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int6
         err_code = e;
         return;
       }
-      if (int e = ensure_smem_attr(dev, 1ull << (44 + MODE), quant_rot_16k_fp16_kernel<MODE, false, true>,
+      if (int e = ensure_smem_attr(dev, 1ull << (44 + MODE), quant_rot_16k_fp16_kernel<MODE, true>,
                                    kQ16Smem)) {
         err_code = e;
         return;
       }
-      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, false, true>, dim3(grid),
+      err_code = cuda_status(launch_kernel(quant_rot_16k_fp16_kernel<MODE, true>, dim3(grid),
                                            dim3(kQuantThreads), kQ16Smem, stream, 1, xmap, m, codes,
                                            row_scale, isk, g_wait_limit_ns.load(), xmap,
                                            static_cast<__half*>(nullptr), 0ll));
@@ -851,6 +851,10 @@ int check_weight(const w4a4_weight& w, int32_t k, int idx) {
                   "row-major packed W row stride (%d words) must be a multiple of 4 words; pad the rows "
                   "(w4a4_pad_rows / the K/8+8 load-time pad)",
                   w.row_words);
+  } else if (w.layout == W4A4_LAYOUT_INT8) {
+    if (w.row_words != k / 4 + 4)
+      return fail(W4A4_ERR_INVALID, "int8 weights must use the K/4+4 row stride (w4a4_repack_int8)");
+    return W4A4_OK;
   } else if (w.layout == W4A4_LAYOUT_FRAGMENT_MAJOR) {
     if (w.row_words != k / 8 + 9)
       return fail(W4A4_ERR_INVALID, "WMMA-fragment-major weights must use the K/8+9 marker stride");
@@ -878,7 +882,7 @@ std::atomic<int> g_gemm_variant{[] {
 // bit-identical; below ~200 tokens the single-CTA kernel is faster.
 constexpr int64_t kPairMinRows = 768;
 bool use_pair_kernel(int variant, int layout, int64_t m) {
-  return variant == W4A4_GEMM_CTA_PAIR ||
+  return variant == W4A4_GEMM_CTA_PAIR || layout == W4A4_LAYOUT_INT8 ||
          (variant == W4A4_GEMM_SINGLE_CTA && layout == W4A4_LAYOUT_FRAGMENT_MAJOR &&
           m >= kPairMinRows);
 }
@@ -912,6 +916,8 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
 
   // K > kMagicMaxK: the WIDE single-CTA kernel (exact int -> float of acc / 16)
   const bool wide = k > kMagicMaxK && !acc_out;
+  if (wide && layout == W4A4_LAYOUT_INT8)
+    return fail(W4A4_ERR_UNSUPPORTED, "int8 weights support K <= %d", kMagicMaxK);
   const int variant = wide ? W4A4_GEMM_NO_SPLIT : g_gemm_variant.load();
   const bool pair = !wide && use_pair_kernel(variant, layout, m);
   const int rows_per_wtile = pair ? 2 * kBlockW : kBlockW;
@@ -921,7 +927,14 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
   for (int i = 0; i < n_weights; ++i) {
     const w4a4_weight& w = weights[i];
     GemmSegment& s = p.seg[i];
-    if (layout == W4A4_LAYOUT_ROW_MAJOR) {
+    if (layout == W4A4_LAYOUT_INT8) {
+      if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, w.n,
+                              static_cast<uint64_t>(w.row_words) * 4, kBlockK, kBlockW,
+                              CU_TENSOR_MAP_SWIZZLE_128B, true))
+        return e;
+      s.scale = reinterpret_cast<const float*>(w.data + k / 4);
+      s.scale_stride = w.row_words;
+    } else if (layout == W4A4_LAYOUT_ROW_MAJOR) {
       if (int e = make_map_2d(&s.tmap_w, w.data, CU_TENSOR_MAP_DATA_TYPE_UINT32, k / 8, w.n,
                               static_cast<uint64_t>(w.row_words) * 4, kBlockK / 8, kBlockW,
                               CU_TENSOR_MAP_SWIZZLE_64B, true))
@@ -999,7 +1012,17 @@ int launch_gemm(const void* codes, const float* row_scale, int64_t m, int32_t k,
                                   gemm_smem_bytes(tok_tile), stream, 1, p));                  \
     }                                                                                         \
   } while (0)
-  if (wide) {
+  if (layout == W4A4_LAYOUT_INT8) {
+    const auto go = [&](auto kernel, uint64_t bit) -> int {
+      if (int e = ensure_smem_attr(dev, bit, kernel, kSmemLimit)) return e;
+      W4A4_CUDA_TRY(launch_kernel(kernel, grid, dim3(kPairI8Threads), gemm_pair_i8_smem_bytes(tok_tile),
+                                  stream, 2, p));
+      return W4A4_OK;
+    };
+    if (int e = acc_out ? go(w4a4_gemm_pair_i8_kernel<true>, 1ull << 29)
+                        : go(w4a4_gemm_pair_i8_kernel<false>, 1ull << 28))
+      return e;
+  } else if (wide) {
     const auto go = [&](auto kernel, uint64_t bit) -> int {
       if (int e = ensure_smem_attr(dev, bit, kernel, kSmemLimit)) return e;
       W4A4_CUDA_TRY(launch_kernel(kernel, grid, dim3(kGemmThreads), gemm_smem_bytes(tok_tile), stream, 1, p));
@@ -1155,6 +1178,22 @@ int w4a4_prefix_tables(const uint8_t* pad, int32_t batch, int32_t seq, const flo
                        void* stream) {
   return launch_prefix_tables(pad, batch, seq, inv_freq, half, key_valid, kv_len, cos_t, sin_t,
                               static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_repack_int8(const w4a4_weight* src, int32_t k, int32_t* dst, void* stream) {
+  if (!src || !dst) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (k <= 0 || k % 64 != 0) return fail(W4A4_ERR_INVALID, "K must be a multiple of 64, got %d", k);
+  if (k > kMagicMaxK) return fail(W4A4_ERR_UNSUPPORTED, "int8 weights support K <= %d", kMagicMaxK);
+  if (src->layout == W4A4_LAYOUT_INT8) return fail(W4A4_ERR_INVALID, "the source is already int8");
+  if (int e = check_weight(*src, k, 0)) return e;
+  if (!aligned(dst, 16)) return fail(W4A4_ERR_INVALID, "dst must be 16-byte aligned");
+  const int64_t total = static_cast<int64_t>(src->n) * (k / 8 + 1);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4096));
+  repack_int8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      src->data, src->n, k, src->row_words, src->layout == W4A4_LAYOUT_ROW_MAJOR ? kRowMajor : kFragmentMajor,
+      dst);
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
 }
 
 int w4a4_pad_rows(const int32_t* src, int32_t n, int32_t src_row_words, int32_t dst_row_words,

@@ -230,6 +230,7 @@ class W4A4PrefixLM:
             raise ValueError("the sharded MLP quantises its segmented rows with fp16 staging only")
         self._ws: dict = {}
         self._lib = nat.lib()
+        self._int8: dict = {}  # data_ptr of a packed weight -> its int8 repack (repack_int8)
 
     # ------------------------------------------------------------- builders
     @classmethod
@@ -317,8 +318,30 @@ class W4A4PrefixLM:
     def _stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
+    def repack_int8(self, names=("gate", "up")) -> None:
+        """Repack the named projections of every layer once into the int8
+        layout (w4a4_repack_int8: 16 x code bytes + scale per row, twice the
+        packed bytes), which the GEMM runs on CTA pairs with both operands in
+        shared memory.  Results are bit-identical to the packed weights'."""
+        for layer in self.layers:
+            for name in names:
+                w = getattr(layer, name)
+                if w.data_ptr() in self._int8:
+                    continue
+                fragment = name in ("gate", "up")
+                k = self.cfg.intermediate if name == "down" else self.cfg.hidden
+                dst = torch.empty((int(w.shape[0]), k // 4 + 4), dtype=torch.int32, device=self.device)
+                layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment else nat.LAYOUT_ROW_MAJOR
+                desc = nat.weights_array([(w.data_ptr(), int(w.shape[0]), int(w.shape[1]), layout)])
+                nat.check(self._lib.w4a4_repack_int8(desc, k, dst.data_ptr(), self._stream()))
+                self._int8[w.data_ptr()] = dst
+        torch.cuda.synchronize(self.device)
+
     def _gemm(self, ws: _Workspace, rows: int, k: int, weights, outs, fragment: bool) -> None:
         layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment else nat.LAYOUT_ROW_MAJOR
+        if self._int8 and all(w.data_ptr() in self._int8 for w in weights):
+            weights = [self._int8[w.data_ptr()] for w in weights]
+            layout = nat.LAYOUT_INT8
         descs = nat.weights_array([(w.data_ptr(), int(w.shape[0]), int(w.shape[1]), layout)
                                    for w in weights])
         ptrs = nat.pointer_array([o.data_ptr() for o in outs])

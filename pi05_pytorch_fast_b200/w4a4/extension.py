@@ -263,7 +263,12 @@ def quantize(x: torch.Tensor, staging: int | None = None, fmt: str = "int8",
 def gemm_from_codes(codes: torch.Tensor, scales: torch.Tensor, weights, fragment_major=False):
     """GEMM of int8 codes [M, K] in the GEMM byte order (``quantize(fmt="gemm")``)
     + scales [M] against 1..3 packed weights."""
+    if codes.dim() != 2 or codes.dtype != torch.int8 or not codes.is_contiguous():
+        raise ValueError("gemm_from_codes: codes must be a contiguous int8 [M, K] tensor")
     m, k = codes.shape
+    if (scales.dtype != torch.float32 or scales.numel() != m or not scales.is_contiguous()
+            or scales.device != codes.device):
+        raise ValueError("gemm_from_codes: scales must be a contiguous fp32 [M] tensor on the codes' device")
     layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment_major else nat.LAYOUT_ROW_MAJOR
     dev = codes.device
     with torch.cuda.device(dev):

@@ -182,6 +182,7 @@ GEMM_CASES = [
     (257, 1024, [384, 128], "row"),
     (200, 4096, [256], "fragment"),            # split-K candidate, fragment-major
     (776, 2048, [2048, 2048, 2048], "row"),    # split-K: more tiles than clusters
+    (776, 2048, [200, 328], "fragment"),       # CTA pair with a ragged last 256-row weight tile
 ]
 
 
@@ -226,6 +227,64 @@ def test_gemm_fp16_epilogue_bit_exact(m, k, ns, layout, variant):
         qw, sw = orc.weight_codes_scales(p, k, "row")
         ref = orc.dequant(orc.int_accumulate(qa, qw), sa, sw)
         assert_fp16_equal_and_within_tol(to_np(y), ref)
+
+
+# ----------------------------------------------------------------------------- int8 repack
+def repack_int8(w: torch.Tensor, k: int, fragment: bool) -> torch.Tensor:
+    layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment else nat.LAYOUT_ROW_MAJOR
+    dst = torch.empty((int(w.size(0)), k // 4 + 4), dtype=torch.int32, device=w.device)
+    desc = nat.weights_array([(w.data_ptr(), int(w.size(0)), int(w.size(1)), layout)])
+    nat.check(nat.lib().w4a4_repack_int8(desc, k, dst.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    return dst
+
+
+def gemm_int8(codes: torch.Tensor, scales, weights, acc_out: bool):
+    m, k = codes.shape
+    dt = torch.int32 if acc_out else torch.float16
+    ys = [torch.empty((m, int(w.size(0))), dtype=dt, device=codes.device) for w in weights]
+    descs = nat.weights_array([(w.data_ptr(), int(w.size(0)), int(w.size(1)), nat.LAYOUT_INT8) for w in weights])
+    outs = nat.pointer_array([y.data_ptr() for y in ys])
+    st = torch.cuda.current_stream().cuda_stream
+    if acc_out:
+        nat.check(nat.lib().w4a4_gemm_accumulators(codes.data_ptr(), m, k, len(weights), descs, outs, st))
+    else:
+        nat.check(nat.lib().w4a4_gemm(codes.data_ptr(), scales.data_ptr(), m, k, len(weights), descs, outs, st))
+    return ys
+
+
+def test_repack_int8_layout():
+    """Row n of the repack: 16 x code in the GEMM's K byte order, then the
+    fp32 scale and three zero words; both source layouts give the same."""
+    k, n = 256, 40
+    p = orc.random_packed_weight(n, k, seed=9)
+    qw, sw = orc.weight_codes_scales(p, k, "row")
+    want = np.zeros((n, k // 4 + 4), dtype=np.int32)
+    want.view(np.int8)[:, :k] = gemm_order(qw.astype(np.int8)) * 16
+    want[:, k // 4] = sw.view(np.int32)
+    for frag in (False, True):
+        w = to_dev(orc.preshuffle_wmma_weight(p, k)) if frag else _row_major(p)
+        np.testing.assert_array_equal(to_np(repack_int8(w, k, frag)), want)
+
+
+@pytest.mark.parametrize("m,k,ns,layout", GEMM_CASES)
+def test_int8_repacked_gemm_bit_exact(m, k, ns, layout):
+    """The SS CTA-pair kernel on repacked weights: accumulators bit-exact with
+    the oracle, fp16 outputs bit-exact with the dequant contract."""
+    rng = np.random.default_rng(m * 7 + k)
+    qa = rng.integers(-7, 8, size=(m, k)).astype(np.int8)
+    sa = (rng.random(m, dtype=np.float32) * np.float32(0.5) + np.float32(1e-3)).astype(np.float32)
+    packs = [orc.random_packed_weight(n, k, seed=5 * i + m) for i, n in enumerate(ns)]
+    frag = layout == "fragment"
+    ws = [to_dev(orc.preshuffle_wmma_weight(p, k)) if frag else _row_major(p) for p in packs]
+    w8 = [repack_int8(w, k, frag) for w in ws]
+    codes = to_dev(gemm_order(qa))
+    accs = gemm_int8(codes, None, w8, acc_out=True)
+    ys = gemm_int8(codes, to_dev(sa), w8, acc_out=False)
+    for p, acc, y in zip(packs, accs, ys):
+        qw, sw = orc.weight_codes_scales(p, k, "row")
+        ia = orc.int_accumulate(qa, qw)
+        np.testing.assert_array_equal(to_np(acc), ia)
+        assert_fp16_equal_and_within_tol(to_np(y), orc.dequant(ia, sa, sw))
 
 
 @pytest.mark.parametrize("m", [1, 15, 16, 17, 100, 255, 256, 257, 640, 768, 776, 1000])

@@ -87,11 +87,11 @@ def assert_codes_match_oracle(h: torch.Tensor, codes, scales, staging):
 
 
 # ----------------------------------------------------------------------------- GeGLU
-def test_gelu_of_every_finite_fp16_value_matches_torch():
-    """gelu_tanh(x) for all 63,488 finite fp16 x (up = 1, so h = fl16(gelu))."""
+def test_gelu_of_every_fp16_value_matches_torch():
+    """gelu_tanh(x) for all 65,536 fp16 bit patterns x, infinities and NaNs
+    included (up = 1, so h = fl16(gelu))."""
     bits = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16)
     vals = bits.view(torch.float16)
-    vals = vals[torch.isfinite(vals)]
     k = 16384
     m = -(-vals.numel() // k)
     gate = torch.zeros(m * k, dtype=torch.float16)
@@ -100,6 +100,27 @@ def test_gelu_of_every_finite_fp16_value_matches_torch():
     up = torch.ones_like(gate)
     _, _, h = geglu_quant(gate, up, nat.STAGING_FP16)
     ref = F.gelu(gate, approximate="tanh")
+    torch.cuda.synchronize()
+    assert_half_equal(h, ref)
+
+
+def test_geglu_product_of_every_finite_up_value_matches_torch():
+    """fl16(fl16(gelu(g)) * u) for all finite fp16 u, against gates whose GELU
+    spans tiny to large magnitudes, so products land in the fp16 subnormal
+    range, overflow to infinity and round at every exponent."""
+    bits = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16)
+    vals = bits.view(torch.float16)
+    vals = vals[torch.isfinite(vals)]
+    k = 16384
+    rows = -(-vals.numel() // k)
+    up = torch.zeros(rows * k, dtype=torch.float16)
+    up[: vals.numel()] = vals
+    gates = [-4.0, -0.75, -1e-3, 3e-5, 0.37, 1.0, 2.5, 300.0]
+    up = up.view(rows, k).repeat(len(gates), 1).to(DEV)
+    gate = torch.tensor(gates, dtype=torch.float16).repeat_interleave(rows)[:, None].expand(-1, k)
+    gate = gate.contiguous().to(DEV)
+    _, _, h = geglu_quant(gate, up, nat.STAGING_FP16)
+    ref = F.gelu(gate, approximate="tanh") * up
     torch.cuda.synchronize()
     assert_half_equal(h, ref)
 

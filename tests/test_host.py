@@ -170,6 +170,27 @@ def test_ops_refuse_cpu_tensors():
             op()
 
 
+def test_gemm_from_codes_checks_codes_and_scales():
+    """Codes must be contiguous int8 [M, K] and scales fp32 [M]: a sliced or
+    mistyped view is refused before anything reaches the library."""
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    codes = torch.zeros(4, 128, dtype=torch.int8)
+    scales = torch.ones(4)
+    w = [torch.zeros(16, 25, dtype=torch.int32)]
+    bad = [
+        (codes.float(), scales),
+        (torch.zeros(4, 256, dtype=torch.int8)[:, :128], scales),
+        (codes[0], scales),
+        (codes, scales.half()),
+        (codes, torch.ones(3)),
+        (codes, torch.ones(8)[::2]),
+    ]
+    for c, sc in bad:
+        with pytest.raises(ValueError, match="gemm_from_codes"):
+            ext.gemm_from_codes(c, sc, w)
+
+
 def test_extension_module_serves_as_the_reference_compiled_module():
     """The integration binding assigns this module to the reference's `_mod`
     (the object load_int4_gemm() returns): it must expose the compiled
