@@ -43,13 +43,14 @@ constexpr int kAttnKBytes = kAttnKeyBlock * kAttnHeadDim * 2;      // 32 KB
 constexpr int kAttnVBytes = kAttnHeadDim * kAttnKeyBlock * 2;      // 32 KB
 constexpr int kAttnStages = 2;
 constexpr int kAttnThreads = 192;                                  // 6 warps
-constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 1;      // q, k/v full/empty, s/p full/free, o
+constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 2;      // q, k/v full/empty, s/p full/free, o, p tail
 constexpr int kAttnSmem = kAttnQBytes + kAttnStages * (kAttnKBytes + kAttnVBytes) +
                           kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + 1024;
 // TMEM columns: O [0, 256), S buffers at 256 and 320 (64 each), P buffers at
-// 384 and 416 (32 columns: 64 fp16 per row).
+// 384 and 416 (32 columns: 64 fp16 per row), the tail blocks' constant P at
+// 448.
 constexpr uint32_t kAttnTmemCols = 512;
-constexpr uint32_t kAttnOCol = 0, kAttnSCol = 256, kAttnPCol = 384;
+constexpr uint32_t kAttnOCol = 0, kAttnSCol = 256, kAttnPCol = 384, kAttnPTailCol = 448;
 
 struct alignas(64) AttnParams {
   CUtensorMap tmap_q;   // fp16 {256 d, heads, L, B}, box {64, heads, 128 / heads, 1}, SW128
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(v_ring + kAttnStages * kAttnVBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kAttnNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* nkb_slot = reinterpret_cast<int*>(tmem_slot + 2);
+  int* nkb_slot = reinterpret_cast<int*>(tmem_slot + 2);  // [0]: real-key blocks, [1]: all blocks
   unsigned long long* kmask = reinterpret_cast<unsigned long long*>(tmem_slot + 4);  // 8-byte aligned
 
   const auto bar_q = [&] { return smem_addr(bars); };
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const auto bar_pfull = [&](int s) { return smem_addr(bars + 13 + s); };
   const auto bar_pfree = [&](int s) { return smem_addr(bars + 15 + s); };
   const uint32_t bar_o = smem_addr(bars + 17);
+  const uint32_t bar_ptail = smem_addr(bars + 18);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y;
@@ -171,6 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(bar_pfree(s), 1);
     }
     mbar_init(bar_o, 1);
+    mbar_init(bar_ptail, 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tmap_q);
@@ -183,19 +186,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
   pdl_wait();  // q, k, v and the masks are earlier kernels' outputs
   const uint8_t* kv_row = p.key_valid + static_cast<long long>(b) * L;
-  // Key blocks to visit: up to the last real key, or all of them when a
-  // padded (or past-the-end) query row is in the tile (uniform over L keys).
-  // One load per lane (tpt <= 128 tokens: up to 4 per lane), then a vote.
+  // Key blocks to visit.  Real query rows see the keys up to the last real
+  // one: blocks [0, nkr) run Q K^T and the softmax.  A padded (or
+  // past-the-end) query row's softmax is uniform over all L keys (p = 1 for
+  // every key < L): when the tile has one, blocks [nkr, nka) up to L are
+  // "tail" blocks, P V only, with a constant P (1 for padded rows, 0 for real
+  // ones, whose keys there are all padding).  One load per lane (tpt <= 128
+  // tokens: up to 4 per lane), then two votes.
   if (warp == 0) {
-    bool pad_row = false;
+    bool pad_row = false, real_row = false;
 #pragma unroll
     for (int i = 0; i < kAttnRows / 32; ++i) {
       const int t = t0 + lane + 32 * i;
-      if (lane + 32 * i < tpt) pad_row |= t >= L || !kv_row[t];
+      if (lane + 32 * i < tpt) {
+        const bool real = t < L && kv_row[t];
+        pad_row |= !real;
+        real_row |= real;
+      }
     }
     const int kv_len = p.kv_len[b];
     pad_row = __any_sync(0xffffffffu, pad_row);
-    if (lane == 0) *nkb_slot = ((pad_row ? L : max(0, min(L, kv_len))) + kAttnKeyBlock - 1) / kAttnKeyBlock;
+    real_row = __any_sync(0xffffffffu, real_row);
+    const int nkr = real_row ? (max(0, min(L, kv_len)) + kAttnKeyBlock - 1) / kAttnKeyBlock : 0;
+    if (lane == 0) {
+      nkb_slot[0] = nkr;
+      nkb_slot[1] = pad_row ? (L + kAttnKeyBlock - 1) / kAttnKeyBlock : nkr;
+    }
   }
   // 64-bit masks of the real keys of every block (warps 2-5; the loads of a
   // warp's blocks are independent and issued together)
@@ -214,44 +230,49 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int nkb = *nkb_slot;
+  const int nkb = nkb_slot[0];   // blocks with Q K^T and the softmax
+  const int nka = nkb_slot[1];   // all blocks (nka >= nkb)
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (lane 0)
-    if (lane == 0 && nkb > 0) {
-      mbar_arrive_expect_tx(bar_q(), kAttnQBytes);
-      for (int s = 0; s < kAttnSlices; ++s)
-        tma_load_4d(smem_addr(q_smem + s * (kAttnQBytes / kAttnSlices)), &p.tmap_q, 64 * s, 0, t0, b,
-                    bar_q());
-      int n = 0;
-      // key block kb: K into k slot kb % 2, V^T into v slot kb % 2
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int slot = kb & 1;
-        if (kb >= kAttnStages &&
-            !mbar_wait_spin(bar_kempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
-          break;
-        mbar_arrive_expect_tx(bar_kfull(slot), kAttnKBytes);
+    if (lane == 0 && nka > 0) {
+      if (nkb > 0) {
+        mbar_arrive_expect_tx(bar_q(), kAttnQBytes);
         for (int s = 0; s < kAttnSlices; ++s)
-          tma_load_3d(smem_addr(k_ring + slot * kAttnKBytes + s * (kAttnKBytes / kAttnSlices)), &p.tmap_k,
-                      64 * s, kb * kAttnKeyBlock, b, bar_kfull(slot));
-        if (kb >= kAttnStages &&
-            !mbar_wait_spin(bar_vempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit)) {
-          // the K copy of this block is in flight: account for it in the drain
-          volatile int no_abort = 0;
-          mbar_wait_bounded(bar_kfull(slot), (kb >> 1) & 1, &no_abort, err, kErrWaitDrain, limit);
-          break;
+          tma_load_4d(smem_addr(q_smem + s * (kAttnQBytes / kAttnSlices)), &p.tmap_q, 64 * s, 0, t0, b,
+                      bar_q());
+      }
+      int nk = 0, nv = 0;
+      // key block kb: K (blocks < nkb) into k slot kb % 2, V^T into v slot kb % 2
+      for (int kb = 0; kb < nka; ++kb) {
+        const int slot = kb & 1;
+        if (kb < nkb) {
+          if (kb >= kAttnStages &&
+              !mbar_wait_spin(bar_kempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
+            break;
+          mbar_arrive_expect_tx(bar_kfull(slot), kAttnKBytes);
+          for (int s = 0; s < kAttnSlices; ++s)
+            tma_load_3d(smem_addr(k_ring + slot * kAttnKBytes + s * (kAttnKBytes / kAttnSlices)), &p.tmap_k,
+                        64 * s, kb * kAttnKeyBlock, b, bar_kfull(slot));
+          ++nk;
         }
+        if (kb >= kAttnStages &&
+            !mbar_wait_spin(bar_vempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
+          break;
         mbar_arrive_expect_tx(bar_vfull(slot), kAttnVBytes);
         tma_load_3d(smem_addr(v_ring + slot * kAttnVBytes), &p.tmap_vt, kb * kAttnKeyBlock, 0, b,
                     bar_vfull(slot));
-        ++n;
+        ++nv;
       }
       // Drain: no copy may still be in flight at exit.
       volatile int no_abort = 0;
-      mbar_wait_bounded(bar_q(), 0, &no_abort, err, kErrWaitDrain, limit);
-      for (int i = 0; i < kAttnStages && i < n; ++i) {
-        const int last = i + ((n - 1 - i) / kAttnStages) * kAttnStages;
+      if (nkb > 0) mbar_wait_bounded(bar_q(), 0, &no_abort, err, kErrWaitDrain, limit);
+      for (int i = 0; i < kAttnStages && i < nk; ++i) {
+        const int last = i + ((nk - 1 - i) / kAttnStages) * kAttnStages;
         mbar_wait_bounded(bar_kfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
+      }
+      for (int i = 0; i < kAttnStages && i < nv; ++i) {
+        const int last = i + ((nv - 1 - i) / kAttnStages) * kAttnStages;
         mbar_wait_bounded(bar_vfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
       }
     }
@@ -262,7 +283,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t idesc_s = idesc_f16(kAttnRows, kAttnKeyBlock);
     const uint32_t idesc_o = idesc_f16(kAttnRows, kAttnHeadDim);
     const uint64_t qdesc = smem_desc_sw128(smem_addr(q_smem));
-    bool alive = nkb > 0 && warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit));
+    bool alive = nka > 0 &&
+                 (nkb == 0 || warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit)));
     // S(kb) = Q K(kb)^T into score buffer kb % 2
     const auto issue_s = [&](int kb) -> bool {
       const int slot = kb & 1;
@@ -290,32 +312,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       return true;
     };
-    if (alive) alive = issue_s(0);
-    for (int kb = 0; alive && kb < nkb; ++kb) {
+    if (alive && nkb > 0) alive = issue_s(0);
+    for (int kb = 0; alive && kb < nka; ++kb) {
       if (kb + 1 < nkb && !(alive = issue_s(kb + 1))) break;
       const int slot = kb & 1;
+      const bool tail = kb >= nkb;
       bool ok = mbar_wait_spin(bar_vfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
-      if (ok) ok = mbar_wait_spin(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
+      if (ok)
+        ok = tail ? mbar_wait_spin(bar_ptail, 0, abort_flag, err, kErrWaitUnpack, limit)
+                  : mbar_wait_spin(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
       if (!warp_all(ok)) {
         alive = false;
         break;
       }
       tc_fence_after();
       const uint64_t vdesc = smem_desc_sw128(smem_addr(v_ring + slot * kAttnVBytes));
+      const uint32_t pcol = tail ? kAttnPTailCol : kAttnPCol + slot * 32;
 #pragma unroll
       for (int kk = 0; kk < kAttnKeyBlock / 16; ++kk)
         if (issuer)
-          umma_f16_ts(tmem_base + kAttnOCol, tmem_base + kAttnPCol + slot * 32 + 8 * kk,
+          umma_f16_ts(tmem_base + kAttnOCol, tmem_base + pcol + 8 * kk,
                       vdesc + static_cast<uint64_t>(kk * 2), idesc_o, (kb | kk) != 0);
       if (issuer) {
         umma_commit(bar_vempty(slot));
-        umma_commit(bar_pfree(slot));
+        if (!tail) umma_commit(bar_pfree(slot));
       }
       __syncwarp();
     }
     // Every MMA of this CTA has completed once this commit arrives (also
     // after an abort: the epilogue's bounded wait then gives up or passes).
-    if (issuer && nkb > 0) umma_commit(bar_o);
+    if (issuer && nka > 0) umma_commit(bar_o);
     __syncwarp();
   } else {
     // ------------------------------------------------ softmax + epilogue (warps 2-5)
@@ -332,7 +358,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const bool q_real = tok < L && p.key_valid[static_cast<long long>(b) * L + tok];
     const float scale = p.scale_log2;
     float m = -INFINITY, l = 0.f;
-    bool alive = nkb > 0;
+    bool alive = nka > 0;
+    if (alive && nka > nkb) {
+      // the tail blocks' P: 1 (fp16) for a padded row, 0 for a real one
+      uint32_t pw[32];
+      const uint32_t one = q_real ? 0u : 0x3C003C00u;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) pw[c] = one;
+      tmem_st_32x32b_x32(tmem_base + lane_addr + kAttnPTailCol, pw);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_ptail);
+    }
     for (int kb = 0; alive && kb < nkb; ++kb) {
       const int slot = kb & 1;
       if (!warp_all(mbar_wait_spin(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
@@ -421,7 +459,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull(slot));
     }
-    // epilogue: O / l -> fp16 rows
+    // epilogue: O / l -> fp16 rows; a padded row's l is L (p = 1 for every
+    // key < L, the sum the normal blocks would reach)
+    if (!q_real) l = static_cast<float>(L);
     if (alive && warp_all(mbar_wait_bounded(bar_o, 0, abort_flag, err, kErrWaitAccum, limit))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
@@ -446,7 +486,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   // ---- teardown: every MMA has completed (bar_o, or the issuer's last
   // commits when it gave up) before TMEM is freed
-  if (warp == 1 && nkb > 0) {
+  if (warp == 1 && nka > 0) {
     volatile int no_abort = 0;
     mbar_wait_bounded(bar_o, 0, &no_abort, err, kErrWaitDrain, limit);
   }
