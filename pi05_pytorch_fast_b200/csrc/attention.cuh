@@ -397,13 +397,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                  : (L - j0 >= 64 ? ~0ull : ((1ull << (L - j0)) - 1ull));
       const unsigned vlo = static_cast<unsigned>(vm), vhi = static_cast<unsigned>(vm >> 32);
       float bm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // 4 chains: ILP
+      if (q_real && vm == ~0ull) {  // a real row, every key of the block real
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float v = q_real ? __uint_as_float(raw[c]) : 0.f;
-        const bool ok = ((c < 32 ? vlo >> c : vhi >> (c - 32)) & 1u) != 0;
-        const float mv = ok ? v : -INFINITY;
-        raw[c] = __float_as_uint(mv);
-        bm4[c & 3] = fmaxf(bm4[c & 3], mv);
+        for (int c = 0; c < 64; ++c) bm4[c & 3] = fmaxf(bm4[c & 3], __uint_as_float(raw[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float v = q_real ? __uint_as_float(raw[c]) : 0.f;
+          const bool ok = ((c < 32 ? vlo >> c : vhi >> (c - 32)) & 1u) != 0;
+          const float mv = ok ? v : -INFINITY;
+          raw[c] = __float_as_uint(mv);
+          bm4[c & 3] = fmaxf(bm4[c & 3], mv);
+        }
       }
       // scale > 0: the max of the scaled scores
       const float bmax = fmaxf(fmaxf(bm4[0], bm4[1]), fmaxf(bm4[2], bm4[3])) * scale;
@@ -467,19 +472,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim;
       const bool store = tok < L;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kAttnHeadDim; c0 += 16) {
-        uint32_t o[16];
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + kAttnOCol + c0, o);
-        tmem_ld_wait();
-        uint32_t w[8];
+      const uint32_t ocol = tmem_base + lane_addr + kAttnOCol;
+      // 32 columns per group, the next group's TMEM loads in flight while
+      // this one is scaled and stored
+      const auto emit = [&](const uint32_t (&o)[32], int c0) {
+        uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 16; ++i)
           w[i] = pack_half2_bits(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        if (store) {
-          *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
-        }
+        if (store)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint4*>(orow + c0 + 8 * i) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      };
+      uint32_t oa[32], ob[32];
+      const auto load = [&](uint32_t (&o)[32], int c0) {
+        tmem_ld_32x32b_x16(ocol + c0, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+        tmem_ld_32x32b_x16(ocol + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+      };
+      load(oa, 0);
+#pragma unroll
+      for (int c0 = 0; c0 < kAttnHeadDim; c0 += 64) {
+        tmem_ld_wait();
+        load(ob, c0 + 32);
+        emit(oa, c0);
+        tmem_ld_wait();
+        if (c0 + 64 < kAttnHeadDim) load(oa, c0 + 64);
+        emit(ob, c0 + 32);
       }
     }
   }

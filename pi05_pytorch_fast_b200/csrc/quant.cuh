@@ -732,15 +732,17 @@ __device__ __forceinline__ void q16k_row(unsigned char* base, int u, long long r
 // column shards delivers), read with one box per row; same smem layout.
 // GEGLU: xmap is the gate and umap the up projection (same shape), loaded
 // into two row buffers; the row quantised is gelu_tanh(gate) * up, formed in
-// phase A (geglu8) and, when h_out is not null, written there too; two CTAs
-// per SM so that the GELU's registers fit.  A table of the GELU's 65,536
-// fp16 results in shared memory instead of tanhf was measured slower (32.4
-// vs 31.9 us at M = 776, one persistent CTA of two rows per SM): the kernel
-// is bound by the latency of its row pipeline, not by the GELU's arithmetic.
+// a pass over each thread's line before phase A (geglu8, written back into
+// the gate row and, when h_out is not null, to h_out), so the row body keeps
+// the plain quant's registers and three CTAs fit per SM.  A table of the
+// GELU's 65,536 fp16 results in shared memory instead of tanhf was measured
+// slower (one persistent CTA of two rows per SM: 32.4 us at M = 776): the
+// kernel is bound by the latency of its row pipeline, not by the GELU's
+// arithmetic.
 constexpr int kQ16SmemGeglu = 2 * kQ16RowBytes + 1024;
 
 template <int MODE, bool SEGMENTED = false, bool GEGLU = false>
-__global__ void __launch_bounds__(kQuantThreads, GEGLU ? 2 : kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
+__global__ void __launch_bounds__(kQuantThreads, kQ16CtasPerSm) quant_rot_16k_fp16_kernel(
     const __grid_constant__ CUtensorMap xmap, long long m, void* __restrict__ codes,
     float* __restrict__ row_scale, float inv_sqrt_k, unsigned long long limit_ns,
     const __grid_constant__ CUtensorMap umap, __half* __restrict__ h_out, long long ldh) {
@@ -773,20 +775,21 @@ __global__ void __launch_bounds__(kQuantThreads, GEGLU ? 2 : kQ16CtasPerSm) quan
   mbar_wait_bounded(bar_a, 0, &abort_flag, &g_w4a4_device_error, kErrWaitTma, limit_ns);
   __syncthreads();  // a timed-out wait sets abort_flag first: every thread leaves together
   if (abort_flag) return;
-  const uint4* buf = reinterpret_cast<const uint4*>(base);
+  uint4* buf = reinterpret_cast<uint4*>(base);
+  if constexpr (GEGLU) {
+    // h = gelu(gate) * up over this thread's line, in place in the gate row
+    // (no other thread reads the line before phase A's barrier)
+#pragma unroll 2
+    for (int c = 0; c < 8; ++c) {
+      const int slot = 8 * u + (c ^ (u & 7));
+      const uint4 r = geglu8(buf[slot], buf[2048 + slot]);
+      buf[slot] = r;
+      if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 64 * u + 8 * c) = r;
+    }
+  }
   q16k_row<MODE>(
       base, u, row, codes, row_scale, inv_sqrt_k, warp_amax,
-      [&](int c) {
-        const int slot = 8 * u + (c ^ (u & 7));
-        if constexpr (GEGLU) {
-          const uint4 r = geglu8(buf[slot], buf[2048 + slot]);
-          if (h_out) *reinterpret_cast<uint4*>(h_out + row * ldh + 64 * u + 8 * c) = r;
-          return r;
-        } else {
-          return buf[slot];
-        }
-      },
-      [] { __syncthreads(); }, [] {});
+      [&](int c) { return buf[8 * u + (c ^ (u & 7))]; }, [] { __syncthreads(); }, [] {});
 }
 
 // Any K (multiple of 64) without rotation: one warp per row, two passes
