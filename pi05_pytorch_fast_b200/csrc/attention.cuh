@@ -8,7 +8,8 @@
 // padded query sees no key, so its softmax is uniform over all L keys (the
 // result of the all-masked row in the reference's fp32 softmax).
 //
-// Design (one CTA per 128 (token, head) rows of one observation):
+// Design (a cluster of two CTAs per 128 (token, head) rows of one
+// observation, each taking about half of the key blocks):
 //  * the CTA's rows are `128 / heads` consecutive tokens x all heads, so every
 //    row shares the one key/value head: Q is one 64 KB TMA load (4-D map
 //    {d, head, token, batch}, 128-byte swizzle), K and V^T stream in blocks
@@ -22,6 +23,9 @@
 //    exceeds it by more than 2^8; then they scale O by 1 / sum and store fp16
 //    rows;
 //  * key blocks past the last real key are skipped for tiles of real queries;
+//    for a padded query they are "tail" blocks, P V only with a constant P;
+//  * the pair exchanges halves of O (with each row's m and l) through
+//    distributed shared memory and each CTA finishes 128 output columns;
 //  * every wait is bounded (the device error word, an abort flag, teardown
 //    that drains its copies and MMAs and frees TMEM).
 // Softmax is base 2: s2 = acc * (scale * log2 e), p = exp2(s2 - m).
@@ -43,7 +47,12 @@ constexpr int kAttnKBytes = kAttnKeyBlock * kAttnHeadDim * 2;      // 32 KB
 constexpr int kAttnVBytes = kAttnHeadDim * kAttnKeyBlock * 2;      // 32 KB
 constexpr int kAttnStages = 2;
 constexpr int kAttnThreads = 192;                                  // 6 warps
-constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 2;      // q, k/v full/empty, s/p full/free, o, p tail
+constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 4;      // q, k/v full/empty, s/p full/free, o, p tail, pair
+// The pair's exchange (in the idle K/V ring once both CTAs' MMAs are done):
+// per row 128 fp32 of O (the columns the partner finishes, 16-byte chunk c
+// of row r at chunk c ^ (r & 31)) and a 16-byte (m, l) record.
+constexpr int kAttnXchgO = kAttnRows * (kAttnHeadDim / 2) * 4;        // 64 KB
+constexpr int kAttnXchgBytes = kAttnXchgO + kAttnRows * 16;
 constexpr int kAttnSmem = kAttnQBytes + kAttnStages * (kAttnKBytes + kAttnVBytes) +
                           kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + 1024;
 // TMEM columns: O [0, 256), S buffers at 256 and 320 (64 each), P buffers at
@@ -146,12 +155,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const auto bar_pfree = [&](int s) { return smem_addr(bars + 15 + s); };
   const uint32_t bar_o = smem_addr(bars + 17);
   const uint32_t bar_ptail = smem_addr(bars + 18);
+  const uint32_t bar_recv = smem_addr(bars + 19);   // the partner's O half and (m, l) landed
+  const uint32_t bar_rdy = smem_addr(bars + 20);    // the partner's ring is free to receive
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y;
   const int L = p.seq;
   const int tpt = kAttnRows / p.heads;  // tokens per tile
-  const int t0 = blockIdx.x * tpt;
+  // a cluster of two CTAs per tile: rank r takes about half of the tile's
+  // key blocks, then the two exchange halves of O and each finishes 128 of
+  // the 256 output columns
+  const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+  const int t0 = (blockIdx.x >> 1) * tpt;
   unsigned* err = &g_w4a4_device_error;
   const uint64_t limit = p.wait_limit_ns;
 
@@ -174,6 +189,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     mbar_init(bar_o, 1);
     mbar_init(bar_ptail, 4);
+    mbar_init(bar_recv, 1);
+    mbar_init(bar_rdy, 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tmap_q);
@@ -230,25 +247,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int nkb = nkb_slot[0];   // blocks with Q K^T and the softmax
-  const int nka = nkb_slot[1];   // all blocks (nka >= nkb)
+  const int nkb = nkb_slot[0];   // the tile's blocks with Q K^T and the softmax
+  const int nka = nkb_slot[1];   // all of the tile's blocks (nka >= nkb)
+  // This CTA's blocks: nn normal ones from n0, then nt tail ones from tb;
+  // local step i < n is block kb_of(i).
+  const int h0 = (nkb + 1) / 2, th = nkb + (nka - nkb + 1) / 2;
+  const int n0 = rank ? h0 : 0, nn = rank ? nkb - h0 : h0;
+  const int tb = rank ? th : nkb, nt = rank ? nka - th : th - nkb;
+  const int n = nn + nt;
+  const auto kb_of = [&](int i) { return i < nn ? n0 + i : tb + (i - nn); };
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (lane 0)
-    if (lane == 0 && nka > 0) {
-      if (nkb > 0) {
+    if (lane == 0 && n > 0) {
+      if (nn > 0) {
         mbar_arrive_expect_tx(bar_q(), kAttnQBytes);
         for (int s = 0; s < kAttnSlices; ++s)
           tma_load_4d(smem_addr(q_smem + s * (kAttnQBytes / kAttnSlices)), &p.tmap_q, 64 * s, 0, t0, b,
                       bar_q());
       }
       int nk = 0, nv = 0;
-      // key block kb: K (blocks < nkb) into k slot kb % 2, V^T into v slot kb % 2
-      for (int kb = 0; kb < nka; ++kb) {
-        const int slot = kb & 1;
-        if (kb < nkb) {
-          if (kb >= kAttnStages &&
-              !mbar_wait_spin(bar_kempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
+      // step i (block kb): K (normal blocks) into k slot i % 2, V^T into v slot i % 2
+      for (int i = 0; i < n; ++i) {
+        const int kb = kb_of(i), slot = i & 1;
+        if (i < nn) {
+          if (i >= kAttnStages &&
+              !mbar_wait_spin(bar_kempty(slot), ((i >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
             break;
           mbar_arrive_expect_tx(bar_kfull(slot), kAttnKBytes);
           for (int s = 0; s < kAttnSlices; ++s)
@@ -256,8 +280,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         64 * s, kb * kAttnKeyBlock, b, bar_kfull(slot));
           ++nk;
         }
-        if (kb >= kAttnStages &&
-            !mbar_wait_spin(bar_vempty(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
+        if (i >= kAttnStages &&
+            !mbar_wait_spin(bar_vempty(slot), ((i >> 1) - 1) & 1, abort_flag, err, kErrWaitEmpty, limit))
           break;
         mbar_arrive_expect_tx(bar_vfull(slot), kAttnVBytes);
         tma_load_3d(smem_addr(v_ring + slot * kAttnVBytes), &p.tmap_vt, kb * kAttnKeyBlock, 0, b,
@@ -266,7 +290,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // Drain: no copy may still be in flight at exit.
       volatile int no_abort = 0;
-      if (nkb > 0) mbar_wait_bounded(bar_q(), 0, &no_abort, err, kErrWaitDrain, limit);
+      if (nn > 0) mbar_wait_bounded(bar_q(), 0, &no_abort, err, kErrWaitDrain, limit);
       for (int i = 0; i < kAttnStages && i < nk; ++i) {
         const int last = i + ((nk - 1 - i) / kAttnStages) * kAttnStages;
         mbar_wait_bounded(bar_kfull(i), (last / kAttnStages) & 1, &no_abort, err, kErrWaitDrain, limit);
@@ -283,14 +307,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t idesc_s = idesc_f16(kAttnRows, kAttnKeyBlock);
     const uint32_t idesc_o = idesc_f16(kAttnRows, kAttnHeadDim);
     const uint64_t qdesc = smem_desc_sw128(smem_addr(q_smem));
-    bool alive = nka > 0 &&
-                 (nkb == 0 || warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit)));
-    // S(kb) = Q K(kb)^T into score buffer kb % 2
-    const auto issue_s = [&](int kb) -> bool {
-      const int slot = kb & 1;
-      bool ok = mbar_wait_spin(bar_kfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
-      if (ok && kb >= 2)
-        ok = mbar_wait_spin(bar_sfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
+    bool alive = n > 0 &&
+                 (nn == 0 || warp_all(mbar_wait_bounded(bar_q(), 0, abort_flag, err, kErrWaitTma, limit)));
+    // S(i) = Q K(kb_of(i))^T into score buffer i % 2
+    const auto issue_s = [&](int i) -> bool {
+      const int slot = i & 1;
+      bool ok = mbar_wait_spin(bar_kfull(slot), (i >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+      if (ok && i >= 2)
+        ok = mbar_wait_spin(bar_sfree(slot), ((i >> 1) - 1) & 1, abort_flag, err, kErrWaitAccum, limit);
       if (!warp_all(ok)) return false;
       tc_fence_after();
       const uint64_t kdesc = smem_desc_sw128(smem_addr(k_ring + slot * kAttnKBytes));
@@ -312,15 +336,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       return true;
     };
-    if (alive && nkb > 0) alive = issue_s(0);
-    for (int kb = 0; alive && kb < nka; ++kb) {
-      if (kb + 1 < nkb && !(alive = issue_s(kb + 1))) break;
-      const int slot = kb & 1;
-      const bool tail = kb >= nkb;
-      bool ok = mbar_wait_spin(bar_vfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
+    if (alive && nn > 0) alive = issue_s(0);
+    for (int i = 0; alive && i < n; ++i) {
+      if (i + 1 < nn && !(alive = issue_s(i + 1))) break;
+      const int slot = i & 1;
+      const bool tail = i >= nn;
+      bool ok = mbar_wait_spin(bar_vfull(slot), (i >> 1) & 1, abort_flag, err, kErrWaitTma, limit);
       if (ok)
         ok = tail ? mbar_wait_spin(bar_ptail, 0, abort_flag, err, kErrWaitUnpack, limit)
-                  : mbar_wait_spin(bar_pfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
+                  : mbar_wait_spin(bar_pfull(slot), (i >> 1) & 1, abort_flag, err, kErrWaitUnpack, limit);
       if (!warp_all(ok)) {
         alive = false;
         break;
@@ -332,7 +356,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int kk = 0; kk < kAttnKeyBlock / 16; ++kk)
         if (issuer)
           umma_f16_ts(tmem_base + kAttnOCol, tmem_base + pcol + 8 * kk,
-                      vdesc + static_cast<uint64_t>(kk * 2), idesc_o, (kb | kk) != 0);
+                      vdesc + static_cast<uint64_t>(kk * 2), idesc_o, (i | kk) != 0);
       if (issuer) {
         umma_commit(bar_vempty(slot));
         if (!tail) umma_commit(bar_pfree(slot));
@@ -341,7 +365,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     // Every MMA of this CTA has completed once this commit arrives (also
     // after an abort: the epilogue's bounded wait then gives up or passes).
-    if (issuer && nka > 0) umma_commit(bar_o);
+    if (issuer && n > 0) umma_commit(bar_o);
     __syncwarp();
   } else {
     // ------------------------------------------------ softmax + epilogue (warps 2-5)
@@ -358,8 +382,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const bool q_real = tok < L && p.key_valid[static_cast<long long>(b) * L + tok];
     const float scale = p.scale_log2;
     float m = -INFINITY, l = 0.f;
-    bool alive = nka > 0;
-    if (alive && nka > nkb) {
+    bool alive = n > 0;
+    if (alive && nt > 0) {
       // the tail blocks' P: 1 (fp16) for a padded row, 0 for a real one
       uint32_t pw[32];
       const uint32_t one = q_real ? 0u : 0x3C003C00u;
@@ -371,9 +395,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_ptail);
     }
-    for (int kb = 0; alive && kb < nkb; ++kb) {
-      const int slot = kb & 1;
-      if (!warp_all(mbar_wait_spin(bar_sfull(slot), (kb >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
+    for (int i = 0; alive && i < nn; ++i) {
+      const int kb = n0 + i, slot = i & 1;
+      if (!warp_all(mbar_wait_spin(bar_sfull(slot), (i >> 1) & 1, abort_flag, err, kErrWaitAccum, limit))) {
         alive = false;
         break;
       }
@@ -419,10 +443,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m = bmax;
         l *= f;
       }
-      if (__any_sync(0xffffffffu, grow && f != 0.f) && kb >= 1) {
+      if (__any_sync(0xffffffffu, grow && f != 0.f) && i >= 1) {
         // O holds P V of earlier blocks: wait for the last of them, rescale
         // this warp's rows (whole-warp TMEM access; others multiply by 1)
-        if (!warp_all(mbar_wait_spin(bar_pfree((kb - 1) & 1), ((kb - 1) >> 1) & 1, abort_flag, err,
+        if (!warp_all(mbar_wait_spin(bar_pfree((i - 1) & 1), ((i - 1) >> 1) & 1, abort_flag, err,
                                         kErrWaitAccum, limit))) {
           alive = false;
           break;
@@ -452,8 +476,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         pw[c] = pack_half2_bits(p0, p1);
       }
       l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
-      if (kb >= 2 && !warp_all(mbar_wait_spin(bar_pfree(slot), ((kb >> 1) - 1) & 1, abort_flag, err,
-                                                  kErrWaitAccum, limit))) {
+      if (i >= 2 && !warp_all(mbar_wait_spin(bar_pfree(slot), ((i >> 1) - 1) & 1, abort_flag, err,
+                                                 kErrWaitAccum, limit))) {
         alive = false;
         break;
       }
@@ -464,53 +488,96 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull(slot));
     }
-    // epilogue: O / l -> fp16 rows; a padded row's l is L (p = 1 for every
-    // key < L, the sum the normal blocks would reach)
-    if (!q_real) l = static_cast<float>(L);
-    if (alive && warp_all(mbar_wait_bounded(bar_o, 0, abort_flag, err, kErrWaitAccum, limit))) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim;
+    // ---- epilogue: the pair combines its two halves of the key range.  Once
+    // this CTA's MMAs are done its K/V ring is idle: it tells the partner,
+    // waits for the partner's ring to be idle, pushes the partner's 128
+    // columns of O with its (m, l) into it (st.async on the partner's
+    // bar_recv), and finishes its own 128 columns from its O and the
+    // partner's:  O = O_0 2^(m_0 - m) + O_1 2^(m_1 - m), m = max(m_0, m_1),
+    // likewise l.  A padded row (p = 1 everywhere, in both halves) adds the
+    // halves and divides by L.  A CTA without blocks contributes O = 0.
+    const bool have = n > 0;
+    bool ok = !have || (alive && warp_all(mbar_wait_bounded(bar_o, 0, abort_flag, err, kErrWaitAccum, limit)));
+    tc_fence_after();
+    if (warp == 2 && lane == 0) mbar_arrive_expect_tx(bar_recv, kAttnXchgBytes);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_remote(mapa_shared(bar_rdy, peer));
+    ok = warp_all(ok && mbar_wait_spin(bar_rdy, 0, abort_flag, err, kErrWaitAccum, limit));
+    const uint32_t ocol = tmem_base + lane_addr + kAttnOCol;
+    const uint32_t recv_local = smem_addr(k_ring);
+    if (ok) {
+      const uint32_t dst = mapa_shared(recv_local, peer), dst_bar = mapa_shared(bar_recv, peer);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t o[16];
+        if (have) {
+          tmem_ld_32x32b_x16(ocol + peer * 128 + 16 * cc, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = 4 * cc + j;
+          st_async_v4(dst + r * 512 + ((c ^ (r & 31)) << 4), o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3],
+                      dst_bar);
+        }
+      }
+      st_async_v4(dst + kAttnXchgO + r * 16, __float_as_uint(m), __float_as_uint(l), 0u, 0u, dst_bar);
+      ok = warp_all(mbar_wait_spin(bar_recv, 0, abort_flag, err, kErrWaitAccum, limit));
+    }
+    if (ok) {
+      const float4 ml = *reinterpret_cast<const float4*>(k_ring + kAttnXchgO + r * 16);
+      const float mp = ml.x, lp = ml.y;
+      float fo = 1.f, fp = 1.f, lt = static_cast<float>(L);
+      if (q_real) {
+        const float mm = fmaxf(m, mp);
+        fo = m == -INFINITY ? 0.f : ex2_approx(m - mm);
+        fp = mp == -INFINITY ? 0.f : ex2_approx(mp - mm);
+        lt = l * fo + lp * fp;
+      }
+      const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+      const float so = fo * inv, sp = fp * inv;
+      __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim + rank * 128;
       const bool store = tok < L;
-      const uint32_t ocol = tmem_base + lane_addr + kAttnOCol;
-      // 32 columns per group, the next group's TMEM loads in flight while
-      // this one is scaled and stored
-      const auto emit = [&](const uint32_t (&o)[32], int c0) {
-        uint32_t w[16];
+      const float* recv = reinterpret_cast<const float*>(k_ring) + r * 128;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[i] = pack_half2_bits(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        if (store)
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t o[16];
+        if (have) {
+          tmem_ld_32x32b_x16(ocol + rank * 128 + 16 * cc, o);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            *reinterpret_cast<uint4*>(orow + c0 + 8 * i) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-      };
-      uint32_t oa[32], ob[32];
-      const auto load = [&](uint32_t (&o)[32], int c0) {
-        tmem_ld_32x32b_x16(ocol + c0, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-        tmem_ld_32x32b_x16(ocol + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
-      };
-      load(oa, 0);
+          for (int j = 0; j < 16; ++j) o[j] = 0u;
+        }
+        uint32_t w[8];
 #pragma unroll
-      for (int c0 = 0; c0 < kAttnHeadDim; c0 += 64) {
-        tmem_ld_wait();
-        load(ob, c0 + 32);
-        emit(oa, c0);
-        tmem_ld_wait();
-        if (c0 + 64 < kAttnHeadDim) load(oa, c0 + 64);
-        emit(ob, c0 + 32);
+        for (int j = 0; j < 4; ++j) {
+          const int c = 4 * cc + j;
+          const float4 q = *reinterpret_cast<const float4*>(recv + ((c ^ (r & 31)) << 2));
+          w[2 * j] = pack_half2_bits(__uint_as_float(o[4 * j]) * so + q.x * sp,
+                                     __uint_as_float(o[4 * j + 1]) * so + q.y * sp);
+          w[2 * j + 1] = pack_half2_bits(__uint_as_float(o[4 * j + 2]) * so + q.z * sp,
+                                         __uint_as_float(o[4 * j + 3]) * so + q.w * sp);
+        }
+        if (store) {
+          *reinterpret_cast<uint4*>(orow + 16 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(orow + 16 * cc + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       }
     }
   }
 
   // ---- teardown: every MMA has completed (bar_o, or the issuer's last
   // commits when it gave up) before TMEM is freed
-  if (warp == 1 && nka > 0) {
+  if (warp == 1 && n > 0) {
     volatile int no_abort = 0;
     mbar_wait_bounded(bar_o, 0, &no_abort, err, kErrWaitDrain, limit);
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still write into its ring
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kAttnTmemCols);

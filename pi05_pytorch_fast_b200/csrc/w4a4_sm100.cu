@@ -728,9 +728,10 @@ int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const voi
   p.wait_limit_ns = g_wait_limit_ns.load();
   if (int e = ensure_smem_attr(dev, 1ull << 40, prefix_attention_kernel, kAttnSmem)) return e;
   const int tpt = kAttnRows / heads;
+  // two CTAs (a cluster) per tile of tpt tokens, each half of its key range
   W4A4_CUDA_TRY(launch_kernel(prefix_attention_kernel,
-                              dim3(static_cast<unsigned>((seq + tpt - 1) / tpt), static_cast<unsigned>(batch)),
-                              dim3(kAttnThreads), kAttnSmem, stream, 1, p));
+                              dim3(2u * static_cast<unsigned>((seq + tpt - 1) / tpt), static_cast<unsigned>(batch)),
+                              dim3(kAttnThreads), kAttnSmem, stream, 2, p));
   W4A4_CUDA_TRY(cudaGetLastError());
   return ok();
 }
