@@ -469,7 +469,8 @@ def run_ours(args, rank, world, local_rank, dist_on):
             "layers": args.layers,
             "staging": staging_name,
             "staging_parity": "fp32: pinned to the reference's golden vectors; fp16: the HIP kernel's "
-                              "rounding, parity unpinned (no reference output exists for it)",
+                              "rounding, pinned to the reference's quant_rot_rb source compiled for host "
+                              "threads (oracle/ref_quant)",
             "parallelism": (f"tp{world} MLP (N-sharded gate/up; per layer an NCCL all-to-all of the GeGLU "
                             "shards and an all-gather of the down_proj rows; attention replicated)")
                            if sharded else

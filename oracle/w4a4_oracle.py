@@ -21,10 +21,12 @@ Parity status
   against golden vectors produced by running the unmodified reference code
   (``tests/golden/make_golden.py``).
 * ``staging="fp16"`` (the reference's HIP ``quant_rot_rb``) is restated from
-  ``int4_gemm.cu:396-449``.  The HIP kernel cannot run on this hardware, so
-  this mode is "parity unpinned"; it is cross-checked against a second,
-  independent loop-level restatement of the kernel's thread structure
-  (``quant_rot_rb_loops``) instead.
+  ``int4_gemm.cu:396-449`` and PINNED to that kernel's own source:
+  ``oracle/ref_quant`` compiles it from the reference checkout for host
+  threads, and ``tests/test_oracle_ref_quant.py`` requires equal codes and
+  row scales (where the checkout is present; the library lands in
+  ``oracle/_ref``).  A second, loop-level restatement of the kernel's thread
+  structure (``quant_rot_rb_loops``) cross-checks it too.
 """
 
 from __future__ import annotations
@@ -127,7 +129,10 @@ def _quant_rows(xf: np.ndarray, rot: bool, staging: str, k: int):
             xf = fwht_fp32(xf)
         else:
             raise ValueError(f"unknown staging {staging!r}")
-    amax = np.abs(xf).max(axis=-1)
+    # The HIP kernels reduce with fmaxf (a NaN operand is ignored:
+    # int4_gemm.cu:426-436), the torch CPU code with amax (NaN propagates);
+    # they differ only for a row whose FWHT overflowed fp16.
+    amax = np.fmax.reduce(np.abs(xf), axis=-1) if staging == "fp16" else np.abs(xf).max(axis=-1)
     sdiv = (amax / F32(7.0)).astype(F32) + F32(1e-12)
     scale = (sdiv * inv_sqrt_k(k)).astype(F32) if rot else sdiv.astype(F32)
     with np.errstate(invalid="ignore"):

@@ -229,6 +229,22 @@ def test_gemm_fp16_epilogue_bit_exact(m, k, ns, layout, variant):
         assert_fp16_equal_and_within_tol(to_np(y), ref)
 
 
+@pytest.mark.filterwarnings("ignore::RuntimeWarning")
+def test_fp16_staging_quant_matches_the_reference_kernel():
+    """The CUDA quant (fp16 staging, the timed mode) against the reference's
+    own quant_rot_rb compiled for host threads (oracle/_ref): codes and row
+    scales bit for bit, an fp16-overflowing row included."""
+    import test_oracle_ref_quant as refq
+
+    lib = refq._ref_lib()
+    for k in (1024, 2048, 16384):
+        x = refq._inputs(k, seed=5)
+        codes, sc = refq.ref_quant(lib, x)
+        q_dev, s_dev = ext.quantize(to_dev(x), staging=nat.STAGING_FP16)
+        np.testing.assert_array_equal(to_np(q_dev), codes)
+        np.testing.assert_array_equal(to_np(s_dev).view(np.int32), sc.view(np.int32))
+
+
 # ----------------------------------------------------------------------------- int8 repack
 def repack_int8(w: torch.Tensor, k: int, fragment: bool) -> torch.Tensor:
     layout = nat.LAYOUT_FRAGMENT_MAJOR if fragment else nat.LAYOUT_ROW_MAJOR
