@@ -53,6 +53,13 @@ constexpr int kAttnNumBars = 1 + 4 * kAttnStages + 4 * 2 + 4;      // q, k/v ful
 // of row r at chunk c ^ (r & 31)) and a 16-byte (m, l) record.
 constexpr int kAttnXchgO = kAttnRows * (kAttnHeadDim / 2) * 4;        // 64 KB
 constexpr int kAttnXchgBytes = kAttnXchgO + kAttnRows * 16;
+// The output staging (two 64-column slices of 128 rows, 128-byte swizzle, the
+// TMA store's layout) in the ring after the exchange's receive region and
+// send record.
+constexpr int kAttnOutStage = 68 * 1024;
+static_assert(kAttnOutStage >= kAttnXchgBytes + kAttnRows * 16 && kAttnOutStage % 1024 == 0 &&
+                  kAttnOutStage + 2 * kAttnRows * 128 <= kAttnStages * (kAttnKBytes + kAttnVBytes),
+              "attention smem map");
 constexpr int kAttnSmem = kAttnQBytes + kAttnStages * (kAttnKBytes + kAttnVBytes) +
                           kAttnNumBars * 8 + 16 + (kAttnMaxKeys / 64) * 8 + 1024;
 // TMEM columns: O [0, 256), S buffers at 256 and 320 (64 each), P buffers at
@@ -65,6 +72,7 @@ struct alignas(64) AttnParams {
   CUtensorMap tmap_q;   // fp16 {256 d, heads, L, B}, box {64, heads, 128 / heads, 1}, SW128
   CUtensorMap tmap_k;   // fp16 {256 d, L, B}, box {64, 64, 1}, SW128
   CUtensorMap tmap_vt;  // fp16 {L, 256 d, B} (V transposed per observation), box {64, 256, 1}, SW128
+  CUtensorMap tmap_o;   // fp16 output, the same 4-D shape and box as tmap_q
   const uint8_t* key_valid;  // [B, L]: 1 = real token
   const int* kv_len;         // [B]: keys past this index are all padding
   __half* out;               // [B * L, ldo], row (b, t) columns head * 256 + d
@@ -502,31 +510,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (warp == 2 && lane == 0) mbar_arrive_expect_tx(bar_recv, kAttnXchgBytes);
     __syncwarp();
     if (lane == 0) mbar_arrive_remote(mapa_shared(bar_rdy, peer));
-    ok = warp_all(ok && mbar_wait_spin(bar_rdy, 0, abort_flag, err, kErrWaitAccum, limit));
     const uint32_t ocol = tmem_base + lane_addr + kAttnOCol;
-    const uint32_t recv_local = smem_addr(k_ring);
-    if (ok) {
-      const uint32_t dst = mapa_shared(recv_local, peer), dst_bar = mapa_shared(bar_recv, peer);
+    // this CTA's send staging: the partner's 128 columns of O in the idle Q
+    // buffer (same swizzled layout as the receive buffer), (m, l) after the
+    // receive region of the ring
+    float4* send = reinterpret_cast<float4*>(q_smem) + r * 32;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint32_t o[16];
-        if (have) {
-          tmem_ld_32x32b_x16(ocol + peer * 128 + 16 * cc, o);
-          tmem_ld_wait();
-        } else {
+    for (int cc = 0; cc < 8; ++cc) {
+      uint32_t o[16];
+      if (have && ok) {
+        tmem_ld_32x32b_x16(ocol + peer * 128 + 16 * cc, o);
+        tmem_ld_wait();
+      } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = 0u;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = 4 * cc + j;
-          st_async_v4(dst + r * 512 + ((c ^ (r & 31)) << 4), o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3],
-                      dst_bar);
-        }
+        for (int j = 0; j < 16; ++j) o[j] = 0u;
       }
-      st_async_v4(dst + kAttnXchgO + r * 16, __float_as_uint(m), __float_as_uint(l), 0u, 0u, dst_bar);
-      ok = warp_all(mbar_wait_spin(bar_recv, 0, abort_flag, err, kErrWaitAccum, limit));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        send[(4 * cc + j) ^ (r & 31)] = make_float4(__uint_as_float(o[4 * j]), __uint_as_float(o[4 * j + 1]),
+                                                    __uint_as_float(o[4 * j + 2]), __uint_as_float(o[4 * j + 3]));
     }
+    reinterpret_cast<float4*>(k_ring + kAttnXchgBytes)[r] = make_float4(m, l, 0.f, 0.f);
+    fence_proxy_async_smem();  // the bulk copy reads these through the async proxy
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 softmax warps
+    if (warp == 2) {
+      // one thread sends both blocks once the partner's ring is free
+      bool sent = ok && mbar_wait_spin(bar_rdy, 0, abort_flag, err, kErrWaitAccum, limit);
+      if (sent && lane == 0) {
+        const uint32_t dst = mapa_shared(smem_addr(k_ring), peer), dst_bar = mapa_shared(bar_recv, peer);
+        bulk_copy_s2cluster(dst, smem_addr(q_smem), kAttnXchgO, dst_bar);
+        bulk_copy_s2cluster(dst + kAttnXchgO, smem_addr(k_ring + kAttnXchgBytes), kAttnRows * 16, dst_bar);
+      }
+      __syncwarp();
+    }
+    ok = warp_all(ok && mbar_wait_spin(bar_recv, 0, abort_flag, err, kErrWaitAccum, limit));
     if (ok) {
       const float4 ml = *reinterpret_cast<const float4*>(k_ring + kAttnXchgO + r * 16);
       const float mp = ml.x, lp = ml.y;
@@ -539,9 +556,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float inv = lt > 0.f ? 1.0f / lt : 0.f;
       const float so = fo * inv, sp = fp * inv;
-      __half* orow = p.out + (static_cast<long long>(b) * L + tok) * p.ldo + head * kAttnHeadDim + rank * 128;
-      const bool store = tok < L;
       const float* recv = reinterpret_cast<const float*>(k_ring) + r * 128;
+      uint8_t* stage = k_ring + kAttnOutStage + r * 128;  // + slice * 16 KB, chunk c at c ^ (r & 7)
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         uint32_t o[16];
@@ -562,11 +578,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           w[2 * j + 1] = pack_half2_bits(__uint_as_float(o[4 * j + 2]) * so + q.z * sp,
                                          __uint_as_float(o[4 * j + 3]) * so + q.w * sp);
         }
-        if (store) {
-          *reinterpret_cast<uint4*>(orow + 16 * cc) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(orow + 16 * cc + 8) = make_uint4(w[4], w[5], w[6], w[7]);
-        }
+        // 16 columns = 2 chunks of 8 fp16 in slice cc / 4
+        const int slice = cc >> 2, c0 = 2 * (cc & 3);
+        uint8_t* srow = stage + slice * (kAttnRows * 128);
+        *reinterpret_cast<uint4*>(srow + ((c0 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(srow + (((c0 + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
       }
+    }
+    // one thread stores the two slices (rows past L are clipped by the TMA)
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (ok && warp == 2 && lane == 0) {
+      for (int sl = 0; sl < 2; ++sl)
+        tma_store_4d(&p.tmap_o, smem_addr(k_ring + kAttnOutStage + sl * (kAttnRows * 128)),
+                     static_cast<int>(rank) * 128 + 64 * sl, 0, t0, b);
+      bulk_commit_group();
+      bulk_wait_group0();
     }
   }
 

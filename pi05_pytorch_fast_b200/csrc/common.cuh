@@ -195,6 +195,27 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint32_t a, u
       ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(cluster_bar)
       : "memory");
 }
+// TMA store of a 4-D box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has completed
+// (its writes performed).
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into the shared memory of a CTA of the
+// cluster (dst and its mbarrier given by shared::cluster addresses), counted
+// as completed transaction bytes on that mbarrier.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                                    uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst_cluster), "r"(src), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
 // Arrive on an mbarrier given by its shared::cluster address (may be remote)
 // with the default (CTA-scope) release: a pure signal, for when the waiting
 // side needs no generic-memory data from this thread (TMEM stores are ordered

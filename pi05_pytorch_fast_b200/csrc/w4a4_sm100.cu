@@ -699,6 +699,11 @@ int launch_attention(void* q, int64_t ldq, const void* k, int64_t ldk, const voi
     if (int e = make_map(&p.tmap_q, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B))
       return e;
+    const uint64_t ostrides[3] = {kAttnHeadDim * 2, static_cast<uint64_t>(ldo) * 2,
+                                  static_cast<uint64_t>(ldo) * 2 * static_cast<uint64_t>(seq)};
+    if (int e = make_map(&p.tmap_o, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, dims, ostrides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
   }
   {
     const uint64_t dims[3] = {kAttnHeadDim, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch)};
