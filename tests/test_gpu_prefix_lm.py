@@ -308,3 +308,28 @@ def test_graph_replay_equals_eager_forward(gemma2):
     assert torch.equal(out.hidden.view(torch.int16), eager_h.view(torch.int16))
     for k1, k2 in zip(out.keys, eager_k):
         assert torch.equal(k1.view(torch.int16), k2.view(torch.int16))
+
+
+@pytest.mark.parametrize("lang_tokens", [64, 192, 200])  # prefixes of 640, 768 and 776 tokens
+def test_batched_forward_equals_each_observation_alone(gemma2, lang_tokens):
+    """Observations of one batch do not influence each other: a batch of
+    three (with 1, 40 and all real language tokens) gives, row for row, the
+    bits of each observation run alone -- every kernel works per row or per
+    observation, and an integer GEMM's outputs depend only on their row and
+    column, whatever the token tiles of the launch."""
+    model = plm.W4A4PrefixLM.from_gemma(gemma2, DEV)
+    embeds, pad = plm.synthetic_prefix(3, lang_tokens=lang_tokens, device=DEV, seed=11)
+    n_img = 576
+    pad[0, n_img + 1:] = False
+    pad[1, n_img + 40:] = False
+    pad[2, n_img:] = True
+    with torch.no_grad():
+        both = model.forward(embeds, pad)
+        hb = both.hidden.clone()
+        kb = [k.clone() for k in both.keys]
+        for i in range(3):
+            one = model.forward(embeds[i:i + 1].contiguous(), pad[i:i + 1].contiguous())
+            torch.cuda.synchronize()
+            assert torch.equal(one.hidden.view(torch.int16), hb[i:i + 1].view(torch.int16)), i
+            for k1, k2 in zip(one.keys, kb):
+                assert torch.equal(k1.view(torch.int16), k2[i:i + 1].view(torch.int16)), i
