@@ -236,6 +236,21 @@ int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, cons
                           const void* cos_t, const void* sin_t, void* k_out, int64_t ldko,
                           void* stream);
 
+/* Load-time weight pack on the GPU: Linear.weight [n, k] (row stride ldw
+ * elements; dtype 0 = fp32, 1 = fp16, 2 = bf16) -> the reference's packed INT4
+ * weight, bit for bit (pi05_fast/w4a4/pack.py:85-101 pack_linear_weight; the
+ * fragment-major order of :45-68 preshuffle_wmma_weight): fp32 FWHT when
+ * rotating (rotate = W4A4_ROTATE_BY_K: K in {1024, 2048, 16384}), times
+ * fl(1/sqrt K), per-row scale amax/7, codes rint(w/scale) clamped to +-7.
+ *   layout W4A4_LAYOUT_ROW_MAJOR: out int32 [n, out_row_words], out_row_words
+ *          >= k/8 + 1 (payload, scale word, zero padding: the K/8+8 load-time
+ *          pad of apply.py:68-69 included);
+ *   layout W4A4_LAYOUT_FRAGMENT_MAJOR: out [n, k/8 + 9] as the preshuffle
+ *          writes it (n even).
+ * k a multiple of 64, at most 16384. */
+int w4a4_pack_weight(const void* w, int32_t dtype, int64_t ldw, int32_t n, int32_t k, int32_t rotate,
+                     int32_t layout, int32_t* out, int32_t out_row_words, void* stream);
+
 /* Repack a packed weight (row-major or fragment-major, as w4a4_gemm takes
  * it) into W4A4_LAYOUT_INT8: dst int32 [src->n, k/4 + 4], 16-byte aligned.
  * The GEMM of the repacked weight is bit-identical to that of the packed

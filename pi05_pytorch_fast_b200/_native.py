@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "w4a4_quant_segments",
     "w4a4_pad_rows",
     "w4a4_repack_int8",
+    "w4a4_pack_weight",
     "w4a4_last_error",
     "w4a4_device_error",
     "w4a4_set_wait_limit_ns",
@@ -106,6 +107,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_quant_segments.argtypes = [vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_i32, c_i32, vp, vp, vp]
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_repack_int8.argtypes = [vp, c_i32, vp, vp]
+    lib.w4a4_pack_weight.argtypes = [vp, c_i32, c_i64, c_i32, c_i32, c_i32, c_i32, vp, c_i32, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]
     lib.w4a4_set_wait_limit_ns.argtypes = [c_u64]

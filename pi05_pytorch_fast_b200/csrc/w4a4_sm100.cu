@@ -24,6 +24,7 @@
 #include "gemm_pair.cuh"
 #include "attention.cuh"
 #include "layer.cuh"
+#include "pack.cuh"
 #include "quant.cuh"
 
 // Scratch of w4a4_int4_gemm_noalloc: the intermediate activation codes and
@@ -1184,6 +1185,40 @@ int w4a4_prefix_tables(const uint8_t* pad, int32_t batch, int32_t seq, const flo
                        void* stream) {
   return launch_prefix_tables(pad, batch, seq, inv_freq, half, key_valid, kv_len, cos_t, sin_t,
                               static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_pack_weight(const void* w, int32_t dtype, int64_t ldw, int32_t n, int32_t k, int32_t rotate,
+                     int32_t layout, int32_t* out, int32_t out_row_words, void* stream) {
+  if (k <= 0 || k % 64 != 0) return fail(W4A4_ERR_INVALID, "K must be a multiple of 64, got %d", k);
+  if (k > kPackMaxK) return fail(W4A4_ERR_UNSUPPORTED, "pack_weight supports K <= %d, got %d", kPackMaxK, k);
+  if (n < 0) return fail(W4A4_ERR_INVALID, "N must be non-negative, got %d", n);
+  if (dtype != kPackF32 && dtype != kPackF16 && dtype != kPackBF16)
+    return fail(W4A4_ERR_INVALID, "unknown weight dtype %d", dtype);
+  if (rotate != W4A4_ROTATE_BY_K && rotate != 0 && rotate != 1)
+    return fail(W4A4_ERR_INVALID, "rotate must be -1 (by K), 0 or 1, got %d", rotate);
+  const bool rot = rotate == W4A4_ROTATE_BY_K ? (k == 1024 || k == 2048 || k == 16384) : rotate == 1;
+  if (rot && (k & (k - 1))) return fail(W4A4_ERR_INVALID, "rotation needs a power-of-two K, got %d", k);
+  if (ldw < k) return fail(W4A4_ERR_INVALID, "weight row stride %lld < K", (long long)ldw);
+  if (layout == W4A4_LAYOUT_ROW_MAJOR) {
+    if (out_row_words < k / 8 + 1)
+      return fail(W4A4_ERR_INVALID, "row-major packed rows need >= K/8+1 words, got %d", out_row_words);
+  } else if (layout == W4A4_LAYOUT_FRAGMENT_MAJOR) {
+    if (out_row_words != k / 8 + 9 || k % 16 != 0 || n % 2 != 0)
+      return fail(W4A4_ERR_INVALID, "fragment-major packing needs the K/8+9 stride, K %% 16 == 0 and an even N");
+  } else {
+    return fail(W4A4_ERR_INVALID, "unknown weight layout %d", layout);
+  }
+  if (n == 0) return ok();
+  if (!w || !out) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  int dev;
+  if (int e = current_device(&dev)) return e;
+  const int smem = k * 4;
+  if (int e = ensure_smem_attr(dev, 1ull << 53, pack_weight_kernel, kPackMaxK * 4)) return e;
+  const float isk = static_cast<float>(1.0 / std::sqrt(static_cast<double>(k)));
+  pack_weight_kernel<<<static_cast<unsigned>(n), kPackThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      w, dtype, ldw, n, k, rot ? 1 : 0, isk, layout == W4A4_LAYOUT_ROW_MAJOR ? 0 : 1, out, out_row_words);
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
 }
 
 int w4a4_repack_int8(const w4a4_weight* src, int32_t k, int32_t* dst, void* stream) {

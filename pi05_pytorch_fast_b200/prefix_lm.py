@@ -108,6 +108,17 @@ def pack_layer(lin: dict, input_norm: torch.Tensor, post_norm: torch.Tensor, dev
         lin = dict(lin)
         cols = shard.cols(lin["gate"].shape[0])
         lin["gate"], lin["up"] = lin["gate"][cols], lin["up"][cols]
+    if torch.device(device).type == "cuda":
+        # the GPU pack kernel writes each layout directly
+        def row(w):
+            return wpack.pack_weight_cuda(w, "row", w.shape[1] // 8 + wpack.DEFAULT_ROW_PAD_WORDS, device=device)
+
+        def frag(w):
+            return wpack.pack_weight_cuda(w, "fragment", device=device)
+
+        return PackedLayer(q=row(lin["q"]), k=row(lin["k"]), v=row(lin["v"]), o=row(lin["o"]),
+                           gate=frag(lin["gate"]), up=frag(lin["up"]), down=row(lin["down"]),
+                           input_gain=_gain(input_norm, device), post_gain=_gain(post_norm, device))
     p = {n: wpack.pack_linear_weight(w, device=device) for n, w in lin.items()}
     return PackedLayer(
         q=_row_major(p["q"]), k=_row_major(p["k"]), v=_row_major(p["v"]), o=_row_major(p["o"]),

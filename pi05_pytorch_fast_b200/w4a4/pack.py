@@ -11,9 +11,10 @@ by ``scripts/pack_w4a4_prefix.py`` load unchanged:
 * fragment-major: payload flat as [K/16][N][2 words] followed by the N
   scales, declared [N, K/8 + 9] (pack.py:45-68).
 
-Weight packing runs on the CPU in fp32, as the reference's does, so packed
-checkpoints are bit-identical to the reference's.  None of this is on the
-inference path; the GEMM reads these layouts directly on the GPU.
+Weight packing runs in fp32, on the CPU as the reference's does, or on the
+GPU by this library's ``w4a4_pack_weight`` kernel (``pack_weight_cuda``); both
+are bit-identical to the reference's pack.  None of this is on the inference
+path; the GEMM reads these layouts directly on the GPU.
 """
 
 from __future__ import annotations
@@ -70,16 +71,58 @@ def unpack_nibbles(packed: torch.Tensor, k: int) -> torch.Tensor:
     return torch.where(nib >= 8, nib - 16, nib).to(torch.int32).reshape(*packed.shape[:-1], k)
 
 
+_PACK_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def pack_weight_cuda(weight: torch.Tensor, layout: str = "row", row_words: int | None = None,
+                     rotate: bool | None = None, device: torch.device | str | None = None) -> torch.Tensor:
+    """Linear.weight [N, K] -> packed int32 on a CUDA device by the
+    ``w4a4_pack_weight`` kernel, in its final layout: ``layout="row"`` gives
+    [N, row_words] (default K/8 + 1; K/8 + 8 is the load-time pad), and
+    ``"fragment"`` the fragment-major [N, K/8 + 9].  Bit-identical to
+    ``pack_linear_weight`` (and its padding / preshuffle)."""
+    from .. import _native as nat
+
+    if weight.dim() != 2:
+        raise ValueError(f"expected 2D weight, got {tuple(weight.shape)}")
+    n, k = weight.shape
+    dev = torch.device(device) if device is not None else weight.device
+    if dev.type != "cuda":
+        raise ValueError("pack_weight_cuda packs on a CUDA device")
+    w = weight.detach()
+    if w.dtype not in _PACK_DTYPES:
+        w = w.float()
+    w = w.to(dev)
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    if layout == "row":
+        words = k // 8 + 1 if row_words is None else row_words
+        lay = nat.LAYOUT_ROW_MAJOR
+    elif layout == "fragment":
+        words = k // 8 + WMMA_PRESHUFFLE_PAD_WORDS
+        lay = nat.LAYOUT_FRAGMENT_MAJOR
+    else:
+        raise ValueError(f"unknown layout {layout!r}")
+    out = torch.empty((n, words), dtype=torch.int32, device=dev)
+    rot = nat.ROTATE_BY_K if rotate is None else int(bool(rotate))
+    with torch.cuda.device(dev):
+        nat.check(nat.lib().w4a4_pack_weight(w.data_ptr(), _PACK_DTYPES[w.dtype], w.stride(0), n, k, rot, lay,
+                                             out.data_ptr(), words, torch.cuda.current_stream(dev).cuda_stream))
+    return out
+
+
 def pack_linear_weight(weight: torch.Tensor, rotate: bool | None = None,
                        device: torch.device | str = "cpu") -> torch.Tensor:
     """Linear.weight [N, K] -> int32 [N, K/8 + 1], computed in fp32 on ``device``
-    (CPU by default, as the reference packs).  Divisions are tensor/tensor so
-    that a CUDA pack is bit-identical to the CPU pack."""
+    (CPU by default, as the reference packs; a CUDA device runs the
+    ``w4a4_pack_weight`` kernel)."""
     if weight.dim() != 2:
         raise ValueError(f"expected 2D weight, got {tuple(weight.shape)}")
     n, k = weight.shape
     if k % 64 != 0:
         raise ValueError(f"K must be a multiple of 64 for gemm_iu4, got {k}")
+    if torch.device(device).type == "cuda":
+        return pack_weight_cuda(weight, rotate=rotate, device=device)
     w = weight.detach().to(device=device, dtype=torch.float32)
     if should_rotate(k, rotate):
         w = fwht_unnormalized(w) * (1.0 / math.sqrt(k))

@@ -218,3 +218,30 @@ def test_cuda_graph_capture_replays_identically():
     for a, b in zip(eager, outs):
         assert torch.equal(a, b)
     del g
+
+
+# ----------------------------------------------------------------------------- GPU weight pack
+@pytest.mark.parametrize("n,k", [(1, 64), (7, 1024), (256, 2048), (38, 16384), (12, 4096)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_gpu_weight_pack_equals_the_cpu_pack(n, k, dtype):
+    """w4a4_pack_weight (the load-time pack kernel) against the fp32 CPU pack
+    (pinned to the reference's golden vectors), in the row-major, padded and
+    fragment-major layouts; rotation by K and forced either way."""
+    from pi05_pytorch_fast_b200.w4a4 import pack as wpack
+
+    gen = torch.Generator().manual_seed(n * 7 + k)
+    w = (torch.randn(n, k, generator=gen) * 0.05).to(dtype)
+    w[0, : k // 2] = 0.0                       # a half-zero row
+    if n > 2:
+        w[2] = (torch.arange(k) % 15 - 7).to(dtype) * 0.125   # ties after the division
+    for rotate in (None, False, True):
+        if rotate and k & (k - 1):
+            continue
+        ref = wpack.pack_linear_weight(w.float(), rotate=rotate)
+        got = wpack.pack_weight_cuda(w, "row", rotate=rotate, device="cuda:0")
+        assert torch.equal(got.cpu(), ref)
+        got = wpack.pack_weight_cuda(w, "row", k // 8 + 8, rotate=rotate, device="cuda:0")
+        assert torch.equal(got.cpu(), wpack.pad_row_words(ref, k // 8 + 8))
+        if n % 2 == 0:
+            got = wpack.pack_weight_cuda(w, "fragment", rotate=rotate, device="cuda:0")
+            assert torch.equal(got.cpu(), wpack.preshuffle_wmma_weight(ref, k))

@@ -170,6 +170,26 @@ def test_ops_refuse_cpu_tensors():
             op()
 
 
+def test_pack_weight_argument_validation_without_gpu():
+    lib = nat.lib()
+    out = ctypes.c_void_p(16)
+    w = ctypes.c_void_p(16)
+    bad = [
+        (w, 0, 64, 4, 60, -1, nat.LAYOUT_ROW_MAJOR, out, 9),        # K not a multiple of 64
+        (w, 0, 32768, 4, 32768, -1, nat.LAYOUT_ROW_MAJOR, out, 4097),  # K above 16384
+        (w, 3, 64, 4, 64, -1, nat.LAYOUT_ROW_MAJOR, out, 9),        # dtype
+        (w, 0, 64, 4, 64, 2, nat.LAYOUT_ROW_MAJOR, out, 9),         # rotate
+        (w, 0, 192, 4, 192, 1, nat.LAYOUT_ROW_MAJOR, out, 25),      # rotation of a non-power-of-two K
+        (w, 0, 32, 4, 64, -1, nat.LAYOUT_ROW_MAJOR, out, 9),        # row stride below K
+        (w, 0, 64, 4, 64, -1, nat.LAYOUT_ROW_MAJOR, out, 8),        # rows without the scale word
+        (w, 0, 64, 4, 64, -1, nat.LAYOUT_FRAGMENT_MAJOR, out, 16),  # not the K/8+9 stride
+        (w, 0, 64, 3, 64, -1, nat.LAYOUT_FRAGMENT_MAJOR, out, 17),  # odd N
+        (w, 0, 64, 4, 64, -1, 7, out, 9),                           # layout
+    ]
+    for args in bad:
+        assert lib.w4a4_pack_weight(*args, None) != 0, args
+
+
 def test_gemm_from_codes_checks_codes_and_scales():
     """Codes must be contiguous int8 [M, K] and scales fp32 [M]: a sliced or
     mistyped view is refused before anything reaches the library."""
