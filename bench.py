@@ -589,6 +589,37 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
        "gate + up fp16 in, packed codes + scale out; replaces F.gelu(gate)*up and the down_proj quant")
     bw("rmsnorm_quant_k2048", normq, 3 * 2 * m * HIDDEN + m * HIDDEN // 2 + 4 * m,
        "x + delta in, x out (residual), packed codes + scale out; replaces add, RMSNorm and quant")
+    # prep + attention as the forward runs them (RoPE of q and k, V^T, the
+    # padded-prefix attention on CTA pairs), one observation batch
+    from pi05_pytorch_fast_b200 import prefix_lm as plm
+
+    batch, seq = args.batch, args.prefix
+    _, pad = plm.synthetic_prefix(batch, lang_tokens=seq - N_IMG, device=device, seed=3)
+    q = synthetic_activations(m, N_Q, device, seed=11)
+    kk = synthetic_activations(m, N_KV, device, seed=12)
+    vv = synthetic_activations(m, N_KV, device, seed=13)
+    key_valid = pad.to(torch.uint8).contiguous()
+    kv_len = (pad * torch.arange(1, seq + 1, device=device)).amax(dim=1).to(torch.int32)
+    pos = (torch.cumsum(pad.long(), 1) - 1).clamp_min(0).reshape(-1).float()
+    fr = pos[:, None] * model.inv_freq[None].float()
+    emb = torch.cat((fr, fr), dim=-1)
+    cos_t, sin_t = emb.cos().half().contiguous(), emb.sin().half().contiguous()
+    vt = torch.empty((batch, N_KV, nat.attn_vt_stride(seq)), dtype=torch.float16, device=device)
+    ao = torch.empty((m, N_Q), dtype=torch.float16, device=device)
+    kc = torch.empty_like(kk)
+
+    def attention():
+        nat.check(lib.w4a4_prefix_attention(q.data_ptr(), N_Q, kk.data_ptr(), N_KV, vv.data_ptr(), N_KV,
+                                            key_valid.data_ptr(), kv_len.data_ptr(), batch, seq, N_Q // N_KV,
+                                            vt.data_ptr(), ao.data_ptr(), N_Q, cos_t.data_ptr(), sin_t.data_ptr(),
+                                            kc.data_ptr(), N_KV, stream()))
+
+    t = graph_ms(attention, reps, dist_on, device, per_graph=10)
+    real = int(pad.sum())
+    flops = 4.0 * real * (N_Q // N_KV) * int(kv_len.max()) * N_KV  # S and P V of the real queries
+    out["attention_rope"] = {"ms": t, "tflops": flops / (t * 1e-3) / 1e12,
+                             "note": "RoPE + V transpose launch and the attention on CTA pairs; latency bound "
+                                     "at one observation (98 CTAs), tflops over the real queries' keys"}
     gu = out["gemm_gateup"]
     return {
         "roofline": {
