@@ -333,3 +333,16 @@ def test_batched_forward_equals_each_observation_alone(gemma2, lang_tokens):
             assert torch.equal(one.hidden.view(torch.int16), hb[i:i + 1].view(torch.int16)), i
             for k1, k2 in zip(one.keys, kb):
                 assert torch.equal(k1.view(torch.int16), k2[i:i + 1].view(torch.int16)), i
+
+
+def test_forward_with_int8_repacked_weights_is_bit_identical(gemma2):
+    """repack_int8 (the int8 layout run by the SS CTA-pair GEMM) for every
+    projection changes no bit of the forward."""
+    model = plm.W4A4PrefixLM.from_gemma(gemma2, DEV)
+    embeds, pad = plm.synthetic_prefix(2, device=DEV, seed=5)
+    with torch.no_grad():
+        ref = model.forward(embeds, pad).hidden.clone()
+        model.repack_int8(("q", "k", "v", "o", "gate", "up", "down"))
+        got = model.forward(embeds, pad).hidden.clone()
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
