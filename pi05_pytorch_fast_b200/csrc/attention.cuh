@@ -498,10 +498,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     // ---- epilogue: the pair combines its two halves of the key range.  Once
     // this CTA's MMAs are done its K/V ring is idle: it tells the partner,
-    // waits for the partner's ring to be idle, pushes the partner's 128
-    // columns of O with its (m, l) into it (st.async on the partner's
-    // bar_recv), and finishes its own 128 columns from its O and the
-    // partner's:  O = O_0 2^(m_0 - m) + O_1 2^(m_1 - m), m = max(m_0, m_1),
+    // stages the partner's 128 columns of O with its (m, l) in its idle Q
+    // buffer, and once the partner's ring is idle sends them there with bulk
+    // copies (completion counted on the partner's bar_recv); then it finishes
+    // its own 128 columns from its O and the partner's:  O = O_0 2^(m_0 - m) + O_1 2^(m_1 - m), m = max(m_0, m_1),
     // likewise l.  A padded row (p = 1 everywhere, in both halves) adds the
     // halves and divides by L.  A CTA without blocks contributes O = 0.
     const bool have = n > 0;
