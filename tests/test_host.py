@@ -170,6 +170,22 @@ def test_ops_refuse_cpu_tensors():
             op()
 
 
+def test_repack_int8_argument_validation_without_gpu():
+    lib = nat.lib()
+    dst = ctypes.c_void_p(16)
+    row = nat.weights_array([(16, 8, 2048 // 8 + 8, nat.LAYOUT_ROW_MAJOR)])
+    frag = nat.weights_array([(16, 8, 2048 // 8 + 9, nat.LAYOUT_FRAGMENT_MAJOR)])
+    already = nat.weights_array([(16, 8, 2048 // 4 + 4, nat.LAYOUT_INT8)])
+    assert lib.w4a4_repack_int8(row, 2000, dst, None) != 0          # K not a multiple of 64
+    assert lib.w4a4_repack_int8(row, 131072, dst, None) != 0        # above the magic-number K
+    assert lib.w4a4_repack_int8(already, 2048, dst, None) != 0      # already int8
+    assert lib.w4a4_repack_int8(row, 2048, ctypes.c_void_p(8), None) != 0  # unaligned dst
+    assert lib.w4a4_repack_int8(None, 2048, dst, None) != 0
+    bad_frag = nat.weights_array([(16, 8, 2048 // 8 + 8, nat.LAYOUT_FRAGMENT_MAJOR)])
+    assert lib.w4a4_repack_int8(bad_frag, 2048, dst, None) != 0     # fragment-major needs K/8+9
+    del frag
+
+
 def test_pack_weight_argument_validation_without_gpu():
     lib = nat.lib()
     out = ctypes.c_void_p(16)
