@@ -78,6 +78,9 @@ def parse_args():
                     help="comma-separated projections (q,k,v,o,gate,up,down) repacked once into the "
                          "int8 layout (SS CTA-pair GEMM); default: none")
     ap.add_argument("--roofline-reps", type=int, default=20)
+    ap.add_argument("--snapflow", action="store_true",
+                    help="config 4: the SnapFlow 1-NFE action chunk (SigLIP + the W4A4 prefix LM + the "
+                         "action expert); --batch observations per GPU (config 4: 64 over 8 GPUs)")
     ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k",
                                        "normquant", "geglu", "attn", "forward"),
                     default=None, help="run one op (or one forward) 3 times at the bench shape and "
@@ -640,6 +643,93 @@ def kernel_figures(args, model, m: int, staging: int, dist_on: bool, device) -> 
     }
 
 
+def run_snapflow(args, rank, world, local_rank, dist_on) -> dict:
+    """Config 4 on each rank: B observations per GPU through the whole
+    SnapFlow step in one CUDA graph (independent observations per GPU)."""
+    import torch
+
+    from pi05_pytorch_fast_b200 import prefix_lm as plm
+    from pi05_pytorch_fast_b200 import snapflow as sf
+    from pi05_pytorch_fast_b200.w4a4 import extension as ext
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ext.preload()
+    cfg = sf.SnapFlowConfig()
+    lm = plm.W4A4PrefixLM.random(cfg.lm, device, seed=1234)
+    policy = sf.SnapFlowPolicy(cfg, lm, device, seed=4321)
+    b = args.batch
+    obs = sf.synthetic_observation(cfg, b, seed=300 + rank, device=device)
+    with torch.no_grad():
+        # the three stages, each captured alone in a CUDA graph: SigLIP + the
+        # prefix assembly, the W4A4 prefix LM, the action expert
+        images, ids, mask, noise = obs
+        embeds, pad = policy.embed_prefix(images, ids, mask)
+        out = lm.forward(embeds, pad)
+        x_t, t1 = noise.to(policy.dtype), torch.ones(b, device=device)
+        reps = max(5, args.steps // 2)
+        stages = {
+            "siglip_and_prefix_assembly": graph_ms(lambda: policy.embed_prefix(images, ids, mask), reps,
+                                                   dist_on, device),
+            "w4a4_prefix_lm": graph_ms(lambda: lm.forward(embeds, pad, out=out), reps, dist_on, device),
+            "action_expert": graph_ms(lambda: policy.expert(x_t, t1, t1, pad, out.keys, out.values), reps,
+                                      dist_on, device),
+        }
+        g = sf.GraphedSnapFlow(policy, b)
+        g.run(*obs)
+        with ClockSampler(local_rank) as clocks:
+            ms = time_device(g.replay, args.steps, args.warmup, dist_on, device)
+        # end to end: pinned host observations in, actions out, every step
+        host = [t.cpu().pin_memory() for t in sf.synthetic_observation(cfg, b, seed=400 + rank)]
+        act_host = torch.empty(g.actions.shape, dtype=g.actions.dtype).pin_memory()
+
+        def e2e_step():
+            g.run(*host)
+            act_host.copy_(g.actions, non_blocking=True)
+        e2e_steps = max(5, min(args.steps, 30))
+        ms_e2e = time_device(e2e_step, e2e_steps, max(3, args.warmup), dist_on, device)
+    unit = "action chunks/s (observations/s; 50 x 32 actions each)"
+    return {
+        "metric": "pi0.5 SnapFlow 1-NFE action chunks per second (config 4)",
+        "value": job_throughput(ms, b, world),
+        "unit": unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 SigLIP-So400m and action expert (cuBLAS / SDPA); the prefix LM W4A4 (int4 x int4 "
+                 "-> int32 on tcgen05, fp16 activations)",
+        "data": "synthetic: random-init weights (N(0, 0.02)); 2 real cameras of 224 x 224 pixels ~ U[-1, 1], "
+                "the empty camera cached and pooled 4:1, 200 language tokens (52 real ids), noise ~ N(0, 1)",
+        "config": {
+            "workload": f"config 4: SnapFlow 1-NFE action chunk, {b} observation(s) per GPU per step "
+                        "(SigLIP on 2 cameras, 776-token W4A4 prefix LM, 18-layer expert over 50 "
+                        "action tokens)",
+            "batch_per_gpu": b,
+            "parallelism": f"dp{world} (independent observations per GPU, no collective in the step)",
+            "timing": "CUDA graph replay of the whole step, CUDA events, max over ranks",
+            "l2": "weights ~2.9 GB per step >> 126 MB L2 (no flush needed)",
+        },
+        "stages_ms": stages,
+        "gpu_launches": lm.launches_per_forward() * args.steps,
+        "gpu_launches_note": "kernels of libw4a4_sm100.so per timed region (the prefix LM); SigLIP and "
+                             "the expert run cuBLAS / PyTorch kernels",
+        "clocks": clocks.summary(),
+        "e2e": {
+            "value": job_throughput(ms_e2e, b, world),
+            "unit": unit,
+            "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in host)),
+            "d2h_bytes_per_step": int(act_host.numel() * act_host.element_size()),
+            "mode": "GraphedSnapFlow.run: every step's pinned-host images, language ids, mask and noise "
+                    "copied in and the actions copied out inside the timed region (one stream)",
+            "steps": e2e_steps,
+        },
+    }
+
+
 def run_sweep(args) -> None:
     """Config 3 on one GPU: the forward at every (prefix, batch) of the
     sweep, one model, one JSON line per point with its own clock record and
@@ -820,6 +910,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and args.snapflow:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "config 4 runs lerobot's PI05 policy "
+                              "(SigLIP, expert, SnapFlow step), which is not part of the reference "
+                              "checkout; only its W4A4 path has a CPU implementation"}), flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
@@ -836,7 +932,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        res = run_ours(args, rank, world, local_rank, dist_on)
+        res = (run_snapflow if args.snapflow else run_ours)(args, rank, world, local_rank, dist_on)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

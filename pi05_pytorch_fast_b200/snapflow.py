@@ -1,0 +1,380 @@
+"""Config 4: one pi0.5 SnapFlow 1-NFE action chunk around the W4A4 prefix LM.
+
+The reference runs this step through lerobot's ``PI05Pytorch`` with the
+SnapFlow student subclass (pi05_fast/snapflow_pi05.py:127-195:
+``sample_actions_1step`` -> ``embed_prefix`` -> prefix LM with a KV cache ->
+``denoise_step`` at time 1 with the target-time MLP -> ``x_t - v_t``) and the
+batched SigLIP prefix of pi05_fast/rocm_pi05_optim.py:88-133 (the real
+cameras through SigLIP in one batch; the empty camera is a constant -1 image
+whose embedding is computed once and sum-pooled 4:1 to 64 tokens, so the
+prefix is 256 + 256 + 64 image tokens + 200 language tokens = 776).  The
+prefix LM runs fp16 (rocm_pi05_optim.py:146-154); SigLIP and the action
+expert run bf16.
+
+lerobot is not part of the reference, so the neighbours of the W4A4 path are
+rebuilt here from their published structure, with random weights:
+
+* SigLIP-So400m (transformers' ``SiglipVisionModel``: width 1152, 27 layers,
+  16 heads, MLP 4304, patch 14 at 224 x 224 -> 256 tokens, no pooling head)
+  and PaliGemma's multi-modal projector (1152 -> 2048), bf16, cuBLAS /
+  PyTorch SDPA, as the reference runs them;
+* the language embedding table (257,152 x 2048) scaled by sqrt(2048), as
+  Gemma scales embeddings;
+* the W4A4 prefix LM of this package (``prefix_lm.W4A4PrefixLM``), whose
+  per-layer keys (after RoPE) and values are the expert's prefix KV cache,
+  cast to bf16 as ``clone_kv_cache(..., dtype=expert dtype)`` does
+  (snapflow_pi05.py:155-157);
+* the Gemma-300M action expert (width 1024, 18 layers, MLP 4096 GeGLU, 8
+  query heads / 1 KV head, head_dim 256) with pi0.5's adaptive RMSNorm (scale,
+  shift and a residual gate from the time condition); its 50 action tokens
+  attend to every real prefix token and to each other (the suffix attention
+  mask [1, 0, ..., 0] of snapflow_pi05.py:114 makes one bidirectional block),
+  at positions ``sum(prefix mask) + i`` (snapflow_pi05.py:150-151);
+* the suffix embedding of snapflow_pi05.py:67-116: the sinusoidal time
+  embedding (periods log-spaced from min_period to max_period), plus the
+  SnapFlow target-time MLP (Linear, SiLU, Linear) of the target time, then
+  the time MLP (Linear, SiLU, Linear, SiLU) -> the adaptive-norm condition;
+  ``action_in_proj`` / ``action_out_proj`` (32 <-> 1024).
+
+The exact lerobot module layout (and so a checkpoint's tensor names) is not
+reproduced; shapes, dtypes, masks, positions and the order of operations
+are.  ``GraphedSnapFlow`` captures the whole step (SigLIP, the prefix
+assembly, the W4A4 prefix LM, the expert) in one CUDA graph.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import prefix_lm as plm
+
+
+@dataclass(frozen=True)
+class SnapFlowConfig:
+    """BASELINE config 4's shapes."""
+
+    # SigLIP-So400m
+    vision_hidden: int = 1152
+    vision_intermediate: int = 4304
+    vision_layers: int = 27
+    vision_heads: int = 16
+    image_size: int = 224
+    patch: int = 14
+    real_cameras: int = 2
+    empty_pool: int = 4          # the empty camera's 256 tokens sum-pooled 4:1 -> 64
+    # language
+    lang_tokens: int = 200
+    vocab: int = 257152
+    # the W4A4 prefix LM (Gemma-2B)
+    lm: plm.PrefixLMConfig = field(default_factory=plm.PrefixLMConfig)
+    # the action expert (Gemma-300M)
+    expert_hidden: int = 1024
+    expert_intermediate: int = 4096
+    expert_layers: int = 18
+    expert_heads: int = 8
+    expert_kv_heads: int = 1
+    head_dim: int = 256
+    rms_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    # the flow step
+    chunk: int = 50
+    action_dim: int = 32
+    min_period: float = 4e-3
+    max_period: float = 4.0
+
+    @property
+    def image_tokens(self) -> int:
+        return (self.image_size // self.patch) ** 2
+
+    @property
+    def prefix_len(self) -> int:
+        return self.real_cameras * self.image_tokens + self.image_tokens // self.empty_pool + self.lang_tokens
+
+
+def sinusoidal_time_embedding(t: torch.Tensor, dim: int, min_period: float, max_period: float) -> torch.Tensor:
+    """[B] times -> [B, dim]: sin and cos of t * 2 pi / period for dim / 2
+    periods spaced geometrically from min_period to max_period (computed in
+    float64, returned float32)."""
+    if dim % 2:
+        raise ValueError("dim must be even")
+    frac = torch.linspace(0.0, 1.0, dim // 2, dtype=torch.float64, device=t.device)
+    period = min_period * (max_period / min_period) ** frac
+    arg = (2.0 * math.pi / period)[None, :] * t.to(torch.float64)[:, None]
+    return torch.cat((torch.sin(arg), torch.cos(arg)), dim=1).float()
+
+
+def pool_tokens(emb: torch.Tensor, pool: int) -> torch.Tensor:
+    """[B, T, D] -> [B, T / pool, D]: the sum of each run of `pool`
+    consecutive tokens (the empty camera's 4:1 pool)."""
+    b, t, d = emb.shape
+    if t % pool:
+        raise ValueError(f"{t} tokens do not pool {pool}:1")
+    return emb.reshape(b, t // pool, pool, d).sum(dim=2)
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def rope_tables(positions: torch.Tensor, head_dim: int, theta: float, dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    """positions [B, S] -> cos, sin [B, 1, S, head_dim] (fp32 angles, cast to
+    dtype), the rotary tables of transformers' Gemma."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=positions.device) / head_dim))
+    ang = positions.float()[..., None] * inv
+    emb = torch.cat((ang, ang), dim=-1)[:, None]
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+class AdaRMSNorm(nn.Module):
+    """RMSNorm conditioned on the flow time: [scale, shift, gate] =
+    Linear(cond); y = rms_norm(x) * (1 + scale) + shift (fp32, cast back);
+    gate multiplies the sublayer's output on the residual."""
+
+    def __init__(self, dim: int, cond_dim: int, eps: float):
+        super().__init__()
+        self.eps = eps
+        self.mod = nn.Linear(cond_dim, 3 * dim)
+
+    def forward(self, x: torch.Tensor, cond: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        scale, shift, gate = self.mod(cond)[:, None, :].chunk(3, dim=-1)
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
+        return (y * (1.0 + scale.float()) + shift.float()).to(x.dtype), gate
+
+
+class ExpertLayer(nn.Module):
+    """One Gemma-300M decoder layer of the action expert with adaptive norms;
+    attention over [prefix KV cache ; own keys]."""
+
+    def __init__(self, cfg: SnapFlowConfig):
+        super().__init__()
+        h, hd = cfg.expert_hidden, cfg.head_dim
+        self.heads, self.kv_heads, self.hd = cfg.expert_heads, cfg.expert_kv_heads, hd
+        self.in_norm = AdaRMSNorm(h, h, cfg.rms_eps)
+        self.post_norm = AdaRMSNorm(h, h, cfg.rms_eps)
+        self.q = nn.Linear(h, self.heads * hd, bias=False)
+        self.k = nn.Linear(h, self.kv_heads * hd, bias=False)
+        self.v = nn.Linear(h, self.kv_heads * hd, bias=False)
+        self.o = nn.Linear(self.heads * hd, h, bias=False)
+        self.gate = nn.Linear(h, cfg.expert_intermediate, bias=False)
+        self.up = nn.Linear(h, cfg.expert_intermediate, bias=False)
+        self.down = nn.Linear(cfg.expert_intermediate, h, bias=False)
+
+    def forward(self, x, cond, cos, sin, prefix_k, prefix_v, mask):
+        """x [B, S, h]; prefix_k / prefix_v [B, kv_heads, L, hd] (keys after
+        RoPE); mask [B, 1, S, L + S] bool (True = attend)."""
+        b, s, _ = x.shape
+        n, g1 = self.in_norm(x, cond)
+        q = self.q(n).view(b, s, self.heads, self.hd).transpose(1, 2)
+        k = self.k(n).view(b, s, self.kv_heads, self.hd).transpose(1, 2)
+        v = self.v(n).view(b, s, self.kv_heads, self.hd).transpose(1, 2)
+        q = q * cos + rotate_half(q) * sin
+        k = k * cos + rotate_half(k) * sin
+        k = torch.cat((prefix_k, k), dim=2)
+        v = torch.cat((prefix_v, v), dim=2)
+        a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=self.kv_heads != self.heads)
+        x = x + g1 * self.o(a.transpose(1, 2).reshape(b, s, self.heads * self.hd))
+        n, g2 = self.post_norm(x, cond)
+        return x + g2 * self.down(F.gelu(self.gate(n), approximate="tanh") * self.up(n))
+
+
+class ActionExpert(nn.Module):
+    """The suffix path of the SnapFlow step: time embedding (+ target-time
+    MLP), the time MLP -> condition, action_in_proj, the expert layers over
+    the prefix KV cache, the final adaptive norm and action_out_proj."""
+
+    def __init__(self, cfg: SnapFlowConfig):
+        super().__init__()
+        h = cfg.expert_hidden
+        self.cfg = cfg
+        self.action_in_proj = nn.Linear(cfg.action_dim, h)
+        self.action_out_proj = nn.Linear(h, cfg.action_dim)
+        self.time_mlp_in = nn.Linear(h, h)
+        self.time_mlp_out = nn.Linear(h, h)
+        hid = max(h, 256)
+        self.target_time_mlp = nn.Sequential(nn.Linear(h, hid), nn.SiLU(), nn.Linear(hid, h))
+        self.layers = nn.ModuleList(ExpertLayer(cfg) for _ in range(cfg.expert_layers))
+        self.final_norm = AdaRMSNorm(h, h, cfg.rms_eps)
+
+    def condition(self, t: torch.Tensor, target_t: torch.Tensor | None) -> torch.Tensor:
+        cfg, dt = self.cfg, self.time_mlp_in.weight.dtype
+        emb = sinusoidal_time_embedding(t, cfg.expert_hidden, cfg.min_period, cfg.max_period).to(dt)
+        if target_t is not None:
+            tt = sinusoidal_time_embedding(target_t, cfg.expert_hidden, cfg.min_period, cfg.max_period)
+            emb = emb + self.target_time_mlp(tt.to(dt))
+        return F.silu(self.time_mlp_out(F.silu(self.time_mlp_in(emb))))
+
+    def forward(self, x_t, t, target_t, prefix_pad, keys, values) -> torch.Tensor:
+        """x_t [B, chunk, action_dim] in the expert's dtype; prefix_pad bool
+        [B, L]; keys / values: per layer [B, L, kv_heads * hd] (any float
+        dtype).  Returns v_t [B, chunk, action_dim] in the expert's dtype."""
+        cfg = self.cfg
+        dt = self.action_in_proj.weight.dtype
+        b, s = x_t.shape[0], cfg.chunk
+        cond = self.condition(t, target_t)
+        x = self.action_in_proj(x_t)
+        # suffix positions continue after the real prefix tokens
+        pos = prefix_pad.sum(dim=1, keepdim=True) + torch.arange(s, device=x.device)[None, :]
+        cos, sin = rope_tables(pos, cfg.head_dim, cfg.rope_theta, dt)
+        mask = torch.cat((prefix_pad[:, None, None, :].expand(b, 1, s, prefix_pad.shape[1]),
+                          torch.ones((b, 1, s, s), dtype=torch.bool, device=x.device)), dim=3)
+        kvh, hd = cfg.expert_kv_heads, cfg.head_dim
+        for layer, k, v in zip(self.layers, keys, values):
+            pk = k.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
+            pv = v.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
+            x = layer(x, cond, cos, sin, pk, pv, mask)
+        x, _ = self.final_norm(x, cond)
+        return self.action_out_proj(x[:, -s:])
+
+
+class VisionPrefix(nn.Module):
+    """SigLIP-So400m + PaliGemma's projector, and the prefix assembly of
+    rocm_pi05_optim.py:88-133 (real cameras batched, the empty camera's
+    cached embedding pooled 4:1, then the language embeddings)."""
+
+    def __init__(self, cfg: SnapFlowConfig):
+        super().__init__()
+        from transformers import SiglipVisionConfig, SiglipVisionModel
+
+        vcfg = SiglipVisionConfig(hidden_size=cfg.vision_hidden, intermediate_size=cfg.vision_intermediate,
+                                  num_hidden_layers=cfg.vision_layers, num_attention_heads=cfg.vision_heads,
+                                  image_size=cfg.image_size, patch_size=cfg.patch, vision_use_head=False)
+        self.cfg = cfg
+        self.siglip = SiglipVisionModel(vcfg)
+        self.projector = nn.Linear(cfg.vision_hidden, cfg.lm.hidden)
+        self.register_buffer("empty_cam", torch.zeros(0), persistent=False)
+
+    def embed_images(self, images: torch.Tensor) -> torch.Tensor:
+        """[N, 3, H, W] -> [N, tokens, lm hidden] in the tower's dtype."""
+        dt = self.projector.weight.dtype
+        return self.projector(self.siglip(pixel_values=images.to(dt)).last_hidden_state)
+
+    @torch.no_grad()
+    def cache_empty_camera(self) -> None:
+        """The empty camera is a constant -1 image: its pooled embedding is
+        computed once (rocm_pi05_optim.py:72-87)."""
+        cfg, dev = self.cfg, self.projector.weight.device
+        blank = torch.full((1, 3, cfg.image_size, cfg.image_size), -1.0, device=dev)
+        self.empty_cam = pool_tokens(self.embed_images(blank), cfg.empty_pool)
+
+    def forward(self, images: torch.Tensor, lang_emb: torch.Tensor, lang_mask: torch.Tensor):
+        """images [B, real_cameras, 3, H, W]; lang_emb [B, T, hidden] (already
+        scaled); lang_mask bool [B, T] -> (embeds fp16 [B, L, hidden], pad bool
+        [B, L])."""
+        b, ncam = images.shape[:2]
+        emb = self.embed_images(images.transpose(0, 1).reshape(ncam * b, *images.shape[2:]))
+        emb = emb.view(ncam, b, emb.shape[1], emb.shape[2])
+        parts = [emb[i] for i in range(ncam)] + [self.empty_cam.expand(b, -1, -1)]
+        n_img = sum(p.shape[1] for p in parts)
+        embeds = torch.cat([p.to(torch.float16) for p in parts] + [lang_emb.to(torch.float16)], dim=1)
+        pad = torch.cat((torch.ones((b, n_img), dtype=torch.bool, device=lang_mask.device), lang_mask), dim=1)
+        return embeds, pad
+
+
+class SnapFlowPolicy:
+    """The config-4 step on one GPU: ``sample_actions(images, lang_ids,
+    lang_mask, noise)`` -> actions [B, chunk, action_dim] = x_t - v_t, x_t the
+    noise in the expert's dtype and v_t the expert's velocity at t = target
+    t = 1, in the noise's dtype (snapflow_pi05.py:170-195)."""
+
+    def __init__(self, cfg: SnapFlowConfig, lm: plm.W4A4PrefixLM, device, seed: int = 0,
+                 dtype=torch.bfloat16, std: float = 0.02):
+        self.cfg, self.lm, self.device, self.dtype = cfg, lm, torch.device(device), dtype
+        torch.manual_seed(seed)
+        with torch.device(self.device):
+            self.vision = VisionPrefix(cfg)
+            self.expert = ActionExpert(cfg)
+        for mod in (self.vision, self.expert):
+            for name, p in mod.named_parameters():
+                if p.dim() >= 2 and "embeddings" not in name:
+                    nn.init.normal_(p, std=std)
+            mod.to(dtype).eval()
+        gen = torch.Generator(device=self.device).manual_seed(seed + 1)
+        self.lang_table = torch.randn(cfg.vocab, cfg.lm.hidden, device=self.device, generator=gen,
+                                      dtype=torch.float16)
+        self.lang_scale = torch.tensor(math.sqrt(cfg.lm.hidden), dtype=torch.float16, device=self.device)
+        self.vision.cache_empty_camera()
+        self._prefix_out: dict = {}
+
+    def _out(self, b: int, seq: int) -> plm.PrefixOutput:
+        key = (b, seq)
+        if key not in self._prefix_out:
+            kv = self.lm.cfg.kv_heads * self.lm.cfg.head_dim
+            f16 = dict(dtype=torch.float16, device=self.device)
+            self._prefix_out[key] = plm.PrefixOutput(
+                hidden=torch.empty((b, seq, self.lm.cfg.hidden), **f16),
+                keys=[torch.empty((b, seq, kv), **f16) for _ in self.lm.layers],
+                values=[torch.empty((b, seq, kv), **f16) for _ in self.lm.layers])
+        return self._prefix_out[key]
+
+    @torch.no_grad()
+    def embed_prefix(self, images, lang_ids, lang_mask):
+        lang = self.lang_table[lang_ids] * self.lang_scale
+        return self.vision(images, lang, lang_mask)
+
+    @torch.no_grad()
+    def sample_actions(self, images, lang_ids, lang_mask, noise) -> torch.Tensor:
+        embeds, pad = self.embed_prefix(images, lang_ids, lang_mask)
+        out = self.lm.forward(embeds, pad, out=self._out(*pad.shape))
+        b = noise.shape[0]
+        t = torch.ones(b, dtype=torch.float32, device=self.device)
+        x_t = noise.to(self.dtype)
+        v = self.expert(x_t, t, t, pad, out.keys, out.values)
+        return (x_t - v).to(noise.dtype)
+
+
+class GraphedSnapFlow:
+    """``SnapFlowPolicy.sample_actions`` at a fixed batch captured in one CUDA
+    graph with static inputs: ``run(images, lang_ids, lang_mask, noise)``
+    copies the inputs in and replays; the result is ``self.actions``."""
+
+    def __init__(self, policy: SnapFlowPolicy, batch: int):
+        cfg, dev = policy.cfg, policy.device
+        self.policy = policy
+        self.images = torch.zeros((batch, cfg.real_cameras, 3, cfg.image_size, cfg.image_size),
+                                  dtype=torch.float32, device=dev)
+        self.lang_ids = torch.zeros((batch, cfg.lang_tokens), dtype=torch.long, device=dev)
+        self.lang_mask = torch.ones((batch, cfg.lang_tokens), dtype=torch.bool, device=dev)
+        self.noise = torch.zeros((batch, cfg.chunk, cfg.action_dim), dtype=torch.float32, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                policy.sample_actions(self.images, self.lang_ids, self.lang_mask, self.noise)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.actions = policy.sample_actions(self.images, self.lang_ids, self.lang_mask, self.noise)
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def run(self, images, lang_ids, lang_mask, noise) -> torch.Tensor:
+        self.images.copy_(images, non_blocking=True)
+        self.lang_ids.copy_(lang_ids, non_blocking=True)
+        self.lang_mask.copy_(lang_mask, non_blocking=True)
+        self.noise.copy_(noise, non_blocking=True)
+        self.graph.replay()
+        return self.actions
+
+
+def synthetic_observation(cfg: SnapFlowConfig, batch: int, real_lang: int = 52, seed: int = 0, device="cpu"):
+    """Config 4's inputs: real-camera images with pixels ~ U[-1, 1], language
+    ids (the first ``real_lang`` real, uniform over the vocabulary; the rest
+    padding) and the flow noise ~ N(0, 1).  Returns (images fp32 [B, cams, 3,
+    H, W], lang_ids [B, T], lang_mask bool [B, T], noise fp32 [B, chunk,
+    action_dim])."""
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    images = torch.rand(batch, cfg.real_cameras, 3, cfg.image_size, cfg.image_size, generator=gen) * 2 - 1
+    ids = torch.randint(0, cfg.vocab, (batch, cfg.lang_tokens), generator=gen)
+    ids[:, real_lang:] = 0
+    mask = torch.zeros(batch, cfg.lang_tokens, dtype=torch.bool)
+    mask[:, :real_lang] = True
+    noise = torch.randn(batch, cfg.chunk, cfg.action_dim, generator=gen)
+    return images.to(device), ids.to(device), mask.to(device), noise.to(device)

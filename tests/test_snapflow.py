@@ -1,0 +1,188 @@
+"""Config 4 (the SnapFlow 1-NFE step around the W4A4 prefix LM): the expert's
+masks, positions and prefix-KV attention against a direct restatement, the
+time embedding, the empty-camera pool and the prefix assembly on CPU (tiny
+shapes, fp32); the full-size step on a B200 (graph replay against eager,
+the KV handoff from the W4A4 prefix LM)."""
+
+from __future__ import annotations
+
+import math
+from dataclasses import replace
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from pi05_pytorch_fast_b200 import prefix_lm as plm
+from pi05_pytorch_fast_b200 import snapflow as sf
+
+TINY = sf.SnapFlowConfig(vision_hidden=32, vision_intermediate=64, vision_layers=2, vision_heads=4,
+                         image_size=56, patch=14, lang_tokens=6, vocab=100,
+                         lm=replace(plm.PrefixLMConfig(), hidden=48),
+                         expert_hidden=40, expert_intermediate=96, expert_layers=2, expert_heads=4,
+                         expert_kv_heads=1, head_dim=16, chunk=5, action_dim=3)
+
+
+def test_time_embedding_matches_the_formula():
+    t = torch.tensor([1.0, 0.25, 0.0])
+    emb = sf.sinusoidal_time_embedding(t, 8, 4e-3, 4.0)
+    for b, tb in enumerate(t.tolist()):
+        for i in range(4):
+            period = 4e-3 * (4.0 / 4e-3) ** (i / 3)
+            assert emb[b, i].item() == pytest.approx(math.sin(2 * math.pi * tb / period), abs=1e-6)
+            assert emb[b, 4 + i].item() == pytest.approx(math.cos(2 * math.pi * tb / period), abs=1e-6)
+
+
+def test_pool_sums_runs_of_tokens():
+    x = torch.arange(2 * 8 * 3, dtype=torch.float32).view(2, 8, 3)
+    p = sf.pool_tokens(x, 4)
+    assert p.shape == (2, 2, 3)
+    assert torch.equal(p[1, 1], x[1, 4:8].sum(0))
+    with pytest.raises(ValueError):
+        sf.pool_tokens(x, 3)
+
+
+def test_prefix_length_of_config_4_is_config_2s():
+    assert sf.SnapFlowConfig().prefix_len == 776
+
+
+def _expert_direct(expert: sf.ActionExpert, x_t, pad, keys, values):
+    """The expert restated over the whole [prefix ; suffix] sequence: an
+    additive fp64 mask (prefix key j visible iff real, every suffix key
+    visible), explicit softmax, positions sum(pad) + i, GQA by repetition."""
+    cfg = expert.cfg
+    dev = x_t.device
+    b, s = x_t.shape[0], cfg.chunk
+    t = torch.ones(b, device=dev)
+    cond = expert.condition(t, t).double()
+    x = F.linear(x_t.double(), expert.action_in_proj.weight.double(), expert.action_in_proj.bias.double())
+    pos = pad.sum(1, keepdim=True).double() + torch.arange(s, dtype=torch.float64, device=dev)[None]
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.head_dim, 2, dtype=torch.float32, device=dev)
+                                    / cfg.head_dim))
+    ang = (pos.float()[..., None] * inv).double()
+    cos = torch.cat((ang, ang), -1).cos()[:, None]
+    sin = torch.cat((ang, ang), -1).sin()[:, None]
+    visible = torch.cat((pad, torch.ones(b, s, dtype=torch.bool, device=dev)), 1)
+    add = torch.where(visible, 0.0, -math.inf)[:, None, None, :]
+
+    def norm(mod, x):
+        scale, shift, gate = F.linear(cond, mod.mod.weight.double(), mod.mod.bias.double())[:, None].chunk(3, -1)
+        y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + mod.eps)
+        return y * (1 + scale) + shift, gate
+
+    def lin(m, x):
+        return F.linear(x, m.weight.double(), None if m.bias is None else m.bias.double())
+
+    for layer, k, v in zip(expert.layers, keys, values):
+        n, g1 = norm(layer.in_norm, x)
+        q = lin(layer.q, n).view(b, s, cfg.expert_heads, -1).transpose(1, 2)
+        kk = lin(layer.k, n).view(b, s, 1, -1).transpose(1, 2)
+        vv = lin(layer.v, n).view(b, s, 1, -1).transpose(1, 2)
+        q = q * cos + sf.rotate_half(q) * sin
+        kk = kk * cos + sf.rotate_half(kk) * sin
+        kk = torch.cat((k.double().view(b, -1, 1, cfg.head_dim).transpose(1, 2), kk), 2)
+        vv = torch.cat((v.double().view(b, -1, 1, cfg.head_dim).transpose(1, 2), vv), 2)
+        sc = q @ kk.transpose(-1, -2) / math.sqrt(cfg.head_dim) + add
+        a = torch.softmax(sc, -1) @ vv
+        x = x + g1 * lin(layer.o, a.transpose(1, 2).reshape(b, s, -1))
+        n, g2 = norm(layer.post_norm, x)
+        x = x + g2 * lin(layer.down, F.gelu(lin(layer.gate, n), approximate="tanh") * lin(layer.up, n))
+    x, _ = norm(expert.final_norm, x)
+    return lin(expert.action_out_proj, x)
+
+
+def test_expert_over_the_prefix_cache_matches_the_direct_restatement():
+    torch.manual_seed(0)
+    expert = sf.ActionExpert(TINY).eval()
+    b, L = 2, 9
+    pad = torch.ones(b, L, dtype=torch.bool)
+    pad[0, 6:] = False
+    pad[1, 3:] = False
+    keys = [torch.randn(b, L, TINY.head_dim) for _ in range(TINY.expert_layers)]
+    values = [torch.randn(b, L, TINY.head_dim) for _ in range(TINY.expert_layers)]
+    x_t = torch.randn(b, TINY.chunk, TINY.action_dim)
+    t = torch.ones(b)
+    with torch.no_grad():
+        v = expert(x_t, t, t, pad, keys, values)
+        ref = _expert_direct(expert, x_t, pad, keys, values)
+    torch.testing.assert_close(v.double(), ref, rtol=1e-4, atol=1e-5)
+    # a padded prefix key never matters
+    keys2 = [k.clone() for k in keys]
+    keys2[0][0, 7] += 100.0
+    values2 = [x.clone() for x in values]
+    values2[1][1, 5] -= 50.0
+    with torch.no_grad():
+        torch.testing.assert_close(expert(x_t, t, t, pad, keys2, values2), v)
+
+
+def test_vision_prefix_assembles_cameras_empty_camera_and_language():
+    torch.manual_seed(1)
+    vis = sf.VisionPrefix(TINY).eval()
+    vis.cache_empty_camera()
+    tok = TINY.image_tokens
+    assert vis.empty_cam.shape == (1, tok // TINY.empty_pool, TINY.lm.hidden)
+    b = 2
+    images, ids, mask, _ = sf.synthetic_observation(TINY, b, real_lang=4, seed=3)
+    lang = torch.randn(b, TINY.lang_tokens, TINY.lm.hidden)
+    with torch.no_grad():
+        embeds, pad = vis(images, lang, mask)
+        cam1 = vis.embed_images(images[:, 1])
+        blank = vis.embed_images(torch.full((1, 3, TINY.image_size, TINY.image_size), -1.0))
+    assert embeds.shape == (b, TINY.prefix_len, TINY.lm.hidden) and embeds.dtype == torch.float16
+    assert torch.equal(embeds[:, tok:2 * tok], cam1.half())
+    torch.testing.assert_close(embeds[0, 2 * tok:2 * tok + tok // 4].float(),
+                               sf.pool_tokens(blank, 4)[0].half().float())
+    assert torch.equal(embeds[:, -TINY.lang_tokens:], lang.half())
+    assert pad[:, :2 * tok + tok // 4].all()
+    assert torch.equal(pad[:, -TINY.lang_tokens:], mask)
+
+
+# ----------------------------------------------------------------------------- B200
+@pytest.fixture(scope="module")
+def policy():
+    dev = torch.device("cuda:0")
+    lm = plm.W4A4PrefixLM.random(plm.PrefixLMConfig(), dev, seed=5)
+    return sf.SnapFlowPolicy(sf.SnapFlowConfig(), lm, dev, seed=6)
+
+
+@pytest.mark.gpu
+def test_snapflow_step_graph_replay_equals_eager(policy):
+    cfg = policy.cfg
+    obs = sf.synthetic_observation(cfg, 2, seed=7, device="cuda:0")
+    eager = policy.sample_actions(*obs)
+    g = sf.GraphedSnapFlow(policy, 2)
+    out = g.run(*obs)
+    torch.cuda.synchronize()
+    assert out.shape == (2, cfg.chunk, cfg.action_dim) and out.dtype == torch.float32
+    assert torch.isfinite(out).all()
+    assert torch.equal(out, eager)
+    # a second observation batch through the same graph
+    obs2 = sf.synthetic_observation(cfg, 2, seed=8, device="cuda:0")
+    out2 = g.run(*obs2).clone()
+    torch.testing.assert_close(out2, policy.sample_actions(*obs2), rtol=0, atol=0)
+    assert not torch.equal(out2, eager)
+
+
+@pytest.mark.gpu
+def test_snapflow_expert_reads_the_w4a4_prefix_cache(policy):
+    """The expert's velocity from the W4A4 prefix LM's KV cache, against the
+    fp64 restatement over the same cache (bf16 expert: loose tolerance), and
+    the observations of a batch stay independent."""
+    cfg = policy.cfg
+    images, ids, mask, noise = sf.synthetic_observation(cfg, 2, seed=9, device="cuda:0")
+    with torch.no_grad():
+        embeds, pad = policy.embed_prefix(images, ids, mask)
+        out = policy.lm.forward(embeds, pad)
+        x_t = noise.to(policy.dtype)
+        t = torch.ones(2, device="cuda:0")
+        v = policy.expert(x_t, t, t, pad, out.keys, out.values).double()
+        expert64 = sf.ActionExpert(cfg).to("cuda:0")
+        expert64.load_state_dict(policy.expert.state_dict())
+        ref = _expert_direct(expert64.double(), x_t.double(), pad, out.keys, out.values)
+        one = policy.sample_actions(images[1:], ids[1:], mask[1:], noise[1:])
+        both = policy.sample_actions(images, ids, mask, noise)
+    rel = (v - ref).norm() / ref.norm()
+    assert rel < 0.05, float(rel)
+    # bf16 library GEMMs may pick other kernels for another batch size
+    rel_b = (both[1:] - one).norm() / one.norm()
+    assert rel_b < 0.02, float(rel_b)
