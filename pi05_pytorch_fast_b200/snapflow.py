@@ -131,33 +131,27 @@ def rope_tables(positions: torch.Tensor, head_dim: int, theta: float, dtype) -> 
     return emb.cos().to(dtype), emb.sin().to(dtype)
 
 
-class AdaRMSNorm(nn.Module):
-    """RMSNorm conditioned on the flow time: [scale, shift, gate] =
-    Linear(cond); y = rms_norm(x) * (1 + scale) + shift (fp32, cast back);
-    gate multiplies the sublayer's output on the residual."""
-
-    def __init__(self, dim: int, cond_dim: int, eps: float):
-        super().__init__()
-        self.eps = eps
-        self.mod = nn.Linear(cond_dim, 3 * dim)
-
-    def forward(self, x: torch.Tensor, cond: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        scale, shift, gate = self.mod(cond)[:, None, :].chunk(3, dim=-1)
-        xf = x.float()
-        y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
-        return (y * (1.0 + scale.float()) + shift.float()).to(x.dtype), gate
+def ada_rms_norm(x: torch.Tensor, mod: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """pi0.5's adaptive RMSNorm: mod [B, 3, h] = [scale, shift, gate] (a
+    Linear of the flow-time condition); y = rms_norm(x) * (1 + scale) + shift
+    in fp32, cast back to x's dtype; the gate multiplies the sublayer's output
+    on the residual."""
+    scale, shift, gate = mod[:, 0, None], mod[:, 1, None], mod[:, 2, None]
+    y = F.rms_norm(x.float(), (x.shape[-1],), eps=eps)
+    return torch.addcmul(shift.float(), y, 1.0 + scale.float()).to(x.dtype), gate
 
 
 class ExpertLayer(nn.Module):
     """One Gemma-300M decoder layer of the action expert with adaptive norms;
-    attention over [prefix KV cache ; own keys]."""
+    attention over [prefix KV cache ; own keys] as transformers' eager
+    attention computes it (bf16 scores with the additive mask, softmax in
+    fp32, rounded to bf16, times V), the query heads of a KV head stacked
+    as rows of one matrix product."""
 
     def __init__(self, cfg: SnapFlowConfig):
         super().__init__()
         h, hd = cfg.expert_hidden, cfg.head_dim
-        self.heads, self.kv_heads, self.hd = cfg.expert_heads, cfg.expert_kv_heads, hd
-        self.in_norm = AdaRMSNorm(h, h, cfg.rms_eps)
-        self.post_norm = AdaRMSNorm(h, h, cfg.rms_eps)
+        self.heads, self.kv_heads, self.hd, self.eps = cfg.expert_heads, cfg.expert_kv_heads, hd, cfg.rms_eps
         self.q = nn.Linear(h, self.heads * hd, bias=False)
         self.k = nn.Linear(h, self.kv_heads * hd, bias=False)
         self.v = nn.Linear(h, self.kv_heads * hd, bias=False)
@@ -166,28 +160,37 @@ class ExpertLayer(nn.Module):
         self.up = nn.Linear(h, cfg.expert_intermediate, bias=False)
         self.down = nn.Linear(cfg.expert_intermediate, h, bias=False)
 
-    def forward(self, x, cond, cos, sin, prefix_k, prefix_v, mask):
-        """x [B, S, h]; prefix_k / prefix_v [B, kv_heads, L, hd] (keys after
-        RoPE); mask [B, 1, S, L + S] bool (True = attend)."""
+    def forward(self, x, mod_in, mod_post, cos, sin, prefix_k, prefix_v, mask_add):
+        """x [B, S, h]; mod_* [B, 3, h]; cos / sin [B, S, 1, hd]; prefix_k /
+        prefix_v [B, kv_heads, L, hd] (keys after RoPE); mask_add [B, 1, L + S]
+        (0 or the dtype's lowest value)."""
         b, s, _ = x.shape
-        n, g1 = self.in_norm(x, cond)
-        q = self.q(n).view(b, s, self.heads, self.hd).transpose(1, 2)
-        k = self.k(n).view(b, s, self.kv_heads, self.hd).transpose(1, 2)
-        v = self.v(n).view(b, s, self.kv_heads, self.hd).transpose(1, 2)
+        kvh, g, hd = self.kv_heads, self.heads // self.kv_heads, self.hd
+        n, g1 = ada_rms_norm(x, mod_in, self.eps)
+        q = self.q(n).view(b, s, self.heads, hd)
+        k = self.k(n).view(b, s, kvh, hd)
+        v = self.v(n).view(b, s, kvh, hd)
         q = q * cos + rotate_half(q) * sin
         k = k * cos + rotate_half(k) * sin
-        k = torch.cat((prefix_k, k), dim=2)
-        v = torch.cat((prefix_v, v), dim=2)
-        a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=self.kv_heads != self.heads)
-        x = x + g1 * self.o(a.transpose(1, 2).reshape(b, s, self.heads * self.hd))
-        n, g2 = self.post_norm(x, cond)
-        return x + g2 * self.down(F.gelu(self.gate(n), approximate="tanh") * self.up(n))
+        # rows (KV head, query head of the group, token); keys [prefix ; suffix]
+        q = q.view(b, s, kvh, g, hd).permute(0, 2, 3, 1, 4).reshape(b * kvh, g * s, hd)
+        k = torch.cat((prefix_k, k.transpose(1, 2)), dim=2).view(b * kvh, -1, hd)
+        v = torch.cat((prefix_v, v.transpose(1, 2)), dim=2).view(b * kvh, -1, hd)
+        mask = mask_add if kvh == 1 else mask_add.repeat_interleave(kvh, dim=0)
+        scores = torch.baddbmm(mask, q, k.transpose(1, 2), alpha=hd ** -0.5)
+        p = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
+        a = torch.bmm(p, v).view(b, kvh, g, s, hd).permute(0, 3, 1, 2, 4).reshape(b, s, self.heads * hd)
+        x = torch.addcmul(x, g1, self.o(a))
+        n, g2 = ada_rms_norm(x, mod_post, self.eps)
+        return torch.addcmul(x, g2, self.down(F.gelu(self.gate(n), approximate="tanh") * self.up(n)))
 
 
 class ActionExpert(nn.Module):
     """The suffix path of the SnapFlow step: time embedding (+ target-time
     MLP), the time MLP -> condition, action_in_proj, the expert layers over
-    the prefix KV cache, the final adaptive norm and action_out_proj."""
+    the prefix KV cache, the final adaptive norm and action_out_proj.  The
+    [scale, shift, gate] of all 2 x layers + 1 adaptive norms come from one
+    Linear of the condition (``modulation``: norm i's at rows 3 h i ..)."""
 
     def __init__(self, cfg: SnapFlowConfig):
         super().__init__()
@@ -200,7 +203,8 @@ class ActionExpert(nn.Module):
         hid = max(h, 256)
         self.target_time_mlp = nn.Sequential(nn.Linear(h, hid), nn.SiLU(), nn.Linear(hid, h))
         self.layers = nn.ModuleList(ExpertLayer(cfg) for _ in range(cfg.expert_layers))
-        self.final_norm = AdaRMSNorm(h, h, cfg.rms_eps)
+        self.n_norms = 2 * cfg.expert_layers + 1
+        self.modulation = nn.Linear(h, self.n_norms * 3 * h)
 
     def condition(self, t: torch.Tensor, target_t: torch.Tensor | None) -> torch.Tensor:
         cfg, dt = self.cfg, self.time_mlp_in.weight.dtype
@@ -216,20 +220,23 @@ class ActionExpert(nn.Module):
         dtype).  Returns v_t [B, chunk, action_dim] in the expert's dtype."""
         cfg = self.cfg
         dt = self.action_in_proj.weight.dtype
-        b, s = x_t.shape[0], cfg.chunk
-        cond = self.condition(t, target_t)
+        b, s, h = x_t.shape[0], cfg.chunk, cfg.expert_hidden
+        mods = self.modulation(self.condition(t, target_t)).view(b, self.n_norms, 3, h)
         x = self.action_in_proj(x_t)
         # suffix positions continue after the real prefix tokens
         pos = prefix_pad.sum(dim=1, keepdim=True) + torch.arange(s, device=x.device)[None, :]
         cos, sin = rope_tables(pos, cfg.head_dim, cfg.rope_theta, dt)
-        mask = torch.cat((prefix_pad[:, None, None, :].expand(b, 1, s, prefix_pad.shape[1]),
-                          torch.ones((b, 1, s, s), dtype=torch.bool, device=x.device)), dim=3)
+        cos, sin = cos.transpose(1, 2), sin.transpose(1, 2)
+        # the prefix's real tokens and every suffix token are visible
+        visible = torch.cat((prefix_pad, torch.ones((b, s), dtype=torch.bool, device=x.device)), dim=1)
+        mask_add = torch.zeros(visible.shape, dtype=dt, device=x.device).masked_fill_(
+            ~visible, torch.finfo(dt).min)[:, None, :]
         kvh, hd = cfg.expert_kv_heads, cfg.head_dim
-        for layer, k, v in zip(self.layers, keys, values):
+        for i, (layer, k, v) in enumerate(zip(self.layers, keys, values)):
             pk = k.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
             pv = v.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
-            x = layer(x, cond, cos, sin, pk, pv, mask)
-        x, _ = self.final_norm(x, cond)
+            x = layer(x, mods[:, 2 * i], mods[:, 2 * i + 1], cos, sin, pk, pv, mask_add)
+        x, _ = ada_rms_norm(x, mods[:, -1], cfg.rms_eps)
         return self.action_out_proj(x[:, -s:])
 
 

@@ -65,16 +65,19 @@ def _expert_direct(expert: sf.ActionExpert, x_t, pad, keys, values):
     visible = torch.cat((pad, torch.ones(b, s, dtype=torch.bool, device=dev)), 1)
     add = torch.where(visible, 0.0, -math.inf)[:, None, None, :]
 
-    def norm(mod, x):
-        scale, shift, gate = F.linear(cond, mod.mod.weight.double(), mod.mod.bias.double())[:, None].chunk(3, -1)
-        y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + mod.eps)
+    mods = F.linear(cond, expert.modulation.weight.double(), expert.modulation.bias.double())
+    mods = mods.view(b, expert.n_norms, 3, -1)
+
+    def norm(i, x):
+        scale, shift, gate = mods[:, i, 0, None], mods[:, i, 1, None], mods[:, i, 2, None]
+        y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.rms_eps)
         return y * (1 + scale) + shift, gate
 
     def lin(m, x):
         return F.linear(x, m.weight.double(), None if m.bias is None else m.bias.double())
 
-    for layer, k, v in zip(expert.layers, keys, values):
-        n, g1 = norm(layer.in_norm, x)
+    for li, (layer, k, v) in enumerate(zip(expert.layers, keys, values)):
+        n, g1 = norm(2 * li, x)
         q = lin(layer.q, n).view(b, s, cfg.expert_heads, -1).transpose(1, 2)
         kk = lin(layer.k, n).view(b, s, 1, -1).transpose(1, 2)
         vv = lin(layer.v, n).view(b, s, 1, -1).transpose(1, 2)
@@ -85,9 +88,9 @@ def _expert_direct(expert: sf.ActionExpert, x_t, pad, keys, values):
         sc = q @ kk.transpose(-1, -2) / math.sqrt(cfg.head_dim) + add
         a = torch.softmax(sc, -1) @ vv
         x = x + g1 * lin(layer.o, a.transpose(1, 2).reshape(b, s, -1))
-        n, g2 = norm(layer.post_norm, x)
+        n, g2 = norm(2 * li + 1, x)
         x = x + g2 * lin(layer.down, F.gelu(lin(layer.gate, n), approximate="tanh") * lin(layer.up, n))
-    x, _ = norm(expert.final_norm, x)
+    x, _ = norm(-1, x)
     return lin(expert.action_out_proj, x)
 
 
