@@ -82,7 +82,7 @@ def parse_args():
                     help="config 4: the SnapFlow 1-NFE action chunk (SigLIP + the W4A4 prefix LM + the "
                          "action expert); --batch observations per GPU (config 4: 64 over 8 GPUs)")
     ap.add_argument("--case", choices=("qkv", "o", "gateup", "down", "quant2k", "quant16k",
-                                       "normquant", "geglu", "attn", "forward"),
+                                       "normquant", "geglu", "attn", "forward", "snapflow"),
                     default=None, help="run one op (or one forward) 3 times at the bench shape and "
                                        "exit (a small, self-contained case for ncu)")
     return ap.parse_args()
@@ -843,6 +843,20 @@ def run_case(args):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
+    if args.case == "snapflow":
+        # three eager config-4 steps, each in an NVTX range snapflow_step<i>
+        # (ncu --nvtx --nvtx-include "snapflow_step2/" keeps the last)
+        from pi05_pytorch_fast_b200 import snapflow as sf
+
+        cfg = sf.SnapFlowConfig()
+        policy = sf.SnapFlowPolicy(cfg, plm.W4A4PrefixLM.random(cfg.lm, device, seed=1234), device, seed=4321)
+        obs = sf.synthetic_observation(cfg, args.batch, seed=300, device=device)
+        for i in range(3):
+            with torch.cuda.nvtx.range(f"snapflow_step{i}"):
+                policy.sample_actions(*obs)
+        torch.cuda.synchronize(device)
+        print(f"case snapflow done (batch {args.batch})")
+        return
     if args.staging:
         os.environ["PI05_W4A4_STAGING"] = args.staging
     staging = nat.STAGING_FP32 if os.environ.get("PI05_W4A4_STAGING", "fp16") == "fp32" else nat.STAGING_FP16
