@@ -141,6 +141,13 @@ def ada_rms_norm(x: torch.Tensor, mod: torch.Tensor, eps: float) -> tuple[torch.
     return torch.addcmul(shift.float(), y, 1.0 + scale.float()).to(x.dtype), gate
 
 
+def signed_sin(sin: torch.Tensor) -> torch.Tensor:
+    """sin with its first half (over the last dim) negated: rotate_half(x) *
+    sin == roll(x, half) * signed_sin(sin)."""
+    h = sin.shape[-1] // 2
+    return torch.cat((-sin[..., :h], sin[..., h:]), dim=-1)
+
+
 class ExpertLayer(nn.Module):
     """One Gemma-300M decoder layer of the action expert with adaptive norms;
     attention over [prefix KV cache ; own keys] as transformers' eager
@@ -161,7 +168,8 @@ class ExpertLayer(nn.Module):
         self.down = nn.Linear(cfg.expert_intermediate, h, bias=False)
 
     def forward(self, x, mod_in, mod_post, cos, sin, prefix_k, prefix_v, mask_add):
-        """x [B, S, h]; mod_* [B, 3, h]; cos / sin [B, S, 1, hd]; prefix_k /
+        """x [B, S, h]; mod_* [B, 3, h]; cos / sin [B, S, 1, hd], sin with its
+        first half negated (``signed_sin``); prefix_k /
         prefix_v [B, kv_heads, L, hd] (keys after RoPE); mask_add [B, 1, L + S]
         (0 or the dtype's lowest value)."""
         b, s, _ = x.shape
@@ -170,8 +178,10 @@ class ExpertLayer(nn.Module):
         q = self.q(n).view(b, s, self.heads, hd)
         k = self.k(n).view(b, s, kvh, hd)
         v = self.v(n).view(b, s, kvh, hd)
-        q = q * cos + rotate_half(q) * sin
-        k = k * cos + rotate_half(k) * sin
+        # x cos + rotate_half(x) sin, with rotate_half(x) = roll(x, hd / 2) times
+        # the sign carried by sin (negated first half)
+        q = torch.addcmul(q * cos, torch.roll(q, hd // 2, dims=-1), sin)
+        k = torch.addcmul(k * cos, torch.roll(k, hd // 2, dims=-1), sin)
         # rows (KV head, query head of the group, token); keys [prefix ; suffix]
         q = q.view(b, s, kvh, g, hd).permute(0, 2, 3, 1, 4).reshape(b * kvh, g * s, hd)
         k = torch.cat((prefix_k, k.transpose(1, 2)), dim=2).view(b * kvh, -1, hd)
@@ -226,7 +236,7 @@ class ActionExpert(nn.Module):
         # suffix positions continue after the real prefix tokens
         pos = prefix_pad.sum(dim=1, keepdim=True) + torch.arange(s, device=x.device)[None, :]
         cos, sin = rope_tables(pos, cfg.head_dim, cfg.rope_theta, dt)
-        cos, sin = cos.transpose(1, 2), sin.transpose(1, 2)
+        cos, sin = cos.transpose(1, 2), signed_sin(sin.transpose(1, 2))
         # the prefix's real tokens and every suffix token are visible
         visible = torch.cat((prefix_pad, torch.ones((b, s), dtype=torch.bool, device=x.device)), dim=1)
         mask_add = torch.zeros(visible.shape, dtype=dt, device=x.device).masked_fill_(

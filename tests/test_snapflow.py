@@ -33,6 +33,13 @@ def test_time_embedding_matches_the_formula():
             assert emb[b, 4 + i].item() == pytest.approx(math.cos(2 * math.pi * tb / period), abs=1e-6)
 
 
+def test_roll_with_signed_sin_is_rotate_half():
+    x = torch.randn(2, 3, 4, 16, dtype=torch.float64)
+    sin = torch.randn(2, 3, 1, 16, dtype=torch.float64)
+    torch.testing.assert_close(torch.roll(x, 8, dims=-1) * sf.signed_sin(sin), sf.rotate_half(x) * sin,
+                               rtol=0, atol=0)
+
+
 def test_pool_sums_runs_of_tokens():
     x = torch.arange(2 * 8 * 3, dtype=torch.float32).view(2, 8, 3)
     p = sf.pool_tokens(x, 4)
