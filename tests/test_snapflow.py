@@ -177,9 +177,12 @@ def test_snapflow_step_graph_replay_equals_eager(policy):
 def test_snapflow_expert_reads_the_w4a4_prefix_cache(policy):
     """The expert's velocity from the W4A4 prefix LM's KV cache, against the
     fp64 restatement over the same cache (bf16 expert: loose tolerance), and
-    the observations of a batch stay independent."""
+    the observations of a batch stay independent (the two have different
+    language lengths, so different prefix masks and suffix positions)."""
     cfg = policy.cfg
     images, ids, mask, noise = sf.synthetic_observation(cfg, 2, seed=9, device="cuda:0")
+    mask[1, 17:] = False
+    ids[1, 17:] = 0
     with torch.no_grad():
         embeds, pad = policy.embed_prefix(images, ids, mask)
         out = policy.lm.forward(embeds, pad)
