@@ -333,8 +333,9 @@ def test_product_preshuffle_matches_reference(golden, name, k):
 
 REFERENCE = os.environ.get("PI05_REFERENCE_CHECKOUT", "/root/reference")
 
-# Runs in a fresh interpreter: applies the two-line binding of INTEGRATION.md
-# section 2 to the UNMODIFIED reference extension module, then installs W4A4
+# Runs in a fresh interpreter: applies the two-line binding a maintainer adds
+# (mark the reference's op registration done, point its module handle at this
+# package) to the UNMODIFIED reference extension module, then installs W4A4
 # on a small transformers Gemma with the reference's own apply.py / linear.py
 # and traces one forward under FakeTensorMode (CUDA fake tensors; no GPU).
 _BINDING_SCRIPT = r"""
