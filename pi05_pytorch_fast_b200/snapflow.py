@@ -14,10 +14,11 @@ expert run bf16.
 lerobot is not part of the reference, so the neighbours of the W4A4 path are
 rebuilt here from their published structure, with random weights:
 
-* SigLIP-So400m (transformers' ``SiglipVisionModel``: width 1152, 27 layers,
-  16 heads, MLP 4304, patch 14 at 224 x 224 -> 256 tokens, no pooling head)
-  and PaliGemma's multi-modal projector (1152 -> 2048), bf16, cuBLAS /
-  PyTorch SDPA, as the reference runs them;
+* SigLIP-So400m (width 1152, 27 layers, 16 heads, MLP 4304, patch 14 at
+  224 x 224 -> 256 tokens, no pooling head): ``SiglipTower``, the
+  computation of transformers' ``SiglipVisionModel`` with fewer launches
+  (it loads that model's weights), and PaliGemma's multi-modal projector
+  (1152 -> 2048), bf16 through cuBLAS and PyTorch's SDPA;
 * the language embedding table (257,152 x 2048) scaled by sqrt(2048), as
   Gemma scales embeddings;
 * the W4A4 prefix LM of this package (``prefix_lm.W4A4PrefixLM``), whose
@@ -250,6 +251,61 @@ class ActionExpert(nn.Module):
         return self.action_out_proj(x[:, -s:])
 
 
+class SiglipTower(nn.Module):
+    """SigLIP vision encoder without the pooling head, the computation of
+    transformers' ``SiglipVisionModel`` (patch convolution, position
+    embedding, pre-norm layers: LayerNorm -> attention -> residual, LayerNorm
+    -> fc1 -> tanh GELU -> fc2 -> residual, final LayerNorm) laid out for
+    fewer launches: q, k and v come from one GEMM whose output is viewed as
+    [N, T, 3, heads, d] and handed to scaled-dot-product attention as strided
+    views (no head transposes materialised; transformers' attention copies
+    q, k, v and the output per layer)."""
+
+    def __init__(self, cfg: SnapFlowConfig, eps: float = 1e-6):
+        super().__init__()
+        h, self.heads = cfg.vision_hidden, cfg.vision_heads
+        self.patch = nn.Conv2d(3, h, kernel_size=cfg.patch, stride=cfg.patch)
+        self.pos = nn.Parameter(torch.zeros(cfg.image_tokens, h))
+        self.ln1 = nn.ModuleList(nn.LayerNorm(h, eps=eps) for _ in range(cfg.vision_layers))
+        self.qkv = nn.ModuleList(nn.Linear(h, 3 * h) for _ in range(cfg.vision_layers))
+        self.out = nn.ModuleList(nn.Linear(h, h) for _ in range(cfg.vision_layers))
+        self.ln2 = nn.ModuleList(nn.LayerNorm(h, eps=eps) for _ in range(cfg.vision_layers))
+        self.fc1 = nn.ModuleList(nn.Linear(h, cfg.vision_intermediate) for _ in range(cfg.vision_layers))
+        self.fc2 = nn.ModuleList(nn.Linear(cfg.vision_intermediate, h) for _ in range(cfg.vision_layers))
+        self.post_ln = nn.LayerNorm(h, eps=eps)
+
+    @torch.no_grad()
+    def load_transformers(self, model) -> "SiglipTower":
+        """Copies the weights of a transformers ``SiglipVisionModel``."""
+        vm = model.vision_model
+        self.patch.load_state_dict(vm.embeddings.patch_embedding.state_dict())
+        self.pos.copy_(vm.embeddings.position_embedding.weight)
+        for i, layer in enumerate(vm.encoder.layers):
+            at = layer.self_attn
+            self.qkv[i].weight.copy_(torch.cat((at.q_proj.weight, at.k_proj.weight, at.v_proj.weight)))
+            self.qkv[i].bias.copy_(torch.cat((at.q_proj.bias, at.k_proj.bias, at.v_proj.bias)))
+            self.out[i].load_state_dict(at.out_proj.state_dict())
+            self.ln1[i].load_state_dict(layer.layer_norm1.state_dict())
+            self.ln2[i].load_state_dict(layer.layer_norm2.state_dict())
+            self.fc1[i].load_state_dict(layer.mlp.fc1.state_dict())
+            self.fc2[i].load_state_dict(layer.mlp.fc2.state_dict())
+        self.post_ln.load_state_dict(vm.post_layernorm.state_dict())
+        return self
+
+    def forward(self, pixels: torch.Tensor) -> torch.Tensor:
+        """[N, 3, H, W] -> [N, tokens, hidden] in the tower's dtype."""
+        x = self.patch(pixels.to(self.patch.weight.dtype)).flatten(2).transpose(1, 2) + self.pos
+        n, t, h = x.shape
+        d = h // self.heads
+        for i in range(len(self.qkv)):
+            qkv = self.qkv[i](self.ln1[i](x)).view(n, t, 3, self.heads, d)
+            q, k, v = (qkv[:, :, j].transpose(1, 2) for j in range(3))
+            a = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(n, t, h)
+            x = x + self.out[i](a)
+            x = x + self.fc2[i](F.gelu(self.fc1[i](self.ln2[i](x)), approximate="tanh"))
+        return self.post_ln(x)
+
+
 class VisionPrefix(nn.Module):
     """SigLIP-So400m + PaliGemma's projector, and the prefix assembly of
     rocm_pi05_optim.py:88-133 (real cameras batched, the empty camera's
@@ -257,20 +313,14 @@ class VisionPrefix(nn.Module):
 
     def __init__(self, cfg: SnapFlowConfig):
         super().__init__()
-        from transformers import SiglipVisionConfig, SiglipVisionModel
-
-        vcfg = SiglipVisionConfig(hidden_size=cfg.vision_hidden, intermediate_size=cfg.vision_intermediate,
-                                  num_hidden_layers=cfg.vision_layers, num_attention_heads=cfg.vision_heads,
-                                  image_size=cfg.image_size, patch_size=cfg.patch, vision_use_head=False)
         self.cfg = cfg
-        self.siglip = SiglipVisionModel(vcfg)
+        self.siglip = SiglipTower(cfg)
         self.projector = nn.Linear(cfg.vision_hidden, cfg.lm.hidden)
         self.register_buffer("empty_cam", torch.zeros(0), persistent=False)
 
     def embed_images(self, images: torch.Tensor) -> torch.Tensor:
         """[N, 3, H, W] -> [N, tokens, lm hidden] in the tower's dtype."""
-        dt = self.projector.weight.dtype
-        return self.projector(self.siglip(pixel_values=images.to(dt)).last_hidden_state)
+        return self.projector(self.siglip(images))
 
     @torch.no_grad()
     def cache_empty_camera(self) -> None:

@@ -125,6 +125,23 @@ def test_expert_over_the_prefix_cache_matches_the_direct_restatement():
         torch.testing.assert_close(expert(x_t, t, t, pad, keys2, values2), v)
 
 
+def test_siglip_tower_matches_transformers_siglip():
+    from transformers import SiglipVisionConfig, SiglipVisionModel
+
+    torch.manual_seed(2)
+    hf = SiglipVisionModel(SiglipVisionConfig(
+        hidden_size=TINY.vision_hidden, intermediate_size=TINY.vision_intermediate,
+        num_hidden_layers=TINY.vision_layers, num_attention_heads=TINY.vision_heads,
+        image_size=TINY.image_size, patch_size=TINY.patch, vision_use_head=False)).eval()
+    with torch.no_grad():
+        for p in hf.parameters():  # non-trivial norms and biases
+            p.add_(torch.randn_like(p) * 0.05)
+    tower = sf.SiglipTower(TINY).eval().load_transformers(hf)
+    px = torch.rand(3, 3, TINY.image_size, TINY.image_size) * 2 - 1
+    with torch.no_grad():
+        torch.testing.assert_close(tower(px), hf(pixel_values=px).last_hidden_state, rtol=1e-5, atol=1e-5)
+
+
 def test_vision_prefix_assembles_cameras_empty_camera_and_language():
     torch.manual_seed(1)
     vis = sf.VisionPrefix(TINY).eval()
