@@ -256,10 +256,10 @@ class SiglipTower(nn.Module):
     transformers' ``SiglipVisionModel`` (patch convolution, position
     embedding, pre-norm layers: LayerNorm -> attention -> residual, LayerNorm
     -> fc1 -> tanh GELU -> fc2 -> residual, final LayerNorm) laid out for
-    fewer launches: q, k and v come from one GEMM whose output is viewed as
+    fewer launches: the residual stream token-major from the patch
+    embedding on, and q, k and v from one GEMM whose output is viewed as
     [N, T, 3, heads, d] and handed to scaled-dot-product attention as strided
-    views (no head transposes materialised; transformers' attention copies
-    q, k, v and the output per layer)."""
+    views."""
 
     def __init__(self, cfg: SnapFlowConfig, eps: float = 1e-6):
         super().__init__()
@@ -294,7 +294,10 @@ class SiglipTower(nn.Module):
 
     def forward(self, pixels: torch.Tensor) -> torch.Tensor:
         """[N, 3, H, W] -> [N, tokens, hidden] in the tower's dtype."""
-        x = self.patch(pixels.to(self.patch.weight.dtype)).flatten(2).transpose(1, 2) + self.pos
+        # the patch grid made token-major once: the convolution's [N, h, T]
+        # viewed as [N, T, h] would keep every later residual add and Linear
+        # input channel-major (non-vectorised adds, a copy before each GEMM)
+        x = self.patch(pixels.to(self.patch.weight.dtype)).flatten(2).transpose(1, 2).contiguous() + self.pos
         n, t, h = x.shape
         d = h // self.heads
         for i in range(len(self.qkv)):
