@@ -132,14 +132,14 @@ def rope_tables(positions: torch.Tensor, head_dim: int, theta: float, dtype) -> 
     return emb.cos().to(dtype), emb.sin().to(dtype)
 
 
-def ada_rms_norm(x: torch.Tensor, mod: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
-    """pi0.5's adaptive RMSNorm: mod [B, 3, h] = [scale, shift, gate] (a
-    Linear of the flow-time condition); y = rms_norm(x) * (1 + scale) + shift
-    in fp32, cast back to x's dtype; the gate multiplies the sublayer's output
-    on the residual."""
-    scale, shift, gate = mod[:, 0, None], mod[:, 1, None], mod[:, 2, None]
+def ada_rms_norm(x: torch.Tensor, mod: tuple, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """pi0.5's adaptive RMSNorm: mod = (1 + scale, shift) in fp32 and gate,
+    each [B, h], from a Linear of the flow-time condition; y = rms_norm(x) *
+    (1 + scale) + shift in fp32, cast back to x's dtype; the gate multiplies
+    the sublayer's output on the residual."""
+    scale1, shift, gate = mod
     y = F.rms_norm(x.float(), (x.shape[-1],), eps=eps)
-    return torch.addcmul(shift.float(), y, 1.0 + scale.float()).to(x.dtype), gate
+    return torch.addcmul(shift[:, None], y, scale1[:, None]).to(x.dtype), gate[:, None]
 
 
 def signed_sin(sin: torch.Tensor) -> torch.Tensor:
@@ -169,7 +169,8 @@ class ExpertLayer(nn.Module):
         self.down = nn.Linear(cfg.expert_intermediate, h, bias=False)
 
     def forward(self, x, mod_in, mod_post, cos, sin, prefix_k, prefix_v, mask_add):
-        """x [B, S, h]; mod_* [B, 3, h]; cos / sin [B, S, 1, hd], sin with its
+        """x [B, S, h]; mod_* (1 + scale, shift, gate) of the two norms (see
+        ``ada_rms_norm``); cos / sin [B, S, 1, hd], sin with its
         first half negated (``signed_sin``); prefix_k /
         prefix_v [B, kv_heads, L, hd] (keys after RoPE); mask_add [B, 1, L + S]
         (0 or the dtype's lowest value)."""
@@ -233,6 +234,9 @@ class ActionExpert(nn.Module):
         dt = self.action_in_proj.weight.dtype
         b, s, h = x_t.shape[0], cfg.chunk, cfg.expert_hidden
         mods = self.modulation(self.condition(t, target_t)).view(b, self.n_norms, 3, h)
+        # every norm's (1 + scale, shift) in fp32 at once, and its gate
+        scale1, shift, gate = mods[:, :, 0].float() + 1.0, mods[:, :, 1].float(), mods[:, :, 2]
+        mod = [(scale1[:, i], shift[:, i], gate[:, i]) for i in range(self.n_norms)]
         x = self.action_in_proj(x_t)
         # suffix positions continue after the real prefix tokens
         pos = prefix_pad.sum(dim=1, keepdim=True) + torch.arange(s, device=x.device)[None, :]
@@ -246,8 +250,8 @@ class ActionExpert(nn.Module):
         for i, (layer, k, v) in enumerate(zip(self.layers, keys, values)):
             pk = k.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
             pv = v.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
-            x = layer(x, mods[:, 2 * i], mods[:, 2 * i + 1], cos, sin, pk, pv, mask_add)
-        x, _ = ada_rms_norm(x, mods[:, -1], cfg.rms_eps)
+            x = layer(x, mod[2 * i], mod[2 * i + 1], cos, sin, pk, pv, mask_add)
+        x, _ = ada_rms_norm(x, mod[-1], cfg.rms_eps)
         return self.action_out_proj(x[:, -s:])
 
 
