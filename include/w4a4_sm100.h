@@ -300,6 +300,34 @@ int w4a4_gemm_plan(int64_t m, int32_t k, int32_t n_weights, const int32_t* n, in
  * the given limit; the kernel must give up, set its error bit and return. */
 int w4a4_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
+/* ---- bf16 kernels of the config-4 neighbours (SigLIP, the action expert) ----
+ * No counterpart in the reference, whose SnapFlow step (pi05_fast/
+ * snapflow_pi05.py:127-195) runs lerobot's PI05 policy as PyTorch bf16 ops;
+ * each entry point below does in one pass what a chain of those ops does.
+ * All arithmetic fp32, each result rounded once to bf16; row-major,
+ * 16-byte aligned rows. */
+
+/* pi0.5's adaptive RMSNorm: y[r] = x[r] rsqrt(mean(x[r]^2) + eps) *
+ * scale1[b] + shift[b], b = r / rows_per_batch, scale1 = 1 + scale and shift
+ * fp32 rows of h at b * mod_stride floats; x, y bf16 [rows, h] contiguous, h a
+ * multiple of 256 up to 2048. */
+int w4a4_ada_rms_norm_bf16(const void* x, void* y, int64_t rows, int32_t h, int32_t rows_per_batch,
+                           const float* scale1, const float* shift, int64_t mod_stride, float eps,
+                           void* stream);
+
+/* Rotary position embedding in place (transformers' rotate_half form): q
+ * [rows, heads_q, hd] and k [rows, heads_k, hd] (bf16, row strides ldq / ldk
+ * elements), cos / sin bf16 [rows, hd] with each half the same angles; for
+ * i < hd / 2: (x_i, x_{i+hd/2}) -> (x_i c_i - x_{i+hd/2} s_i,
+ * x_{i+hd/2} c_i + x_i s_i).  hd a multiple of 16. */
+int w4a4_rope_qk_bf16(void* q, int64_t ldq, int32_t heads_q, void* k, int64_t ldk, int32_t heads_k,
+                      const void* cos_t, const void* sin_t, int64_t rows, int32_t hd, void* stream);
+
+/* LayerNorm: y = (x - mean) rsqrt(var + eps) w + b per row of x bf16 [rows, h]
+ * (contiguous; h a multiple of 8 up to 2048), w and b bf16 [h]. */
+int w4a4_layer_norm_bf16(const void* x, void* y, int64_t rows, int32_t h, const void* w, const void* b,
+                         float eps, void* stream);
+
 /* Library ABI version (major * 100 + minor). */
 int w4a4_version(void);
 

@@ -52,6 +52,9 @@ EXPORTED_SYMBOLS = (
     "w4a4_pad_rows",
     "w4a4_repack_int8",
     "w4a4_pack_weight",
+    "w4a4_ada_rms_norm_bf16",
+    "w4a4_rope_qk_bf16",
+    "w4a4_layer_norm_bf16",
     "w4a4_last_error",
     "w4a4_device_error",
     "w4a4_set_wait_limit_ns",
@@ -108,6 +111,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.w4a4_pad_rows.argtypes = [vp, c_i32, c_i32, c_i32, vp, vp]
     lib.w4a4_repack_int8.argtypes = [vp, c_i32, vp, vp]
     lib.w4a4_pack_weight.argtypes = [vp, c_i32, c_i64, c_i32, c_i32, c_i32, c_i32, vp, c_i32, vp]
+    lib.w4a4_ada_rms_norm_bf16.argtypes = [vp, vp, c_i64, c_i32, c_i32, vp, vp, c_i64, ctypes.c_float, vp]
+    lib.w4a4_rope_qk_bf16.argtypes = [vp, c_i64, c_i32, vp, c_i64, c_i32, vp, vp, c_i64, c_i32, vp]
+    lib.w4a4_layer_norm_bf16.argtypes = [vp, vp, c_i64, c_i32, vp, vp, ctypes.c_float, vp]
     lib.w4a4_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     lib.w4a4_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_i32]
     lib.w4a4_set_wait_limit_ns.argtypes = [c_u64]

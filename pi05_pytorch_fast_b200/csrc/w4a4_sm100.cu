@@ -26,6 +26,7 @@
 #include "layer.cuh"
 #include "pack.cuh"
 #include "quant.cuh"
+#include "neighbours.cuh"
 
 // Scratch of w4a4_int4_gemm_noalloc: the intermediate activation codes and
 // row scales, as file-scope device arrays (one copy per device, shared by
@@ -535,6 +536,99 @@ int launch_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t
   W4A4_CUDA_TRY(launch_kernel(geglu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
                               static_cast<const __half*>(gate), static_cast<const __half*>(up), ld,
                               static_cast<__half*>(h), ldh, m, n));
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+// ------------------------------------------------------------- config-4 neighbours (bf16)
+int launch_ada_rms_norm_bf16(const void* x, void* y, int64_t rows, int32_t h, int32_t rows_per_batch,
+                             const float* scale1, const float* shift, int64_t mod_stride, float eps,
+                             cudaStream_t stream) {
+  if (rows < 0 || h <= 0 || h % 256 != 0 || h > 2048 || rows_per_batch <= 0 || mod_stride < h)
+    return fail(W4A4_ERR_INVALID, "ada_rms_norm: invalid shape rows=%lld h=%d rows_per_batch=%d "
+                "(h a multiple of 256 up to 2048, mod_stride >= h)", (long long)rows, h, rows_per_batch);
+  if (rows == 0) return ok();
+  if (!x || !y || !scale1 || !shift) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(scale1, 16) || !aligned(shift, 16) || mod_stride % 4)
+    return fail(W4A4_ERR_INVALID, "ada_rms_norm: pointers must be 16-byte aligned, mod_stride a multiple of 4");
+  const int64_t blocks = (rows + kNbThreads / 32 - 1) / (kNbThreads / 32);
+  if (blocks > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "ada_rms_norm: too many rows");
+  const auto go = [&](auto kernel) {
+    return launch_kernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kNbThreads), 0, stream, 1,
+                         static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y),
+                         static_cast<long long>(rows), static_cast<int>(rows_per_batch), scale1, shift,
+                         static_cast<long long>(mod_stride), eps);
+  };
+  cudaError_t e = cudaSuccess;
+  switch (h / 256) {
+    case 1: e = go(ada_rms_norm_bf16_kernel<1>); break;
+    case 2: e = go(ada_rms_norm_bf16_kernel<2>); break;
+    case 3: e = go(ada_rms_norm_bf16_kernel<3>); break;
+    case 4: e = go(ada_rms_norm_bf16_kernel<4>); break;
+    case 5: e = go(ada_rms_norm_bf16_kernel<5>); break;
+    case 6: e = go(ada_rms_norm_bf16_kernel<6>); break;
+    case 7: e = go(ada_rms_norm_bf16_kernel<7>); break;
+    default: e = go(ada_rms_norm_bf16_kernel<8>); break;
+  }
+  W4A4_CUDA_TRY(e);
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int launch_rope_qk_bf16(void* q, int64_t ldq, int32_t heads_q, void* k, int64_t ldk, int32_t heads_k,
+                        const void* cos_t, const void* sin_t, int64_t rows, int32_t hd, cudaStream_t stream) {
+  if (rows < 0 || hd <= 0 || hd % 16 != 0 || heads_q < 0 || heads_k < 0 || heads_q + heads_k == 0 ||
+      ldq < static_cast<int64_t>(heads_q) * hd || ldk < static_cast<int64_t>(heads_k) * hd)
+    return fail(W4A4_ERR_INVALID, "rope_qk: invalid shape rows=%lld hd=%d heads %d + %d (hd a multiple of 16, "
+                "row strides >= heads * hd)", (long long)rows, hd, heads_q, heads_k);
+  if (rows == 0) return ok();
+  if ((heads_q && !q) || (heads_k && !k) || !cos_t || !sin_t)
+    return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if ((heads_q && (!aligned(q, 16) || ldq % 8)) || (heads_k && (!aligned(k, 16) || ldk % 8)) ||
+      !aligned(cos_t, 16) || !aligned(sin_t, 16))
+    return fail(W4A4_ERR_INVALID, "rope_qk: rows must be 16-byte aligned with strides multiples of 8");
+  const int64_t threads = rows * (heads_q + heads_k) * (hd / 16);
+  const int64_t blocks = (threads + kNbThreads - 1) / kNbThreads;
+  if (blocks > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "rope_qk: too many rows");
+  W4A4_CUDA_TRY(launch_kernel(rope_bf16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kNbThreads), 0,
+                              stream, 1, static_cast<__nv_bfloat16*>(q), static_cast<long long>(ldq),
+                              static_cast<int>(heads_q), static_cast<__nv_bfloat16*>(k),
+                              static_cast<long long>(ldk), static_cast<int>(heads_k),
+                              static_cast<const __nv_bfloat16*>(cos_t), static_cast<const __nv_bfloat16*>(sin_t),
+                              static_cast<long long>(rows), static_cast<int>(hd)));
+  W4A4_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int launch_layer_norm_bf16(const void* x, void* y, int64_t rows, int32_t h, const void* w, const void* b,
+                           float eps, cudaStream_t stream) {
+  if (rows < 0 || h <= 0 || h % 8 != 0 || h > 2048)
+    return fail(W4A4_ERR_INVALID, "layer_norm: invalid shape rows=%lld h=%d (h a multiple of 8 up to 2048)",
+                (long long)rows, h);
+  if (rows == 0) return ok();
+  if (!x || !y || !w || !b) return fail(W4A4_ERR_INVALID, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(w, 16) || !aligned(b, 16))
+    return fail(W4A4_ERR_INVALID, "layer_norm: pointers must be 16-byte aligned");
+  const int64_t blocks = (rows + kNbThreads / 32 - 1) / (kNbThreads / 32);
+  if (blocks > 0x7fffffffLL) return fail(W4A4_ERR_UNSUPPORTED, "layer_norm: too many rows");
+  const auto go = [&](auto kernel) {
+    return launch_kernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kNbThreads), 0, stream, 1,
+                         static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y),
+                         static_cast<long long>(rows), static_cast<int>(h),
+                         static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(b), eps);
+  };
+  cudaError_t e = cudaSuccess;
+  switch ((h + 255) / 256) {
+    case 1: e = go(layer_norm_bf16_kernel<1>); break;
+    case 2: e = go(layer_norm_bf16_kernel<2>); break;
+    case 3: e = go(layer_norm_bf16_kernel<3>); break;
+    case 4: e = go(layer_norm_bf16_kernel<4>); break;
+    case 5: e = go(layer_norm_bf16_kernel<5>); break;
+    case 6: e = go(layer_norm_bf16_kernel<6>); break;
+    case 7: e = go(layer_norm_bf16_kernel<7>); break;
+    default: e = go(layer_norm_bf16_kernel<8>); break;
+  }
+  W4A4_CUDA_TRY(e);
   W4A4_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -1171,6 +1265,24 @@ int w4a4_prefix_attention(void* q, int64_t ldq, const void* k, int64_t ldk, cons
 int w4a4_geglu(const void* gate, const void* up, int64_t m, int32_t n, int64_t ld, void* h,
                int64_t ldh, void* stream) {
   return launch_geglu(gate, up, m, n, ld, h, ldh, static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_ada_rms_norm_bf16(const void* x, void* y, int64_t rows, int32_t h, int32_t rows_per_batch,
+                           const float* scale1, const float* shift, int64_t mod_stride, float eps,
+                           void* stream) {
+  return launch_ada_rms_norm_bf16(x, y, rows, h, rows_per_batch, scale1, shift, mod_stride, eps,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_rope_qk_bf16(void* q, int64_t ldq, int32_t heads_q, void* k, int64_t ldk, int32_t heads_k,
+                      const void* cos_t, const void* sin_t, int64_t rows, int32_t hd, void* stream) {
+  return launch_rope_qk_bf16(q, ldq, heads_q, k, ldk, heads_k, cos_t, sin_t, rows, hd,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int w4a4_layer_norm_bf16(const void* x, void* y, int64_t rows, int32_t h, const void* w, const void* b,
+                         float eps, void* stream) {
+  return launch_layer_norm_bf16(x, y, rows, h, w, b, eps, static_cast<cudaStream_t>(stream));
 }
 
 int w4a4_quant_segments(const void* x, int64_t m, int32_t k, int32_t seg, int64_t ld,

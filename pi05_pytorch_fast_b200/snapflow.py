@@ -52,6 +52,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import _native as nat
 from . import prefix_lm as plm
 
 
@@ -132,14 +133,43 @@ def rope_tables(positions: torch.Tensor, head_dim: int, theta: float, dtype) -> 
     return emb.cos().to(dtype), emb.sin().to(dtype)
 
 
+def _on_kernels(x: torch.Tensor) -> bool:
+    """bf16 CUDA tensors go through the library's neighbour kernels; the
+    PyTorch forms below serve CPU tensors (the small-shape CPU tests)."""
+    return x.is_cuda and x.dtype == torch.bfloat16
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
 def ada_rms_norm(x: torch.Tensor, mod: tuple, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
     """pi0.5's adaptive RMSNorm: mod = (1 + scale, shift) in fp32 and gate,
     each [B, h], from a Linear of the flow-time condition; y = rms_norm(x) *
     (1 + scale) + shift in fp32, cast back to x's dtype; the gate multiplies
-    the sublayer's output on the residual."""
+    the sublayer's output on the residual.  x [B, S, h]."""
     scale1, shift, gate = mod
+    if _on_kernels(x):
+        b, s, h = x.shape
+        x = x.contiguous()
+        y = torch.empty_like(x)
+        nat.check(nat.lib().w4a4_ada_rms_norm_bf16(x.data_ptr(), y.data_ptr(), b * s, h, s, scale1.data_ptr(),
+                                                   shift.data_ptr(), scale1.stride(0), eps, _stream()))
+        return y, gate[:, None]
     y = F.rms_norm(x.float(), (x.shape[-1],), eps=eps)
     return torch.addcmul(shift[:, None], y, scale1[:, None]).to(x.dtype), gate[:, None]
+
+
+def layer_norm(ln: nn.LayerNorm, x: torch.Tensor) -> torch.Tensor:
+    """``ln(x)``, through the library's LayerNorm kernel for bf16 on CUDA."""
+    if _on_kernels(x) and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048:
+        x = x.contiguous()
+        y = torch.empty_like(x)
+        h = x.shape[-1]
+        nat.check(nat.lib().w4a4_layer_norm_bf16(x.data_ptr(), y.data_ptr(), x.numel() // h, h,
+                                                 ln.weight.data_ptr(), ln.bias.data_ptr(), ln.eps, _stream()))
+        return y
+    return ln(x)
 
 
 def signed_sin(sin: torch.Tensor) -> torch.Tensor:
@@ -168,22 +198,30 @@ class ExpertLayer(nn.Module):
         self.up = nn.Linear(h, cfg.expert_intermediate, bias=False)
         self.down = nn.Linear(cfg.expert_intermediate, h, bias=False)
 
-    def forward(self, x, mod_in, mod_post, cos, sin, prefix_k, prefix_v, mask_add):
+    def forward(self, x, mod_in, mod_post, rope, prefix_k, prefix_v, mask_add):
         """x [B, S, h]; mod_* (1 + scale, shift, gate) of the two norms (see
-        ``ada_rms_norm``); cos / sin [B, S, 1, hd], sin with its
-        first half negated (``signed_sin``); prefix_k /
-        prefix_v [B, kv_heads, L, hd] (keys after RoPE); mask_add [B, 1, L + S]
-        (0 or the dtype's lowest value)."""
+        ``ada_rms_norm``); rope = (cos, sin) [B * S, hd] for the RoPE kernel,
+        or on CPU (cos, sin with its first half negated (``signed_sin``)), each
+        [B, S, 1, hd]; prefix_k / prefix_v [B, kv_heads, L, hd] (keys after
+        RoPE); mask_add [B, 1, L + S] (0 or the dtype's lowest value)."""
         b, s, _ = x.shape
         kvh, g, hd = self.kv_heads, self.heads // self.kv_heads, self.hd
         n, g1 = ada_rms_norm(x, mod_in, self.eps)
-        q = self.q(n).view(b, s, self.heads, hd)
-        k = self.k(n).view(b, s, kvh, hd)
-        v = self.v(n).view(b, s, kvh, hd)
-        # x cos + rotate_half(x) sin, with rotate_half(x) = roll(x, hd / 2) times
-        # the sign carried by sin (negated first half)
-        q = torch.addcmul(q * cos, torch.roll(q, hd // 2, dims=-1), sin)
-        k = torch.addcmul(k * cos, torch.roll(k, hd // 2, dims=-1), sin)
+        q, k, v = self.q(n), self.k(n), self.v(n)
+        if _on_kernels(q):
+            # q and k rotated in place (the Linear outputs are contiguous rows)
+            nat.check(nat.lib().w4a4_rope_qk_bf16(q.data_ptr(), self.heads * hd, self.heads, k.data_ptr(),
+                                                  kvh * hd, kvh, rope[0].data_ptr(), rope[1].data_ptr(), b * s,
+                                                  hd, _stream()))
+            q, k = q.view(b, s, self.heads, hd), k.view(b, s, kvh, hd)
+        else:
+            # x cos + rotate_half(x) sin, with rotate_half(x) = roll(x, hd / 2)
+            # times the sign carried by sin (negated first half)
+            cos, sin = rope
+            q, k = q.view(b, s, self.heads, hd), k.view(b, s, kvh, hd)
+            q = torch.addcmul(q * cos, torch.roll(q, hd // 2, dims=-1), sin)
+            k = torch.addcmul(k * cos, torch.roll(k, hd // 2, dims=-1), sin)
+        v = v.view(b, s, kvh, hd)
         # rows (KV head, query head of the group, token); keys [prefix ; suffix]
         q = q.view(b, s, kvh, g, hd).permute(0, 2, 3, 1, 4).reshape(b * kvh, g * s, hd)
         k = torch.cat((prefix_k, k.transpose(1, 2)), dim=2).view(b * kvh, -1, hd)
@@ -235,13 +273,18 @@ class ActionExpert(nn.Module):
         b, s, h = x_t.shape[0], cfg.chunk, cfg.expert_hidden
         mods = self.modulation(self.condition(t, target_t)).view(b, self.n_norms, 3, h)
         # every norm's (1 + scale, shift) in fp32 at once, and its gate
-        scale1, shift, gate = mods[:, :, 0].float() + 1.0, mods[:, :, 1].float(), mods[:, :, 2]
+        scale1 = (mods[:, :, 0].float() + 1.0).contiguous()
+        shift, gate = mods[:, :, 1].float().contiguous(), mods[:, :, 2]
         mod = [(scale1[:, i], shift[:, i], gate[:, i]) for i in range(self.n_norms)]
         x = self.action_in_proj(x_t)
         # suffix positions continue after the real prefix tokens
         pos = prefix_pad.sum(dim=1, keepdim=True) + torch.arange(s, device=x.device)[None, :]
         cos, sin = rope_tables(pos, cfg.head_dim, cfg.rope_theta, dt)
-        cos, sin = cos.transpose(1, 2), signed_sin(sin.transpose(1, 2))
+        if _on_kernels(x):
+            rope = (cos[:, 0].reshape(b * s, cfg.head_dim).contiguous(),
+                    sin[:, 0].reshape(b * s, cfg.head_dim).contiguous())
+        else:
+            rope = (cos.transpose(1, 2), signed_sin(sin.transpose(1, 2)))
         # the prefix's real tokens and every suffix token are visible
         visible = torch.cat((prefix_pad, torch.ones((b, s), dtype=torch.bool, device=x.device)), dim=1)
         mask_add = torch.zeros(visible.shape, dtype=dt, device=x.device).masked_fill_(
@@ -250,7 +293,7 @@ class ActionExpert(nn.Module):
         for i, (layer, k, v) in enumerate(zip(self.layers, keys, values)):
             pk = k.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
             pv = v.view(b, -1, kvh, hd).transpose(1, 2).to(dt)
-            x = layer(x, mod[2 * i], mod[2 * i + 1], cos, sin, pk, pv, mask_add)
+            x = layer(x, mod[2 * i], mod[2 * i + 1], rope, pk, pv, mask_add)
         x, _ = ada_rms_norm(x, mod[-1], cfg.rms_eps)
         return self.action_out_proj(x[:, -s:])
 
@@ -305,12 +348,12 @@ class SiglipTower(nn.Module):
         n, t, h = x.shape
         d = h // self.heads
         for i in range(len(self.qkv)):
-            qkv = self.qkv[i](self.ln1[i](x)).view(n, t, 3, self.heads, d)
+            qkv = self.qkv[i](layer_norm(self.ln1[i], x)).view(n, t, 3, self.heads, d)
             q, k, v = (qkv[:, :, j].transpose(1, 2) for j in range(3))
             a = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(n, t, h)
             x = x + self.out[i](a)
-            x = x + self.fc2[i](F.gelu(self.fc1[i](self.ln2[i](x)), approximate="tanh"))
-        return self.post_ln(x)
+            x = x + self.fc2[i](F.gelu(self.fc1[i](layer_norm(self.ln2[i], x)), approximate="tanh"))
+        return layer_norm(self.post_ln, x)
 
 
 class VisionPrefix(nn.Module):

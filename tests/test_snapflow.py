@@ -164,7 +164,92 @@ def test_vision_prefix_assembles_cameras_empty_camera_and_language():
     assert torch.equal(pad[:, -TINY.lang_tokens:], mask)
 
 
+def test_neighbour_kernels_check_their_arguments():
+    """Shape and alignment checks run on the host, before any device work."""
+    from pi05_pytorch_fast_b200 import _native as nat
+
+    lib = nat.lib()
+    fake = 1 << 40
+
+    def err(rc):
+        assert rc != nat.W4A4_OK
+        return nat.last_error()
+
+    assert "multiple of 256" in err(lib.w4a4_ada_rms_norm_bf16(fake, fake, 4, 1000, 2, fake, fake, 1000, 1e-6, None))
+    assert "mod_stride" in err(lib.w4a4_ada_rms_norm_bf16(fake, fake, 4, 1024, 2, fake, fake, 512, 1e-6, None))
+    assert "aligned" in err(lib.w4a4_ada_rms_norm_bf16(fake + 2, fake, 4, 1024, 2, fake, fake, 1024, 1e-6, None))
+    assert lib.w4a4_ada_rms_norm_bf16(None, None, 0, 1024, 1, None, None, 1024, 1e-6, None) == nat.W4A4_OK
+    assert "multiple of 16" in err(lib.w4a4_rope_qk_bf16(fake, 2040, 8, fake, 255, 1, fake, fake, 4, 255, None))
+    assert "strides" in err(lib.w4a4_rope_qk_bf16(fake, 1024, 8, fake, 256, 1, fake, fake, 4, 256, None))
+    assert "aligned" in err(lib.w4a4_rope_qk_bf16(fake, 2052, 8, fake, 256, 1, fake, fake, 4, 256, None))
+    assert "multiple of 8" in err(lib.w4a4_layer_norm_bf16(fake, fake, 4, 1150, fake, fake, 1e-6, None))
+    assert "null" in err(lib.w4a4_layer_norm_bf16(fake, None, 4, 1152, fake, fake, 1e-6, None))
+
+
 # ----------------------------------------------------------------------------- B200
+def _bf16_close(got: torch.Tensor, ref: torch.Tensor):
+    """Within one bf16 rounding of an fp64 reference (plus fp32 reduction
+    order): |got - ref| <= 2^-7 |ref| + 1e-6."""
+    got, ref = got.double(), ref.double()
+    bad = (got - ref).abs() > ref.abs() * 2.0 ** -7 + 1e-6
+    assert not bad.any(), f"{int(bad.sum())} of {bad.numel()} values off"
+
+
+@pytest.mark.gpu
+def test_ada_rms_norm_kernel_matches_the_formula():
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(11)
+    b, s, h, n = 3, 50, 1024, 5
+    x = (torch.randn(b, s, h, device=dev, generator=g) * 3).bfloat16()
+    scale1 = (1 + torch.randn(b, n, h, device=dev, generator=g) * 0.3).contiguous()
+    shift = (torch.randn(b, n, h, device=dev, generator=g) * 0.5).contiguous()
+    gate = torch.randn(b, n, h, device=dev, generator=g).bfloat16()
+    y, gt = sf.ada_rms_norm(x, (scale1[:, 2], shift[:, 2], gate[:, 2]), 1e-6)
+    xd = x.double()
+    ref = xd * torch.rsqrt(xd.pow(2).mean(-1, keepdim=True) + 1e-6) * scale1[:, 2, None].double() \
+        + shift[:, 2, None].double()
+    assert y.dtype == torch.bfloat16 and torch.equal(gt, gate[:, 2, None])
+    _bf16_close(y, ref)
+
+
+@pytest.mark.gpu
+def test_rope_kernel_matches_rotate_half():
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(12)
+    rows, hq, hk, hd = 100, 8, 1, 256
+    q = torch.randn(rows, hq * hd, device=dev, generator=g).bfloat16()
+    k = torch.randn(rows, hk * hd, device=dev, generator=g).bfloat16()
+    pos = torch.arange(rows, device=dev)[None] + 700
+    cos, sin = sf.rope_tables(pos, hd, 10000.0, torch.bfloat16)
+    cos, sin = cos[0, 0].contiguous(), sin[0, 0].contiguous()
+    q0, k0 = q.clone(), k.clone()
+    from pi05_pytorch_fast_b200 import _native as nat
+
+    nat.check(nat.lib().w4a4_rope_qk_bf16(q.data_ptr(), hq * hd, hq, k.data_ptr(), hk * hd, hk, cos.data_ptr(),
+                                          sin.data_ptr(), rows, hd, torch.cuda.current_stream().cuda_stream))
+    for got, x0, heads in ((q, q0, hq), (k, k0, hk)):
+        xd = x0.double().view(rows, heads, hd)
+        ref = xd * cos.double()[:, None] + sf.rotate_half(xd) * sin.double()[:, None]
+        _bf16_close(got.view(rows, heads, hd), ref)
+
+
+@pytest.mark.gpu
+def test_layer_norm_kernel_matches_torch():
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(13)
+    ln = torch.nn.LayerNorm(1152, eps=1e-6).to(dev)
+    with torch.no_grad():
+        ln.weight.normal_(1.0, 0.2, generator=g)
+        ln.bias.normal_(0.0, 0.2, generator=g)
+    ln = ln.bfloat16()
+    x = (torch.randn(2, 300, 1152, device=dev, generator=g) * 2 + 0.5).bfloat16()
+    with torch.no_grad():
+        y = sf.layer_norm(ln, x)
+        ref = F.layer_norm(x.double(), (1152,), ln.weight.double(), ln.bias.double(), 1e-6)
+    _bf16_close(y, ref)
+
+
+
 @pytest.fixture(scope="module")
 def policy():
     dev = torch.device("cuda:0")
